@@ -1,0 +1,282 @@
+/*
+ * stageml_b200.h -- C ABI of the B200 (sm_100a) implementation of StageML's
+ * request-time multi-tenant MoE-LoRA residual program.
+ *
+ * Plain C: device pointers, sizes, dtype codes and a CUDA stream handle. No
+ * torch types. Every entry point is asynchronous on `stream`, allocates
+ * nothing (scratch comes from the caller's `workspace`, sized by the matching
+ * *_workspace_bytes query) and returns STAGEML_OK or an error code whose text is
+ * available from stageml_last_error() on the calling thread. Argument checks
+ * happen on the host before anything is launched; data-dependent faults found
+ * on the device (an expert id or tenant id out of range, a bounded wait that
+ * expired) are recorded in the caller-supplied device status word instead of
+ * trapping, and the offending pair or row is skipped.
+ *
+ * Reference interfaces replaced (paths inside the uwm-se/stageML project):
+ *   csrc/stageml_residual_op.cpp:8-19        residual_moe custom op (skeleton that throws)
+ *   stageml/custom_op_registry.py:23-37     _fallback_moe (per-token Python loop)
+ *   stageml/moe_lora_layers.py:45-142       DynamicMoELoRALayer / MaterializedMoELoRALayer
+ *   stageml/moe_lora_layers.py:178-183      normalize_routing_weights
+ *   stageml/adapter_bank.py:42-135          DynamicLoRALinear / StageMLAdapterBankLinear / OnTheFlyMergeLinear
+ *   stageml/adapter_cache.py:37-100         StageMLCostBasedAdapterCache
+ *   stageml/triton_generator.py:175-191     materialize_residual_weight
+ *   benchmarks/multitenant_bta_system_bench.py:379-443   RequestExecutor (SwiGLU expert MLP + LoRA)
+ *   benchmarks/real_moe_lora_residual_bench.py:360-386   make_routing (softmax / top-k / renorm)
+ *   benchmarks/triton_lora_equivalence_check.py:11-22    single LoRA linear, [in,out] layout
+ */
+#ifndef STAGEML_B200_H
+#define STAGEML_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* stageml_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+/* Return codes. */
+enum {
+  STAGEML_OK = 0,
+  STAGEML_ERR_INVALID_ARG = 1, /* shape, dtype, pointer or alignment rejected on the host */
+  STAGEML_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed */
+  STAGEML_ERR_UNSUPPORTED = 3, /* valid request this build does not implement */
+  STAGEML_ERR_WORKSPACE = 4    /* workspace pointer NULL or smaller than the query says */
+};
+
+/* Element type codes. */
+enum {
+  STAGEML_F32 = 0,
+  STAGEML_BF16 = 1,
+  STAGEML_F16 = 2,
+  STAGEML_E4M3 = 3, /* float8 e4m3fn, weights only, with fp32 per-output-channel scales */
+  STAGEML_I32 = 4,
+  STAGEML_I64 = 5
+};
+
+/* Device status words (written to `status` by kernels, 0 = ok). */
+enum {
+  STAGEML_DEV_OK = 0,
+  STAGEML_DEV_TIMEOUT = 101,   /* 101..104: a bounded wait in a pipelined kernel expired */
+  STAGEML_DEV_BAD_INDEX = 110  /* an expert / tenant / group id was out of range; that item was skipped */
+};
+
+/* Text of the last error reported on this thread ("" if none). */
+const char* stageml_last_error(void);
+/* ABI version of this library (bumped on any signature or struct change). */
+int stageml_abi_version(void);
+/* sizeof() of the public structs, so bindings can check their mirrors. 0 = plan, 1 = moe args, 2 = lora linear args. */
+size_t stageml_struct_size(int which);
+
+/* ------------------------------------------------------------------ routing
+ * Replaces make_routing (benchmarks/real_moe_lora_residual_bench.py:360-386)
+ * followed by normalize_routing_weights (stageml/moe_lora_layers.py:178-183):
+ *   logits = float(x) . gate_w^T   (fp32 accumulate)       [T, E]
+ *   probs  = softmax(logits)                                [T, E]
+ *   ids, weights = top-k(probs), larger first, ties -> lower expert index
+ *   if renormalize: weights /= max(sum(weights), 1e-12)
+ * x: [T, H] (F32/BF16/F16), gate_w: [E, H] fp32. E <= 256, k <= 8, k <= E.
+ * logits_out may be NULL. ids_out int32 [T, k], weights_out fp32 [T, k].
+ */
+int stageml_route_topk(const void* x, int x_dtype, const float* gate_w, int T, int H, int E, int k,
+                       int renormalize, float* logits_out, int32_t* ids_out, float* weights_out,
+                       stageml_stream_t stream);
+
+/* The softmax / top-k / renorm half of stageml_route_topk on given fp32 logits [T, E]. */
+int stageml_topk_from_logits(const float* logits, int T, int E, int k, int renormalize, int32_t* ids_out,
+                             float* weights_out, stageml_stream_t stream);
+
+/* -------------------------------------------------------------- permutation
+ * Token -> expert permutation (the grouping that RequestExecutor.dynamic_one
+ * does with one torch.nonzero per (slot, expert),
+ * benchmarks/multitenant_bta_system_bench.py:401-406).
+ *
+ * The T*(k+n_shared) pairs (t, j) -- j < k routed slot with expert ids[t, j]
+ * and weight w[t, j]; j >= k always-on shared expert E + (j - k) with weight
+ * 1 -- are stably sorted by key (expert, tenant) (tenant -1 sorts first), and
+ * each expert's segment is padded to a multiple of 128 rows. Pair index
+ * p = t*(k+n_shared) + j is the stable tie order. With group_by_tenant != 0
+ * the grouping key's expert part is tenant*E_total + expert (one weight group
+ * per (adapter, expert), as in MaterializedMoELoRALayer) and rows carry no
+ * LoRA tenant.
+ */
+typedef struct stageml_moe_plan {
+  int32_t* row_token;      /* [rows_cap] token of each padded row, -1 = padding */
+  int32_t* row_tenant;     /* [rows_cap] LoRA tenant of each row, -1 = none / padding */
+  float* row_weight;       /* [rows_cap] routing weight of each row, 0 for padding */
+  int32_t* row_pair;       /* [rows_cap] pair index of each row, -1 = padding */
+  int32_t* pair_row;       /* [T*(k+n_shared)] padded row of each pair, -1 = dropped (bad id) */
+  int32_t* tile_group;     /* [rows_cap/128] weight group (expert) of each 128-row tile */
+  int32_t* group_offsets;  /* [n_groups+1] padded row offset of each group's segment */
+  int32_t* group_counts;   /* [n_groups] real rows per group */
+  int32_t* num_tiles;      /* [1] number of 128-row tiles in use */
+  int64_t rows_cap;        /* capacity of the row arrays; >= stageml_plan_rows_cap(...) */
+} stageml_moe_plan;
+
+/* Row capacity needed for P pairs spread over n_groups groups (each padded to 128). */
+int64_t stageml_plan_rows_cap(int64_t num_pairs, int n_groups);
+size_t stageml_permute_workspace_bytes(int T, int k, int n_shared, int n_experts_total, int n_tenants,
+                                       int group_by_tenant);
+/* ids: [T, k] int32 or int64 (ids_dtype); weights: [T, k] F32/BF16/F16 or NULL (= 1);
+ * tenant_ids: [T] int32 or NULL (= -1). n_experts_total includes the n_shared shared experts. */
+int stageml_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype,
+                    const int32_t* tenant_ids, int T, int k, int n_shared, int n_experts_total, int n_tenants,
+                    int group_by_tenant, const stageml_moe_plan* plan, int32_t* status, void* workspace,
+                    size_t workspace_bytes, stageml_stream_t stream);
+
+/* ------------------------------------------------------- MoE-LoRA layer
+ * The request-time residual program for one MoE FFN layer (R1..R5 + combine):
+ *   route (when topk_ids == NULL) -> permute -> gather + LoRA shrink ->
+ *   grouped gate/up GEMM with LoRA expand and SwiGLU in the epilogue ->
+ *   LoRA shrink of h -> grouped down GEMM with LoRA expand and routing weight
+ *   in the epilogue -> combine.
+ * For token t: out[t] = sum_j w[t,j] * down_e( silu(g) * u ), e = expert of slot j,
+ *   g = x W1_e^T + s_a (x A1[a,e]^T) B1[a,e]^T,   W1_e = gate_up[e, :I]
+ *   u = x W3_e^T + s_a (x A3[a,e]^T) B3[a,e]^T,   W3_e = gate_up[e, I:]
+ *   down_e(h) = h W2_e^T + s_a (h A2[a,e]^T) B2[a,e]^T,  a = tenant_ids[t]
+ * This is RequestExecutor.dynamic_one (benchmarks/multitenant_bta_system_bench.py:398-414,
+ * LoRA on w1) with the same LoRA term on w3 and w2 as DynamicMoELoRALayer.forward
+ * (stageml/moe_lora_layers.py:85-89); with all LoRA pointers NULL it is exactly
+ * _fallback_moe (stageml/custom_op_registry.py:23-37), i.e. the residual_moe op.
+ * Tenants with a folded (materialized) gate_up simply pass tenant -1 and their own
+ * gate_up, as bta_one does (:416-433).
+ *
+ * Layouts (row-major, contiguous):
+ *   x [T,H]; gate_up [E_tot, 2I, H]; down [E_tot, H, I]   (E_tot = E + n_shared)
+ *   gate_up_scale [E_tot, 2I] / down_scale [E_tot, H] fp32 when weight_dtype == E4M3
+ *   lora_a13 [n_tenants, E_tot, 2r, H] rows [0,r) = A1, [r,2r) = A3
+ *   lora_b13 [n_tenants, E_tot, 2I, r] rows [0,I) = B1, [I,2I) = B3
+ *   lora_a2 [n_tenants, E_tot, r, I]; lora_b2 [n_tenants, E_tot, H, r]
+ *   lora_scale [n_tenants] fp32 (alpha / rank)
+ * r must be a multiple of 8 and <= 32 (zero-pad A rows / B columns to get there).
+ * H and I must be multiples of 8 (16-byte TMA row pitch).
+ */
+typedef struct stageml_moe_args {
+  int T, H, I, E, k, n_shared;
+  int act_dtype;         /* BF16 or F16: x, out, LoRA factors */
+  int weight_dtype;      /* == act_dtype, or E4M3 */
+  const void* x;
+  const void* topk_ids;  /* [T,k] int32/int64, or NULL to route with router_w */
+  int ids_dtype;
+  const void* topk_weights; /* [T,k] F32/BF16/F16 (used as given); ignored when routing here */
+  int weights_dtype;
+  const float* router_w; /* [E,H] fp32, used when topk_ids == NULL */
+  int renormalize;       /* routing here: renormalize the top-k weights */
+  const int32_t* tenant_ids; /* [T] or NULL */
+  int n_tenants;
+  int rank;              /* 0 = no LoRA */
+  const void* gate_up;
+  const void* down;
+  const float* gate_up_scale;
+  const float* down_scale;
+  const void* lora_a13;  /* NULL = no LoRA on w1/w3 */
+  const void* lora_b13;
+  const void* lora_a2;   /* NULL = no LoRA on w2 */
+  const void* lora_b2;
+  const float* lora_scale;
+  void* out;             /* [T,H] act_dtype */
+  int32_t* status;       /* device status word, may be NULL */
+  const stageml_moe_plan* plan_out; /* optional: keep the permutation in caller memory */
+} stageml_moe_args;
+
+size_t stageml_moe_workspace_bytes(const stageml_moe_args* args);
+int stageml_moe_forward(const stageml_moe_args* args, void* workspace, size_t workspace_bytes,
+                        stageml_stream_t stream);
+
+/* The 5-argument residual_moe op of csrc/stageml_residual_op.cpp:8-19 with the
+ * semantics of _fallback_moe (stageml/custom_op_registry.py:23-37):
+ *   out[t] = sum_j w[t,j] * down[e] . (silu(gate_up[e,:I] . x_t) * gate_up[e,I:] . x_t), e = ids[t,j].
+ * hidden [T,H] BF16/F16, gate_up [E,2I,H], down [E,H,I] same dtype, topk_weights [T,k]
+ * (F32/BF16/F16), topk_ids [T,k] (I32/I64). out [T,H] hidden dtype. */
+size_t stageml_residual_moe_workspace_bytes(int T, int H, int I, int E, int k);
+int stageml_residual_moe(const void* hidden, const void* gate_up, const void* down, const void* topk_weights,
+                         int weights_dtype, const void* topk_ids, int ids_dtype, int T, int H, int I, int E,
+                         int k, int dtype, void* out, int32_t* status, void* workspace,
+                         size_t workspace_bytes, stageml_stream_t stream);
+
+/* ------------------------------------------- MoE single-linear LoRA layer
+ * DynamicMoELoRALayer.forward (stageml/moe_lora_layers.py:63-90):
+ *   out[t] = sum_j w[t,j] * (x_t W[e]^T + bias[e] + s_a (x_t A[a,e]^T) B[a,e]^T)
+ * and, with lora == NULL and group_by_tenant = 1 on merged weights
+ * [n_adapters*E, N, K], MaterializedMoELoRALayer.forward (:117-142).
+ * x [T,K]; weight [G, N, K]; bias [E, N] or NULL; lora_a [n_tenants, E, r, K];
+ * lora_b [n_tenants, E, N, r]. K, N multiples of 8. */
+size_t stageml_moe_linear_workspace_bytes(int T, int K, int N, int E, int k, int group_by_tenant, int n_tenants,
+                                          int rank);
+int stageml_moe_linear(const void* x, const void* weight, const void* bias, const void* topk_ids, int ids_dtype,
+                       const void* topk_weights, int weights_dtype, const int32_t* tenant_ids, int T, int K, int N,
+                       int E, int k, int group_by_tenant, int n_tenants, int rank, const void* lora_a,
+                       const void* lora_b, const float* lora_scale, int dtype, void* out, int32_t* status,
+                       void* workspace, size_t workspace_bytes, stageml_stream_t stream);
+
+/* ---------------------------------------------------- stage-0 LoRA fold
+ * W' = W + scale * L . R for `batch` independent matrices (R7):
+ *   layout 0 ([out,in], StageML's layout): W [out,in], L = B [out,r], R = A [r,in]
+ *     (materialize_residual_weight, stageml/triton_generator.py:175-191;
+ *      StageMLAdapterBankLinear.__init__, stageml/adapter_bank.py:90-94;
+ *      MaterializedMoELoRALayer.__init__ einsum("eor,eri->eoi"), stageml/moe_lora_layers.py:104-110)
+ *   layout 1 ([in,out]): W [in,out], L = A [in,r], R = B [r,out]
+ *     (the folded single LoRA x(W + sAB), benchmarks/triton_lora_equivalence_check.py:11-22)
+ * Matrix b reads W + b*w_batch_stride, A + b*a_batch_stride, B + b*b_batch_stride
+ * (element strides; 0 broadcasts one W over every adapter) and writes
+ * out + b*rows*cols. scale[b] per matrix. dtype F32 (fp32 FMA, no TF32), BF16 or F16.
+ * out may alias W only when w_batch_stride == rows*cols. */
+int stageml_lora_fold(const void* W, const void* A, const void* B, const float* scale, int batch, int rows,
+                      int cols, int rank, int layout, int64_t w_batch_stride, int64_t a_batch_stride,
+                      int64_t b_batch_stride, int dtype, void* out, stageml_stream_t stream);
+
+/* ------------------------------------------- multi-tenant dense LoRA linear
+ * Mixed-adapter batch y = x W_g^T + bias + s_a (x A_a^T) B_a^T per row (R8):
+ *   row_group[m] selects the weight (0 = base W, g > 0 = folded W'), row_tenant[m]
+ *   selects the dynamic adapter (-1 = none).
+ * DynamicLoRALinear.forward (stageml/adapter_bank.py:58-69): all rows group 0 + tenant;
+ * StageMLAdapterBankLinear.forward (:101-109): group = adapter + 1, no tenant;
+ * StageMLCostBasedAdapterCache.forward (stageml/adapter_cache.py:83-100): cached
+ * adapters by group, the others by tenant.
+ * x [M,K]; w_bank [n_groups, N, K]; bias [N] or NULL; lora_a [n_tenants, r, K];
+ * lora_b [n_tenants, N, r]; lora_scale [n_tenants]. K, N multiples of 8. */
+typedef struct stageml_lora_linear_args {
+  int M, K, N;
+  int dtype;              /* BF16 or F16 */
+  const void* x;
+  const void* w_bank;
+  int n_groups;
+  const void* bias;
+  const int32_t* row_group;   /* NULL = all rows group 0 */
+  const int32_t* row_tenant;  /* NULL = no LoRA */
+  int n_tenants;
+  int rank;
+  const void* lora_a;
+  const void* lora_b;
+  const float* lora_scale;
+  void* y;                /* [M,N] */
+  int32_t* status;
+} stageml_lora_linear_args;
+
+size_t stageml_lora_linear_workspace_bytes(const stageml_lora_linear_args* args);
+int stageml_lora_linear(const stageml_lora_linear_args* args, void* workspace, size_t workspace_bytes,
+                        stageml_stream_t stream);
+
+/* ---------------------------------------------- single LoRA linear, fp32
+ * Config-1 form with W [in,out] (benchmarks/triton_lora_equivalence_check.py:11-22,
+ * stageml/peft_bridge.py:59-63 transposed): y = x W + scale (x A) B, x [M,in],
+ * A [in,r], B [r,out]; A == NULL gives the folded form y = x W'. fp32 FMA only.
+ * M <= 16. */
+size_t stageml_lora_gemv_f32_workspace_bytes(int M, int in_features, int out_features, int rank);
+int stageml_lora_gemv_f32(const float* x, const float* W, const float* A, const float* B, float scale, int M,
+                          int in_features, int out_features, int rank, float* y, void* workspace,
+                          size_t workspace_bytes, stageml_stream_t stream);
+
+/* ------------------------------------------------------- FP8 weights (R6)
+ * Per-output-channel e4m3 quantization of row-major weights [rows, cols]:
+ * scale[r] = max(|w[r,:]|) / 448 (1 when the row is all zero), q = e4m3(w / scale)
+ * with round-to-nearest-even and saturation to +-448. Input F32/BF16/F16. */
+int stageml_quantize_e4m3_rows(const void* w, int dtype, int64_t rows, int64_t cols, uint8_t* q_out,
+                               float* scale_out, stageml_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STAGEML_B200_H */

@@ -1,0 +1,690 @@
+// extern "C" entry points of libstageml_b200.so (include/stageml_b200.h).
+// Each entry validates its arguments on the host, carves its scratch from the
+// caller's workspace and launches the kernels of the path on `stream`.
+#include <algorithm>
+
+#include "common.cuh"
+#include "grouped_gemm.cuh"
+#include "host_util.h"
+#include "kernels.h"
+
+namespace sb {
+namespace {
+
+constexpr int kAbiVersion = 1;
+
+// Bump allocator over the caller's workspace; with base == nullptr it only
+// measures (the *_workspace_bytes queries run the same carve).
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <typename T>
+  T* take(size_t n) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+  void* take_bytes(size_t n) { return take<uint8_t>(n); }
+};
+
+inline size_t esize(int dtype) {
+  switch (dtype) {
+    case STAGEML_F32:
+    case STAGEML_I32:
+      return 4;
+    case STAGEML_BF16:
+    case STAGEML_F16:
+      return 2;
+    case STAGEML_E4M3:
+      return 1;
+    case STAGEML_I64:
+      return 8;
+    default:
+      return 0;
+  }
+}
+
+inline bool is16(int dtype) { return dtype == STAGEML_BF16 || dtype == STAGEML_F16; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+void carve_plan(Carver& c, int64_t P, int n_groups, stageml_moe_plan* plan) {
+  const int64_t rows_cap = stageml_plan_rows_cap(P, n_groups);
+  plan->rows_cap = rows_cap;
+  plan->row_token = c.take<int32_t>(rows_cap);
+  plan->row_tenant = c.take<int32_t>(rows_cap);
+  plan->row_weight = c.take<float>(rows_cap);
+  plan->row_pair = c.take<int32_t>(rows_cap);
+  plan->pair_row = c.take<int32_t>(std::max<int64_t>(P, 1));
+  plan->tile_group = c.take<int32_t>(rows_cap / 128);
+  plan->group_offsets = c.take<int32_t>(n_groups + 1);
+  plan->group_counts = c.take<int32_t>(n_groups);
+  plan->num_tiles = c.take<int32_t>(1);
+}
+
+// ------------------------------------------------------------------ MoE layer
+struct MoeBuffers {
+  stageml_moe_plan plan;
+  float* logits = nullptr;
+  int32_t* ids = nullptr;
+  float* weights = nullptr;
+  void* perm_scratch = nullptr;
+  void* xp = nullptr;    // [rows_cap, H]; reused for Y [rows_cap, H]
+  void* hbuf = nullptr;  // [rows_cap, I]
+  float* spart13 = nullptr;
+  float* s13 = nullptr;
+  float* spart2 = nullptr;
+  float* s2 = nullptr;
+  int32_t* status = nullptr;
+  size_t bytes = 0;
+};
+
+int moe_validate(const stageml_moe_args* a) {
+  SB_CHECK_ARG(a, "moe: null args");
+  SB_CHECK_ARG(a->T >= 0 && a->H > 0 && a->I > 0 && a->E > 0 && a->k >= 0 && a->n_shared >= 0,
+               "moe: bad sizes T=%d H=%d I=%d E=%d k=%d n_shared=%d", a->T, a->H, a->I, a->E, a->k, a->n_shared);
+  SB_CHECK_ARG(a->k + a->n_shared >= 1, "moe: need k + n_shared >= 1");
+  SB_CHECK_ARG(a->k <= a->E && a->k <= 8, "moe: k=%d must be <= min(E, 8)", a->k);
+  SB_CHECK_ARG(a->H % 8 == 0 && a->I % 8 == 0, "moe: H=%d and I=%d must be multiples of 8", a->H, a->I);
+  SB_CHECK_ARG(is16(a->act_dtype), "moe: act_dtype must be BF16 or F16");
+  SB_CHECK_ARG(a->weight_dtype == a->act_dtype || a->weight_dtype == STAGEML_E4M3,
+               "moe: weight_dtype must equal act_dtype or be E4M3");
+  if (a->weight_dtype == STAGEML_E4M3)
+    return set_error(STAGEML_ERR_UNSUPPORTED, "moe: E4M3 weights are not supported by this build");
+  SB_CHECK_ARG(a->rank >= 0 && a->rank % 8 == 0 && a->rank <= 32, "moe: rank=%d must be a multiple of 8 <= 32",
+               a->rank);
+  const bool lora13 = a->rank > 0 && a->lora_a13;
+  const bool lora2 = a->rank > 0 && a->lora_a2;
+  SB_CHECK_ARG(!lora13 || a->lora_b13, "moe: lora_a13 without lora_b13");
+  SB_CHECK_ARG(!lora2 || a->lora_b2, "moe: lora_a2 without lora_b2");
+  SB_CHECK_ARG(!(lora13 || lora2) || (a->tenant_ids && a->n_tenants > 0 && a->lora_scale),
+               "moe: LoRA needs tenant_ids, n_tenants > 0 and lora_scale");
+  SB_CHECK_ARG(a->k == 0 || a->topk_ids || a->router_w, "moe: need topk_ids or router_w");
+  if (a->topk_ids) SB_CHECK_ARG(a->ids_dtype == STAGEML_I32 || a->ids_dtype == STAGEML_I64, "moe: ids dtype");
+  if (a->T > 0) {
+    SB_CHECK_ARG(a->x && a->gate_up && a->down && a->out, "moe: null tensor");
+    SB_CHECK_ARG(aligned16(a->x) && aligned16(a->gate_up) && aligned16(a->down) && aligned16(a->out),
+                 "moe: x, gate_up, down and out must be 16-byte aligned");
+    if (lora13) SB_CHECK_ARG(aligned16(a->lora_a13) && aligned16(a->lora_b13), "moe: LoRA w13 alignment");
+    if (lora2) SB_CHECK_ARG(aligned16(a->lora_a2) && aligned16(a->lora_b2), "moe: LoRA w2 alignment");
+  }
+  return STAGEML_OK;
+}
+
+void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
+  Carver c(ws);
+  const int E_tot = a->E + a->n_shared;
+  const int64_t P = (int64_t)a->T * (a->k + a->n_shared);
+  const size_t es = esize(a->act_dtype);
+  if (a->plan_out)
+    b->plan = *a->plan_out;
+  else
+    carve_plan(c, P, E_tot, &b->plan);
+  const int64_t rows_cap = stageml_plan_rows_cap(P, E_tot);
+  if (!a->topk_ids && a->k > 0) {
+    b->logits = c.take<float>((size_t)a->T * a->E);
+    b->ids = c.take<int32_t>((size_t)a->T * a->k);
+    b->weights = c.take<float>((size_t)a->T * a->k);
+  }
+  const int64_t nkeys = permute_num_keys(0, a->n_tenants, 0, E_tot);
+  b->perm_scratch = c.take_bytes(permute_scratch_bytes(P, nkeys));
+  b->xp = c.take_bytes((size_t)rows_cap * a->H * es);
+  b->hbuf = c.take_bytes((size_t)rows_cap * a->I * es);
+  if (a->rank > 0 && a->lora_a13) {
+    b->spart13 = c.take<float>((size_t)shrink_num_slices(a->H) * rows_cap * 2 * a->rank);
+    b->s13 = c.take<float>((size_t)rows_cap * 2 * a->rank);
+  }
+  if (a->rank > 0 && a->lora_a2) {
+    b->spart2 = c.take<float>((size_t)shrink_num_slices(a->I) * rows_cap * a->rank);
+    b->s2 = c.take<float>((size_t)rows_cap * a->rank);
+  }
+  b->status = c.take<int32_t>(1);
+  b->bytes = c.off;
+}
+
+int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
+  SB_TRY(moe_validate(a));
+  if (a->T == 0) return STAGEML_OK;
+  MoeBuffers b;
+  moe_carve(a, nullptr, &b);
+  if (!ws || ws_bytes < b.bytes)
+    return set_error(STAGEML_ERR_WORKSPACE, "moe: workspace of %zu bytes < required %zu", ws_bytes, b.bytes);
+  moe_carve(a, ws, &b);
+  const int E_tot = a->E + a->n_shared;
+  const int64_t P = (int64_t)a->T * (a->k + a->n_shared);
+  if (a->plan_out)
+    SB_CHECK_ARG(a->plan_out->rows_cap >= stageml_plan_rows_cap(P, E_tot), "moe: plan_out rows_cap too small");
+  int32_t* status = a->status ? a->status : b.status;
+  const int bf = a->act_dtype == STAGEML_BF16;
+  const bool lora13 = a->rank > 0 && a->lora_a13;
+  const bool lora2 = a->rank > 0 && a->lora_a2;
+
+  // R1: routing
+  const void* ids = a->topk_ids;
+  int ids_dtype = a->ids_dtype;
+  const void* wts = a->topk_weights;
+  int wts_dtype = a->weights_dtype;
+  if (!ids && a->k > 0) {
+    SB_TRY(launch_router_logits(a->x, a->act_dtype, a->router_w, a->T, a->H, a->E, b.logits, st));
+    SB_TRY(launch_topk(b.logits, a->T, a->E, a->k, a->renormalize, b.ids, b.weights, st));
+    ids = b.ids;
+    ids_dtype = STAGEML_I32;
+    wts = b.weights;
+    wts_dtype = STAGEML_F32;
+  }
+  // R2: permutation
+  PermuteScratch scr;
+  const int64_t nkeys = permute_num_keys(0, a->n_tenants, 0, E_tot);
+  permute_carve(b.perm_scratch, P, nkeys, &scr);
+  SB_TRY(launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
+                        b.plan, status, scr, st));
+  // gather + R4 shrink of w1|w3
+  {
+    ShrinkLaunch s;
+    s.src = a->x;
+    s.src_row_of = b.plan.row_token;
+    s.gather_dst = b.xp;
+    s.K = a->H;
+    s.dtype_bf16 = bf;
+    s.num_tiles_dev = b.plan.num_tiles;
+    s.rows_cap = b.plan.rows_cap;
+    s.row_tenant = b.plan.row_tenant;
+    s.tile_group = b.plan.tile_group;
+    if (lora13) {
+      s.lora_a = a->lora_a13;
+      s.a_group_stride = (int64_t)2 * a->rank * a->H;
+      s.a_tenant_stride = (int64_t)E_tot * s.a_group_stride;
+      s.R = 2 * a->rank;
+      s.spart = b.spart13;
+      s.s_out = b.s13;
+      s.lora_scale = a->lora_scale;
+    }
+    SB_TRY(launch_gather_shrink(s, st));
+  }
+  // R3 + R5: gate/up GEMM, LoRA expand, SwiGLU
+  {
+    GemmLaunch g;
+    g.a = b.xp;
+    g.a_rows = b.plan.rows_cap;
+    g.K = a->H;
+    g.b = a->gate_up;
+    g.b_rows_total = (int64_t)E_tot * 2 * a->I;
+    g.b_group_rows = 2 * a->I;
+    g.N = a->I;
+    g.swiglu = true;
+    g.in_bf16 = bf;
+    g.num_tiles_dev = b.plan.num_tiles;
+    g.tiles_cap = (int)(b.plan.rows_cap / 128);
+    g.tile_group = b.plan.tile_group;
+    g.row_tenant = b.plan.row_tenant;
+    if (lora13) {
+      g.row_lora = b.s13;
+      g.rank = a->rank;
+      g.lora_b = a->lora_b13;
+      g.lora_b_group_stride = (int64_t)2 * a->I * a->rank;
+      g.lora_b_tenant_stride = (int64_t)E_tot * g.lora_b_group_stride;
+    }
+    g.b_scale = a->gate_up_scale;
+    g.out = b.hbuf;
+    g.ldo = a->I;
+    g.status = status;
+    SB_TRY(launch_grouped_gemm(g, st));
+  }
+  // R4 shrink of h for w2
+  if (lora2) {
+    ShrinkLaunch s;
+    s.src = b.hbuf;
+    s.K = a->I;
+    s.dtype_bf16 = bf;
+    s.num_tiles_dev = b.plan.num_tiles;
+    s.rows_cap = b.plan.rows_cap;
+    s.row_tenant = b.plan.row_tenant;
+    s.tile_group = b.plan.tile_group;
+    s.lora_a = a->lora_a2;
+    s.a_group_stride = (int64_t)a->rank * a->I;
+    s.a_tenant_stride = (int64_t)E_tot * s.a_group_stride;
+    s.R = a->rank;
+    s.spart = b.spart2;
+    s.s_out = b.s2;
+    s.lora_scale = a->lora_scale;
+    SB_TRY(launch_gather_shrink(s, st));
+  }
+  // R3 + R5: down GEMM, LoRA expand, routing weight
+  {
+    GemmLaunch g;
+    g.a = b.hbuf;
+    g.a_rows = b.plan.rows_cap;
+    g.K = a->I;
+    g.b = a->down;
+    g.b_rows_total = (int64_t)E_tot * a->H;
+    g.b_group_rows = a->H;
+    g.N = a->H;
+    g.swiglu = false;
+    g.in_bf16 = bf;
+    g.num_tiles_dev = b.plan.num_tiles;
+    g.tiles_cap = (int)(b.plan.rows_cap / 128);
+    g.tile_group = b.plan.tile_group;
+    g.row_tenant = b.plan.row_tenant;
+    if (lora2) {
+      g.row_lora = b.s2;
+      g.rank = a->rank;
+      g.lora_b = a->lora_b2;
+      g.lora_b_group_stride = (int64_t)a->H * a->rank;
+      g.lora_b_tenant_stride = (int64_t)E_tot * g.lora_b_group_stride;
+    }
+    g.row_scale = b.plan.row_weight;
+    g.b_scale = a->down_scale;
+    g.out = b.xp;
+    g.ldo = a->H;
+    g.status = status;
+    SB_TRY(launch_grouped_gemm(g, st));
+  }
+  // combine
+  SB_TRY(launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st));
+  return STAGEML_OK;
+}
+
+// -------------------------------------------------- MoE single-linear layer
+struct MoeLinearDims {
+  int T, K, N, E, k, n_groups, rank;
+};
+
+size_t moe_linear_carve(const MoeLinearDims& d, int n_tenants, int group_by_tenant, void* ws, stageml_moe_plan* plan,
+                        void** perm, void** xp, float** spart, float** s, void** yp, int32_t** status, int dtype) {
+  Carver c(ws);
+  const int64_t P = (int64_t)d.T * d.k;
+  carve_plan(c, P, d.n_groups, plan);
+  const int64_t rows_cap = plan->rows_cap;
+  const int64_t nkeys = permute_num_keys(0, n_tenants, group_by_tenant, d.E);
+  *perm = c.take_bytes(permute_scratch_bytes(P, nkeys));
+  *xp = c.take_bytes((size_t)rows_cap * d.K * esize(dtype));
+  *spart = d.rank > 0 ? c.take<float>((size_t)shrink_num_slices(d.K) * rows_cap * d.rank) : nullptr;
+  *s = d.rank > 0 ? c.take<float>((size_t)rows_cap * d.rank) : nullptr;
+  *yp = c.take_bytes((size_t)rows_cap * d.N * esize(dtype));
+  *status = c.take<int32_t>(1);
+  return c.off;
+}
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" {
+
+const char* stageml_last_error(void) { return last_error_text(); }
+
+int stageml_abi_version(void) { return kAbiVersion; }
+
+size_t stageml_struct_size(int which) {
+  switch (which) {
+    case 0:
+      return sizeof(stageml_moe_plan);
+    case 1:
+      return sizeof(stageml_moe_args);
+    case 2:
+      return sizeof(stageml_lora_linear_args);
+    default:
+      return 0;
+  }
+}
+
+int stageml_route_topk(const void* x, int x_dtype, const float* gate_w, int T, int H, int E, int k, int renormalize,
+                       float* logits_out, int32_t* ids_out, float* weights_out, stageml_stream_t stream) {
+  clear_error();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SB_CHECK_ARG(logits_out, "route_topk: logits_out is required as scratch ([T, E] fp32)");
+  SB_TRY(launch_router_logits(x, x_dtype, gate_w, T, H, E, logits_out, st));
+  return launch_topk(logits_out, T, E, k, renormalize, ids_out, weights_out, st);
+}
+
+int stageml_topk_from_logits(const float* logits, int T, int E, int k, int renormalize, int32_t* ids_out,
+                             float* weights_out, stageml_stream_t stream) {
+  clear_error();
+  return launch_topk(logits, T, E, k, renormalize, ids_out, weights_out, static_cast<cudaStream_t>(stream));
+}
+
+size_t stageml_permute_workspace_bytes(int T, int k, int n_shared, int n_experts_total, int n_tenants,
+                                       int group_by_tenant) {
+  const int64_t P = (int64_t)T * (k + n_shared);
+  return permute_scratch_bytes(P, permute_num_keys(0, n_tenants, group_by_tenant, n_experts_total));
+}
+
+int stageml_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
+                    int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
+                    const stageml_moe_plan* plan, int32_t* status, void* workspace, size_t workspace_bytes,
+                    stageml_stream_t stream) {
+  clear_error();
+  SB_CHECK_ARG(plan, "permute: null plan");
+  const size_t need = stageml_permute_workspace_bytes(T, k, n_shared, n_experts_total, n_tenants, group_by_tenant);
+  if (!workspace || workspace_bytes < need)
+    return set_error(STAGEML_ERR_WORKSPACE, "permute: workspace of %zu bytes < required %zu", workspace_bytes, need);
+  PermuteScratch scr;
+  const int64_t P = (int64_t)T * (k + n_shared);
+  permute_carve(workspace, P, permute_num_keys(0, n_tenants, group_by_tenant, n_experts_total), &scr);
+  return launch_permute(ids, ids_dtype, weights, weights_dtype, tenant_ids, T, k, n_shared, n_experts_total, n_tenants,
+                        group_by_tenant, *plan, status, scr, static_cast<cudaStream_t>(stream));
+}
+
+size_t stageml_moe_workspace_bytes(const stageml_moe_args* args) {
+  if (!args || moe_validate(args) != STAGEML_OK) return 0;
+  MoeBuffers b;
+  moe_carve(args, nullptr, &b);
+  return b.bytes;
+}
+
+int stageml_moe_forward(const stageml_moe_args* args, void* workspace, size_t workspace_bytes,
+                        stageml_stream_t stream) {
+  clear_error();
+  return moe_forward_impl(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+static void residual_args(stageml_moe_args* a, const void* hidden, const void* gate_up, const void* down,
+                          const void* topk_weights, int weights_dtype, const void* topk_ids, int ids_dtype, int T,
+                          int H, int I, int E, int k, int dtype, void* out, int32_t* status) {
+  *a = stageml_moe_args{};
+  a->T = T;
+  a->H = H;
+  a->I = I;
+  a->E = E;
+  a->k = k;
+  a->n_shared = 0;
+  a->act_dtype = dtype;
+  a->weight_dtype = dtype;
+  a->x = hidden;
+  a->topk_ids = topk_ids;
+  a->ids_dtype = ids_dtype;
+  a->topk_weights = topk_weights;
+  a->weights_dtype = weights_dtype;
+  a->gate_up = gate_up;
+  a->down = down;
+  a->out = out;
+  a->status = status;
+}
+
+size_t stageml_residual_moe_workspace_bytes(int T, int H, int I, int E, int k) {
+  stageml_moe_args a;
+  static const int dummy_ids = 0;
+  residual_args(&a, nullptr, nullptr, nullptr, nullptr, STAGEML_F32, &dummy_ids, STAGEML_I64, T, H, I, E, k,
+                STAGEML_BF16, nullptr, nullptr);
+  a.T = 0;  // validation of pointers is skipped for sizing
+  if (moe_validate(&a) != STAGEML_OK) return 0;
+  a.T = T;
+  MoeBuffers b;
+  moe_carve(&a, nullptr, &b);
+  return b.bytes;
+}
+
+int stageml_residual_moe(const void* hidden, const void* gate_up, const void* down, const void* topk_weights,
+                         int weights_dtype, const void* topk_ids, int ids_dtype, int T, int H, int I, int E, int k,
+                         int dtype, void* out, int32_t* status, void* workspace, size_t workspace_bytes,
+                         stageml_stream_t stream) {
+  clear_error();
+  SB_CHECK_ARG(topk_ids && topk_weights, "residual_moe: topk_ids and topk_weights are required");
+  stageml_moe_args a;
+  residual_args(&a, hidden, gate_up, down, topk_weights, weights_dtype, topk_ids, ids_dtype, T, H, I, E, k, dtype,
+                out, status);
+  return moe_forward_impl(&a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t stageml_moe_linear_workspace_bytes(int T, int K, int N, int E, int k, int group_by_tenant, int n_tenants,
+                                          int rank) {
+  stageml_moe_plan plan;
+  void *perm, *xp, *yp;
+  float *spart, *s;
+  int32_t* st;
+  MoeLinearDims d{T, K, N, E, k, group_by_tenant ? n_tenants * E : E, group_by_tenant ? 0 : rank};
+  return moe_linear_carve(d, n_tenants, group_by_tenant, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &st,
+                          STAGEML_BF16);
+}
+
+int stageml_moe_linear(const void* x, const void* weight, const void* bias, const void* topk_ids, int ids_dtype,
+                       const void* topk_weights, int weights_dtype, const int32_t* tenant_ids, int T, int K, int N,
+                       int E, int k, int group_by_tenant, int n_tenants, int rank, const void* lora_a,
+                       const void* lora_b, const float* lora_scale, int dtype, void* out, int32_t* status,
+                       void* workspace, size_t workspace_bytes, stageml_stream_t stream) {
+  clear_error();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SB_CHECK_ARG(T >= 0 && K > 0 && N > 0 && E > 0 && k >= 1 && k <= E, "moe_linear: bad sizes");
+  SB_CHECK_ARG(K % 8 == 0 && N % 8 == 0, "moe_linear: K=%d and N=%d must be multiples of 8", K, N);
+  SB_CHECK_ARG(is16(dtype), "moe_linear: dtype must be BF16 or F16");
+  SB_CHECK_ARG(ids_dtype == STAGEML_I32 || ids_dtype == STAGEML_I64, "moe_linear: ids dtype");
+  SB_CHECK_ARG(rank >= 0 && rank % 8 == 0 && rank <= 32, "moe_linear: rank=%d must be a multiple of 8 <= 32", rank);
+  const bool lora = rank > 0 && lora_a && !group_by_tenant;
+  SB_CHECK_ARG(!lora || (lora_b && lora_scale && tenant_ids && n_tenants > 0), "moe_linear: incomplete LoRA inputs");
+  SB_CHECK_ARG(!group_by_tenant || (tenant_ids && n_tenants > 0), "moe_linear: group_by_tenant needs tenant ids");
+  if (T == 0) return STAGEML_OK;
+  SB_CHECK_ARG(x && weight && topk_ids && out, "moe_linear: null tensor");
+  SB_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(out), "moe_linear: 16-byte alignment");
+  const int n_groups = group_by_tenant ? n_tenants * E : E;
+  MoeLinearDims d{T, K, N, E, k, n_groups, lora ? rank : 0};
+  stageml_moe_plan plan;
+  void *perm, *xp, *yp;
+  float *spart, *s;
+  int32_t* st_ws;
+  const size_t need =
+      moe_linear_carve(d, n_tenants, group_by_tenant, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &st_ws, dtype);
+  if (!workspace || workspace_bytes < need)
+    return set_error(STAGEML_ERR_WORKSPACE, "moe_linear: workspace of %zu bytes < required %zu", workspace_bytes,
+                     need);
+  moe_linear_carve(d, n_tenants, group_by_tenant, workspace, &plan, &perm, &xp, &spart, &s, &yp, &st_ws, dtype);
+  int32_t* stat = status ? status : st_ws;
+  const int bf = dtype == STAGEML_BF16;
+  PermuteScratch scr;
+  permute_carve(perm, (int64_t)T * k, permute_num_keys(0, n_tenants, group_by_tenant, E), &scr);
+  SB_TRY(launch_permute(topk_ids, ids_dtype, topk_weights, weights_dtype, tenant_ids, T, k, 0, E,
+                        group_by_tenant || lora ? n_tenants : 0, group_by_tenant, plan, stat, scr, st));
+  ShrinkLaunch sh;
+  sh.src = x;
+  sh.src_row_of = plan.row_token;
+  sh.gather_dst = xp;
+  sh.K = K;
+  sh.dtype_bf16 = bf;
+  sh.num_tiles_dev = plan.num_tiles;
+  sh.rows_cap = plan.rows_cap;
+  sh.row_tenant = plan.row_tenant;
+  sh.tile_group = plan.tile_group;
+  if (lora) {
+    sh.lora_a = lora_a;
+    sh.a_group_stride = (int64_t)rank * K;
+    sh.a_tenant_stride = (int64_t)E * sh.a_group_stride;
+    sh.R = rank;
+    sh.spart = spart;
+    sh.s_out = s;
+    sh.lora_scale = lora_scale;
+  }
+  SB_TRY(launch_gather_shrink(sh, st));
+  GemmLaunch g;
+  g.a = xp;
+  g.a_rows = plan.rows_cap;
+  g.K = K;
+  g.b = weight;
+  g.b_rows_total = (int64_t)n_groups * N;
+  g.b_group_rows = N;
+  g.N = N;
+  g.in_bf16 = bf;
+  g.num_tiles_dev = plan.num_tiles;
+  g.tiles_cap = (int)(plan.rows_cap / 128);
+  g.tile_group = plan.tile_group;
+  g.row_tenant = plan.row_tenant;
+  if (lora) {
+    g.row_lora = s;
+    g.rank = rank;
+    g.lora_b = lora_b;
+    g.lora_b_group_stride = (int64_t)N * rank;
+    g.lora_b_tenant_stride = (int64_t)E * g.lora_b_group_stride;
+  }
+  g.bias = bias;
+  g.bias_group_stride = N;
+  g.bias_group_mod = E;
+  g.row_scale = plan.row_weight;
+  g.out = yp;
+  g.ldo = N;
+  g.status = stat;
+  SB_TRY(launch_grouped_gemm(g, st));
+  return launch_combine(yp, plan.pair_row, T, k, N, bf, out, st);
+}
+
+int stageml_lora_fold(const void* W, const void* A, const void* B, const float* scale, int batch, int rows, int cols,
+                      int rank, int layout, int64_t w_batch_stride, int64_t a_batch_stride, int64_t b_batch_stride,
+                      int dtype, void* out, stageml_stream_t stream) {
+  clear_error();
+  return launch_lora_fold(W, A, B, scale, batch, rows, cols, rank, layout, w_batch_stride, a_batch_stride,
+                          b_batch_stride, dtype, out, static_cast<cudaStream_t>(stream));
+}
+
+static size_t lora_linear_carve(const stageml_lora_linear_args* a, void* ws, stageml_moe_plan* plan, void** perm,
+                                void** xp, float** spart, float** s, void** yp, int32_t** tenants, int32_t** status) {
+  Carver c(ws);
+  const bool direct = a->n_groups == 1;
+  const bool lora = a->rank > 0 && a->lora_a && a->row_tenant;
+  *perm = *xp = *yp = nullptr;
+  *tenants = nullptr;
+  if (direct) {
+    *tenants = c.take<int32_t>(std::max(a->M, 1));
+    const int64_t rows = a->M;
+    *spart = lora ? c.take<float>((size_t)shrink_num_slices(a->K) * rows * a->rank) : nullptr;
+    *s = lora ? c.take<float>((size_t)rows * a->rank) : nullptr;
+  } else {
+    carve_plan(c, a->M, a->n_groups, plan);
+    *perm = c.take_bytes(permute_scratch_bytes(a->M, permute_num_keys(0, a->n_tenants, 0, a->n_groups)));
+    *xp = c.take_bytes((size_t)plan->rows_cap * a->K * 2);
+    *spart = lora ? c.take<float>((size_t)shrink_num_slices(a->K) * plan->rows_cap * a->rank) : nullptr;
+    *s = lora ? c.take<float>((size_t)plan->rows_cap * a->rank) : nullptr;
+    *yp = c.take_bytes((size_t)plan->rows_cap * a->N * 2);
+  }
+  *status = c.take<int32_t>(1);
+  return c.off;
+}
+
+size_t stageml_lora_linear_workspace_bytes(const stageml_lora_linear_args* a) {
+  if (!a || a->M < 0 || a->n_groups < 1) return 0;
+  stageml_moe_plan plan;
+  void *perm, *xp, *yp;
+  float *spart, *s;
+  int32_t *ten, *st;
+  return lora_linear_carve(a, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &ten, &st);
+}
+
+int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size_t workspace_bytes,
+                        stageml_stream_t stream) {
+  clear_error();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SB_CHECK_ARG(a, "lora_linear: null args");
+  SB_CHECK_ARG(a->M >= 0 && a->K > 0 && a->N > 0 && a->n_groups >= 1, "lora_linear: bad sizes");
+  SB_CHECK_ARG(a->K % 8 == 0 && a->N % 8 == 0, "lora_linear: K=%d and N=%d must be multiples of 8", a->K, a->N);
+  SB_CHECK_ARG(is16(a->dtype), "lora_linear: dtype must be BF16 or F16");
+  SB_CHECK_ARG(a->rank >= 0 && a->rank % 8 == 0 && a->rank <= 32, "lora_linear: rank=%d must be a multiple of 8 <= 32",
+               a->rank);
+  const bool lora = a->rank > 0 && a->lora_a && a->row_tenant;
+  SB_CHECK_ARG(!lora || (a->lora_b && a->lora_scale && a->n_tenants > 0), "lora_linear: incomplete LoRA inputs");
+  SB_CHECK_ARG(a->n_groups == 1 || a->row_group, "lora_linear: n_groups > 1 needs row_group");
+  if (a->M == 0) return STAGEML_OK;
+  SB_CHECK_ARG(a->x && a->w_bank && a->y, "lora_linear: null tensor");
+  SB_CHECK_ARG(aligned16(a->x) && aligned16(a->w_bank) && aligned16(a->y), "lora_linear: 16-byte alignment");
+  stageml_moe_plan plan;
+  void *perm, *xp, *yp;
+  float *spart, *s;
+  int32_t *ten, *st_ws;
+  const size_t need = lora_linear_carve(a, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &ten, &st_ws);
+  if (!workspace || workspace_bytes < need)
+    return set_error(STAGEML_ERR_WORKSPACE, "lora_linear: workspace of %zu bytes < required %zu", workspace_bytes,
+                     need);
+  lora_linear_carve(a, workspace, &plan, &perm, &xp, &spart, &s, &yp, &ten, &st_ws);
+  int32_t* stat = a->status ? a->status : st_ws;
+  const int bf = a->dtype == STAGEML_BF16;
+  const int n_ten = lora ? a->n_tenants : 0;
+  GemmLaunch g;
+  g.K = a->K;
+  g.b = a->w_bank;
+  g.b_rows_total = (int64_t)a->n_groups * a->N;
+  g.b_group_rows = a->N;
+  g.N = a->N;
+  g.in_bf16 = bf;
+  g.bias = a->bias;
+  g.bias_group_stride = 0;
+  g.status = stat;
+  ShrinkLaunch sh;
+  sh.K = a->K;
+  sh.dtype_bf16 = bf;
+  if (lora) {
+    sh.lora_a = a->lora_a;
+    sh.a_tenant_stride = (int64_t)a->rank * a->K;
+    sh.a_group_stride = 0;
+    sh.R = a->rank;
+    sh.spart = spart;
+    sh.s_out = s;
+    sh.lora_scale = a->lora_scale;
+    g.row_lora = s;
+    g.rank = a->rank;
+    g.lora_b = a->lora_b;
+    g.lora_b_tenant_stride = (int64_t)a->N * a->rank;
+    g.lora_b_group_stride = 0;
+  }
+  if (a->n_groups == 1) {
+    SB_TRY(launch_validate_tenants(lora ? a->row_tenant : nullptr, a->M, n_ten, ten, stat, st));
+    if (lora) {
+      sh.src = a->x;
+      sh.static_rows = a->M;
+      sh.rows_cap = a->M;
+      sh.row_tenant = ten;
+      SB_TRY(launch_gather_shrink(sh, st));
+    }
+    g.a = a->x;
+    g.a_rows = a->M;
+    g.m_rows = a->M;
+    g.row_tenant = ten;
+    g.out = a->y;
+    g.ldo = a->N;
+    return launch_grouped_gemm(g, st);
+  }
+  PermuteScratch scr;
+  permute_carve(perm, a->M, permute_num_keys(0, n_ten, 0, a->n_groups), &scr);
+  SB_TRY(launch_permute(a->row_group, STAGEML_I32, nullptr, STAGEML_F32, lora ? a->row_tenant : nullptr, a->M, 1, 0,
+                        a->n_groups, n_ten, 0, plan, stat, scr, st));
+  sh.src = a->x;
+  sh.src_row_of = plan.row_token;
+  sh.gather_dst = xp;
+  sh.num_tiles_dev = plan.num_tiles;
+  sh.rows_cap = plan.rows_cap;
+  sh.row_tenant = plan.row_tenant;
+  sh.tile_group = plan.tile_group;
+  SB_TRY(launch_gather_shrink(sh, st));
+  g.a = xp;
+  g.a_rows = plan.rows_cap;
+  g.num_tiles_dev = plan.num_tiles;
+  g.tiles_cap = (int)(plan.rows_cap / 128);
+  g.tile_group = plan.tile_group;
+  g.row_tenant = plan.row_tenant;
+  g.out = yp;
+  g.ldo = a->N;
+  SB_TRY(launch_grouped_gemm(g, st));
+  return launch_combine(yp, plan.pair_row, a->M, 1, a->N, bf, a->y, st);
+}
+
+size_t stageml_lora_gemv_f32_workspace_bytes(int M, int in_features, int out_features, int rank) {
+  if (M < 1 || in_features < 1 || out_features < 1) return 0;
+  return gemv_f32_workspace(M, in_features, out_features, rank);
+}
+
+int stageml_lora_gemv_f32(const float* x, const float* W, const float* A, const float* B, float scale, int M,
+                          int in_features, int out_features, int rank, float* y, void* workspace,
+                          size_t workspace_bytes, stageml_stream_t stream) {
+  clear_error();
+  SB_CHECK_ARG(M >= 1 && in_features >= 1 && out_features >= 1, "lora_gemv_f32: bad sizes");
+  const size_t need = gemv_f32_workspace(M, in_features, out_features, rank);
+  if (!workspace || workspace_bytes < need)
+    return set_error(STAGEML_ERR_WORKSPACE, "lora_gemv_f32: workspace of %zu bytes < required %zu",
+                     workspace_bytes, need);
+  return launch_gemv_f32(x, W, A, B, scale, M, in_features, out_features, rank, y, workspace,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int stageml_quantize_e4m3_rows(const void* w, int dtype, int64_t rows, int64_t cols, uint8_t* q_out, float* scale_out,
+                               stageml_stream_t stream) {
+  clear_error();
+  return launch_quantize_e4m3_rows(w, dtype, rows, cols, q_out, scale_out, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

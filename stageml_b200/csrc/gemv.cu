@@ -1,0 +1,145 @@
+// Single LoRA linear in fp32 with the [in,out] layout of the config-1 workload
+// (benchmarks/triton_lora_equivalence_check.py:11-22):
+//   dynamic: y = x W + s (x A) B        folded: y = x W'
+// x [M, in] with M <= 16, W [in, out], A [in, r], B [r, out]. Real fp32 FMAs
+// (no TF32). HBM-bound on the W read: split-K over (column block, K slice)
+// CTAs with float4 loads of W, fp32 partials reduced in a fixed order by a
+// second kernel that also applies the rank-r expansion, so results are
+// deterministic.
+#include "common.cuh"
+#include "host_util.h"
+#include "kernels.h"
+
+namespace sb {
+namespace {
+
+constexpr int GV_COLS = 512;   // columns per CTA (128 threads x float4)
+constexpr int GV_MAXM = 16;
+
+__global__ void __launch_bounds__(128) gemv_partial_kernel(const float* __restrict__ x, const float* __restrict__ W,
+                                                           const float* __restrict__ A, int M, int in_f, int out_f,
+                                                           int rank, int slice, float* __restrict__ part,
+                                                           float* __restrict__ xa_part) {
+  extern __shared__ float xs[];  // [M][slice]
+  const int ks = blockIdx.y;
+  const int i0 = ks * slice, i1 = min(in_f, i0 + slice);
+  const int ni = i1 - i0;
+  for (int t = threadIdx.x; t < M * slice; t += blockDim.x) {
+    const int m = t / slice, i = t % slice;
+    xs[t] = (i < ni) ? x[(int64_t)m * in_f + i0 + i] : 0.f;
+  }
+  __syncthreads();
+  const int c = blockIdx.x * GV_COLS + threadIdx.x * 4;
+  if (c < out_f) {
+    float acc[GV_MAXM][4];
+#pragma unroll
+    for (int m = 0; m < GV_MAXM; ++m)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
+    const bool vec = (c + 4 <= out_f) && (out_f % 4 == 0);
+    for (int i = 0; i < ni; ++i) {
+      float w[4];
+      const float* wr = W + (int64_t)(i0 + i) * out_f + c;
+      if (vec) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(wr));
+        w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w[q] = (c + q < out_f) ? wr[q] : 0.f;
+      }
+#pragma unroll
+      for (int m = 0; m < GV_MAXM; ++m)
+        if (m < M) {
+          const float xv = xs[m * slice + i];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[m][q] = fmaf(xv, w[q], acc[m][q]);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < GV_MAXM; ++m)
+      if (m < M)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (c + q < out_f) part[((int64_t)ks * M + m) * out_f + c + q] = acc[m][q];
+  }
+  if (A && blockIdx.x == 0) {
+    for (int t = threadIdx.x; t < M * rank; t += blockDim.x) {
+      const int m = t / rank, j = t % rank;
+      float a = 0.f;
+      for (int i = 0; i < ni; ++i) a = fmaf(xs[m * slice + i], A[(int64_t)(i0 + i) * rank + j], a);
+      xa_part[((int64_t)ks * M + m) * rank + j] = a;
+    }
+  }
+}
+
+__global__ void gemv_reduce_kernel(const float* __restrict__ part, const float* __restrict__ xa_part,
+                                   const float* __restrict__ B, float scale, int M, int out_f, int rank, int KS,
+                                   float* __restrict__ y) {
+  extern __shared__ float xa[];  // [M][rank]
+  if (B) {
+    for (int t = threadIdx.x; t < M * rank; t += blockDim.x) {
+      float a = 0.f;
+      for (int ks = 0; ks < KS; ++ks) a += xa_part[(int64_t)ks * M * rank + t];
+      xa[t] = a;
+    }
+  }
+  __syncthreads();
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= out_f) return;
+  for (int m = 0; m < M; ++m) {
+    float v = 0.f;
+    for (int ks = 0; ks < KS; ++ks) v += part[((int64_t)ks * M + m) * out_f + n];
+    if (B) {
+      float l = 0.f;
+      for (int j = 0; j < rank; ++j) l = fmaf(xa[m * rank + j], B[(int64_t)j * out_f + n], l);
+      v = fmaf(scale, l, v);
+    }
+    y[(int64_t)m * out_f + n] = v;
+  }
+}
+
+void gemv_plan(int in_f, int out_f, int* KS, int* slice) {
+  const int ncb = (out_f + GV_COLS - 1) / GV_COLS;
+  int ks = std::max(1, (8 * sm_count() + ncb - 1) / ncb);
+  ks = std::min(ks, std::max(1, (in_f + 31) / 32));
+  *slice = (in_f + ks - 1) / ks;
+  *KS = (in_f + *slice - 1) / *slice;
+}
+
+}  // namespace
+
+size_t gemv_f32_workspace(int M, int in_f, int out_f, int rank) {
+  int KS, slice;
+  gemv_plan(in_f, out_f, &KS, &slice);
+  size_t b = (((size_t)KS * M * out_f * 4) + 255) & ~size_t(255);
+  b += (((size_t)KS * M * std::max(rank, 1) * 4) + 255) & ~size_t(255);
+  return b;
+}
+
+int launch_gemv_f32(const float* x, const float* W, const float* A, const float* B, float scale, int M, int in_f,
+                    int out_f, int rank, float* y, void* ws, cudaStream_t stream) {
+  SB_CHECK_ARG(x && W && y, "lora_gemv_f32: null pointer");
+  SB_CHECK_ARG(M >= 1 && M <= GV_MAXM, "lora_gemv_f32: M=%d must be in [1, %d]", M, GV_MAXM);
+  SB_CHECK_ARG(in_f >= 1 && out_f >= 1, "lora_gemv_f32: bad sizes");
+  SB_CHECK_ARG(!A || (B && rank >= 1 && rank <= 256), "lora_gemv_f32: A needs B and 1 <= rank <= 256");
+  SB_CHECK_ARG(ws, "lora_gemv_f32: null workspace");
+  SB_CHECK_ARG(reinterpret_cast<uintptr_t>(W) % 16 == 0, "lora_gemv_f32: W must be 16-byte aligned");
+  int KS, slice;
+  gemv_plan(in_f, out_f, &KS, &slice);
+  float* part = static_cast<float*>(ws);
+  float* xa_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
+                                            ((((size_t)KS * M * out_f * 4) + 255) & ~size_t(255)));
+  const size_t smem1 = (size_t)M * slice * 4;
+  SB_CHECK_ARG(smem1 <= 200 * 1024, "lora_gemv_f32: K slice too large");
+  SB_CUDA_CHECK(cudaFuncSetAttribute(gemv_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
+  dim3 g1((out_f + GV_COLS - 1) / GV_COLS, KS);
+  gemv_partial_kernel<<<g1, 128, smem1, stream>>>(x, W, A, M, in_f, out_f, A ? rank : 0, slice, part, xa_part);
+  SB_CUDA_CHECK(cudaGetLastError());
+  const size_t smem2 = (size_t)M * (A ? rank : 1) * 4;
+  gemv_reduce_kernel<<<(out_f + 255) / 256, 256, smem2, stream>>>(part, xa_part, A ? B : nullptr, scale, M, out_f,
+                                                                   A ? rank : 0, KS, y);
+  SB_CUDA_CHECK(cudaGetLastError());
+  return STAGEML_OK;
+}
+
+}  // namespace sb

@@ -1,0 +1,47 @@
+// Host-side helpers shared by the C ABI translation units: thread-local error
+// text, CUDA error checks, device properties and TMA tensor-map encoding.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/stageml_b200.h"
+
+namespace sb {
+
+// Record an error message for stageml_last_error() and return `code`.
+int set_error(int code, const char* fmt, ...);
+void clear_error();
+const char* last_error_text();
+
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+
+// Encode a 2-D row-major tensor map: `rows` x `cols` elements of `elem_bytes`
+// bytes, row pitch `row_pitch_bytes`, box `box_rows` x `box_cols`, 128-byte
+// swizzle when `swizzle128` (box_cols * elem_bytes must then be 128).
+int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
+                 uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_rows, uint32_t box_cols, bool swizzle128);
+
+}  // namespace sb
+
+#define SB_CUDA_CHECK(expr)                                                                     \
+  do {                                                                                          \
+    cudaError_t _e = (expr);                                                                    \
+    if (_e != cudaSuccess)                                                                      \
+      return ::sb::set_error(STAGEML_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), \
+                             __FILE__, __LINE__);                                               \
+  } while (0)
+
+#define SB_CHECK_ARG(cond, ...)                                    \
+  do {                                                             \
+    if (!(cond)) return ::sb::set_error(STAGEML_ERR_INVALID_ARG, __VA_ARGS__); \
+  } while (0)
+
+#define SB_TRY(expr)            \
+  do {                          \
+    int _rc = (expr);           \
+    if (_rc != STAGEML_OK) return _rc; \
+  } while (0)

@@ -1,0 +1,75 @@
+// Internal launchers shared between the kernel translation units and the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/stageml_b200.h"
+
+namespace sb {
+
+// route.cu
+int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T, int H, int E, float* logits,
+                         cudaStream_t stream);
+int launch_topk(const float* logits, int T, int E, int k, int renorm, int32_t* ids, float* weights,
+                cudaStream_t stream);
+
+// permute.cu
+struct PermuteScratch {
+  uint32_t* sorted;  // [nchunks * 2048]
+  int32_t* hist;     // [nkeys * nchunks]
+  int32_t* off;      // [nchunks * nkeys] destination offsets
+};
+constexpr int kPermChunk = 2048;
+int64_t permute_num_keys(int n_groups_total, int n_tenants, int group_by_tenant, int n_experts_total);
+size_t permute_scratch_bytes(int64_t num_pairs, int64_t nkeys);
+void permute_carve(void* base, int64_t num_pairs, int64_t nkeys, PermuteScratch* out);
+int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
+                   int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
+                   const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream);
+
+// shrink.cu: gather rows and/or LoRA shrink partials (split-K), then reduce.
+struct ShrinkLaunch {
+  const void* src = nullptr;          // [src_rows, K] 16-bit
+  const int32_t* src_row_of = nullptr;  // row -> source row (-1 = zero row); null = identity
+  void* gather_dst = nullptr;         // [rows_cap, K] or null
+  int K = 0;
+  int dtype_bf16 = 1;
+  const int32_t* num_tiles_dev = nullptr;  // active rows = 128 * (*num_tiles_dev); null -> static_rows
+  int64_t static_rows = 0;
+  int64_t rows_cap = 0;
+  const int32_t* row_tenant = nullptr;
+  const int32_t* tile_group = nullptr;  // null -> group 0
+  const void* lora_a = nullptr;         // [tenant][group][R][K]
+  int64_t a_tenant_stride = 0;
+  int64_t a_group_stride = 0;
+  int R = 0;                            // output columns (multiple of 8, <= 64)
+  float* spart = nullptr;               // [KS][rows_cap][R]
+  float* s_out = nullptr;               // [rows_cap][R] (reduced, scaled)
+  const float* lora_scale = nullptr;    // [n_tenants]
+};
+constexpr int kShrinkKSlice = 512;
+inline int shrink_num_slices(int K) { return (K + kShrinkKSlice - 1) / kShrinkKSlice; }
+int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream);
+
+// combine.cu: out[t] = sum_j Y[pair_row[t*kk + j]]
+int launch_combine(const void* y, const int32_t* pair_row, int T, int kk, int H, int dtype_bf16, void* out,
+                   cudaStream_t stream);
+// clamp caller tenant ids into [-1, n_tenants) (invalid -> -1 + status)
+int launch_validate_tenants(const int32_t* in, int64_t n, int n_tenants, int32_t* out, int32_t* status,
+                            cudaStream_t stream);
+
+// fold.cu
+int launch_lora_fold(const void* W, const void* A, const void* B, const float* scale, int batch, int rows, int cols,
+                     int rank, int layout, int64_t w_bs, int64_t a_bs, int64_t b_bs, int dtype, void* out,
+                     cudaStream_t stream);
+
+// gemv.cu
+size_t gemv_f32_workspace(int M, int in_f, int out_f, int rank);
+int launch_gemv_f32(const float* x, const float* W, const float* A, const float* B, float scale, int M, int in_f,
+                    int out_f, int rank, float* y, void* ws, cudaStream_t stream);
+
+// fp8.cu
+int launch_quantize_e4m3_rows(const void* w, int dtype, int64_t rows, int64_t cols, uint8_t* q, float* scale,
+                              cudaStream_t stream);
+
+}  // namespace sb

@@ -1,0 +1,346 @@
+// Token -> expert permutation (R2): a deterministic, stable counting sort of
+// the routed (token, slot) pairs by key (expert, tenant), each expert segment
+// padded to 128 rows so every 128-row GEMM tile belongs to one expert.
+//
+// The reference groups rows with one torch.nonzero per (slot, expert) and a
+// host sync each (benchmarks/multitenant_bta_system_bench.py:401-406); here the
+// whole grouping is three kernels with no host round trip:
+//   count   one CTA per 2048-pair chunk: bitonic sort of (key << 11 | index)
+//           in shared memory, per-key counts of the chunk -> hist[chunk][key]
+//   scan    one CTA: per-key totals, per-group counts, padded group offsets,
+//           tile -> group map, per-(key, chunk) destination offsets
+//   scatter one CTA per chunk: destination = offset[chunk][key] + rank of the
+//           pair inside its key segment of the (already sorted) chunk
+// Sorting (key, pair index) makes the order within a key the pair order, so
+// the permutation is the stable sort the oracle defines, bit for bit.
+#include "common.cuh"
+#include "host_util.h"
+#include "kernels.h"
+
+namespace sb {
+namespace {
+
+constexpr uint32_t kSentKey = 0x1FFFFFu;  // 21-bit key field; dropped pairs and empty slots
+constexpr int kMaxKeys = 32768;           // keys held in shared memory by the scan kernel
+
+struct PairSrc {
+  const void* ids;
+  int ids_i64;
+  const void* weights;
+  int weights_dtype;
+  const int32_t* tenant_ids;
+  int T, k, kk, E_routed, E_tot, n_tenants, group_by_tenant, tkeys;
+  int64_t P;
+};
+
+__device__ __forceinline__ int pair_expert(const PairSrc& a, int t, int j, bool* bad) {
+  if (j >= a.k) return a.E_routed + (j - a.k);
+  const int64_t idx = (int64_t)t * a.k + j;
+  const int64_t e = a.ids_i64 ? static_cast<const int64_t*>(a.ids)[idx] : (int64_t) static_cast<const int32_t*>(a.ids)[idx];
+  if (e < 0 || e >= a.E_routed) {
+    *bad = true;
+    return 0;
+  }
+  return (int)e;
+}
+
+__device__ __forceinline__ int pair_tenant(const PairSrc& a, int t, bool* bad) {
+  if (!a.tenant_ids) return -1;
+  const int tn = a.tenant_ids[t];
+  if (tn < -1 || tn >= a.n_tenants) {
+    *bad = true;
+    return -1;
+  }
+  return tn;
+}
+
+__device__ __forceinline__ float pair_weight(const PairSrc& a, int t, int j) {
+  if (j >= a.k || !a.weights) return 1.f;
+  const int64_t idx = (int64_t)t * a.k + j;
+  if (a.weights_dtype == STAGEML_BF16) return __bfloat162float(static_cast<const bf16*>(a.weights)[idx]);
+  if (a.weights_dtype == STAGEML_F16) return __half2float(static_cast<const f16*>(a.weights)[idx]);
+  return static_cast<const float*>(a.weights)[idx];
+}
+
+// Sort key of pair p, or kSentKey when an id is out of range.
+__device__ __forceinline__ uint32_t pair_key(const PairSrc& a, int64_t p, int32_t* status) {
+  const int t = (int)(p / a.kk);
+  const int j = (int)(p - (int64_t)t * a.kk);
+  bool bad = false;
+  const int e = pair_expert(a, t, j, &bad);
+  const int tn = pair_tenant(a, t, &bad);
+  if (a.group_by_tenant && tn < 0) bad = true;
+  if (bad) {
+    if (status) atomicCAS(status, 0, (int)kDevBadIndex);
+    return kSentKey;
+  }
+  if (a.group_by_tenant) return (uint32_t)(tn * a.E_tot + e);
+  return (uint32_t)(e * a.tkeys + (tn + 1));
+}
+
+__device__ __forceinline__ void bitonic_sort_2048(uint32_t* s) {
+  // 1024 threads, one compare-exchange pair each per stage.
+  const int tid = threadIdx.x;
+  for (int k = 2; k <= kPermChunk; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int i = 2 * tid - (tid & (j - 1));
+      const int ixj = i + j;
+      const bool up = (i & k) == 0;
+      const uint32_t a = s[i], b = s[ixj];
+      if ((a > b) == up) {
+        s[i] = b;
+        s[ixj] = a;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// First index in sorted s[0..n) whose key field is >= key.
+__device__ __forceinline__ int lower_bound_key(const uint32_t* s, int n, uint32_t key) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if ((s[mid] >> 11) < key)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(1024) perm_count_kernel(PairSrc a, int nkeys, uint32_t* sorted_out,
+                                                           int32_t* hist, int32_t* status) {
+  __shared__ uint32_t s[kPermChunk];
+  const int64_t base = (int64_t)blockIdx.x * kPermChunk;
+  for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
+    const int64_t p = base + i;
+    s[i] = (p < a.P) ? ((pair_key(a, p, status) << 11) | (uint32_t)i) : 0xFFFFFFFFu;
+  }
+  __syncthreads();
+  bitonic_sort_2048(s);
+  for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
+    const uint32_t v = s[i];
+    sorted_out[base + i] = v;
+    const uint32_t key = v >> 11;
+    if (key == kSentKey) continue;
+    if (i == kPermChunk - 1 || (s[i + 1] >> 11) != key) {
+      const int start = lower_bound_key(s, i + 1, key);
+      hist[(int64_t)blockIdx.x * nkeys + key] = i - start + 1;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restrict__ hist, int32_t* __restrict__ off,
+                                                          int nkeys, int nchunks, int tkeys, int n_groups,
+                                                          stageml_moe_plan plan) {
+  extern __shared__ int32_t tot[];  // [nkeys]
+  __shared__ int32_t warp_part[32];
+  const int tid = threadIdx.x;
+  // 1. per-key totals (coalesced over keys)
+  for (int key = tid; key < nkeys; key += 1024) {
+    int s = 0;
+    for (int c = 0; c < nchunks; ++c) s += hist[(int64_t)c * nkeys + key];
+    tot[key] = s;
+  }
+  __syncthreads();
+  // 2. per-group real counts; padded sizes parked in group_offsets[g]
+  for (int g = tid; g < n_groups; g += 1024) {
+    int cnt = 0;
+    for (int tk = 0; tk < tkeys; ++tk) cnt += tot[g * tkeys + tk];
+    plan.group_counts[g] = cnt;
+    plan.group_offsets[g] = (cnt + 127) & ~127;
+  }
+  __syncthreads();
+  // 3. exclusive scan of padded sizes (each thread a contiguous run of groups)
+  const int per = (n_groups + 1023) / 1024;
+  const int g0 = min(tid * per, n_groups), g1 = min(g0 + per, n_groups);
+  int local = 0;
+  for (int g = g0; g < g1; ++g) local += plan.group_offsets[g];
+  int incl = local;
+  const int lane = tid & 31, wid = tid >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_part[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    int w = warp_part[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += v;
+    }
+    warp_part[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  int run = incl - local + (wid > 0 ? warp_part[wid - 1] : 0);
+  for (int g = g0; g < g1; ++g) {
+    const int sz = plan.group_offsets[g];
+    plan.group_offsets[g] = run;
+    run += sz;
+  }
+  if (tid == 1023) {
+    plan.group_offsets[n_groups] = run;
+    plan.num_tiles[0] = run / 128;
+  }
+  __syncthreads();
+  // 4. key bases (in place in tot), tile -> group, padding rows
+  for (int g = tid; g < n_groups; g += 1024) {
+    const int o = plan.group_offsets[g];
+    const int cnt = plan.group_counts[g];
+    const int end = o + ((cnt + 127) & ~127);
+    for (int t = o / 128; t < end / 128; ++t) plan.tile_group[t] = g;
+    for (int r = o + cnt; r < end; ++r) {
+      plan.row_token[r] = -1;
+      plan.row_tenant[r] = -1;
+      plan.row_weight[r] = 0.f;
+      plan.row_pair[r] = -1;
+    }
+    int b = o;
+    for (int tk = 0; tk < tkeys; ++tk) {
+      const int key = g * tkeys + tk;
+      const int v = tot[key];
+      tot[key] = b;
+      b += v;
+    }
+  }
+  __syncthreads();
+  // 5. per-(chunk, key) destination offsets
+  for (int key = tid; key < nkeys; key += 1024) {
+    int b = tot[key];
+    for (int c = 0; c < nchunks; ++c) {
+      const int v = hist[(int64_t)c * nkeys + key];
+      off[(int64_t)c * nkeys + key] = b;
+      b += v;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(1024) perm_scatter_kernel(PairSrc a, int nkeys, const uint32_t* __restrict__ sorted,
+                                                             const int32_t* __restrict__ off, stageml_moe_plan plan) {
+  __shared__ uint32_t s[kPermChunk];
+  const int64_t base = (int64_t)blockIdx.x * kPermChunk;
+  for (int i = threadIdx.x; i < kPermChunk; i += 1024) s[i] = sorted[base + i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
+    const uint32_t v = s[i];
+    const int64_t p = base + (v & 2047u);
+    if (p >= a.P) continue;
+    const uint32_t key = v >> 11;
+    if (key == kSentKey) {
+      plan.pair_row[p] = -1;
+      continue;
+    }
+    const int start = lower_bound_key(s, i, key);
+    const int row = off[(int64_t)blockIdx.x * nkeys + key] + (i - start);
+    const int t = (int)(p / a.kk);
+    const int j = (int)(p - (int64_t)t * a.kk);
+    bool dummy = false;
+    const int tn = pair_tenant(a, t, &dummy);
+    plan.row_token[row] = t;
+    plan.row_tenant[row] = a.group_by_tenant ? -1 : tn;
+    plan.row_weight[row] = pair_weight(a, t, j);
+    plan.row_pair[row] = (int32_t)p;
+    plan.pair_row[p] = row;
+  }
+}
+
+}  // namespace
+
+int64_t permute_num_keys(int n_groups_total, int n_tenants, int group_by_tenant, int n_experts_total) {
+  (void)n_groups_total;
+  if (group_by_tenant) return (int64_t)n_tenants * n_experts_total;
+  return (int64_t)n_experts_total * (n_tenants + 1);
+}
+
+static int64_t nchunks_of(int64_t P) { return (P + kPermChunk - 1) / kPermChunk; }
+
+size_t permute_scratch_bytes(int64_t P, int64_t nkeys) {
+  const int64_t nch = nchunks_of(P);
+  size_t b = 0;
+  b += ((size_t)nch * kPermChunk * 4 + 255) & ~size_t(255);
+  b += ((size_t)nkeys * nch * 4 + 255) & ~size_t(255);
+  b += ((size_t)nkeys * nch * 4 + 255) & ~size_t(255);
+  return b;
+}
+
+void permute_carve(void* base, int64_t P, int64_t nkeys, PermuteScratch* out) {
+  const int64_t nch = nchunks_of(P);
+  uint8_t* p = static_cast<uint8_t*>(base);
+  out->sorted = reinterpret_cast<uint32_t*>(p);
+  p += ((size_t)nch * kPermChunk * 4 + 255) & ~size_t(255);
+  out->hist = reinterpret_cast<int32_t*>(p);
+  p += ((size_t)nkeys * nch * 4 + 255) & ~size_t(255);
+  out->off = reinterpret_cast<int32_t*>(p);
+}
+
+int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
+                   int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
+                   const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream) {
+  SB_CHECK_ARG(T >= 0 && k >= 0 && n_shared >= 0, "permute: negative size");
+  SB_CHECK_ARG(k + n_shared >= 1, "permute: need at least one slot per token");
+  SB_CHECK_ARG(n_experts_total > n_shared || (k == 0 && n_experts_total == n_shared),
+               "permute: n_experts_total=%d must exceed n_shared=%d", n_experts_total, n_shared);
+  SB_CHECK_ARG(ids_dtype == STAGEML_I32 || ids_dtype == STAGEML_I64, "permute: ids must be int32 or int64");
+  SB_CHECK_ARG(k == 0 || ids, "permute: null ids");
+  SB_CHECK_ARG(!weights || weights_dtype == STAGEML_F32 || weights_dtype == STAGEML_BF16 ||
+                   weights_dtype == STAGEML_F16,
+               "permute: weights must be f32, bf16 or f16");
+  SB_CHECK_ARG(n_tenants >= 0, "permute: negative tenant count");
+  SB_CHECK_ARG(!group_by_tenant || (tenant_ids && n_tenants > 0), "permute: group_by_tenant needs tenant ids");
+  const int64_t P = (int64_t)T * (k + n_shared);
+  const int64_t nkeys = permute_num_keys(0, n_tenants, group_by_tenant, n_experts_total);
+  const int n_groups = group_by_tenant ? n_tenants * n_experts_total : n_experts_total;
+  SB_CHECK_ARG(nkeys >= 1 && nkeys <= kMaxKeys, "permute: %lld (expert, tenant) keys exceed the limit %d",
+               (long long)nkeys, kMaxKeys);
+  SB_CHECK_ARG(plan.rows_cap >= stageml_plan_rows_cap(P, n_groups), "permute: plan rows_cap %lld < required %lld",
+               (long long)plan.rows_cap, (long long)stageml_plan_rows_cap(P, n_groups));
+  SB_CHECK_ARG(plan.row_token && plan.row_tenant && plan.row_weight && plan.row_pair && plan.tile_group &&
+                   plan.group_offsets && plan.group_counts && plan.num_tiles && (P == 0 || plan.pair_row),
+               "permute: null plan array");
+  SB_CHECK_ARG(P < (int64_t(1) << 31), "permute: too many pairs");
+
+  PairSrc a;
+  a.ids = ids;
+  a.ids_i64 = ids_dtype == STAGEML_I64;
+  a.weights = weights;
+  a.weights_dtype = weights_dtype;
+  a.tenant_ids = tenant_ids;
+  a.T = T;
+  a.k = k;
+  a.kk = k + n_shared;
+  a.E_tot = n_experts_total;
+  a.E_routed = n_experts_total - n_shared;
+  a.n_tenants = n_tenants;
+  a.group_by_tenant = group_by_tenant;
+  a.tkeys = group_by_tenant ? 1 : n_tenants + 1;
+  a.P = P;
+
+  const int64_t nch = nchunks_of(P);
+  if (nch > 0) {
+    SB_CUDA_CHECK(cudaMemsetAsync(scr.hist, 0, (size_t)nkeys * nch * 4, stream));
+    perm_count_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.hist, status);
+    SB_CUDA_CHECK(cudaGetLastError());
+  }
+  const size_t smem = (size_t)nkeys * 4;
+  SB_CUDA_CHECK(cudaFuncSetAttribute(perm_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  perm_scan_kernel<<<1, 1024, smem, stream>>>(scr.hist, scr.off, (int)nkeys, (int)nch, a.tkeys, n_groups, plan);
+  SB_CUDA_CHECK(cudaGetLastError());
+  if (nch > 0) {
+    perm_scatter_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.off, plan);
+    SB_CUDA_CHECK(cudaGetLastError());
+  }
+  return STAGEML_OK;
+}
+
+}  // namespace sb
+
+extern "C" int64_t stageml_plan_rows_cap(int64_t num_pairs, int n_groups) {
+  if (num_pairs <= 0) return 128;
+  const int64_t g = n_groups < num_pairs ? n_groups : num_pairs;
+  const int64_t r = num_pairs + g * 127;
+  return (r + 127) / 128 * 128;
+}
