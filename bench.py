@@ -1,0 +1,457 @@
+"""Benchmark of the StageML MoE-LoRA residual path on B200.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--workload NAME]
+
+One step = one MoE-LoRA FFN layer call (router -> permutation -> SwiGLU experts
+with per-token-tenant LoRA on w1/w3/w2 -> combine) over one batch of tokens
+already resident in HBM. Metric: layer tokens/s (whole job, all ranks).
+
+N = 1: the Mixtral-shape layer (T=2048, H=4096, I=14336, E=8, top-2, rank-16
+LoRA for 32 tenants, bf16). N > 1 (torchrun, one process per GPU, NCCL):
+expert parallel -- each rank routes its own 2048 tokens, experts are sharded
+E/N per rank with their adapter-bank slices, tokens are dispatched and
+combined with all-to-all (weak scaling: per-GPU work fixed).
+
+--impl reference: the oracle port of the reference's CPU path (numpy/OpenBLAS,
+float32) timed on the host cores on a token sample of the same workload; under
+torchrun only rank 0 runs it.
+
+Prints ONE JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            d["source"] = "measured"
+            return d
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU every ~20 ms (NVML, or nvidia-smi)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples: list[tuple[float, int, int]] = []
+        self._stop = threading.Event()
+        self._t = None
+        self.max_mhz = None
+        self._nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _poll(self):
+        while not self._stop.is_set():
+            try:
+                if self._nvml:
+                    sm = self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM)
+                    rs = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                else:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True).stdout
+                    a, b = out.strip().split(",")[:2]
+                    sm, rs = int(a), 0
+                    self.max_mhz = int(b)
+                self.samples.append((time.time(), int(sm), int(rs)))
+            except Exception:
+                pass
+            self._stop.wait(0.02)
+
+    def start(self):
+        self._t = threading.Thread(target=self._poll, daemon=True)
+        self._t.start()
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=2)
+        sms = [s[1] for s in self.samples]
+        reasons = set()
+        for _, _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        reasons.discard("gpu_idle")
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ------------------------------------------------------------------ helpers
+def capi():
+    from stageml_b200._native import load_capi
+
+    return load_capi()
+
+
+def stage_times(lib) -> dict:
+    import ctypes
+
+    from stageml_b200.capi import STAGE_NAMES
+
+    n = len(STAGE_NAMES)
+    ms = (ctypes.c_float * n)()
+    cnt = (ctypes.c_int32 * n)()
+    lib.stageml_stage_timer_read(ms, cnt, n)
+    return {STAGE_NAMES[i]: {"ms": float(ms[i]), "launches": int(cnt[i])} for i in range(n) if cnt[i] > 0}
+
+
+def cpu_threads() -> int:
+    n = os.cpu_count() or 1
+    try:
+        n = len(os.sched_getaffinity(0))
+    except Exception:
+        pass
+    return min(n, 64)  # numpy's OpenBLAS build caps at 64 threads
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------------ CPU arm
+def run_cpu_sample(cfg, w, sample_tokens: int, repeats: int, warmup: int, budget_s: float | None = None):
+    """Time the oracle port on `sample_tokens` tokens of the workload; returns (tokens_per_s, times)."""
+    import numpy as np
+
+    from oracle.moe import MoEExecutorF32
+    from oracle.route import route_topk
+
+    t0 = time.time()
+    f32 = lambda t: None if t is None else t.float().cpu().numpy()
+    ex = MoEExecutorF32(f32(w["gate_up"]), f32(w["down"]), n_shared=cfg.n_shared, lora_a13=f32(w["lora_a13"]),
+                        lora_b13=f32(w["lora_b13"]), lora_a2=f32(w["lora_a2"]), lora_b2=f32(w["lora_b2"]),
+                        lora_scale=f32(w["lora_scale"]))
+    x = f32(w["x"][:sample_tokens])
+    gw = f32(w["router_w"])
+    ten = w["tenant_ids"][:sample_tokens].cpu().numpy()
+    log(f"cpu arm: weights on host in {time.time() - t0:.1f}s; {cpu_threads()} threads, {cpu_model()}")
+
+    def step():
+        ids, wts, _ = route_topk(x, gw, cfg.k, True)
+        return ex(x, ids, wts, ten)
+
+    for _ in range(warmup):
+        step()
+    times = []
+    for i in range(repeats):
+        t = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t)
+        if budget_s is not None and sum(times) > budget_s and i >= 0:
+            break
+    return sample_tokens / statistics.median(times), times
+
+
+def reference_arm(args, cfg, rank: int):
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+
+    from stageml_b200.workloads import make_moe_workload
+
+    torch.cuda.set_device(0)
+    w = make_moe_workload(cfg, device="cuda", seed=0)
+    sample = args.cpu_sample_tokens
+    tps, times = run_cpu_sample(cfg, w, sample, repeats=args.steps, warmup=args.warmup)
+    cores = cpu_threads()
+    line = {
+        "metric": "MoE-LoRA layer tokens/s", "value": round(tps, 3), "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": round(1000 * statistics.mean(times), 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; shapes of the Mixtral layer)",
+        "config": {"workload": cfg.name, "tokens_per_step": sample, "hidden": cfg.H, "intermediate": cfg.I,
+                   "experts": cfg.E, "top_k": cfg.k, "lora_rank": cfg.rank, "tenants": cfg.n_tenants},
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} of {cfg.T} tokens per step (all experts and tenants touched), oracle "
+                                   f"numpy/OpenBLAS float32 grouped executor incl. router, {cpu_model()}"},
+        "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+def layer_call(ops, cfg, w, x, tenant_ids):
+    return ops.moe_forward(x, w["gate_up"], w["down"], router_w=w["router_w"], k=cfg.k, n_shared=cfg.n_shared,
+                           renormalize=True, tenant_ids=tenant_ids, n_tenants=cfg.n_tenants, rank=cfg.rank,
+                           lora_a13=w["lora_a13"], lora_b13=w["lora_b13"], lora_a2=w["lora_a2"],
+                           lora_b2=w["lora_b2"], lora_scale=w["lora_scale"], gate_up_scale=w["gate_up_scale"],
+                           down_scale=w["down_scale"])
+
+
+def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
+    import stageml_b200.ops as ops
+    from stageml_b200.workloads import make_moe_workload, moe_bytes
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = capi()
+    peaks = load_peaks()
+    T = args.tokens or cfg.T
+    t_gen = time.time()
+    if world > 1:
+        from stageml_b200.expert_parallel import EPMoELayer
+
+        w = make_moe_workload(cfg, device=dev, seed=0, T=T)  # identical weights on every rank (seed 0)
+        x_local = make_moe_workload_tokens(cfg, dev, seed=1000 + rank, T=T)
+        w["x"], w["tenant_ids"] = x_local
+        layer = EPMoELayer.from_full_weights(cfg, w, rank=rank, world=world)
+        call = lambda x, ten: layer(x, ten)
+    else:
+        w = make_moe_workload(cfg, device=dev, seed=0, T=T)
+        call = lambda x, ten: layer_call(ops, cfg, w, x, ten)
+    torch.cuda.synchronize()
+    log(f"rank {rank}: workload {cfg.name} T={T} ready in {time.time() - t_gen:.1f}s")
+
+    x, ten = w["x"], w["tenant_ids"]
+    for _ in range(args.warmup):
+        call(x, ten)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+
+    # ---- timed region: device-resident inputs
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.05)
+    lib.stageml_stage_timer_enable(1)
+    n0 = lib.stageml_launch_count()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call(x, ten)
+    e1.record()
+    torch.cuda.synchronize()
+    n1 = lib.stageml_launch_count()
+    lib.stageml_stage_timer_enable(0)
+    clocks = sampler.stop()
+    ms_total = e0.elapsed_time(e1)
+    stages = stage_times(lib)
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = world * T / (ms_step / 1000.0)
+
+    # ---- end to end: pinned host input -> device -> layer -> host output, every step
+    x_host = x.cpu().pin_memory()
+    ten_host = ten.cpu().pin_memory()
+    out_host = torch.empty((T, cfg.H), dtype=x.dtype).pin_memory()
+    x_dev = torch.empty_like(x)
+    ten_dev = torch.empty_like(ten)
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        ten_dev.copy_(ten_host, non_blocking=True)
+        y = call(x_dev, ten_dev)
+        out_host.copy_(y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e_value = world * T / (ms_e2e / e2e_steps / 1000.0)
+    h2d = x_host.numel() * x_host.element_size() + ten_host.numel() * ten_host.element_size()
+    d2h = out_host.numel() * out_host.element_size()
+
+    # ---- batch-1 latency (p50 over 200 calls, CUDA events), N=1 only
+    batch1 = None
+    if world == 1 and not args.skip_batch1:
+        xb, tb = x[:1].contiguous(), ten[:1].contiguous()
+        for _ in range(10):
+            call(xb, tb)
+        lat = []
+        for _ in range(200):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            call(xb, tb)
+            b.record()
+            b.synchronize()
+            lat.append(a.elapsed_time(b) * 1000.0)
+        lat.sort()
+        batch1 = {"p50_us": round(lat[len(lat) // 2], 2), "p95_us": round(lat[int(len(lat) * 0.95)], 2),
+                  "samples": len(lat)}
+
+    if rank != 0:
+        return
+    fl = cfg.flops(T)
+    dom = "gemm_gate_up"
+    dom_ms = stages[dom]["ms"] / max(stages[dom]["launches"], 1) if dom in stages else None
+    dom_flops = fl["gate_up"] + 2.0 * T * (cfg.k + cfg.n_shared) * 2 * cfg.I * cfg.rank
+    peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    achieved = dom_flops / (dom_ms / 1000.0) / 1e12 if dom_ms else None
+    by = moe_bytes(cfg, w, T)
+    layer_bytes = by["weights"] + by["activations"]
+    t_roof = max(fl["total"] / (peak_tf * 1e12), layer_bytes / (float(peaks.get("hbm_gbs", 6650.0)) * 1e9))
+    # DRAM traffic of one gate/up GEMM launch from the committed ncu capture (see profiles/), or None
+    traffic = GATE_UP_DRAM_BYTES.get(cfg.name) if T == cfg.T else None
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        try:
+            tps, times = run_cpu_sample(cfg, w, args.cpu_sample_tokens, repeats=5, warmup=1, budget_s=20.0)
+            cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+                   "sample": f"{args.cpu_sample_tokens} of {T} tokens, median of {len(times)} timed calls after 1 "
+                             f"warm-up; oracle numpy/OpenBLAS float32 grouped executor incl. router; {cpu_model()}"}
+        except Exception as exc:  # pragma: no cover
+            cpu = {"value": None, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+                   "sample": f"failed: {exc}"}
+    line = {
+        "metric": "MoE-LoRA layer tokens/s",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1/fan_in) weights, N(0,1) tokens; no checkpoints available)",
+        "config": {"workload": cfg.name, "tokens_per_gpu": T, "global_batch": T * world, "hidden": cfg.H,
+                   "intermediate": cfg.I, "experts": cfg.E, "top_k": cfg.k, "lora_rank": cfg.rank,
+                   "tenants": cfg.n_tenants, "lora_on": "w1,w3,w2", "router": "in-layer (fp32 logits, softmax, top-2)",
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": f"inputs larger than L2 ({by['weights'] / 1e9:.2f} GB expert weights per step)"},
+        "roofline": {"bound": "tensor", "kernel": "grouped gate/up GEMM (tcgen05) + LoRA expand + SwiGLU",
+                     "achieved": None if achieved is None else round(achieved, 1), "peak": peak_tf,
+                     "unit": "TFLOP/s", "frac": None if achieved is None else round(achieved / peak_tf, 4),
+                     "traffic": traffic, "launch_ms": None if dom_ms is None else round(dom_ms, 4),
+                     "flops_per_launch": dom_flops,
+                     "peak_source": f"{peaks.get('source')} bf16_tflops_sustained (kernel timed inside the step)"},
+        "layer_roofline": {"flops": fl["total"], "bytes": layer_bytes, "t_roof_ms": round(t_roof * 1000, 4),
+                           "frac": round(t_roof * 1000 / ms_step, 4)},
+        "stages_ms_per_step": {k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in stages.items()},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps, "api": "torch.ops.stageml.moe_forward (pinned host in/out, copies timed)"},
+        "gpu_launches": int(n1 - n0),
+        "clocks": clocks,
+        "batch1_latency": batch1,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# DRAM bytes (read + write) of one full-size gate/up GEMM launch, from ncu
+# (profiles/gemm_gate_up_mixtral.md); None until captured.
+GATE_UP_DRAM_BYTES: dict = {}
+
+
+def make_moe_workload_tokens(cfg, dev, seed: int, T: int):
+    from stageml_b200.workloads import _Gen, sample_tenants
+
+    g = _Gen(seed, "cuda", dev)
+    x = g.normal((T, cfg.H), 1.0, torch.bfloat16)
+    ten = torch.tensor(sample_tenants(T, cfg.n_tenants, cfg.tenant_dist, cfg.alpha, seed=seed), dtype=torch.int32,
+                       device=dev)
+    return x, ten
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="mixtral_moe_lora")
+    ap.add_argument("--tokens", type=int, default=0, help="tokens per GPU per step (default: the workload's)")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=256)
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-batch1", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        log("note: warm-up raised to the minimum of 3 steps")
+        args.warmup = 3
+
+    sys.path.insert(0, str(ROOT))
+    from stageml_b200.workloads import MOE_CONFIGS
+
+    cfg = MOE_CONFIGS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, cfg, rank)
+        return
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        ours_arm(args, cfg, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

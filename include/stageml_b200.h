@@ -69,6 +69,31 @@ int stageml_abi_version(void);
 /* sizeof() of the public structs, so bindings can check their mirrors. 0 = plan, 1 = moe args, 2 = lora linear args. */
 size_t stageml_struct_size(int which);
 
+/* Per-stage device timing (benchmark support; no counterpart in the reference,
+ * whose timing is CUDA events around whole calls, stageml/benchmark_stats.py:85-113).
+ * While enabled on the calling thread, the entry points below record a CUDA
+ * event pair around each of their kernel stages on their stream.
+ * stageml_stage_timer_read waits for those events, adds the elapsed
+ * milliseconds of stage s to ms_out[s] and the number of timed launches to
+ * counts_out[s] (s < n), and forgets them. Disabled by default. */
+enum {
+  STAGEML_STAGE_ROUTE = 0,
+  STAGEML_STAGE_PERMUTE = 1,
+  STAGEML_STAGE_GATHER_SHRINK = 2, /* row gather + LoRA shrink of the layer input */
+  STAGEML_STAGE_GEMM_GATE_UP = 3,  /* grouped gate/up GEMM + LoRA expand + SwiGLU */
+  STAGEML_STAGE_SHRINK_H = 4,      /* LoRA shrink of the SwiGLU output */
+  STAGEML_STAGE_GEMM_DOWN = 5,     /* grouped down GEMM + LoRA expand + routing weight */
+  STAGEML_STAGE_COMBINE = 6,
+  STAGEML_STAGE_GEMM = 7,          /* the GEMM of lora_linear / moe_linear */
+  STAGEML_STAGE_FOLD = 8,
+  STAGEML_STAGE_GEMV = 9,
+  STAGEML_NUM_STAGES = 10
+};
+int stageml_stage_timer_enable(int on);
+int stageml_stage_timer_read(float* ms_out, int32_t* counts_out, int n);
+/* Number of kernels this library has launched in the process so far (all threads). */
+unsigned long long stageml_launch_count(void);
+
 /* ------------------------------------------------------------------ routing
  * Replaces make_routing (benchmarks/real_moe_lora_residual_bench.py:360-386)
  * followed by normalize_routing_weights (stageml/moe_lora_layers.py:178-183):

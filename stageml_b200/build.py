@@ -32,6 +32,7 @@ CU_SOURCES = [
     "fold.cu",
     "gemv.cu",
     "fp8.cu",
+    "stage_timer.cu",
     "capi.cu",
 ]
 NVCC_FLAGS = [

@@ -7,6 +7,14 @@
 #include "grouped_gemm.cuh"
 #include "host_util.h"
 #include "kernels.h"
+#include "stage_timer.h"
+
+// Launch `expr` as pipeline stage `stage` (timed when the stage timer is on).
+#define SB_STAGE(stage, expr)           \
+  do {                                  \
+    ::sb::StageScope _scope(stage, st); \
+    SB_TRY(expr);                       \
+  } while (0)
 
 namespace sb {
 namespace {
@@ -166,8 +174,8 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   const void* wts = a->topk_weights;
   int wts_dtype = a->weights_dtype;
   if (!ids && a->k > 0) {
-    SB_TRY(launch_router_logits(a->x, a->act_dtype, a->router_w, a->T, a->H, a->E, b.logits, st));
-    SB_TRY(launch_topk(b.logits, a->T, a->E, a->k, a->renormalize, b.ids, b.weights, st));
+    SB_STAGE(STAGEML_STAGE_ROUTE, launch_router_logits(a->x, a->act_dtype, a->router_w, a->T, a->H, a->E, b.logits, st));
+    SB_STAGE(STAGEML_STAGE_ROUTE, launch_topk(b.logits, a->T, a->E, a->k, a->renormalize, b.ids, b.weights, st));
     ids = b.ids;
     ids_dtype = STAGEML_I32;
     wts = b.weights;
@@ -177,7 +185,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   PermuteScratch scr;
   const int64_t nkeys = permute_num_keys(0, a->n_tenants, 0, E_tot);
   permute_carve(b.perm_scratch, P, nkeys, &scr);
-  SB_TRY(launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
+  SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
                         b.plan, status, scr, st));
   // gather + R4 shrink of w1|w3
   {
@@ -200,7 +208,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       s.s_out = b.s13;
       s.lora_scale = a->lora_scale;
     }
-    SB_TRY(launch_gather_shrink(s, st));
+    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(s, st));
   }
   // R3 + R5: gate/up GEMM, LoRA expand, SwiGLU
   {
@@ -229,7 +237,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
-    SB_TRY(launch_grouped_gemm(g, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, launch_grouped_gemm(g, st));
   }
   // R4 shrink of h for w2
   if (lora2) {
@@ -248,7 +256,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     s.spart = b.spart2;
     s.s_out = b.s2;
     s.lora_scale = a->lora_scale;
-    SB_TRY(launch_gather_shrink(s, st));
+    SB_STAGE(STAGEML_STAGE_SHRINK_H, launch_gather_shrink(s, st));
   }
   // R3 + R5: down GEMM, LoRA expand, routing weight
   {
@@ -278,10 +286,10 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;
-    SB_TRY(launch_grouped_gemm(g, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, launch_grouped_gemm(g, st));
   }
   // combine
-  SB_TRY(launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st));
+  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st));
   return STAGEML_OK;
 }
 
@@ -473,7 +481,7 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
   const int bf = dtype == STAGEML_BF16;
   PermuteScratch scr;
   permute_carve(perm, (int64_t)T * k, permute_num_keys(0, n_tenants, group_by_tenant, E), &scr);
-  SB_TRY(launch_permute(topk_ids, ids_dtype, topk_weights, weights_dtype, tenant_ids, T, k, 0, E,
+  SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(topk_ids, ids_dtype, topk_weights, weights_dtype, tenant_ids, T, k, 0, E,
                         group_by_tenant || lora ? n_tenants : 0, group_by_tenant, plan, stat, scr, st));
   ShrinkLaunch sh;
   sh.src = x;
@@ -494,7 +502,7 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
     sh.s_out = s;
     sh.lora_scale = lora_scale;
   }
-  SB_TRY(launch_gather_shrink(sh, st));
+  SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
   GemmLaunch g;
   g.a = xp;
   g.a_rows = plan.rows_cap;
@@ -522,16 +530,19 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
   g.out = yp;
   g.ldo = N;
   g.status = stat;
-  SB_TRY(launch_grouped_gemm(g, st));
-  return launch_combine(yp, plan.pair_row, T, k, N, bf, out, st);
+  SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
+  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(yp, plan.pair_row, T, k, N, bf, out, st));
+  return STAGEML_OK;
 }
 
 int stageml_lora_fold(const void* W, const void* A, const void* B, const float* scale, int batch, int rows, int cols,
                       int rank, int layout, int64_t w_batch_stride, int64_t a_batch_stride, int64_t b_batch_stride,
                       int dtype, void* out, stageml_stream_t stream) {
   clear_error();
-  return launch_lora_fold(W, A, B, scale, batch, rows, cols, rank, layout, w_batch_stride, a_batch_stride,
-                          b_batch_stride, dtype, out, static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SB_STAGE(STAGEML_STAGE_FOLD, launch_lora_fold(W, A, B, scale, batch, rows, cols, rank, layout, w_batch_stride,
+                                                a_batch_stride, b_batch_stride, dtype, out, st));
+  return STAGEML_OK;
 }
 
 static size_t lora_linear_carve(const stageml_lora_linear_args* a, void* ws, stageml_moe_plan* plan, void** perm,
@@ -629,7 +640,7 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
       sh.static_rows = a->M;
       sh.rows_cap = a->M;
       sh.row_tenant = ten;
-      SB_TRY(launch_gather_shrink(sh, st));
+      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
     }
     g.a = a->x;
     g.a_rows = a->M;
@@ -637,11 +648,12 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
     g.row_tenant = ten;
     g.out = a->y;
     g.ldo = a->N;
-    return launch_grouped_gemm(g, st);
+    SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
+    return STAGEML_OK;
   }
   PermuteScratch scr;
   permute_carve(perm, a->M, permute_num_keys(0, n_ten, 0, a->n_groups), &scr);
-  SB_TRY(launch_permute(a->row_group, STAGEML_I32, nullptr, STAGEML_F32, lora ? a->row_tenant : nullptr, a->M, 1, 0,
+  SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(a->row_group, STAGEML_I32, nullptr, STAGEML_F32, lora ? a->row_tenant : nullptr, a->M, 1, 0,
                         a->n_groups, n_ten, 0, plan, stat, scr, st));
   sh.src = a->x;
   sh.src_row_of = plan.row_token;
@@ -650,7 +662,7 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   sh.rows_cap = plan.rows_cap;
   sh.row_tenant = plan.row_tenant;
   sh.tile_group = plan.tile_group;
-  SB_TRY(launch_gather_shrink(sh, st));
+  SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
   g.a = xp;
   g.a_rows = plan.rows_cap;
   g.num_tiles_dev = plan.num_tiles;
@@ -659,8 +671,9 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   g.row_tenant = plan.row_tenant;
   g.out = yp;
   g.ldo = a->N;
-  SB_TRY(launch_grouped_gemm(g, st));
-  return launch_combine(yp, plan.pair_row, a->M, 1, a->N, bf, a->y, st);
+  SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
+  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(yp, plan.pair_row, a->M, 1, a->N, bf, a->y, st));
+  return STAGEML_OK;
 }
 
 size_t stageml_lora_gemv_f32_workspace_bytes(int M, int in_features, int out_features, int rank) {
@@ -677,8 +690,10 @@ int stageml_lora_gemv_f32(const float* x, const float* W, const float* A, const 
   if (!workspace || workspace_bytes < need)
     return set_error(STAGEML_ERR_WORKSPACE, "lora_gemv_f32: workspace of %zu bytes < required %zu",
                      workspace_bytes, need);
-  return launch_gemv_f32(x, W, A, B, scale, M, in_features, out_features, rank, y, workspace,
-                         static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SB_STAGE(STAGEML_STAGE_GEMV,
+           launch_gemv_f32(x, W, A, B, scale, M, in_features, out_features, rank, y, workspace, st));
+  return STAGEML_OK;
 }
 
 int stageml_quantize_e4m3_rows(const void* w, int dtype, int64_t rows, int64_t cols, uint8_t* q_out, float* scale_out,

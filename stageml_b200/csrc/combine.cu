@@ -58,18 +58,18 @@ int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H
       const int nt = std::min(65535, T_ - t0);
       dim3 g2(grid.x, (unsigned)nt);
       if (dtype_bf16)
-        combine_kernel<bf16><<<g2, block, 0, stream>>>(static_cast<const bf16*>(y), pair_row + (int64_t)t0 * kk, nt,
-                                                        kk, H, static_cast<bf16*>(out) + (int64_t)t0 * H);
+        (combine_kernel<bf16><<<g2, block, 0, stream>>>(static_cast<const bf16*>(y), pair_row + (int64_t)t0 * kk, nt,
+                                                        kk, H, static_cast<bf16*>(out) + (int64_t)t0 * H), ::sb::count_launch());
       else
-        combine_kernel<f16><<<g2, block, 0, stream>>>(static_cast<const f16*>(y), pair_row + (int64_t)t0 * kk, nt,
-                                                       kk, H, static_cast<f16*>(out) + (int64_t)t0 * H);
+        (combine_kernel<f16><<<g2, block, 0, stream>>>(static_cast<const f16*>(y), pair_row + (int64_t)t0 * kk, nt,
+                                                       kk, H, static_cast<f16*>(out) + (int64_t)t0 * H), ::sb::count_launch());
     }
   } else if (dtype_bf16) {
-    combine_kernel<bf16><<<grid, block, 0, stream>>>(static_cast<const bf16*>(y), pair_row, T_, kk, H,
-                                                      static_cast<bf16*>(out));
+    (combine_kernel<bf16><<<grid, block, 0, stream>>>(static_cast<const bf16*>(y), pair_row, T_, kk, H,
+                                                      static_cast<bf16*>(out)), ::sb::count_launch());
   } else {
-    combine_kernel<f16><<<grid, block, 0, stream>>>(static_cast<const f16*>(y), pair_row, T_, kk, H,
-                                                     static_cast<f16*>(out));
+    (combine_kernel<f16><<<grid, block, 0, stream>>>(static_cast<const f16*>(y), pair_row, T_, kk, H,
+                                                     static_cast<f16*>(out)), ::sb::count_launch());
   }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
@@ -78,7 +78,7 @@ int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H
 int launch_validate_tenants(const int32_t* in, int64_t n, int n_tenants, int32_t* out, int32_t* status,
                             cudaStream_t stream) {
   if (n == 0) return STAGEML_OK;
-  validate_tenants_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(in, n, n_tenants, out, status);
+  (validate_tenants_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(in, n, n_tenants, out, status), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }

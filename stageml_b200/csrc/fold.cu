@@ -192,22 +192,22 @@ int launch_lora_fold(const void* W, const void* A, const void* B, const float* s
   if (dtype == STAGEML_F32) {
     const int64_t n_el = (int64_t)rows * cols;
     const unsigned gx = (unsigned)std::min<int64_t>((n_el + 255) / 256, 8 * (int64_t)sm_count());
-    fold_scalar_kernel<float><<<dim3(gx, batch), 256, 0, stream>>>(f);
+    (fold_scalar_kernel<float><<<dim3(gx, batch), 256, 0, stream>>>(f), ::sb::count_launch());
   } else if (dtype == STAGEML_BF16 || dtype == STAGEML_F16) {
     if (aligned16 && rank <= 64) {
       dim3 grid((cols + FT_N - 1) / FT_N, (rows + FT_M - 1) / FT_M, batch);
       SB_CHECK_ARG(grid.y <= 65535u, "lora_fold: too many rows");
       if (dtype == STAGEML_BF16)
-        fold_mma_kernel<bf16><<<grid, 256, 0, stream>>>(f);
+        (fold_mma_kernel<bf16><<<grid, 256, 0, stream>>>(f), ::sb::count_launch());
       else
-        fold_mma_kernel<f16><<<grid, 256, 0, stream>>>(f);
+        (fold_mma_kernel<f16><<<grid, 256, 0, stream>>>(f), ::sb::count_launch());
     } else {
       const int64_t n_el = (int64_t)rows * cols;
       const unsigned gx = (unsigned)std::min<int64_t>((n_el + 255) / 256, 8 * (int64_t)sm_count());
       if (dtype == STAGEML_BF16)
-        fold_scalar_kernel<bf16><<<dim3(gx, batch), 256, 0, stream>>>(f);
+        (fold_scalar_kernel<bf16><<<dim3(gx, batch), 256, 0, stream>>>(f), ::sb::count_launch());
       else
-        fold_scalar_kernel<f16><<<dim3(gx, batch), 256, 0, stream>>>(f);
+        (fold_scalar_kernel<f16><<<dim3(gx, batch), 256, 0, stream>>>(f), ::sb::count_launch());
     }
   } else {
     return set_error(STAGEML_ERR_INVALID_ARG, "lora_fold: unsupported dtype %d", dtype);

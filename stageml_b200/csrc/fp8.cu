@@ -45,11 +45,11 @@ int launch_quantize_e4m3_rows(const void* w, int dtype, int64_t rows, int64_t co
   SB_CHECK_ARG(rows >= 0 && cols >= 0 && rows <= 0x7fffffff, "quantize_e4m3_rows: bad sizes");
   if (rows == 0) return STAGEML_OK;
   if (dtype == STAGEML_F32)
-    quantize_rows_kernel<float><<<(unsigned)rows, 256, 0, stream>>>(static_cast<const float*>(w), cols, q, scale);
+    (quantize_rows_kernel<float><<<(unsigned)rows, 256, 0, stream>>>(static_cast<const float*>(w), cols, q, scale), ::sb::count_launch());
   else if (dtype == STAGEML_BF16)
-    quantize_rows_kernel<bf16><<<(unsigned)rows, 256, 0, stream>>>(static_cast<const bf16*>(w), cols, q, scale);
+    (quantize_rows_kernel<bf16><<<(unsigned)rows, 256, 0, stream>>>(static_cast<const bf16*>(w), cols, q, scale), ::sb::count_launch());
   else if (dtype == STAGEML_F16)
-    quantize_rows_kernel<f16><<<(unsigned)rows, 256, 0, stream>>>(static_cast<const f16*>(w), cols, q, scale);
+    (quantize_rows_kernel<f16><<<(unsigned)rows, 256, 0, stream>>>(static_cast<const f16*>(w), cols, q, scale), ::sb::count_launch());
   else
     return set_error(STAGEML_ERR_INVALID_ARG, "quantize_e4m3_rows: unsupported dtype %d", dtype);
   SB_CUDA_CHECK(cudaGetLastError());

@@ -133,11 +133,11 @@ int launch_gemv_f32(const float* x, const float* W, const float* A, const float*
   SB_CHECK_ARG(smem1 <= 200 * 1024, "lora_gemv_f32: K slice too large");
   SB_CUDA_CHECK(cudaFuncSetAttribute(gemv_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
   dim3 g1((out_f + GV_COLS - 1) / GV_COLS, KS);
-  gemv_partial_kernel<<<g1, 128, smem1, stream>>>(x, W, A, M, in_f, out_f, A ? rank : 0, slice, part, xa_part);
+  (gemv_partial_kernel<<<g1, 128, smem1, stream>>>(x, W, A, M, in_f, out_f, A ? rank : 0, slice, part, xa_part), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   const size_t smem2 = (size_t)M * (A ? rank : 1) * 4;
-  gemv_reduce_kernel<<<(out_f + 255) / 256, 256, smem2, stream>>>(part, xa_part, A ? B : nullptr, scale, M, out_f,
-                                                                   A ? rank : 0, KS, y);
+  (gemv_reduce_kernel<<<(out_f + 255) / 256, 256, smem2, stream>>>(part, xa_part, A ? B : nullptr, scale, M, out_f,
+                                                                   A ? rank : 0, KS, y), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }

@@ -421,7 +421,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
                                          SMEM_BYTES));
       attr_set = true;
     }
-    grouped_gemm_kernel<bf16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, p);
+    (grouped_gemm_kernel<bf16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, p), ::sb::count_launch());
   } else {
     static bool attr_set = false;
     if (!attr_set) {
@@ -429,7 +429,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
                                          SMEM_BYTES));
       attr_set = true;
     }
-    grouped_gemm_kernel<f16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, p);
+    (grouped_gemm_kernel<f16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, p), ::sb::count_launch());
   }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;

@@ -1,4 +1,5 @@
 // Host-side helpers: thread-local error text, SM count, TMA tensor maps.
+#include <atomic>
 #include <mutex>
 #include <string.h>
 
@@ -19,6 +20,16 @@ int set_error(int code, const char* fmt, ...) {
 void clear_error() { g_last_error[0] = 0; }
 
 const char* last_error_text() { return g_last_error; }
+
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+}  // namespace sb
+
+extern "C" unsigned long long stageml_launch_count(void) { return sb::g_launches.load(std::memory_order_relaxed); }
+
+namespace sb {
 
 int sm_count() {
   static int cached[64] = {0};

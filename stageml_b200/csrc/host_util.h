@@ -16,6 +16,9 @@ int set_error(int code, const char* fmt, ...);
 void clear_error();
 const char* last_error_text();
 
+// Count one kernel launch made by this library (reported by stageml_launch_count).
+void count_launch();
+
 // Multiprocessor count of the current device (cached per device).
 int sm_count();
 

@@ -322,15 +322,15 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
   const int64_t nch = nchunks_of(P);
   if (nch > 0) {
     SB_CUDA_CHECK(cudaMemsetAsync(scr.hist, 0, (size_t)nkeys * nch * 4, stream));
-    perm_count_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.hist, status);
+    (perm_count_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.hist, status), ::sb::count_launch());
     SB_CUDA_CHECK(cudaGetLastError());
   }
   const size_t smem = (size_t)nkeys * 4;
   SB_CUDA_CHECK(cudaFuncSetAttribute(perm_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  perm_scan_kernel<<<1, 1024, smem, stream>>>(scr.hist, scr.off, (int)nkeys, (int)nch, a.tkeys, n_groups, plan);
+  (perm_scan_kernel<<<1, 1024, smem, stream>>>(scr.hist, scr.off, (int)nkeys, (int)nch, a.tkeys, n_groups, plan), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   if (nch > 0) {
-    perm_scatter_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.off, plan);
+    (perm_scatter_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.off, plan), ::sb::count_launch());
     SB_CUDA_CHECK(cudaGetLastError());
   }
   return STAGEML_OK;

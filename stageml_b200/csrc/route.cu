@@ -150,7 +150,7 @@ int launch_topk(const float* logits, int T_, int E, int k, int renorm, int32_t* 
   if (T_ == 0) return STAGEML_OK;
   SB_CHECK_ARG(logits && ids && weights, "top-k: null pointer");
   const int wpb = 8;
-  topk_kernel<<<(T_ + wpb - 1) / wpb, wpb * 32, 0, stream>>>(logits, T_, E, k, renorm, ids, weights);
+  (topk_kernel<<<(T_ + wpb - 1) / wpb, wpb * 32, 0, stream>>>(logits, T_, E, k, renorm, ids, weights), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
@@ -166,18 +166,18 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
   if (x_dtype == STAGEML_BF16) {
     SB_CUDA_CHECK(cudaFuncSetAttribute(router_logits_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
-    router_logits_kernel<bf16><<<grid, RT_THREADS, smem, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E,
-                                                                    logits);
+    (router_logits_kernel<bf16><<<grid, RT_THREADS, smem, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E,
+                                                                    logits), ::sb::count_launch());
   } else if (x_dtype == STAGEML_F16) {
     SB_CUDA_CHECK(cudaFuncSetAttribute(router_logits_kernel<f16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
-    router_logits_kernel<f16><<<grid, RT_THREADS, smem, stream>>>(static_cast<const f16*>(x), gate_w, T_, H, E,
-                                                                   logits);
+    (router_logits_kernel<f16><<<grid, RT_THREADS, smem, stream>>>(static_cast<const f16*>(x), gate_w, T_, H, E,
+                                                                   logits), ::sb::count_launch());
   } else if (x_dtype == STAGEML_F32) {
     SB_CUDA_CHECK(cudaFuncSetAttribute(router_logits_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
-    router_logits_kernel<float><<<grid, RT_THREADS, smem, stream>>>(static_cast<const float*>(x), gate_w, T_, H,
-                                                                     E, logits);
+    (router_logits_kernel<float><<<grid, RT_THREADS, smem, stream>>>(static_cast<const float*>(x), gate_w, T_, H,
+                                                                     E, logits), ::sb::count_launch());
   } else {
     return set_error(STAGEML_ERR_INVALID_ARG, "router: unsupported x dtype %d", x_dtype);
   }

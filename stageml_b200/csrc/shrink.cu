@@ -204,14 +204,14 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   dim3 grid(KS, (unsigned)((rows_max + 63) / 64));
   SB_CHECK_ARG(grid.y <= 65535u, "shrink: too many rows for one launch");
   if (s.dtype_bf16)
-    gather_shrink_kernel<bf16><<<grid, 128, 0, stream>>>(p);
+    (gather_shrink_kernel<bf16><<<grid, 128, 0, stream>>>(p), ::sb::count_launch());
   else
-    gather_shrink_kernel<f16><<<grid, 128, 0, stream>>>(p);
+    (gather_shrink_kernel<f16><<<grid, 128, 0, stream>>>(p), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {
     const int64_t n = rows_max * s.R;
-    shrink_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-        s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale, s.s_out);
+    (shrink_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+        s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale, s.s_out), ::sb::count_launch());
     SB_CUDA_CHECK(cudaGetLastError());
   }
   return STAGEML_OK;

@@ -1,0 +1,24 @@
+// Optional per-stage CUDA-event timing of the pipeline entry points.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace sb {
+
+bool stage_timer_on();
+void stage_timer_record(int stage, cudaStream_t stream, bool begin);
+
+// Records a begin event on construction and an end event on destruction
+// (only while the calling thread has the timer enabled).
+struct StageScope {
+  int stage;
+  cudaStream_t stream;
+  bool on;
+  StageScope(int s, cudaStream_t st) : stage(s), stream(st), on(stage_timer_on()) {
+    if (on) stage_timer_record(stage, stream, true);
+  }
+  ~StageScope() {
+    if (on) stage_timer_record(stage, stream, false);
+  }
+};
+
+}  // namespace sb
