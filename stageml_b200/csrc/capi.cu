@@ -81,9 +81,11 @@ struct MoeBuffers {
   void* xp = nullptr;    // [rows_cap, H]; reused for Y [rows_cap, H]
   void* hbuf = nullptr;  // [rows_cap, I]
   float* spart13 = nullptr;
-  float* s13 = nullptr;
+  void* s13 = nullptr;   // [rows_cap, 2r] 16-bit
   float* spart2 = nullptr;
-  float* s2 = nullptr;
+  void* s2 = nullptr;    // [rows_cap, r] 16-bit
+  int32_t* runs = nullptr;   // [tiles_cap, 128, 5]
+  int32_t* nruns = nullptr;  // [tiles_cap]
   int32_t* status = nullptr;
   size_t bytes = 0;
 };
@@ -100,8 +102,8 @@ int moe_validate(const stageml_moe_args* a) {
                "moe: weight_dtype must equal act_dtype or be E4M3");
   if (a->weight_dtype == STAGEML_E4M3)
     return set_error(STAGEML_ERR_UNSUPPORTED, "moe: E4M3 weights are not supported by this build");
-  SB_CHECK_ARG(a->rank >= 0 && a->rank % 8 == 0 && a->rank <= 32, "moe: rank=%d must be a multiple of 8 <= 32",
-               a->rank);
+  SB_CHECK_ARG(a->rank == 0 || a->rank == 16 || a->rank == 32,
+               "moe: rank=%d must be 0, 16 or 32 (zero-pad smaller ranks)", a->rank);
   const bool lora13 = a->rank > 0 && a->lora_a13;
   const bool lora2 = a->rank > 0 && a->lora_a2;
   SB_CHECK_ARG(!lora13 || a->lora_b13, "moe: lora_a13 without lora_b13");
@@ -141,11 +143,15 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
   b->hbuf = c.take_bytes((size_t)rows_cap * a->I * es);
   if (a->rank > 0 && a->lora_a13) {
     b->spart13 = c.take<float>((size_t)shrink_num_slices(a->H) * rows_cap * 2 * a->rank);
-    b->s13 = c.take<float>((size_t)rows_cap * 2 * a->rank);
+    b->s13 = c.take_bytes((size_t)rows_cap * 2 * a->rank * es);
   }
   if (a->rank > 0 && a->lora_a2) {
     b->spart2 = c.take<float>((size_t)shrink_num_slices(a->I) * rows_cap * a->rank);
-    b->s2 = c.take<float>((size_t)rows_cap * a->rank);
+    b->s2 = c.take_bytes((size_t)rows_cap * a->rank * es);
+  }
+  if (a->rank > 0 && (a->lora_a13 || a->lora_a2)) {
+    b->runs = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
+    b->nruns = c.take<int32_t>((size_t)(rows_cap / 128));
   }
   b->status = c.take<int32_t>(1);
   b->bytes = c.off;
@@ -187,6 +193,10 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   permute_carve(b.perm_scratch, P, nkeys, &scr);
   SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
                         b.plan, status, scr, st));
+  const int tiles_cap = (int)(b.plan.rows_cap / 128);
+  if (b.runs)
+    SB_STAGE(STAGEML_STAGE_PERMUTE,
+             launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   // gather + R4 shrink of w1|w3
   {
     ShrinkLaunch s;
@@ -225,13 +235,16 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.num_tiles_dev = b.plan.num_tiles;
     g.tiles_cap = (int)(b.plan.rows_cap / 128);
     g.tile_group = b.plan.tile_group;
-    g.row_tenant = b.plan.row_tenant;
     if (lora13) {
-      g.row_lora = b.s13;
+      g.s16 = b.s13;
+      g.s_rows = b.plan.rows_cap;
       g.rank = a->rank;
       g.lora_b = a->lora_b13;
       g.lora_b_group_stride = (int64_t)2 * a->I * a->rank;
       g.lora_b_tenant_stride = (int64_t)E_tot * g.lora_b_group_stride;
+      g.lora_b_rows_total = (int64_t)a->n_tenants * E_tot * 2 * a->I;
+      g.tile_runs = b.runs;
+      g.tile_nruns = b.nruns;
     }
     g.b_scale = a->gate_up_scale;
     g.out = b.hbuf;
@@ -273,13 +286,16 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.num_tiles_dev = b.plan.num_tiles;
     g.tiles_cap = (int)(b.plan.rows_cap / 128);
     g.tile_group = b.plan.tile_group;
-    g.row_tenant = b.plan.row_tenant;
     if (lora2) {
-      g.row_lora = b.s2;
+      g.s16 = b.s2;
+      g.s_rows = b.plan.rows_cap;
       g.rank = a->rank;
       g.lora_b = a->lora_b2;
       g.lora_b_group_stride = (int64_t)a->H * a->rank;
       g.lora_b_tenant_stride = (int64_t)E_tot * g.lora_b_group_stride;
+      g.lora_b_rows_total = (int64_t)a->n_tenants * E_tot * a->H;
+      g.tile_runs = b.runs;
+      g.tile_nruns = b.nruns;
     }
     g.row_scale = b.plan.row_weight;
     g.b_scale = a->down_scale;
@@ -293,25 +309,47 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   return STAGEML_OK;
 }
 
-// -------------------------------------------------- MoE single-linear layer
-struct MoeLinearDims {
-  int T, K, N, E, k, n_groups, rank;
+// ------------------------------------------ routed / grouped linear layers
+// Buffers shared by stageml_moe_linear and stageml_lora_linear.
+struct LinBuffers {
+  stageml_moe_plan plan{};
+  void* perm = nullptr;
+  void* xp = nullptr;     // permuted input rows [rows_cap, K]
+  float* spart = nullptr;
+  void* s = nullptr;      // 16-bit S [rows, rank]
+  void* yp = nullptr;     // permuted output rows [rows_cap, N]
+  int32_t* runs = nullptr;
+  int32_t* nruns = nullptr;
+  int32_t* tenants = nullptr;  // direct mode: validated row tenants
+  int32_t* status = nullptr;
+  size_t bytes = 0;
 };
 
-size_t moe_linear_carve(const MoeLinearDims& d, int n_tenants, int group_by_tenant, void* ws, stageml_moe_plan* plan,
-                        void** perm, void** xp, float** spart, float** s, void** yp, int32_t** status, int dtype) {
+// permuted: P pairs over n_groups groups (nkeys from n_tenants / group_by_tenant);
+// direct: rows = M, no permutation.
+void lin_carve(bool permuted, int64_t P_or_M, int n_groups, int n_tenants, int group_by_tenant, int K, int N, int rank,
+               int nkeys_groups, size_t es, void* ws, LinBuffers* b) {
   Carver c(ws);
-  const int64_t P = (int64_t)d.T * d.k;
-  carve_plan(c, P, d.n_groups, plan);
-  const int64_t rows_cap = plan->rows_cap;
-  const int64_t nkeys = permute_num_keys(0, n_tenants, group_by_tenant, d.E);
-  *perm = c.take_bytes(permute_scratch_bytes(P, nkeys));
-  *xp = c.take_bytes((size_t)rows_cap * d.K * esize(dtype));
-  *spart = d.rank > 0 ? c.take<float>((size_t)shrink_num_slices(d.K) * rows_cap * d.rank) : nullptr;
-  *s = d.rank > 0 ? c.take<float>((size_t)rows_cap * d.rank) : nullptr;
-  *yp = c.take_bytes((size_t)rows_cap * d.N * esize(dtype));
-  *status = c.take<int32_t>(1);
-  return c.off;
+  int64_t rows;
+  if (permuted) {
+    carve_plan(c, P_or_M, n_groups, &b->plan);
+    rows = b->plan.rows_cap;
+    b->perm = c.take_bytes(permute_scratch_bytes(P_or_M, permute_num_keys(0, n_tenants, group_by_tenant, nkeys_groups)));
+    b->xp = c.take_bytes((size_t)rows * K * es);
+    b->yp = c.take_bytes((size_t)rows * N * es);
+  } else {
+    rows = P_or_M;
+    b->tenants = c.take<int32_t>((size_t)std::max<int64_t>(rows, 1));
+  }
+  if (rank > 0) {
+    b->spart = c.take<float>((size_t)shrink_num_slices(K) * rows * rank);
+    b->s = c.take_bytes((size_t)rows * rank * es);
+    const int64_t tiles = (rows + 127) / 128;
+    b->runs = c.take<int32_t>((size_t)tiles * kMaxRunsPerTile * 5);
+    b->nruns = c.take<int32_t>((size_t)tiles);
+  }
+  b->status = c.take<int32_t>(1);
+  b->bytes = c.off;
 }
 
 }  // namespace
@@ -438,13 +476,11 @@ int stageml_residual_moe(const void* hidden, const void* gate_up, const void* do
 
 size_t stageml_moe_linear_workspace_bytes(int T, int K, int N, int E, int k, int group_by_tenant, int n_tenants,
                                           int rank) {
-  stageml_moe_plan plan;
-  void *perm, *xp, *yp;
-  float *spart, *s;
-  int32_t* st;
-  MoeLinearDims d{T, K, N, E, k, group_by_tenant ? n_tenants * E : E, group_by_tenant ? 0 : rank};
-  return moe_linear_carve(d, n_tenants, group_by_tenant, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &st,
-                          STAGEML_BF16);
+  LinBuffers b;
+  const int n_groups = group_by_tenant ? n_tenants * E : E;
+  lin_carve(true, (int64_t)T * k, n_groups, n_tenants, group_by_tenant, K, N, group_by_tenant ? 0 : rank, E, 2,
+            nullptr, &b);
+  return b.bytes;
 }
 
 int stageml_moe_linear(const void* x, const void* weight, const void* bias, const void* topk_ids, int ids_dtype,
@@ -458,80 +494,85 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
   SB_CHECK_ARG(K % 8 == 0 && N % 8 == 0, "moe_linear: K=%d and N=%d must be multiples of 8", K, N);
   SB_CHECK_ARG(is16(dtype), "moe_linear: dtype must be BF16 or F16");
   SB_CHECK_ARG(ids_dtype == STAGEML_I32 || ids_dtype == STAGEML_I64, "moe_linear: ids dtype");
-  SB_CHECK_ARG(rank >= 0 && rank % 8 == 0 && rank <= 32, "moe_linear: rank=%d must be a multiple of 8 <= 32", rank);
+  SB_CHECK_ARG(rank == 0 || rank == 16 || rank == 32, "moe_linear: rank=%d must be 0, 16 or 32", rank);
   const bool lora = rank > 0 && lora_a && !group_by_tenant;
   SB_CHECK_ARG(!lora || (lora_b && lora_scale && tenant_ids && n_tenants > 0), "moe_linear: incomplete LoRA inputs");
   SB_CHECK_ARG(!group_by_tenant || (tenant_ids && n_tenants > 0), "moe_linear: group_by_tenant needs tenant ids");
   if (T == 0) return STAGEML_OK;
   SB_CHECK_ARG(x && weight && topk_ids && out, "moe_linear: null tensor");
   SB_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(out), "moe_linear: 16-byte alignment");
+  if (lora) SB_CHECK_ARG(aligned16(lora_a) && aligned16(lora_b), "moe_linear: LoRA alignment");
   const int n_groups = group_by_tenant ? n_tenants * E : E;
-  MoeLinearDims d{T, K, N, E, k, n_groups, lora ? rank : 0};
-  stageml_moe_plan plan;
-  void *perm, *xp, *yp;
-  float *spart, *s;
-  int32_t* st_ws;
-  const size_t need =
-      moe_linear_carve(d, n_tenants, group_by_tenant, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &st_ws, dtype);
-  if (!workspace || workspace_bytes < need)
+  const int r = lora ? rank : 0;
+  LinBuffers b;
+  lin_carve(true, (int64_t)T * k, n_groups, n_tenants, group_by_tenant, K, N, r, E, esize(dtype), nullptr, &b);
+  if (!workspace || workspace_bytes < b.bytes)
     return set_error(STAGEML_ERR_WORKSPACE, "moe_linear: workspace of %zu bytes < required %zu", workspace_bytes,
-                     need);
-  moe_linear_carve(d, n_tenants, group_by_tenant, workspace, &plan, &perm, &xp, &spart, &s, &yp, &st_ws, dtype);
-  int32_t* stat = status ? status : st_ws;
+                     b.bytes);
+  lin_carve(true, (int64_t)T * k, n_groups, n_tenants, group_by_tenant, K, N, r, E, esize(dtype), workspace, &b);
+  int32_t* stat = status ? status : b.status;
   const int bf = dtype == STAGEML_BF16;
   PermuteScratch scr;
-  permute_carve(perm, (int64_t)T * k, permute_num_keys(0, n_tenants, group_by_tenant, E), &scr);
-  SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(topk_ids, ids_dtype, topk_weights, weights_dtype, tenant_ids, T, k, 0, E,
-                        group_by_tenant || lora ? n_tenants : 0, group_by_tenant, plan, stat, scr, st));
+  permute_carve(b.perm, (int64_t)T * k, permute_num_keys(0, n_tenants, group_by_tenant, E), &scr);
+  SB_STAGE(STAGEML_STAGE_PERMUTE,
+           launch_permute(topk_ids, ids_dtype, topk_weights, weights_dtype, tenant_ids, T, k, 0, E,
+                          group_by_tenant || lora ? n_tenants : 0, group_by_tenant, b.plan, stat, scr, st));
+  const int tiles_cap = (int)(b.plan.rows_cap / 128);
+  if (lora)
+    SB_STAGE(STAGEML_STAGE_PERMUTE,
+             launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   ShrinkLaunch sh;
   sh.src = x;
-  sh.src_row_of = plan.row_token;
-  sh.gather_dst = xp;
+  sh.src_row_of = b.plan.row_token;
+  sh.gather_dst = b.xp;
   sh.K = K;
   sh.dtype_bf16 = bf;
-  sh.num_tiles_dev = plan.num_tiles;
-  sh.rows_cap = plan.rows_cap;
-  sh.row_tenant = plan.row_tenant;
-  sh.tile_group = plan.tile_group;
+  sh.num_tiles_dev = b.plan.num_tiles;
+  sh.rows_cap = b.plan.rows_cap;
+  sh.row_tenant = b.plan.row_tenant;
+  sh.tile_group = b.plan.tile_group;
   if (lora) {
     sh.lora_a = lora_a;
     sh.a_group_stride = (int64_t)rank * K;
     sh.a_tenant_stride = (int64_t)E * sh.a_group_stride;
     sh.R = rank;
-    sh.spart = spart;
-    sh.s_out = s;
+    sh.spart = b.spart;
+    sh.s_out = b.s;
     sh.lora_scale = lora_scale;
   }
   SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
   GemmLaunch g;
-  g.a = xp;
-  g.a_rows = plan.rows_cap;
+  g.a = b.xp;
+  g.a_rows = b.plan.rows_cap;
   g.K = K;
   g.b = weight;
   g.b_rows_total = (int64_t)n_groups * N;
   g.b_group_rows = N;
   g.N = N;
   g.in_bf16 = bf;
-  g.num_tiles_dev = plan.num_tiles;
-  g.tiles_cap = (int)(plan.rows_cap / 128);
-  g.tile_group = plan.tile_group;
-  g.row_tenant = plan.row_tenant;
+  g.num_tiles_dev = b.plan.num_tiles;
+  g.tiles_cap = tiles_cap;
+  g.tile_group = b.plan.tile_group;
   if (lora) {
-    g.row_lora = s;
+    g.s16 = b.s;
+    g.s_rows = b.plan.rows_cap;
     g.rank = rank;
     g.lora_b = lora_b;
     g.lora_b_group_stride = (int64_t)N * rank;
     g.lora_b_tenant_stride = (int64_t)E * g.lora_b_group_stride;
+    g.lora_b_rows_total = (int64_t)n_tenants * E * N;
+    g.tile_runs = b.runs;
+    g.tile_nruns = b.nruns;
   }
   g.bias = bias;
   g.bias_group_stride = N;
   g.bias_group_mod = E;
-  g.row_scale = plan.row_weight;
-  g.out = yp;
+  g.row_scale = b.plan.row_weight;
+  g.out = b.yp;
   g.ldo = N;
   g.status = stat;
   SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
-  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(yp, plan.pair_row, T, k, N, bf, out, st));
+  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.yp, b.plan.pair_row, T, k, N, bf, out, st));
   return STAGEML_OK;
 }
 
@@ -545,37 +586,18 @@ int stageml_lora_fold(const void* W, const void* A, const void* B, const float* 
   return STAGEML_OK;
 }
 
-static size_t lora_linear_carve(const stageml_lora_linear_args* a, void* ws, stageml_moe_plan* plan, void** perm,
-                                void** xp, float** spart, float** s, void** yp, int32_t** tenants, int32_t** status) {
-  Carver c(ws);
-  const bool direct = a->n_groups == 1;
+static void lora_linear_carve(const stageml_lora_linear_args* a, void* ws, LinBuffers* b) {
   const bool lora = a->rank > 0 && a->lora_a && a->row_tenant;
-  *perm = *xp = *yp = nullptr;
-  *tenants = nullptr;
-  if (direct) {
-    *tenants = c.take<int32_t>(std::max(a->M, 1));
-    const int64_t rows = a->M;
-    *spart = lora ? c.take<float>((size_t)shrink_num_slices(a->K) * rows * a->rank) : nullptr;
-    *s = lora ? c.take<float>((size_t)rows * a->rank) : nullptr;
-  } else {
-    carve_plan(c, a->M, a->n_groups, plan);
-    *perm = c.take_bytes(permute_scratch_bytes(a->M, permute_num_keys(0, a->n_tenants, 0, a->n_groups)));
-    *xp = c.take_bytes((size_t)plan->rows_cap * a->K * 2);
-    *spart = lora ? c.take<float>((size_t)shrink_num_slices(a->K) * plan->rows_cap * a->rank) : nullptr;
-    *s = lora ? c.take<float>((size_t)plan->rows_cap * a->rank) : nullptr;
-    *yp = c.take_bytes((size_t)plan->rows_cap * a->N * 2);
-  }
-  *status = c.take<int32_t>(1);
-  return c.off;
+  const int n_ten = lora ? a->n_tenants : 0;
+  lin_carve(a->n_groups > 1, a->M, a->n_groups, n_ten, 0, a->K, a->N, lora ? a->rank : 0, a->n_groups,
+            esize(a->dtype) ? esize(a->dtype) : 2, ws, b);
 }
 
 size_t stageml_lora_linear_workspace_bytes(const stageml_lora_linear_args* a) {
   if (!a || a->M < 0 || a->n_groups < 1) return 0;
-  stageml_moe_plan plan;
-  void *perm, *xp, *yp;
-  float *spart, *s;
-  int32_t *ten, *st;
-  return lora_linear_carve(a, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &ten, &st);
+  LinBuffers b;
+  lora_linear_carve(a, nullptr, &b);
+  return b.bytes;
 }
 
 int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size_t workspace_bytes,
@@ -586,24 +608,21 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   SB_CHECK_ARG(a->M >= 0 && a->K > 0 && a->N > 0 && a->n_groups >= 1, "lora_linear: bad sizes");
   SB_CHECK_ARG(a->K % 8 == 0 && a->N % 8 == 0, "lora_linear: K=%d and N=%d must be multiples of 8", a->K, a->N);
   SB_CHECK_ARG(is16(a->dtype), "lora_linear: dtype must be BF16 or F16");
-  SB_CHECK_ARG(a->rank >= 0 && a->rank % 8 == 0 && a->rank <= 32, "lora_linear: rank=%d must be a multiple of 8 <= 32",
-               a->rank);
+  SB_CHECK_ARG(a->rank == 0 || a->rank == 16 || a->rank == 32, "lora_linear: rank=%d must be 0, 16 or 32", a->rank);
   const bool lora = a->rank > 0 && a->lora_a && a->row_tenant;
   SB_CHECK_ARG(!lora || (a->lora_b && a->lora_scale && a->n_tenants > 0), "lora_linear: incomplete LoRA inputs");
   SB_CHECK_ARG(a->n_groups == 1 || a->row_group, "lora_linear: n_groups > 1 needs row_group");
   if (a->M == 0) return STAGEML_OK;
   SB_CHECK_ARG(a->x && a->w_bank && a->y, "lora_linear: null tensor");
   SB_CHECK_ARG(aligned16(a->x) && aligned16(a->w_bank) && aligned16(a->y), "lora_linear: 16-byte alignment");
-  stageml_moe_plan plan;
-  void *perm, *xp, *yp;
-  float *spart, *s;
-  int32_t *ten, *st_ws;
-  const size_t need = lora_linear_carve(a, nullptr, &plan, &perm, &xp, &spart, &s, &yp, &ten, &st_ws);
-  if (!workspace || workspace_bytes < need)
+  if (lora) SB_CHECK_ARG(aligned16(a->lora_a) && aligned16(a->lora_b), "lora_linear: LoRA alignment");
+  LinBuffers b;
+  lora_linear_carve(a, nullptr, &b);
+  if (!workspace || workspace_bytes < b.bytes)
     return set_error(STAGEML_ERR_WORKSPACE, "lora_linear: workspace of %zu bytes < required %zu", workspace_bytes,
-                     need);
-  lora_linear_carve(a, workspace, &plan, &perm, &xp, &spart, &s, &yp, &ten, &st_ws);
-  int32_t* stat = a->status ? a->status : st_ws;
+                     b.bytes);
+  lora_linear_carve(a, workspace, &b);
+  int32_t* stat = a->status ? a->status : b.status;
   const int bf = a->dtype == STAGEML_BF16;
   const int n_ten = lora ? a->n_tenants : 0;
   GemmLaunch g;
@@ -624,55 +643,66 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
     sh.a_tenant_stride = (int64_t)a->rank * a->K;
     sh.a_group_stride = 0;
     sh.R = a->rank;
-    sh.spart = spart;
-    sh.s_out = s;
+    sh.spart = b.spart;
+    sh.s_out = b.s;
     sh.lora_scale = a->lora_scale;
-    g.row_lora = s;
+    g.s16 = b.s;
     g.rank = a->rank;
     g.lora_b = a->lora_b;
     g.lora_b_tenant_stride = (int64_t)a->N * a->rank;
     g.lora_b_group_stride = 0;
+    g.lora_b_rows_total = (int64_t)a->n_tenants * a->N;
+    g.tile_runs = b.runs;
+    g.tile_nruns = b.nruns;
   }
   if (a->n_groups == 1) {
-    SB_TRY(launch_validate_tenants(lora ? a->row_tenant : nullptr, a->M, n_ten, ten, stat, st));
     if (lora) {
+      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK,
+               launch_validate_tenants(a->row_tenant, a->M, n_ten, b.tenants, stat, st));
+      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK,
+               launch_tile_runs(b.tenants, nullptr, a->M, (int)((a->M + 127) / 128), b.runs, b.nruns, st));
       sh.src = a->x;
       sh.static_rows = a->M;
       sh.rows_cap = a->M;
-      sh.row_tenant = ten;
+      sh.row_tenant = b.tenants;
       SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
+      g.s_rows = a->M;
     }
     g.a = a->x;
     g.a_rows = a->M;
     g.m_rows = a->M;
-    g.row_tenant = ten;
     g.out = a->y;
     g.ldo = a->N;
     SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
     return STAGEML_OK;
   }
   PermuteScratch scr;
-  permute_carve(perm, a->M, permute_num_keys(0, n_ten, 0, a->n_groups), &scr);
-  SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(a->row_group, STAGEML_I32, nullptr, STAGEML_F32, lora ? a->row_tenant : nullptr, a->M, 1, 0,
-                        a->n_groups, n_ten, 0, plan, stat, scr, st));
+  permute_carve(b.perm, a->M, permute_num_keys(0, n_ten, 0, a->n_groups), &scr);
+  SB_STAGE(STAGEML_STAGE_PERMUTE,
+           launch_permute(a->row_group, STAGEML_I32, nullptr, STAGEML_F32, lora ? a->row_tenant : nullptr, a->M, 1, 0,
+                          a->n_groups, n_ten, 0, b.plan, stat, scr, st));
+  const int tiles_cap = (int)(b.plan.rows_cap / 128);
+  if (lora)
+    SB_STAGE(STAGEML_STAGE_PERMUTE,
+             launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   sh.src = a->x;
-  sh.src_row_of = plan.row_token;
-  sh.gather_dst = xp;
-  sh.num_tiles_dev = plan.num_tiles;
-  sh.rows_cap = plan.rows_cap;
-  sh.row_tenant = plan.row_tenant;
-  sh.tile_group = plan.tile_group;
+  sh.src_row_of = b.plan.row_token;
+  sh.gather_dst = b.xp;
+  sh.num_tiles_dev = b.plan.num_tiles;
+  sh.rows_cap = b.plan.rows_cap;
+  sh.row_tenant = b.plan.row_tenant;
+  sh.tile_group = b.plan.tile_group;
   SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
-  g.a = xp;
-  g.a_rows = plan.rows_cap;
-  g.num_tiles_dev = plan.num_tiles;
-  g.tiles_cap = (int)(plan.rows_cap / 128);
-  g.tile_group = plan.tile_group;
-  g.row_tenant = plan.row_tenant;
-  g.out = yp;
+  g.a = b.xp;
+  g.a_rows = b.plan.rows_cap;
+  g.num_tiles_dev = b.plan.num_tiles;
+  g.tiles_cap = tiles_cap;
+  g.tile_group = b.plan.tile_group;
+  g.s_rows = b.plan.rows_cap;
+  g.out = b.yp;
   g.ldo = a->N;
   SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
-  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(yp, plan.pair_row, a->M, 1, a->N, bf, a->y, st));
+  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.yp, b.plan.pair_row, a->M, 1, a->N, bf, a->y, st));
   return STAGEML_OK;
 }
 

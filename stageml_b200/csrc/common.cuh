@@ -156,6 +156,20 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// Same MMA, restricted to the accumulator rows (TMEM lanes) whose bit is 0 in
+// the 128-bit disable mask {m0, m1, m2, m3} (bit i of word w = lane 32*w + i);
+// masked lanes keep their previous value.
+__device__ __forceinline__ void tc_mma_f16_masked(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate, uint32_t m0, uint32_t m1, uint32_t m2,
+                                                  uint32_t m3) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op previously issued by this thread completes.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -187,6 +201,18 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   d |= static_cast<uint64_t>(1024 >> 4) << 32;    // SBO: 8 rows x 128 B
   d |= static_cast<uint64_t>(1) << 46;            // descriptor version for sm_100
   d |= static_cast<uint64_t>(2) << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Same for a K-major tile written by TMA with 32-byte swizzle: rows of 32 B
+// (16 x 16-bit), 8-row swizzle atoms 256 B apart. Layout code 6 = SWIZZLE_32B.
+__device__ __forceinline__ uint64_t smem_desc_sw32(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;            // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(256 >> 4) << 32;     // SBO: 8 rows x 32 B
+  d |= static_cast<uint64_t>(1) << 46;            // descriptor version for sm_100
+  d |= static_cast<uint64_t>(6) << 61;            // SWIZZLE_32B
   return d;
 }
 

@@ -9,12 +9,17 @@
 // Two 256-column accumulators in TMEM let the epilogue of tile i overlap the
 // main loop of tile i+1.
 //
-// Epilogue (fused, CUDA cores, fp32):
-//   LoRA expand: + sum_j S[row, j] * B_lora[tenant(row), group, col, j] (S already scaled)
-//   SwiGLU:      h = silu(g) * u over the paired gate / up accumulators
-//   plain:       (acc * b_scale[col] + bias[col] + lora) * row_scale[row]
-// This is the per-(slot, expert) body of RequestExecutor.dynamic_one
-// (benchmarks/multitenant_bta_system_bench.py:408-413) for a whole 128-row tile.
+// Per-token-tenant LoRA expand is fused on the tensor cores: after a tile's K
+// loop, the producer streams "LoRA blocks" through the same ring -- the
+// tile's 16-bit shrink output S (32B-swizzled, K = 16 per chunk) and, for each
+// distinct tenant of the tile, the matching rows of its B factor -- and the MMA
+// thread adds S . B^T into the same TMEM accumulator with the
+// disable-output-lane mask set to every row that does not belong to that
+// tenant. The epilogue is then only SwiGLU (or bias / routing weight) and the
+// 16-bit store. This is the per-(slot, expert) body of
+// RequestExecutor.dynamic_one (benchmarks/multitenant_bta_system_bench.py:408-413)
+// for a whole 128-row tile, with the LoRA branch of
+// DynamicMoELoRALayer.forward (stageml/moe_lora_layers.py:88-89) on every projection.
 #include "common.cuh"
 #include "grouped_gemm.cuh"
 #include "host_util.h"
@@ -32,6 +37,7 @@ constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 2 * BN;                  // double-buffered accumulator
 constexpr int NUM_THREADS = 192;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int LCHUNK = 128 * 32;                   // one 128-row x 16-column 16-bit LoRA tile (4 KB)
 
 struct KParams {
   int K;
@@ -43,13 +49,17 @@ struct KParams {
   int tiles_cap;
   const int32_t* tile_group;
   int64_t m_rows;
-  const int32_t* row_tenant;
-  const float* row_lora;
+  // LoRA
   int rank;
-  int lora_cols;
-  const void* lora_b;
-  int64_t lora_b_tenant_stride;
-  int64_t lora_b_group_stride;
+  int lchunks;         // rank / 16
+  int s_bytes;         // S bytes per LoRA block
+  int run_bytes;       // B bytes per run
+  int runs_per_block;
+  int64_t lb_tenant_rows;
+  int64_t lb_group_rows;
+  const int32_t* tile_runs;
+  const int32_t* tile_nruns;
+  // epilogue
   const float* row_scale;
   const void* bias;
   int64_t bias_group_stride;
@@ -71,29 +81,6 @@ struct IsBf16<bf16> {
 };
 
 template <typename T>
-__device__ __forceinline__ void lora_expand16(float (&acc)[16], const float (&s)[32], int r8, const T* bp,
-                                              int rank, int ncols_valid) {
-  // acc[i] += sum_j s[j] * bp[i*rank + j] for the first ncols_valid columns.
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    if (i < ncols_valid) {
-      float sum = 0.f;
-#pragma unroll
-      for (int j8 = 0; j8 < 4; ++j8) {
-        if (j8 < r8) {
-          const uint4 u = __ldg(reinterpret_cast<const uint4*>(bp + (int64_t)i * rank + j8 * 8));
-          float f[8];
-          unpack8<T>(u, f);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) sum = fmaf(s[j8 * 8 + q], f[q], sum);
-        }
-      }
-      acc[i] += sum;
-    }
-  }
-}
-
-template <typename T>
 __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_valid, bool vec_ok) {
   if (vec_ok && ncols_valid >= 16) {
     float lo[8], hi[8];
@@ -111,9 +98,16 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
   }
 }
 
+__device__ __forceinline__ int tile_lora_runs(const KParams& p, int m_tile) {
+  if (p.rank == 0) return 0;
+  const int n = p.tile_nruns[m_tile];
+  return n < kMaxRunsPerTile ? n : kMaxRunsPerTile;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_lb,
                         const KParams p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms.
@@ -163,6 +157,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ producer
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    if (p.rank) {
+      tma_prefetch_desc(&tm_s);
+      tma_prefetch_desc(&tm_lb);
+    }
     const uint64_t pol_a = l2_policy_evict_last();
     const uint64_t pol_b = l2_policy_evict_normal();
     int last_phase[STAGES];
@@ -174,14 +172,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int n_tile = tile / num_m_tiles;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int a_row = m_tile * BM;
-      int b_row0, b_row1;
-      if (p.swiglu) {
-        b_row0 = group * p.b_group_rows + n_tile * 128;
-        b_row1 = b_row0 + p.N;
-      } else {
-        b_row0 = group * p.b_group_rows + n_tile * BN;
-        b_row1 = b_row0 + 128;
-      }
+      const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
+      const int b_row0 = group * p.b_group_rows + n0;
+      const int b_row1 = p.swiglu ? b_row0 + p.N : b_row0 + 128;
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -197,6 +190,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_load_2d(sbm + 128 * BK * 2, &tm_b, full_bar(s), kb * BK, b_row1, pol_b);
         last_phase[s] = (int)ph;
       }
+      // LoRA blocks: S of the tile + B rows of each tenant run
+      const int nruns = ok ? tile_lora_runs(p, m_tile) : 0;
+      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
+        const int nr = min(p.runs_per_block, nruns - r0);
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(empty_bar(s), ph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const uint32_t base = smem_base + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(full_bar(s), p.s_bytes + nr * p.run_bytes);
+        for (int ch = 0; ch < p.lchunks; ++ch) {
+          tma_load_2d(base + ch * LCHUNK, &tm_s, full_bar(s), ch * 16, a_row, pol_a);
+          if (p.swiglu)
+            tma_load_2d(base + (p.lchunks + ch) * LCHUNK, &tm_s, full_bar(s), p.rank + ch * 16, a_row, pol_a);
+        }
+        for (int jj = 0; jj < nr; ++jj) {
+          const int tenant = p.tile_runs[((int64_t)m_tile * kMaxRunsPerTile + r0 + jj) * 5];
+          const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
+          const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
+          for (int ch = 0; ch < p.lchunks; ++ch) {
+            if (p.swiglu) {
+              tma_load_2d(rb + ch * LCHUNK, &tm_lb, full_bar(s), ch * 16, brow, pol_b);
+              tma_load_2d(rb + (p.lchunks + ch) * LCHUNK, &tm_lb, full_bar(s), ch * 16, brow + p.N, pol_b);
+            } else {
+              tma_load_2d(rb + ch * 2 * LCHUNK, &tm_lb, full_bar(s), ch * 16, brow, pol_b);
+              tma_load_2d(rb + ch * 2 * LCHUNK + LCHUNK, &tm_lb, full_bar(s), ch * 16, brow + 128, pol_b);
+            }
+          }
+        }
+        last_phase[s] = (int)ph;
+      }
     }
     if (!ok) {
       // Let the copies already in flight land before the CTA exits.
@@ -207,6 +233,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (threadIdx.x == 32) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc = idesc_f16(BM, BN, IsBf16<T>::value);
+    const uint32_t idesc_n128 = idesc_f16(BM, 128, IsBf16<T>::value);
     uint32_t it = 0;
     int tcount = 0;
     bool ok = true;
@@ -214,6 +241,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
+      const int m_tile = tile % num_m_tiles;
       if (!mbar_wait(tempty_bar(acc), aph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
         ok = false;
         break;
@@ -237,6 +265,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_commit(empty_bar(s));
         issued_any = true;
       }
+      const int nruns = ok ? tile_lora_runs(p, m_tile) : 0;
+      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
+        const int nr = min(p.runs_per_block, nruns - r0);
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = smem_base + s * STAGE_BYTES;
+        for (int jj = 0; jj < nr; ++jj) {
+          const int32_t* run = p.tile_runs + ((int64_t)m_tile * kMaxRunsPerTile + r0 + jj) * 5;
+          const uint32_t d0 = ~(uint32_t)run[1], d1 = ~(uint32_t)run[2], d2 = ~(uint32_t)run[3],
+                         d3 = ~(uint32_t)run[4];
+          const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
+          for (int ch = 0; ch < p.lchunks; ++ch) {
+            if (p.swiglu) {
+              tc_mma_f16_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * LCHUNK),
+                                idesc_n128, 1u, d0, d1, d2, d3);
+              tc_mma_f16_masked(d_tmem + 128, smem_desc_sw32(base + (p.lchunks + ch) * LCHUNK),
+                                smem_desc_sw32(rb + (p.lchunks + ch) * LCHUNK), idesc_n128, 1u, d0, d1, d2, d3);
+            } else {
+              tc_mma_f16_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * 2 * LCHUNK),
+                                idesc, 1u, d0, d1, d2, d3);
+            }
+          }
+        }
+        tc_commit(empty_bar(s));
+      }
       if (!ok) break;
       tc_commit(tfull_bar(acc));
     }
@@ -248,8 +306,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
-    const int r8 = p.rank / 8;
-    const T* lora_b = reinterpret_cast<const T*>(p.lora_b);
     const T* bias = reinterpret_cast<const T*>(p.bias);
     T* out = reinterpret_cast<T*>(p.out);
     const bool vec_ok = (p.ldo % 8 == 0) && (p.N % 8 == 0);
@@ -264,26 +320,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int64_t row = (int64_t)m_tile * BM + row_in_tile;
       const bool row_ok = p.tile_group ? true : (row < p.m_rows);
-      int tenant = -1;
-      if (row_ok && p.row_tenant && p.rank > 0) tenant = p.row_tenant[row];
-      float s_a[32], s_b[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        s_a[j] = 0.f;
-        s_b[j] = 0.f;
-      }
-      if (tenant >= 0) {
-        const float* sp = p.row_lora + row * p.lora_cols;
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j < p.rank) {
-            s_a[j] = sp[j];
-            if (p.swiglu) s_b[j] = sp[p.rank + j];
-          }
-      }
       const float rscale = (row_ok && p.row_scale) ? p.row_scale[row] : 1.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      const T* lb = (tenant >= 0) ? lora_b + tenant * p.lora_b_tenant_stride + group * p.lora_b_group_stride : nullptr;
 
       if (p.swiglu) {
         const int n0 = n_tile * 128;
@@ -294,28 +332,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_wait_ld();
           const int col = n0 + c;
           const int nvalid = min(16, p.N - col);
-          float g[16], u[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            g[i] = __uint_as_float(rg[i]);
-            u[i] = __uint_as_float(ru[i]);
-          }
+          float h[16];
           if (p.b_scale && nvalid > 0) {
             const float* bsg = p.b_scale + (int64_t)group * p.b_group_rows + col;
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (i < nvalid) {
-                g[i] *= bsg[i];
-                u[i] *= bsg[p.N + i];
-              }
-          }
-          if (lb && nvalid > 0) {
-            lora_expand16<T>(g, s_a, r8, lb + (int64_t)col * p.rank, p.rank, nvalid);
-            lora_expand16<T>(u, s_b, r8, lb + (int64_t)(p.N + col) * p.rank, p.rank, nvalid);
-          }
-          float h[16];
+            for (int i = 0; i < 16; ++i) {
+              const float sg = i < nvalid ? bsg[i] : 0.f, su = i < nvalid ? bsg[p.N + i] : 0.f;
+              h[i] = silu_f32(__uint_as_float(rg[i]) * sg) * (__uint_as_float(ru[i]) * su);
+            }
+          } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) h[i] = silu_f32(g[i]) * u[i];
+            for (int i = 0; i < 16; ++i) h[i] = silu_f32(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+          }
           if (row_ok && nvalid > 0) store16<T>(out + row * p.ldo + col, h, nvalid, vec_ok);
         }
       } else {
@@ -326,10 +354,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_wait_ld();
           const int col = n0 + c;
           const int nvalid = min(16, p.N - col);
-          float v[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rv[i]);
           if (nvalid > 0) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rv[i]);
             if (p.b_scale) {
               const float* bs = p.b_scale + (int64_t)group * p.b_group_rows + col;
 #pragma unroll
@@ -343,7 +371,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               for (int i = 0; i < 16; ++i)
                 if (i < nvalid) v[i] += to_f32<T>(bp[i]);
             }
-            if (lb) lora_expand16<T>(v, s_a, r8, lb + (int64_t)col * p.rank, p.rank, nvalid);
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] *= rscale;
             if (row_ok) store16<T>(out + row * p.ldo + col, v, nvalid, vec_ok);
@@ -363,24 +390,98 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// One warp per 128-row tile: distinct tenants (in first-seen order over the
+// 4 row quarters) and the 128-bit mask of the rows each one owns.
+__global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restrict__ row_tenant,
+                                                        const int32_t* __restrict__ num_tiles_dev,
+                                                        int64_t static_rows, int tiles_cap, int32_t* __restrict__ runs,
+                                                        int32_t* __restrict__ nruns) {
+  __shared__ int32_t s_ten[4][kMaxRunsPerTile];
+  __shared__ uint32_t s_mask[4][kMaxRunsPerTile][4];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x * 4 + w;
+  const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
+  if (tile >= ntiles) return;
+  const int64_t rows_active = num_tiles_dev ? (int64_t)ntiles * 128 : static_rows;
+  int count = 0;
+  for (int q = 0; q < 4; ++q) {
+    const int64_t row = (int64_t)tile * 128 + q * 32 + lane;
+    const int t = row < rows_active ? row_tenant[row] : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, t);
+    const bool leader = (t >= 0) && ((peers & ((1u << lane) - 1u)) == 0u);
+    int found = -1;
+    if (leader)
+      for (int j = 0; j < count; ++j)
+        if (s_ten[w][j] == t) {
+          found = j;
+          break;
+        }
+    const unsigned is_new = __ballot_sync(0xffffffffu, leader && found < 0);
+    if (leader) {
+      int idx = found;
+      if (found < 0) {
+        idx = count + __popc(is_new & ((1u << lane) - 1u));
+        s_ten[w][idx] = t;
+        for (int qq = 0; qq < 4; ++qq) s_mask[w][idx][qq] = 0u;
+      }
+      s_mask[w][idx][q] = peers;
+    }
+    count += __popc(is_new);
+    __syncwarp();
+  }
+  for (int j = lane; j < count; j += 32) {
+    int32_t* r = runs + ((int64_t)tile * kMaxRunsPerTile + j) * 5;
+    r[0] = s_ten[w][j];
+    r[1] = (int32_t)s_mask[w][j][0];
+    r[2] = (int32_t)s_mask[w][j][1];
+    r[3] = (int32_t)s_mask[w][j][2];
+    r[4] = (int32_t)s_mask[w][j][3];
+  }
+  if (lane == 0) nruns[tile] = count;
+}
+
 }  // namespace
+
+int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
+                     int32_t* runs, int32_t* nruns, cudaStream_t stream) {
+  SB_CHECK_ARG(row_tenant && runs && nruns, "tile_runs: null pointer");
+  const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
+  if (tiles == 0) return STAGEML_OK;
+  (tile_runs_kernel<<<(unsigned)((tiles + 3) / 4), 128, 0, stream>>>(row_tenant, num_tiles_dev, static_rows,
+                                                                     tiles_cap, runs, nruns),
+   ::sb::count_launch());
+  SB_CUDA_CHECK(cudaGetLastError());
+  return STAGEML_OK;
+}
 
 int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   SB_CHECK_ARG(g.a && g.b && g.out, "grouped gemm: null operand");
   SB_CHECK_ARG(g.K > 0 && g.K % 8 == 0, "grouped gemm: K=%d must be a positive multiple of 8", g.K);
   SB_CHECK_ARG(g.N > 0, "grouped gemm: N must be positive");
-  SB_CHECK_ARG(g.rank % 8 == 0 && g.rank <= 32, "grouped gemm: LoRA rank %d must be a multiple of 8 <= 32", g.rank);
-  SB_CHECK_ARG(g.rank == 0 || (g.row_lora && g.lora_b), "grouped gemm: LoRA rank > 0 needs S and B");
+  SB_CHECK_ARG(g.rank == 0 || g.rank == 16 || g.rank == 32, "grouped gemm: LoRA rank %d must be 0, 16 or 32", g.rank);
+  SB_CHECK_ARG(g.rank == 0 || (g.s16 && g.lora_b && g.tile_runs && g.tile_nruns && g.s_rows > 0 &&
+                               g.lora_b_rows_total > 0),
+               "grouped gemm: LoRA rank > 0 needs S, B, the tile runs and their sizes");
   SB_CHECK_ARG((reinterpret_cast<uintptr_t>(g.a) % 16) == 0 && (reinterpret_cast<uintptr_t>(g.b) % 16) == 0,
                "grouped gemm: operands must be 16-byte aligned");
   SB_CHECK_ARG(g.b_rows_total < (int64_t(1) << 31) && g.a_rows < (int64_t(1) << 31),
                "grouped gemm: operand rows exceed the TMA coordinate range");
-  if (g.rank > 0) SB_CHECK_ARG(reinterpret_cast<uintptr_t>(g.lora_b) % 16 == 0, "grouped gemm: lora_b alignment");
+  SB_CHECK_ARG(g.lora_b_rows_total < (int64_t(1) << 31), "grouped gemm: LoRA bank exceeds the TMA coordinate range");
 
   const CUtensorMapDataType dt = g.in_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap tm_a, tm_b;
-  SB_TRY(make_tmap_2d(&tm_a, g.a, dt, 2, (uint64_t)g.a_rows, (uint64_t)g.K, (uint64_t)g.K * 2, BM, BK, true));
-  SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, true));
+  CUtensorMap tm_a, tm_b, tm_s, tm_lb;
+  SB_TRY(make_tmap_2d(&tm_a, g.a, dt, 2, (uint64_t)g.a_rows, (uint64_t)g.K, (uint64_t)g.K * 2, BM, BK, 128));
+  SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
+  const int lora_cols = g.swiglu ? 2 * g.rank : g.rank;
+  if (g.rank) {
+    SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
+                        16, 32));
+    SB_TRY(make_tmap_2d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.lora_b_rows_total, (uint64_t)g.rank,
+                        (uint64_t)g.rank * 2, 128, 16, 32));
+  } else {
+    tm_s = tm_a;  // unused
+    tm_lb = tm_a;
+  }
 
   KParams p;
   p.K = g.K;
@@ -392,13 +493,15 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.tiles_cap = g.tiles_cap;
   p.tile_group = g.tile_group;
   p.m_rows = g.m_rows;
-  p.row_tenant = g.row_tenant;
-  p.row_lora = g.row_lora;
   p.rank = g.rank;
-  p.lora_cols = g.swiglu ? 2 * g.rank : g.rank;
-  p.lora_b = g.lora_b;
-  p.lora_b_tenant_stride = g.lora_b_tenant_stride;
-  p.lora_b_group_stride = g.lora_b_group_stride;
+  p.lchunks = g.rank / 16;
+  p.s_bytes = (g.swiglu ? 2 : 1) * p.lchunks * LCHUNK;
+  p.run_bytes = 2 * p.lchunks * LCHUNK;
+  p.runs_per_block = g.rank ? (STAGE_BYTES - p.s_bytes) / p.run_bytes : 1;
+  p.lb_tenant_rows = g.rank ? g.lora_b_tenant_stride / g.rank : 0;
+  p.lb_group_rows = g.rank ? g.lora_b_group_stride / g.rank : 0;
+  p.tile_runs = g.tile_runs;
+  p.tile_nruns = g.tile_nruns;
   p.row_scale = g.row_scale;
   p.bias = g.bias;
   p.bias_group_stride = g.bias_group_stride;
@@ -415,21 +518,15 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   const int grid = (int)std::min<int64_t>(tiles_upper, sm_count());
 
   if (g.in_bf16) {
-    static bool attr_set = false;
-    if (!attr_set) {
-      SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES));
-      attr_set = true;
-    }
-    (grouped_gemm_kernel<bf16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, p), ::sb::count_launch());
+    SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES));
+    (grouped_gemm_kernel<bf16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, tm_s, tm_lb, p),
+     ::sb::count_launch());
   } else {
-    static bool attr_set = false;
-    if (!attr_set) {
-      SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<f16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES));
-      attr_set = true;
-    }
-    (grouped_gemm_kernel<f16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, p), ::sb::count_launch());
+    SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<f16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES));
+    (grouped_gemm_kernel<f16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, tm_s, tm_lb, p),
+     ::sb::count_launch());
   }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;

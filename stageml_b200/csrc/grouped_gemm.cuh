@@ -5,17 +5,24 @@
 
 namespace sb {
 
-// out[row, n] = epilogue( sum_k A[row, k] * B[group(row) * b_group_rows + n, k] )
+// out[row, n] = epilogue( sum_k A[row, k] * B[group(row) * b_group_rows + n, k]
+//                         + lora(row, n) )
 //
 // A rows are either the padded permuted rows of a MoE plan (tile_group != nullptr:
 // 128-row tile m belongs to group tile_group[m], the number of tiles is read from
 // num_tiles_dev) or the rows of a plain matrix (tile_group == nullptr: group 0,
 // rows >= m_rows are masked).
 //
-// SwiGLU mode: B group = [W1 (N rows); W3 (N rows)]; out = silu(g) * u with
-//   g = acc(W1 rows) + lora(S[:, 0:r], lora_b rows [0,N)),
-//   u = acc(W3 rows) + lora(S[:, r:2r], lora_b rows [N,2N)).
-// Plain mode: out = (acc * b_scale + bias + lora(S[:, 0:r])) * row_scale.
+// LoRA expand (rank > 0) runs on the tensor cores into the same accumulator:
+// for every tenant run of a tile (tile_runs: tenant + 128-bit row mask),
+//   acc[rows of the run, n] += S[row, :] . Bl[tenant, group, n, :]
+// with S the pre-scaled shrink output (16-bit, [s_rows, lora_cols]) and Bl the
+// LoRA B bank (16-bit, element (tenant, group, n, j) at
+// tenant*lora_b_tenant_stride + group*lora_b_group_stride + n*rank + j).
+//
+// SwiGLU mode: B group = [W1 (N rows); W3 (N rows)], S = [s1 | s3] (2*rank
+// columns), Bl rows [0,N) for W1 and [N,2N) for W3; out = silu(g) * u.
+// Plain mode: out = (acc * b_scale[col] + bias[col]) * row_scale[row].
 struct GemmLaunch {
   const void* a = nullptr;       // [a_rows, K] 16-bit
   int64_t a_rows = 0;
@@ -31,13 +38,17 @@ struct GemmLaunch {
   int tiles_cap = 0;
   const int32_t* tile_group = nullptr;
   int64_t m_rows = 0;            // direct mode row count
-  // epilogue inputs
-  const int32_t* row_tenant = nullptr;   // [rows] or null
-  const float* row_lora = nullptr;       // [rows, lora_cols] pre-scaled shrink output
-  int rank = 0;                          // multiple of 8, <= 32; 0 = no LoRA
-  const void* lora_b = nullptr;          // 16-bit
+  // LoRA (tensor-core expand)
+  int rank = 0;                          // 0, 16 or 32
+  const void* s16 = nullptr;             // [s_rows, lora_cols] 16-bit, pre-scaled shrink output
+  int64_t s_rows = 0;
+  const void* lora_b = nullptr;          // 16-bit bank
   int64_t lora_b_tenant_stride = 0;      // elements
   int64_t lora_b_group_stride = 0;       // elements
+  int64_t lora_b_rows_total = 0;         // bank elements / rank
+  const int32_t* tile_runs = nullptr;    // [tiles][128][5]: tenant, row-mask words 0..3
+  const int32_t* tile_nruns = nullptr;   // [tiles]
+  // epilogue
   const float* row_scale = nullptr;      // [rows] or null
   const void* bias = nullptr;            // 16-bit [G, N] or null
   int64_t bias_group_stride = 0;
@@ -49,5 +60,13 @@ struct GemmLaunch {
 };
 
 int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
+
+// Distinct LoRA tenants of every 128-row tile and the rows each one owns:
+// runs[(tile*128 + j)*5 + 0] = tenant, [1..4] = row mask words; nruns[tile].
+// Rows with tenant < 0 belong to no run. Active rows: 128 * (*num_tiles_dev)
+// (capped at tiles_cap tiles) or static_rows when num_tiles_dev is null.
+int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
+                     int32_t* runs, int32_t* nruns, cudaStream_t stream);
+constexpr int kMaxRunsPerTile = 128;
 
 }  // namespace sb

@@ -61,7 +61,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
-                 uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+                 uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_rows, uint32_t box_cols, int swizzle_bytes) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(STAGEML_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
@@ -69,14 +69,32 @@ int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, 
   if (row_pitch_bytes % 16 != 0)
     return set_error(STAGEML_ERR_INVALID_ARG, "TMA row pitch %llu is not a multiple of 16 bytes",
                      (unsigned long long)row_pitch_bytes);
-  if (swizzle128 && box_cols * (uint32_t)elem_bytes != 128)
-    return set_error(STAGEML_ERR_INVALID_ARG, "128B swizzle needs a 128-byte box row");
+  CUtensorMapSwizzle sw;
+  switch (swizzle_bytes) {
+    case 0:
+      sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+      break;
+    case 32:
+      sw = CU_TENSOR_MAP_SWIZZLE_32B;
+      break;
+    case 64:
+      sw = CU_TENSOR_MAP_SWIZZLE_64B;
+      break;
+    case 128:
+      sw = CU_TENSOR_MAP_SWIZZLE_128B;
+      break;
+    default:
+      return set_error(STAGEML_ERR_INVALID_ARG, "unsupported TMA swizzle %d", swizzle_bytes);
+  }
+  if (swizzle_bytes && box_cols * (uint32_t)elem_bytes != (uint32_t)swizzle_bytes)
+    return set_error(STAGEML_ERR_INVALID_ARG, "%dB swizzle needs a %d-byte box row", swizzle_bytes, swizzle_bytes);
+  if (box_rows == 0 || box_rows > 256 || box_cols == 0 || box_cols > 256)
+    return set_error(STAGEML_ERR_INVALID_ARG, "TMA box %ux%u out of range", box_rows, box_cols);
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {row_pitch_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(out, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+  CUresult r = fn(out, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(STAGEML_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu", (int)r,

@@ -23,10 +23,11 @@ void count_launch();
 int sm_count();
 
 // Encode a 2-D row-major tensor map: `rows` x `cols` elements of `elem_bytes`
-// bytes, row pitch `row_pitch_bytes`, box `box_rows` x `box_cols`, 128-byte
-// swizzle when `swizzle128` (box_cols * elem_bytes must then be 128).
+// bytes, row pitch `row_pitch_bytes`, box `box_rows` x `box_cols`, with a
+// `swizzle_bytes`-byte swizzle (0, 32, 64 or 128; the box row must then be
+// exactly that many bytes).
 int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
-                 uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_rows, uint32_t box_cols, bool swizzle128);
+                 uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
 
 }  // namespace sb
 

@@ -44,7 +44,7 @@ struct ShrinkLaunch {
   int64_t a_group_stride = 0;
   int R = 0;                            // output columns (multiple of 8, <= 64)
   float* spart = nullptr;               // [KS][rows_cap][R]
-  float* s_out = nullptr;               // [rows_cap][R] (reduced, scaled)
+  void* s_out = nullptr;                // [rows_cap][R] 16-bit (reduced, scaled): the LoRA-expand MMA operand
   const float* lora_scale = nullptr;    // [n_tenants]
 };
 constexpr int kShrinkKSlice = 512;

@@ -157,10 +157,11 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
   }
 }
 
+template <typename T>
 __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, int64_t rows_cap, int R,
                                      const int32_t* __restrict__ num_tiles_dev, int64_t static_rows,
                                      const int32_t* __restrict__ row_tenant, const float* __restrict__ scale,
-                                     float* __restrict__ s_out) {
+                                     T* __restrict__ s_out) {
   const int64_t rows_active = active_rows(num_tiles_dev, static_rows, rows_cap);
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows_active * R) return;
@@ -171,7 +172,7 @@ __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, in
     for (int ks = 0; ks < KS; ++ks) v += spart[((int64_t)ks * rows_cap + row) * R + (idx - row * R)];
     v *= scale ? scale[tn] : 1.f;
   }
-  s_out[idx] = v;
+  s_out[idx] = from_f32<T>(v);
 }
 
 }  // namespace
@@ -210,8 +211,16 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {
     const int64_t n = rows_max * s.R;
-    (shrink_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-        s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale, s.s_out), ::sb::count_launch());
+    if (s.dtype_bf16)
+      (shrink_reduce_kernel<bf16><<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+           s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
+           static_cast<bf16*>(s.s_out)),
+       ::sb::count_launch());
+    else
+      (shrink_reduce_kernel<f16><<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+           s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
+           static_cast<f16*>(s.s_out)),
+       ::sb::count_launch());
     SB_CUDA_CHECK(cudaGetLastError());
   }
   return STAGEML_OK;
