@@ -90,7 +90,7 @@ struct MoeBuffers {
   size_t bytes = 0;
 };
 
-int moe_validate(const stageml_moe_args* a) {
+int moe_validate(const stageml_moe_args* a, bool check_ptrs = true) {
   SB_CHECK_ARG(a, "moe: null args");
   SB_CHECK_ARG(a->T >= 0 && a->H > 0 && a->I > 0 && a->E > 0 && a->k >= 0 && a->n_shared >= 0,
                "moe: bad sizes T=%d H=%d I=%d E=%d k=%d n_shared=%d", a->T, a->H, a->I, a->E, a->k, a->n_shared);
@@ -112,7 +112,7 @@ int moe_validate(const stageml_moe_args* a) {
                "moe: LoRA needs tenant_ids, n_tenants > 0 and lora_scale");
   SB_CHECK_ARG(a->k == 0 || a->topk_ids || a->router_w, "moe: need topk_ids or router_w");
   if (a->topk_ids) SB_CHECK_ARG(a->ids_dtype == STAGEML_I32 || a->ids_dtype == STAGEML_I64, "moe: ids dtype");
-  if (a->T > 0) {
+  if (a->T > 0 && check_ptrs) {
     SB_CHECK_ARG(a->x && a->gate_up && a->down && a->out, "moe: null tensor");
     SB_CHECK_ARG(aligned16(a->x) && aligned16(a->gate_up) && aligned16(a->down) && aligned16(a->out),
                  "moe: x, gate_up, down and out must be 16-byte aligned");
@@ -414,7 +414,7 @@ int stageml_permute(const void* ids, int ids_dtype, const void* weights, int wei
 }
 
 size_t stageml_moe_workspace_bytes(const stageml_moe_args* args) {
-  if (!args || moe_validate(args) != STAGEML_OK) return 0;
+  if (!args || moe_validate(args, false) != STAGEML_OK) return 0;
   MoeBuffers b;
   moe_carve(args, nullptr, &b);
   return b.bytes;
@@ -454,9 +454,7 @@ size_t stageml_residual_moe_workspace_bytes(int T, int H, int I, int E, int k) {
   static const int dummy_ids = 0;
   residual_args(&a, nullptr, nullptr, nullptr, nullptr, STAGEML_F32, &dummy_ids, STAGEML_I64, T, H, I, E, k,
                 STAGEML_BF16, nullptr, nullptr);
-  a.T = 0;  // validation of pointers is skipped for sizing
-  if (moe_validate(&a) != STAGEML_OK) return 0;
-  a.T = T;
+  if (moe_validate(&a, false) != STAGEML_OK) return 0;
   MoeBuffers b;
   moe_carve(&a, nullptr, &b);
   return b.bytes;

@@ -285,7 +285,7 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
   SB_CHECK_ARG(n_experts_total > n_shared || (k == 0 && n_experts_total == n_shared),
                "permute: n_experts_total=%d must exceed n_shared=%d", n_experts_total, n_shared);
   SB_CHECK_ARG(ids_dtype == STAGEML_I32 || ids_dtype == STAGEML_I64, "permute: ids must be int32 or int64");
-  SB_CHECK_ARG(k == 0 || ids, "permute: null ids");
+  SB_CHECK_ARG(k == 0 || T == 0 || ids, "permute: null ids");
   SB_CHECK_ARG(!weights || weights_dtype == STAGEML_F32 || weights_dtype == STAGEML_BF16 ||
                    weights_dtype == STAGEML_F16,
                "permute: weights must be f32, bf16 or f16");

@@ -70,6 +70,60 @@ __global__ void __launch_bounds__(RT_THREADS) router_logits_kernel(const T* __re
   }
 }
 
+// Gate resident in shared memory (E*H fp32 <= 200 KB): each CTA copies G once,
+// then every warp takes whole tokens; lane l accumulates E partial dot products
+// over columns 4l + 128i with float4 reads of G and 8-byte reads of x, and the
+// warp reduces them with shuffles. E <= 32.
+template <typename T, int E_MAX>
+__global__ void __launch_bounds__(256) router_logits_smem_kernel(const T* __restrict__ x, const float* __restrict__ gw,
+                                                                 int T_, int H, int E, float* __restrict__ logits) {
+  extern __shared__ float4 gsm4[];
+  float* gsm = reinterpret_cast<float*>(gsm4);
+  const int n = E * H;
+  for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+    *reinterpret_cast<float4*>(gsm + i) = __ldg(reinterpret_cast<const float4*>(gw + i));
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  for (int t = blockIdx.x * wpb + warp; t < T_; t += gridDim.x * wpb) {
+    const T* xr = x + (int64_t)t * H;
+    float acc[E_MAX];
+#pragma unroll
+    for (int e = 0; e < E_MAX; ++e) acc[e] = 0.f;
+    for (int h = lane * 4; h < H; h += 128) {
+      float xv[4];
+      if (sizeof(T) == 2) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(xr + h));
+        const T* hv = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xv[q] = to_f32<T>(hv[q]);
+      } else {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(xr + h));
+        xv[0] = f.x, xv[1] = f.y, xv[2] = f.z, xv[3] = f.w;
+      }
+#pragma unroll
+      for (int e = 0; e < E_MAX; ++e) {
+        if (e < E) {
+          const float4 gv = *reinterpret_cast<const float4*>(gsm + e * H + h);
+          acc[e] = fmaf(xv[0], gv.x, acc[e]);
+          acc[e] = fmaf(xv[1], gv.y, acc[e]);
+          acc[e] = fmaf(xv[2], gv.z, acc[e]);
+          acc[e] = fmaf(xv[3], gv.w, acc[e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < E_MAX; ++e) {
+      if (e < E) {
+        float v = acc[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) logits[(int64_t)t * E + e] = v;
+      }
+    }
+  }
+}
+
 // One warp per token.
 __global__ void topk_kernel(const float* __restrict__ logits, int T_, int E, int k, int renorm,
                             int32_t* __restrict__ ids, float* __restrict__ weights) {
@@ -161,6 +215,34 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
   SB_CHECK_ARG(H >= 1, "router: H must be positive");
   if (T_ == 0) return STAGEML_OK;
   SB_CHECK_ARG(x && gate_w && logits, "router: null pointer");
+  const size_t gbytes = sizeof(float) * (size_t)E * H;
+  const bool aligned = (reinterpret_cast<uintptr_t>(gate_w) % 16 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+  if (E <= 32 && H % 4 == 0 && gbytes <= 200 * 1024 && aligned &&
+      (x_dtype == STAGEML_BF16 || x_dtype == STAGEML_F16 || x_dtype == STAGEML_F32)) {
+    const int grid = std::min<int>(sm_count(), (T_ + 7) / 8);
+    auto launch = [&](auto kern, const auto* xp) -> int {
+      SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gbytes));
+      (kern<<<grid, 256, gbytes, stream>>>(xp, gate_w, T_, H, E, logits), ::sb::count_launch());
+      SB_CUDA_CHECK(cudaGetLastError());
+      return STAGEML_OK;
+    };
+    if (x_dtype == STAGEML_BF16) {
+      const bf16* xp = static_cast<const bf16*>(x);
+      if (E <= 8) return launch(router_logits_smem_kernel<bf16, 8>, xp);
+      if (E <= 16) return launch(router_logits_smem_kernel<bf16, 16>, xp);
+      return launch(router_logits_smem_kernel<bf16, 32>, xp);
+    }
+    if (x_dtype == STAGEML_F16) {
+      const f16* xp = static_cast<const f16*>(x);
+      if (E <= 8) return launch(router_logits_smem_kernel<f16, 8>, xp);
+      if (E <= 16) return launch(router_logits_smem_kernel<f16, 16>, xp);
+      return launch(router_logits_smem_kernel<f16, 32>, xp);
+    }
+    const float* xp = static_cast<const float*>(x);
+    if (E <= 8) return launch(router_logits_smem_kernel<float, 8>, xp);
+    if (E <= 16) return launch(router_logits_smem_kernel<float, 16>, xp);
+    return launch(router_logits_smem_kernel<float, 32>, xp);
+  }
   const size_t smem = sizeof(float) * (size_t)(RT_TOK + E) * (RT_KC + 1);
   const int grid = (T_ + RT_TOK - 1) / RT_TOK;
   if (x_dtype == STAGEML_BF16) {

@@ -65,7 +65,41 @@ __device__ __forceinline__ void mma_16816<f16>(float (&c)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t ld32(const void* p) { return __ldg(reinterpret_cast<const uint32_t*>(p)); }
+__device__ __forceinline__ uint4 ld16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+// One 32-wide K chunk of the shrink for a warp's 16 rows: each lane holds 8
+// consecutive K elements (16 bytes) of rows g and g+8 and of B-row g of every
+// 8-column block. The two m16n8k16 MMAs consume those registers as if lane
+// (g, tig) held logical k = {2tig, 2tig+1, 2tig+8, 2tig+9}; the same
+// logical->physical K permutation is applied to both operands, so the sum over
+// K is unchanged while every global load is a full 16-byte vector.
+struct ShrinkChunk {
+  uint4 xl, xh;
+  uint4 b[8];
+};
+
+template <typename T>
+__device__ __forceinline__ void shrink_load(ShrinkChunk& c, const T* x_lo, const T* x_hi, const T* A, int K, int nbs,
+                                            int g, int kk) {
+  const bool v = kk < K;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  c.xl = (v && x_lo) ? ld16(x_lo + kk) : z;
+  c.xh = (v && x_hi) ? ld16(x_hi + kk) : z;
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb)
+    if (nb < nbs) c.b[nb] = v ? ld16(A + (int64_t)(nb * 8 + g) * K + kk) : z;
+}
+
+template <typename T>
+__device__ __forceinline__ void shrink_mma(float (&acc)[8][4], const ShrinkChunk& c, int nbs) {
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb) {
+    if (nb < nbs) {
+      mma_16816<T>(acc[nb], c.xl.x, c.xh.x, c.xl.y, c.xh.y, c.b[nb].x, c.b[nb].y);
+      mma_16816<T>(acc[nb], c.xl.z, c.xh.z, c.xl.w, c.xh.w, c.b[nb].z, c.b[nb].w);
+    }
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p) {
@@ -80,6 +114,7 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
 
   if (p.gather_dst) {
     T* dstb = static_cast<T*>(p.gather_dst);
+#pragma unroll 4
     for (int r = 0; r < 16; ++r) {
       const int64_t row = row0 + r;
       if (row >= rows_active) break;
@@ -88,7 +123,7 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
       const T* s = srow >= 0 ? src + srow * K : nullptr;
       for (int c = k_begin + lane * 8; c < k_end; c += 256) {
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (s) v = __ldg(reinterpret_cast<const uint4*>(s + c));
+        if (s) v = ld16(s + c);
         *reinterpret_cast<uint4*>(dst + c) = v;
       }
     }
@@ -126,23 +161,13 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
     for (int nb = 0; nb < 8; ++nb)
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[nb][q] = 0.f;
-#pragma unroll 2
-    for (int k0 = k_begin; k0 < k_end; k0 += 16) {
-      const int ka = k0 + tig * 2, kb = ka + 8;
-      const bool va = ka < K, vb = kb < K;
-      const uint32_t a0 = (x_lo && va) ? ld32(x_lo + ka) : 0u;
-      const uint32_t a1 = (x_hi && va) ? ld32(x_hi + ka) : 0u;
-      const uint32_t a2 = (x_lo && vb) ? ld32(x_lo + kb) : 0u;
-      const uint32_t a3 = (x_hi && vb) ? ld32(x_hi + kb) : 0u;
-#pragma unroll
-      for (int nb = 0; nb < 8; ++nb) {
-        if (nb < nbs) {
-          const T* arow = A + (int64_t)(nb * 8 + g) * K;
-          const uint32_t b0 = va ? ld32(arow + ka) : 0u;
-          const uint32_t b1 = vb ? ld32(arow + kb) : 0u;
-          mma_16816<T>(acc[nb], a0, a1, a2, a3, b0, b1);
-        }
-      }
+    ShrinkChunk cur, nxt;
+    shrink_load<T>(cur, x_lo, x_hi, A, K, nbs, g, k_begin + tig * 8);
+    for (int k0 = k_begin; k0 < k_end; k0 += 32) {
+      const bool more = k0 + 32 < k_end;
+      if (more) shrink_load<T>(nxt, x_lo, x_hi, A, K, nbs, g, k0 + 32 + tig * 8);
+      shrink_mma<T>(acc, cur, nbs);
+      if (more) cur = nxt;
     }
     float* sp = p.spart + (int64_t)blockIdx.x * p.rows_cap * p.R;
     const bool lo_sel = (sel >> g) & 1u, hi_sel = (sel >> (g + 8)) & 1u;

@@ -1,0 +1,176 @@
+"""Tenant router for a vLLM fused-MoE interception point (reference: stageml/vllm_stage_router.py).
+
+Tokens of tenants that have a StageML residual kernel go to the
+``stageml::residual_moe`` op (here: the sm_100a grouped GEMM path); the others
+go to vLLM's ``fused_experts``. Same classes and functions as the reference.
+
+Difference in the split: the reference moves the tenant ids to the host to
+build the mask (``tenant_ids.cpu().tolist()``, stageml/vllm_stage_router.py:60-63).
+Here the mask is a device-side table lookup; the host only learns the number
+of selected tokens (one scalar) to size the two sub-batches.
+"""
+
+from __future__ import annotations
+
+import importlib
+import json
+from dataclasses import asdict, dataclass
+from pathlib import Path
+from typing import Any, Callable
+
+import torch
+
+from .custom_op_registry import ensure_stageml_custom_op
+
+
+@dataclass(frozen=True)
+class KernelManifestEntry:
+    tenant_id: int
+    adapter_id: int
+    backend: str
+    artifact: str
+    symbol: str = "stageml_residual_moe"
+    enabled: bool = True
+
+
+@dataclass(frozen=True)
+class KernelManifest:
+    version: int
+    model: str
+    entries: tuple[KernelManifestEntry, ...]
+
+    def to_dict(self) -> dict[str, Any]:
+        return {"version": self.version, "model": self.model, "entries": [asdict(e) for e in self.entries]}
+
+
+def read_kernel_manifest(path: str | Path) -> KernelManifest:
+    """Tenant -> artifact manifest, JSON format of stageml/baremetal_backend.py:159-193."""
+    data = json.loads(Path(path).read_text())
+    entries = tuple(KernelManifestEntry(**e) for e in data.get("entries", []))
+    return KernelManifest(version=int(data.get("version", 1)), model=str(data.get("model", "unknown")), entries=entries)
+
+
+def write_kernel_manifest(path: str | Path, manifest: KernelManifest) -> Path:
+    out = Path(path)
+    out.parent.mkdir(parents=True, exist_ok=True)
+    out.write_text(json.dumps(manifest.to_dict(), indent=2, sort_keys=True) + "\n")
+    return out
+
+
+@dataclass(frozen=True)
+class TenantKernel:
+    tenant_id: int
+    adapter_id: int
+    backend: str
+    artifact: str
+    symbol: str
+    enabled: bool = True
+
+
+class StageMLTenantRouter:
+    def __init__(self, kernels: dict[int, TenantKernel]):
+        self.kernels = dict(kernels)
+        self._tables: dict[torch.device, torch.Tensor] = {}
+
+    @classmethod
+    def from_manifest(cls, path: str | Path) -> "StageMLTenantRouter":
+        m = read_kernel_manifest(path)
+        return cls({e.tenant_id: TenantKernel(tenant_id=e.tenant_id, adapter_id=e.adapter_id, backend=e.backend,
+                                              artifact=e.artifact, symbol=e.symbol, enabled=e.enabled)
+                    for e in m.entries if e.enabled})
+
+    def has_kernel(self, tenant_id: int) -> bool:
+        e = self.kernels.get(int(tenant_id))
+        return e is not None and e.enabled
+
+    def _table(self, device: torch.device) -> torch.Tensor:
+        t = self._tables.get(device)
+        if t is None:
+            enabled = [tid for tid, k in self.kernels.items() if k.enabled and tid >= 0]
+            t = torch.zeros(max(enabled, default=-1) + 2, dtype=torch.bool, device=device)
+            if enabled:
+                t[torch.tensor(enabled, device=device)] = True
+            self._tables[device] = t
+        return t
+
+    def materialized_mask(self, tenant_ids: torch.Tensor) -> torch.Tensor:
+        """Per-token bool mask of tenants with a kernel, computed where tenant_ids live."""
+        table = self._table(tenant_ids.device)
+        ids = tenant_ids.reshape(-1).to(torch.long)
+        in_range = (ids >= 0) & (ids < table.numel() - 1)
+        return table[torch.where(in_range, ids, torch.full_like(ids, table.numel() - 1))] & in_range
+
+
+def resolve_vllm_fused_experts() -> tuple[Callable[..., Any] | None, str]:
+    candidates = [("vllm.model_executor.layers.fused_moe.fused_moe", "fused_experts"),
+                  ("vllm.model_executor.layers.fused_moe", "fused_experts")]
+    errors: list[str] = []
+    for mod_name, attr in candidates:
+        try:
+            fn = getattr(importlib.import_module(mod_name), attr)
+            if callable(fn):
+                return fn, f"{mod_name}.{attr}"
+            errors.append(f"{mod_name}.{attr} exists but is not callable")
+        except Exception as exc:
+            errors.append(f"{mod_name}.{attr}: {exc}")
+    return None, "; ".join(errors)
+
+
+def call_vllm_fused_experts(fn: Callable[..., Any], hidden, gate_up, down, topk_weights, topk_ids):
+    topk_ids = topk_ids.to(dtype=torch.long).contiguous()
+    topk_weights = topk_weights.contiguous()
+    attempts = [
+        lambda: fn(hidden_states=hidden, w1=gate_up, w2=down, topk_weights=topk_weights, topk_ids=topk_ids,
+                   inplace=False),
+        lambda: fn(hidden, gate_up, down, topk_weights, topk_ids, False),
+        lambda: fn(hidden, gate_up, down, topk_weights, topk_ids),
+    ]
+    last: Exception | None = None
+    for attempt in attempts:
+        try:
+            return attempt()
+        except Exception as exc:
+            last = exc
+    raise RuntimeError(f"could not call vLLM fused_experts: {last}")
+
+
+def call_stageml_residual_op(hidden, gate_up, down, topk_weights, topk_ids):
+    if not ensure_stageml_custom_op(allow_python_fallback=True):
+        raise RuntimeError("StageML residual custom op is not available")
+    return torch.ops.stageml.residual_moe(hidden, gate_up, down, topk_weights, topk_ids)
+
+
+def route_fused_experts(*, hidden, gate_up, down, topk_weights, topk_ids, tenant_ids, router: StageMLTenantRouter,
+                        vllm_fused_experts: Callable[..., Any] | None = None,
+                        stageml_op: Callable[..., torch.Tensor] | None = None):
+    """Route tokens between the StageML residual op and vLLM fused experts (stageml/vllm_stage_router.py:114-157)."""
+    if hidden.shape[0] != tenant_ids.numel():
+        raise ValueError("tenant_ids must contain one tenant id per token")
+    if vllm_fused_experts is None:
+        vllm_fused_experts, source = resolve_vllm_fused_experts()
+        if vllm_fused_experts is None:
+            raise RuntimeError(f"vLLM fused experts could not be resolved: {source}")
+    stageml_op = stageml_op or call_stageml_residual_op
+    mask = router.materialized_mask(tenant_ids.to(hidden.device))
+    n_sel = int(mask.sum())
+    if n_sel == hidden.shape[0]:
+        return stageml_op(hidden, gate_up, down, topk_weights, topk_ids)
+    if n_sel == 0:
+        return call_vllm_fused_experts(vllm_fused_experts, hidden, gate_up, down, topk_weights, topk_ids)
+    out = torch.empty((hidden.shape[0], down.shape[1]), device=hidden.device, dtype=hidden.dtype)
+    for selected, fn in ((mask, stageml_op), (~mask, None)):
+        idx = torch.nonzero(selected, as_tuple=False).flatten()
+        sub_h = hidden.index_select(0, idx).contiguous()
+        sub_w = topk_weights.index_select(0, idx).contiguous()
+        sub_i = topk_ids.index_select(0, idx).contiguous()
+        if fn is None:
+            sub = call_vllm_fused_experts(vllm_fused_experts, sub_h, gate_up, down, sub_w, sub_i)
+        else:
+            sub = fn(sub_h, gate_up, down, sub_w, sub_i)
+        out.index_copy_(0, idx, sub)
+    return out
+
+
+__all__ = ["KernelManifestEntry", "KernelManifest", "read_kernel_manifest", "write_kernel_manifest", "TenantKernel",
+           "StageMLTenantRouter", "resolve_vllm_fused_experts", "call_vllm_fused_experts", "call_stageml_residual_op",
+           "route_fused_experts"]
