@@ -293,6 +293,32 @@ int stageml_lora_gemv_f32(const float* x, const float* W, const float* A, const 
                           int in_features, int out_features, int rank, float* y, void* workspace,
                           size_t workspace_bytes, stageml_stream_t stream);
 
+/* Allocation-free variant of stageml_lora_gemv_f32 (no counterpart in the
+ * reference; it exists for callers of this library that cannot allocate).
+ * Same inputs, outputs and results, but no workspace argument: the split-K
+ * partial sums go to a 16 MiB scratch array in device global memory that the
+ * library itself holds, on every GPU that loads it, until the process exits.
+ * Meant for callers that cannot call cudaMalloc where they run this layer:
+ * a plugin reached only through this C ABI with no allocator of its own, a
+ * serving loop that must never allocate or free device memory (both can
+ * synchronize the device), or a host that plans its device memory in a fixed
+ * arena. Inputs and the output y are still the caller's memory.
+ *  - Shapes whose partial sums exceed the 16 MiB scratch return
+ *    STAGEML_ERR_INVALID_ARG (in = out = 4096 on a 148-SM B200 fits up to M = 7);
+ *    stageml_lora_gemv_f32 with a workspace has no such limit.
+ *  - The first call on a device looks up the scratch array's device address
+ *    (cudaGetSymbolAddress, with that device current) and caches it; make that
+ *    first call before any stream capture.
+ *  - All calls share the one array, which keeps the last call's contents. No
+ *    part of it needs to start at zero (each partial is written before it is
+ *    read), but two calls whose kernels can overlap on the GPU (different
+ *    streams or threads without ordering between them) race on it and give
+ *    wrong results: order such calls, e.g. on one stream.
+ *  - No allocation of any kind: no cudaMalloc, cudaFree or allocating library
+ *    routine is called. */
+int stageml_lora_gemv_f32_noalloc(const float* x, const float* W, const float* A, const float* B, float scale, int M,
+                                  int in_features, int out_features, int rank, float* y, stageml_stream_t stream);
+
 /* ------------------------------------------------------- FP8 weights (R6)
  * Per-output-channel e4m3 quantization of row-major weights [rows, cols]:
  * scale[r] = max(|w[r,:]|) / 448 (1 when the row is all zero), q = e4m3(w / scale)

@@ -124,6 +124,8 @@ SIGNATURES = {
     "stageml_lora_gemv_f32_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "stageml_lora_gemv_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_int,
                                       c_void_p, c_void_p, c_size_t, c_void_p]),
+    "stageml_lora_gemv_f32_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_int,
+                                              c_int, c_void_p, c_void_p]),
     "stageml_quantize_e4m3_rows": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "stageml_stage_timer_enable": (c_int, [c_int]),
     "stageml_stage_timer_read": (c_int, [c_float_p, c_int32_p, c_int]),

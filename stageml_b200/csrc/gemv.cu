@@ -6,9 +6,12 @@
 // CTAs with float4 loads of W, fp32 partials reduced in a fixed order by a
 // second kernel that also applies the rank-r expansion, so results are
 // deterministic.
+#include <mutex>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "kernels.h"
+#include "stage_timer.h"
 
 namespace sb {
 namespace {
@@ -143,3 +146,67 @@ int launch_gemv_f32(const float* x, const float* W, const float* A, const float*
 }
 
 }  // namespace sb
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the fp32 single-LoRA GEMV.
+//
+// stageml_lora_gemv_f32 keeps its split-K partial sums in a workspace the
+// caller allocates. Some callers cannot allocate device memory where they run
+// this layer: a plugin reached only through the C ABI with no allocator of its
+// own, an inference loop that must never call cudaMalloc/cudaFree (both can
+// synchronize the device and stall concurrent work), or a host whose memory
+// lives in a fixed, pre-planned arena. For them the partial sums go to the
+// array below, which belongs to this library: a file-scope device array of
+// kGemvNoAllocScratchBytes bytes, created when the library's code is loaded on
+// a GPU and held on every GPU that loads it until the process exits.
+namespace sb {
+namespace {
+
+constexpr size_t kGemvNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_gemv_noalloc_scratch[kGemvNoAllocScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {nullptr};  // device address of the array, per device ordinal
+
+// Device address of the scratch array on the current device. Host code cannot
+// use the array's name as a device pointer, so the address is queried once per
+// device with that device current and cached.
+int gemv_noalloc_scratch(void** out) {
+  int dev = 0;
+  SB_CUDA_CHECK(cudaGetDevice(&dev));
+  SB_CHECK_ARG(dev >= 0 && dev < 64, "lora_gemv_f32_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(STAGEML_ERR_CUDA, "lora_gemv_f32_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                       cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return STAGEML_OK;
+}
+
+}  // namespace
+}  // namespace sb
+
+extern "C" int stageml_lora_gemv_f32_noalloc(const float* x, const float* W, const float* A, const float* B,
+                                             float scale, int M, int in_features, int out_features, int rank, float* y,
+                                             stageml_stream_t stream) {
+  using namespace sb;
+  clear_error();
+  SB_CHECK_ARG(M >= 1 && in_features >= 1 && out_features >= 1, "lora_gemv_f32_noalloc: bad sizes");
+  const size_t need = gemv_f32_workspace(M, in_features, out_features, A ? rank : 0);
+  if (need > kGemvNoAllocScratchBytes)
+    return set_error(STAGEML_ERR_INVALID_ARG,
+                     "lora_gemv_f32_noalloc: M=%d in=%d out=%d rank=%d needs %zu bytes of scratch, more than the "
+                     "%zu-byte static scratch; call stageml_lora_gemv_f32 with a workspace instead",
+                     M, in_features, out_features, rank, need, kGemvNoAllocScratchBytes);
+  void* scratch = nullptr;
+  SB_TRY(gemv_noalloc_scratch(&scratch));
+  // Every partial sum is written before it is read, so nothing in the scratch needs clearing.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  StageScope scope(STAGEML_STAGE_GEMV, st);
+  return launch_gemv_f32(x, W, A, B, scale, M, in_features, out_features, rank, y, scratch, st);
+}
