@@ -150,6 +150,13 @@ int stageml_permute(const void* ids, int ids_dtype, const void* weights, int wei
                     int group_by_tenant, const stageml_moe_plan* plan, int32_t* status, void* workspace,
                     size_t workspace_bytes, stageml_stream_t stream);
 
+/* Combine (the index_add_ of RequestExecutor.dynamic_one,
+ * benchmarks/multitenant_bta_system_bench.py:413, done once per token):
+ * out[t, :] = sum_{j < kk} y[pair_row[t*kk + j], :] in fp32 with one rounding,
+ * slots in order; pair_row < 0 is skipped. y / out: [*, H] BF16 or F16, H % 8 == 0. */
+int stageml_combine_rows(const void* y, const int32_t* pair_row, int T, int kk, int H, int dtype, void* out,
+                         stageml_stream_t stream);
+
 /* ------------------------------------------------------- MoE-LoRA layer
  * The request-time residual program for one MoE FFN layer (R1..R5 + combine):
  *   route (when topk_ids == NULL) -> permute -> gather + LoRA shrink ->

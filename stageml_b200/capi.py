@@ -108,6 +108,7 @@ SIGNATURES = {
     "stageml_permute_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "stageml_permute": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                 POINTER(MoePlan), c_void_p, c_void_p, c_size_t, c_void_p]),
+    "stageml_combine_rows": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "stageml_moe_workspace_bytes": (c_size_t, [POINTER(MoeArgs)]),
     "stageml_moe_forward": (c_int, [POINTER(MoeArgs), c_void_p, c_size_t, c_void_p]),
     "stageml_residual_moe_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),

@@ -413,6 +413,19 @@ int stageml_permute(const void* ids, int ids_dtype, const void* weights, int wei
                         group_by_tenant, *plan, status, scr, static_cast<cudaStream_t>(stream));
 }
 
+int stageml_combine_rows(const void* y, const int32_t* pair_row, int T, int kk, int H, int dtype, void* out,
+                         stageml_stream_t stream) {
+  clear_error();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SB_CHECK_ARG(T >= 0 && kk >= 1 && H > 0, "combine_rows: bad sizes");
+  SB_CHECK_ARG(is16(dtype), "combine_rows: dtype must be BF16 or F16");
+  if (T == 0) return STAGEML_OK;
+  SB_CHECK_ARG(y && pair_row && out, "combine_rows: null pointer");
+  SB_CHECK_ARG(aligned16(y) && aligned16(out), "combine_rows: 16-byte alignment");
+  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(y, pair_row, T, kk, H, dtype == STAGEML_BF16, out, st));
+  return STAGEML_OK;
+}
+
 size_t stageml_moe_workspace_bytes(const stageml_moe_args* args) {
   if (!args || moe_validate(args, false) != STAGEML_OK) return 0;
   MoeBuffers b;

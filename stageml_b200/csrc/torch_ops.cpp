@@ -370,6 +370,19 @@ std::tuple<Tensor, Tensor> quantize_e4m3_rows(const Tensor& w) {
   return {q, s};
 }
 
+Tensor combine_rows(const Tensor& y, const Tensor& pair_row, int64_t T, int64_t kk) {
+  check_cuda(y, "y", y);
+  check_cuda(pair_row, "pair_row", y);
+  TORCH_CHECK(y.dim() == 2 && pair_row.scalar_type() == at::kInt && pair_row.numel() >= T * kk,
+              "combine_rows: y [rows, H], pair_row int32 [T*kk]");
+  c10::cuda::CUDAGuard guard(y.device());
+  auto out = at::empty({T, y.size(1)}, y.options());
+  check_rc(stageml_combine_rows(y.data_ptr(), pair_row.data_ptr<int32_t>(), (int)T, (int)kk, (int)y.size(1),
+                                dtype_code(y), out.data_ptr(), cur_stream()),
+           "combine_rows");
+  return out;
+}
+
 // Returns the device status word (synchronising on it) and clears it.
 int64_t take_status(const Tensor& like) {
   c10::cuda::CUDAGuard guard(like.device());
@@ -404,6 +417,7 @@ TORCH_LIBRARY(stageml, m) {
       "Tensor? lora_scale) -> Tensor");
   m.def("lora_gemv_f32(Tensor x, Tensor W, Tensor? A, Tensor? B, float scale) -> Tensor");
   m.def("quantize_e4m3_rows(Tensor w) -> (Tensor, Tensor)");
+  m.def("combine_rows(Tensor y, Tensor pair_row, int T, int kk) -> Tensor");
   m.def("take_status(Tensor like) -> int");
 }
 
@@ -418,5 +432,6 @@ TORCH_LIBRARY_IMPL(stageml, CUDA, m) {
   m.impl("moe_linear", &moe_linear);
   m.impl("lora_gemv_f32", &lora_gemv_f32);
   m.impl("quantize_e4m3_rows", &quantize_e4m3_rows);
+  m.impl("combine_rows", &combine_rows);
   m.impl("take_status", &take_status);
 }

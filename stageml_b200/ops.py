@@ -56,6 +56,10 @@ def _register_fakes() -> None:
           lora_b, lora_scale):
         return x.new_empty((x.shape[0], weight.shape[1]))
 
+    @lib.register_fake("stageml::combine_rows")
+    def _(y, pair_row, T, kk):
+        return y.new_empty((T, y.shape[1]))
+
     @lib.register_fake("stageml::lora_gemv_f32")
     def _(x, W, A, B, scale):
         return x.new_empty((x.shape[0], W.shape[1]))
@@ -150,6 +154,12 @@ def quantize_e4m3_rows(w):
     return _ops.quantize_e4m3_rows(w.contiguous())
 
 
+def combine_rows(y, pair_row, T: int, kk: int):
+    """out[t] = sum_j y[pair_row[t*kk + j]] (rows < 0 skipped), fp32 sum, one rounding."""
+    ensure_cuda_device(y)
+    return _ops.combine_rows(y.contiguous(), pair_row.to(torch.int32).contiguous(), int(T), int(kk))
+
+
 def take_status(like) -> int:
     """Synchronise and return (then clear) the device status word of like's device (0 = ok)."""
     return int(_ops.take_status(like))
@@ -166,6 +176,7 @@ __all__ = [
     "moe_linear",
     "lora_gemv_f32",
     "quantize_e4m3_rows",
+    "combine_rows",
     "take_status",
     "PLAN_FIELDS",
 ]
