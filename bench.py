@@ -166,7 +166,12 @@ def run_cpu_sample(cfg, w, sample_tokens: int, repeats: int, warmup: int, budget
 
     t0 = time.time()
     f32 = lambda t: None if t is None else t.float().cpu().numpy()
-    ex = MoEExecutorF32(f32(w["gate_up"]), f32(w["down"]), n_shared=cfg.n_shared, lora_a13=f32(w["lora_a13"]),
+
+    def weights(name):  # e4m3 weights are dequantised with their per-row scales (q * scale[:, None])
+        s = w.get(name + "_scale")
+        return f32(w[name]) if s is None else f32(w[name]) * f32(s)[..., None]
+
+    ex = MoEExecutorF32(weights("gate_up"), weights("down"), n_shared=cfg.n_shared, lora_a13=f32(w["lora_a13"]),
                         lora_b13=f32(w["lora_b13"]), lora_a2=f32(w["lora_a2"]), lora_b2=f32(w["lora_b2"]),
                         lora_scale=f32(w["lora_scale"]))
     x = f32(w["x"][:sample_tokens])
@@ -220,7 +225,7 @@ def reference_arm(args, cfg, rank: int):
 # ------------------------------------------------------------------ GPU arm
 def layer_call(ops, cfg, w, x, tenant_ids):
     return ops.moe_forward(x, w["gate_up"], w["down"], router_w=w["router_w"], k=cfg.k, n_shared=cfg.n_shared,
-                           renormalize=True, tenant_ids=tenant_ids, n_tenants=cfg.n_tenants, rank=cfg.rank,
+                           renormalize=True, tenant_ids=tenant_ids, n_tenants=cfg.n_tenants, rank=cfg.bank_rank,
                            lora_a13=w["lora_a13"], lora_b13=w["lora_b13"], lora_a2=w["lora_a2"],
                            lora_b2=w["lora_b2"], lora_scale=w["lora_scale"], gate_up_scale=w["gate_up_scale"],
                            down_scale=w["down_scale"])
@@ -403,6 +408,175 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
 GATE_UP_DRAM_BYTES: dict = {}
 
 
+# ------------------------------------------------------------------ other configurations
+def _timed(fn, steps: int, warmup: int, lib=None):
+    """Device time of `steps` calls after `warmup` calls; returns (ms per call, stage times, launches)."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    if lib is not None:
+        lib.stageml_stage_timer_enable(1)
+        n0 = lib.stageml_launch_count()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    stages, launches = {}, None
+    if lib is not None:
+        launches = int(lib.stageml_launch_count() - n0)
+        lib.stageml_stage_timer_enable(0)
+        stages = stage_times(lib)
+    return e0.elapsed_time(e1) / steps, stages, launches
+
+
+def _line(metric, value, unit, steps, warmup, ms, hib, dtype, config, **extra):
+    d = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": steps, "warmup": warmup,
+         "ms_per_step": round(ms, 5), "higher_is_better": hib, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+         "data": "synthetic (seeded; shapes of the configuration)", "config": config}
+    d.update(extra)
+    print(json.dumps(d), flush=True)
+
+
+def dense_arm(args):
+    """Configurations 1-3 and the fine-grained MoE layer with bf16 weights, one JSON line each.
+
+    These are the parity configurations beside the headline MoE-LoRA layer; the driver's
+    headline line is the default workload.
+    """
+    import numpy as np
+
+    import stageml_b200.ops as ops
+    from stageml_b200 import workloads as wl
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = capi()
+    peaks = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    peak_tf = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    name = args.workload
+    sampler = ClockSampler(0)
+    sampler.start()
+    if name == "single_lora":
+        # x[1,4096] fp32, W[4096,4096] ([in,out]), rank 16, scale 2; 4 rotating weight sets (268 MB > L2)
+        sets = [wl.make_single_lora(seed=s, device=dev) for s in range(4)]
+        folded = [ops.lora_fold(s["W"], s["A"], s["B"], s["scale"], 1) for s in sets]
+        ms_dyn, st_dyn, n_dyn = _timed(lambda i: ops.lora_gemv_f32(sets[i % 4]["x"], sets[i % 4]["W"], sets[i % 4]["A"],
+                                                                    sets[i % 4]["B"], sets[i % 4]["scale"]),
+                                       args.steps, args.warmup, lib)
+        ms_fold, _, _ = _timed(lambda i: ops.lora_gemv_f32(sets[i % 4]["x"], folded[i % 4]), args.steps, args.warmup)
+        byt = 4 * 4096 * 4096 + 2 * 4 * 4096 * 16 + 8 * 4096
+        ms_k = st_dyn.get("gemv", {}).get("ms", 0) / max(st_dyn.get("gemv", {}).get("launches", 1), 1)
+        s0 = sets[0]
+        f = lambda t: t.cpu().numpy()
+        from oracle.lora import single_lora
+
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 2.0:
+            single_lora(f(s0["x"]), f(s0["W"]), f(s0["A"]), f(s0["B"]), s0["scale"], dtype=np.float32)
+            reps += 1
+        cpu_us = (time.perf_counter() - t0) / reps * 1e6
+        _line("single LoRA linear latency (dynamic x W + s (x A) B)", round(ms_dyn * 1000, 3), "us", args.steps,
+              args.warmup, ms_dyn, False, "f32",
+              {"workload": "single_lora", "x": [1, 4096], "W": [4096, 4096], "rank": 16, "scale": 2.0,
+               "l2": "4 rotating weight sets, 268 MB > L2"},
+              folded_latency_us=round(ms_fold * 1000, 3), gpu_launches=n_dyn, clocks=sampler.stop(),
+              roofline={"bound": "hbm", "kernel": "gemv_partial_kernel + reduce",
+                        "achieved": round(byt / (ms_k / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(byt / (ms_k / 1e3) / 1e9 / hbm, 4), "traffic": None},
+              cpu_baseline={"value": round(cpu_us, 2), "unit": "us", "cores": cpu_threads(), "kind": "port",
+                            "sample": "the same call, numpy float32"})
+    elif name == "adapter_bank":
+        from stageml_b200.adapter_bank import AdapterSpec
+        from stageml_b200.adapter_cache import StageMLCostBasedAdapterCache
+
+        w = wl.make_adapter_bank(seed=0, device=dev)
+        ads = [AdapterSpec(f"adapter_{i}", w["A"][i], w["B"][i], w["scale"]) for i in range(w["A"].shape[0])]
+        names = [f"adapter_{i}" for i in w["adapter_ids"]]
+        cached = [f"adapter_{i}" for i in w["folded"]]
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        layers = []
+        e0.record()
+        layers.append(StageMLCostBasedAdapterCache(w["W"], ads, cached_adapter_names=cached))
+        e1.record()
+        torch.cuda.synchronize()
+        fold_ms = e0.elapsed_time(e1)
+        layers += [StageMLCostBasedAdapterCache(w["W"] * (1 + 1e-3 * j), ads, cached_adapter_names=cached)
+                   for j in range(1, 3)]  # 3 layers x 302 MB of weights rotate past L2
+        ms, st, n = _timed(lambda i: layers[i % 3](w["x"], names), args.steps, args.warmup, lib)
+        byt = 4096 * 4096 * 2 * (1 + len(cached)) + 2 * 256 * 4096 * 2
+        _line("multi-tenant LoRA bank tokens/s (64 adapters, top-8 folded)", round(256 / (ms / 1e3), 1), "tokens/s",
+              args.steps, args.warmup, ms, True, "bf16",
+              {"workload": "adapter_bank", "tokens": 256, "dim": 4096, "adapters": 64, "rank": 16,
+               "folded": len(cached), "l2": "3 rotating layers"},
+              stages_ms_per_step={k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in st.items()},
+              stage0_fold_ms=round(fold_ms, 4), gpu_launches=n, clocks=sampler.stop(),
+              roofline={"bound": "hbm", "kernel": "grouped GEMM over [W, W'_1..8] + tensor-core LoRA expand",
+                        "achieved": round(byt / (ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(byt / (ms / 1e3) / 1e9 / hbm, 4), "traffic": None})
+    elif name == "llama_block":
+        blk = wl.make_llama_block(seed=0, device=dev)
+        P = blk["proj"]
+        r, nT = 16, 16
+        ten = blk["row_tenant"]
+        sc = torch.full((nT,), blk["scale"], dtype=torch.float32, device=dev)
+        # MLP = one-expert SwiGLU MoE layer: gate_up = [W_gate; W_up], LoRA A13 = [A_gate; A_up], B13 = [B_gate; B_up]
+        gu = torch.cat([P["gate"]["W"], P["up"]["W"]], 0)[None].contiguous()
+        dn = P["down"]["W"][None].contiguous()
+        a13 = torch.cat([P["gate"]["A"], P["up"]["A"]], 1)[:, None].contiguous()
+        b13 = torch.cat([P["gate"]["B"], P["up"]["B"]], 1)[:, None].contiguous()
+        a2 = P["down"]["A"][:, None].contiguous()
+        b2 = P["down"]["B"][:, None].contiguous()
+        M = blk["x"].shape[0]
+        ids = torch.zeros(M, 1, dtype=torch.int32, device=dev)
+        ones = torch.ones(M, 1, dtype=torch.float32, device=dev)
+
+        def step(i):
+            outs = [ops.lora_linear(blk["x"] if p != "o" else blk["x_o"], P[p]["W"][None], row_tenant=ten, n_tenants=nT,
+                                    rank=r, lora_a=P[p]["A"], lora_b=P[p]["B"], lora_scale=sc) for p in "qkvo"]
+            outs.append(ops.moe_forward(blk["x"], gu, dn, topk_ids=ids, topk_weights=ones, tenant_ids=ten,
+                                        n_tenants=nT, rank=r, lora_a13=a13, lora_b13=b13, lora_a2=a2, lora_b2=b2,
+                                        lora_scale=sc))
+            return outs
+
+        ms, st, n = _timed(step, args.steps, args.warmup, lib)
+        fl = 2.0 * M * (4 * 4096 * 4096 + 3 * 4096 * 11008) + 2.0 * M * r * (4 * 2 * 4096 + 3 * (4096 + 11008))
+        _line("LLaMA-7B block projections with LoRA tokens/s", round(M / (ms / 1e3), 1), "tokens/s", args.steps,
+              args.warmup, ms, True, "fp16",
+              {"workload": "llama_block", "tokens": M, "projections": "q,k,v,o,gate,up,down", "rank": r,
+               "tenants": nT, "attention": "excluded"},
+              stages_ms_per_step={k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in st.items()},
+              gpu_launches=n, clocks=sampler.stop(),
+              roofline={"bound": "tensor", "kernel": "all grouped GEMMs of the block", "flops": fl,
+                        "achieved": round(fl / (ms / 1e3) / 1e12, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                        "frac": round(fl / (ms / 1e3) / 1e12 / peak_tf, 4), "traffic": None})
+    elif name == "fine_grained_moe_lora_bf16":
+        cfg = wl.MoEConfig("fine_grained_moe_lora_bf16", T=8192, H=2048, I=1408, E=64, k=6, n_shared=2,
+                           n_tenants=128, rank=16, tenant_dist="zipf")  # rank 8 zero-padded to 16
+        w = wl.make_moe_workload(cfg, device=dev, seed=0)
+        ms, st, n = _timed(lambda i: layer_call(ops, cfg, w, w["x"], w["tenant_ids"]), args.steps, args.warmup, lib)
+        fl = cfg.flops()
+        _line("fine-grained MoE-LoRA layer tokens/s (bf16 weights)", round(cfg.T / (ms / 1e3), 1), "tokens/s",
+              args.steps, args.warmup, ms, True, "bf16",
+              {"workload": cfg.name, "tokens": cfg.T, "hidden": 2048, "intermediate": 1408, "experts": 64, "top_k": 6,
+               "shared_experts": 2, "tenants": 128, "lora_rank": "16 (the cost of rank 8 zero-padded to 16)",
+               "weights": "bf16"},
+              stages_ms_per_step={k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in st.items()},
+              gpu_launches=n, clocks=sampler.stop(),
+              layer_roofline={"flops": fl["total"], "t_roof_ms": round(fl["total"] / (peak_tf * 1e12) * 1e3, 4),
+                              "frac": round(fl["total"] / (peak_tf * 1e12) * 1e3 / ms, 4)})
+    else:
+        raise SystemExit(f"unknown workload {name}")
+
+
+DENSE_WORKLOADS = ("single_lora", "adapter_bank", "llama_block", "fine_grained_moe_lora_bf16")
+
+
 def make_moe_workload_tokens(cfg, dev, seed: int, T: int):
     from stageml_b200.workloads import _Gen, sample_tenants
 
@@ -432,6 +606,9 @@ def main():
     sys.path.insert(0, str(ROOT))
     from stageml_b200.workloads import MOE_CONFIGS
 
+    if args.workload in DENSE_WORKLOADS:
+        dense_arm(args)
+        return
     cfg = MOE_CONFIGS[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

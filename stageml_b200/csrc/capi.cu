@@ -100,8 +100,12 @@ int moe_validate(const stageml_moe_args* a, bool check_ptrs = true) {
   SB_CHECK_ARG(is16(a->act_dtype), "moe: act_dtype must be BF16 or F16");
   SB_CHECK_ARG(a->weight_dtype == a->act_dtype || a->weight_dtype == STAGEML_E4M3,
                "moe: weight_dtype must equal act_dtype or be E4M3");
-  if (a->weight_dtype == STAGEML_E4M3)
-    return set_error(STAGEML_ERR_UNSUPPORTED, "moe: E4M3 weights are not supported by this build");
+  if (a->weight_dtype == STAGEML_E4M3) {
+    SB_CHECK_ARG(a->H % 16 == 0 && a->I % 16 == 0, "moe: E4M3 weights need H=%d and I=%d to be multiples of 16",
+                 a->H, a->I);
+    SB_CHECK_ARG(!check_ptrs || a->T == 0 || (a->gate_up_scale && a->down_scale),
+                 "moe: E4M3 weights need gate_up_scale and down_scale");
+  }
   SB_CHECK_ARG(a->rank == 0 || a->rank == 16 || a->rank == 32,
                "moe: rank=%d must be 0, 16 or 32 (zero-pad smaller ranks)", a->rank);
   const bool lora13 = a->rank > 0 && a->lora_a13;
@@ -247,6 +251,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       g.tile_nruns = b.nruns;
     }
     g.b_scale = a->gate_up_scale;
+    g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
@@ -299,6 +304,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     }
     g.row_scale = b.plan.row_weight;
     g.b_scale = a->down_scale;
+    g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;

@@ -2,12 +2,15 @@
 // cores: TMA -> 128B-swizzled shared memory -> tcgen05.mma (cta_group::1,
 // M=128, N=256, K=16, fp32 accumulators in TMEM) -> tcgen05.ld epilogue.
 //
-// One persistent CTA per SM, 6 warps:
-//   warp 0      TMA producer (one thread), 4-stage ring of 48 KB stages
+// One persistent CTA per SM:
+//   warp 0      TMA producer (one thread)
 //   warp 1      TMEM allocator + MMA issuer (one thread)
 //   warps 2..5  epilogue: TMEM lane quarter (warp % 4), one accumulator row per thread
+//   warps 6..13 (FP8 weights only) converters: e4m3 -> 16-bit with the
+//               per-output-channel scale, written in the MMA's swizzled layout
 // Two 256-column accumulators in TMEM let the epilogue of tile i overlap the
-// main loop of tile i+1.
+// main loop of tile i+1. 16-bit weights: 4 stages of 48 KB; FP8 weights: 3
+// stages of 64 KB (A 16 KB, 16-bit B 32 KB, e4m3 staging 16 KB).
 //
 // Per-token-tenant LoRA expand is fused on the tensor cores: after a tile's K
 // loop, the producer streams "LoRA blocks" through the same ring -- the
@@ -30,19 +33,27 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 256;            // accumulator columns per tile (SwiGLU: 128 gate + 128 up)
 constexpr int BK = 64;             // 64 x 16-bit = one 128 B swizzle row
-constexpr int STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * BK * 2;         // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;         // 32 KB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int MMA_STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;  // operands the MMA reads (48 KB)
+constexpr int RAW_B_BYTES = BN * BK;               // e4m3 B staging (16 KB)
 constexpr int TMEM_COLS = 2 * BN;                  // double-buffered accumulator
-constexpr int NUM_THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int LCHUNK = 128 * 32;                   // one 128-row x 16-column 16-bit LoRA tile (4 KB)
+constexpr int CONVERTER_THREADS = 256;
+
+template <bool FP8B>
+struct Cfg {
+  static constexpr int STAGES = FP8B ? 3 : 4;
+  static constexpr int STAGE_BYTES = FP8B ? MMA_STAGE_BYTES + RAW_B_BYTES : MMA_STAGE_BYTES;
+  static constexpr int THREADS = FP8B ? 192 + CONVERTER_THREADS : 192;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
 
 struct KParams {
   int K;
   int N;
   int b_group_rows;
+  int64_t b_rows_total;
   int num_n_tiles;
   int swiglu;
   const int32_t* num_tiles_dev;
@@ -64,7 +75,8 @@ struct KParams {
   const void* bias;
   int64_t bias_group_stride;
   int bias_group_mod;
-  const float* b_scale;
+  const float* b_scale;       // 16-bit weights: per-B-row scale applied in the epilogue (or null)
+  const float* b_row_scale;   // FP8 weights: per-B-row dequantisation scale applied by the converters
   void* out;
   int64_t ldo;
   int32_t* status;
@@ -104,17 +116,42 @@ __device__ __forceinline__ int tile_lora_runs(const KParams& p, int m_tile) {
   return n < kMaxRunsPerTile ? n : kMaxRunsPerTile;
 }
 
+// 16 e4m3 values (one 16-byte chunk) -> 16 x 16-bit, scaled.
 template <typename T>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__device__ __forceinline__ void dequant16(const uint4& q, float s, uint4& lo, uint4& hi) {
+  const __nv_fp8x2_storage_t* p2 = reinterpret_cast<const __nv_fp8x2_storage_t*>(&q);
+  float f[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(p2[i], __NV_E4M3);
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    f[2 * i] = v.x * s;
+    f[2 * i + 1] = v.y * s;
+  }
+  float a[8], b[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    a[i] = f[i];
+    b[i] = f[8 + i];
+  }
+  lo = pack8<T>(a);
+  hi = pack8<T>(b);
+}
+
+template <typename T, bool FP8B>
+__global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_lb,
                         const KParams p) {
+  constexpr int STAGES = Cfg<FP8B>::STAGES;
+  constexpr int STAGE_BYTES = Cfg<FP8B>::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  // bars[0..S) full, [S..2S) empty, [2S..2S+2) tmem_full, [2S+2..2S+4) tmem_empty, [2S+4] drain
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  // bars: [0,S) full (operands ready for the MMA), [S,2S) empty, [2S,2S+2) tmem_full,
+  // [2S+2,2S+4) tmem_empty, [2S+4] drain, [2S+5,3S+5) raw (TMA landed; FP8 weights only)
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -125,11 +162,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + a]); };
   auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + 2 + a]); };
   const uint32_t drain_bar = smem_u32(&bars[2 * STAGES + 4]);
+  auto raw_bar = [&](int s) { return smem_u32(&bars[2 * STAGES + 5 + s]); };
+  // the barrier TMA completes on: the MMA's own for 16-bit weights, the converters' for FP8
+  auto land_bar = [&](int s) { return FP8B ? raw_bar(s) : full_bar(s); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full_bar(s), 1);
+      mbar_init(full_bar(s), FP8B ? CONVERTER_THREADS : 1);
       mbar_init(empty_bar(s), 1);
+      if (FP8B) mbar_init(raw_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
@@ -183,11 +224,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         const uint32_t sa = smem_base + s * STAGE_BYTES;
-        const uint32_t sbm = sa + A_STAGE_BYTES;
-        mbar_arrive_expect_tx(full_bar(s), STAGE_BYTES);
-        tma_load_2d(sa, &tm_a, full_bar(s), kb * BK, a_row, pol_a);
-        tma_load_2d(sbm, &tm_b, full_bar(s), kb * BK, b_row0, pol_b);
-        tma_load_2d(sbm + 128 * BK * 2, &tm_b, full_bar(s), kb * BK, b_row1, pol_b);
+        if (FP8B) {
+          const uint32_t sraw = sa + MMA_STAGE_BYTES;
+          mbar_arrive_expect_tx(raw_bar(s), A_STAGE_BYTES + RAW_B_BYTES);
+          tma_load_2d(sa, &tm_a, raw_bar(s), kb * BK, a_row, pol_a);
+          tma_load_2d(sraw, &tm_b, raw_bar(s), kb * BK, b_row0, pol_b);
+          tma_load_2d(sraw + 128 * BK, &tm_b, raw_bar(s), kb * BK, b_row1, pol_b);
+        } else {
+          const uint32_t sbm = sa + A_STAGE_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), MMA_STAGE_BYTES);
+          tma_load_2d(sa, &tm_a, full_bar(s), kb * BK, a_row, pol_a);
+          tma_load_2d(sbm, &tm_b, full_bar(s), kb * BK, b_row0, pol_b);
+          tma_load_2d(sbm + 128 * BK * 2, &tm_b, full_bar(s), kb * BK, b_row1, pol_b);
+        }
         last_phase[s] = (int)ph;
       }
       // LoRA blocks: S of the tile + B rows of each tenant run
@@ -201,11 +250,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         const uint32_t base = smem_base + s * STAGE_BYTES;
-        mbar_arrive_expect_tx(full_bar(s), p.s_bytes + nr * p.run_bytes);
+        const uint32_t bar = land_bar(s);
+        mbar_arrive_expect_tx(bar, p.s_bytes + nr * p.run_bytes);
         for (int ch = 0; ch < p.lchunks; ++ch) {
-          tma_load_2d(base + ch * LCHUNK, &tm_s, full_bar(s), ch * 16, a_row, pol_a);
-          if (p.swiglu)
-            tma_load_2d(base + (p.lchunks + ch) * LCHUNK, &tm_s, full_bar(s), p.rank + ch * 16, a_row, pol_a);
+          tma_load_2d(base + ch * LCHUNK, &tm_s, bar, ch * 16, a_row, pol_a);
+          if (p.swiglu) tma_load_2d(base + (p.lchunks + ch) * LCHUNK, &tm_s, bar, p.rank + ch * 16, a_row, pol_a);
         }
         for (int jj = 0; jj < nr; ++jj) {
           const int tenant = p.tile_runs[((int64_t)m_tile * kMaxRunsPerTile + r0 + jj) * 5];
@@ -213,11 +262,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
             if (p.swiglu) {
-              tma_load_2d(rb + ch * LCHUNK, &tm_lb, full_bar(s), ch * 16, brow, pol_b);
-              tma_load_2d(rb + (p.lchunks + ch) * LCHUNK, &tm_lb, full_bar(s), ch * 16, brow + p.N, pol_b);
+              tma_load_2d(rb + ch * LCHUNK, &tm_lb, bar, ch * 16, brow, pol_b);
+              tma_load_2d(rb + (p.lchunks + ch) * LCHUNK, &tm_lb, bar, ch * 16, brow + p.N, pol_b);
             } else {
-              tma_load_2d(rb + ch * 2 * LCHUNK, &tm_lb, full_bar(s), ch * 16, brow, pol_b);
-              tma_load_2d(rb + ch * 2 * LCHUNK + LCHUNK, &tm_lb, full_bar(s), ch * 16, brow + 128, pol_b);
+              tma_load_2d(rb + ch * 2 * LCHUNK, &tm_lb, bar, ch * 16, brow, pol_b);
+              tma_load_2d(rb + ch * 2 * LCHUNK + LCHUNK, &tm_lb, bar, ch * 16, brow + 128, pol_b);
             }
           }
         }
@@ -228,7 +277,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Let the copies already in flight land before the CTA exits.
       for (int s = 0; s < STAGES; ++s)
         if (last_phase[s] >= 0)
-          mbar_wait(full_bar(s), (uint32_t)last_phase[s], &never_abort, p.status, 1000000000ull, kDevTimeoutDrain);
+          mbar_wait(land_bar(s), (uint32_t)last_phase[s], &never_abort, p.status, 1000000000ull, kDevTimeoutDrain);
     }
   } else if (threadIdx.x == 32) {
     // ------------------------------------------------------------ MMA issuer
@@ -302,7 +351,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_commit(drain_bar);
       mbar_wait(drain_bar, 0, &never_abort, p.status, 1000000000ull, kDevTimeoutDrain);
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
@@ -381,6 +430,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
     }
+  } else if (FP8B && warp >= 6) {
+    // ------------------------------------------------------------ e4m3 -> 16-bit converters
+    // Item (r, c): row r of the 256-row B tile, 16-byte chunk c (16 weights) of its 64-byte
+    // e4m3 row; written as 16-bit logical chunks 2c, 2c+1 of the 128-byte row, stored at
+    // physical chunk (logical ^ (r & 7)) -- the 128B swizzle the MMA descriptor expects.
+    const int ct = threadIdx.x - 192;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      const int m_tile = tile % num_m_tiles;
+      const int n_tile = tile / num_m_tiles;
+      const int group = p.tile_group ? p.tile_group[m_tile] : 0;
+      const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
+      const int64_t b_row0 = (int64_t)group * p.b_group_rows + n0;
+      const int64_t b_row1 = p.swiglu ? b_row0 + p.N : b_row0 + 128;
+      float sc[4];
+      int rr[4], cc[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = ct + CONVERTER_THREADS * q;
+        rr[q] = idx >> 2;
+        cc[q] = idx & 3;
+        const int64_t grow = rr[q] < 128 ? b_row0 + rr[q] : b_row1 + (rr[q] - 128);
+        sc[q] = grow < p.b_rows_total ? p.b_row_scale[grow] : 0.f;
+      }
+      bool ok = true;
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(raw_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        const uint8_t* raw = st + MMA_STAGE_BYTES;
+        uint8_t* bt = st + A_STAGE_BYTES;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + rr[q] * BK + cc[q] * 16);
+          uint4 lo, hi;
+          dequant16<T>(qv, sc[q], lo, hi);
+          uint8_t* row = bt + rr[q] * 128;
+          const int sw = rr[q] & 7;
+          *reinterpret_cast<uint4*>(row + (((2 * cc[q]) ^ sw) << 4)) = lo;
+          *reinterpret_cast<uint4*>(row + (((2 * cc[q] + 1) ^ sw) << 4)) = hi;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(full_bar(s));
+      }
+      const int nruns = ok ? tile_lora_runs(p, m_tile) : 0;
+      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(raw_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive(full_bar(s));  // LoRA operands are already 16-bit
+      }
+      if (!ok) break;
+    }
   }
 
   __syncthreads();
@@ -440,6 +549,17 @@ __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restric
   if (lane == 0) nruns[tile] = count;
 }
 
+template <typename T, bool FP8B>
+int launch_kernel(int grid, cudaStream_t stream, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
+                  const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const KParams& p) {
+  SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<T, FP8B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg<FP8B>::SMEM_BYTES));
+  (grouped_gemm_kernel<T, FP8B><<<grid, Cfg<FP8B>::THREADS, Cfg<FP8B>::SMEM_BYTES, stream>>>(tm_a, tm_b, tm_s, tm_lb, p),
+   ::sb::count_launch());
+  SB_CUDA_CHECK(cudaGetLastError());
+  return STAGEML_OK;
+}
+
 }  // namespace
 
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
@@ -457,6 +577,8 @@ int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, in
 int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   SB_CHECK_ARG(g.a && g.b && g.out, "grouped gemm: null operand");
   SB_CHECK_ARG(g.K > 0 && g.K % 8 == 0, "grouped gemm: K=%d must be a positive multiple of 8", g.K);
+  SB_CHECK_ARG(!g.b_fp8 || g.K % 16 == 0, "grouped gemm: FP8 weights need K=%d to be a multiple of 16", g.K);
+  SB_CHECK_ARG(!g.b_fp8 || g.b_scale, "grouped gemm: FP8 weights need per-row scales");
   SB_CHECK_ARG(g.N > 0, "grouped gemm: N must be positive");
   SB_CHECK_ARG(g.rank == 0 || g.rank == 16 || g.rank == 32, "grouped gemm: LoRA rank %d must be 0, 16 or 32", g.rank);
   SB_CHECK_ARG(g.rank == 0 || (g.s16 && g.lora_b && g.tile_runs && g.tile_nruns && g.s_rows > 0 &&
@@ -471,7 +593,11 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   const CUtensorMapDataType dt = g.in_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tm_a, tm_b, tm_s, tm_lb;
   SB_TRY(make_tmap_2d(&tm_a, g.a, dt, 2, (uint64_t)g.a_rows, (uint64_t)g.K, (uint64_t)g.K * 2, BM, BK, 128));
-  SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
+  if (g.b_fp8)
+    SB_TRY(make_tmap_2d(&tm_b, g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.b_rows_total, (uint64_t)g.K,
+                        (uint64_t)g.K, 128, BK, 0));
+  else
+    SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
   const int lora_cols = g.swiglu ? 2 * g.rank : g.rank;
   if (g.rank) {
     SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
@@ -487,6 +613,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.K = g.K;
   p.N = g.N;
   p.b_group_rows = g.b_group_rows;
+  p.b_rows_total = g.b_rows_total;
   p.swiglu = g.swiglu ? 1 : 0;
   p.num_n_tiles = g.swiglu ? (g.N + 127) / 128 : (g.N + BN - 1) / BN;
   p.num_tiles_dev = g.num_tiles_dev;
@@ -497,7 +624,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.lchunks = g.rank / 16;
   p.s_bytes = (g.swiglu ? 2 : 1) * p.lchunks * LCHUNK;
   p.run_bytes = 2 * p.lchunks * LCHUNK;
-  p.runs_per_block = g.rank ? (STAGE_BYTES - p.s_bytes) / p.run_bytes : 1;
+  p.runs_per_block = g.rank ? (MMA_STAGE_BYTES - p.s_bytes) / p.run_bytes : 1;
   p.lb_tenant_rows = g.rank ? g.lora_b_tenant_stride / g.rank : 0;
   p.lb_group_rows = g.rank ? g.lora_b_group_stride / g.rank : 0;
   p.tile_runs = g.tile_runs;
@@ -506,7 +633,8 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.bias = g.bias;
   p.bias_group_stride = g.bias_group_stride;
   p.bias_group_mod = g.bias_group_mod;
-  p.b_scale = g.b_scale;
+  p.b_scale = g.b_fp8 ? nullptr : g.b_scale;
+  p.b_row_scale = g.b_fp8 ? g.b_scale : nullptr;
   p.out = g.out;
   p.ldo = g.ldo;
   p.status = g.status;
@@ -517,19 +645,11 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   if (tiles_upper == 0) return STAGEML_OK;
   const int grid = (int)std::min<int64_t>(tiles_upper, sm_count());
 
-  if (g.in_bf16) {
-    SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES));
-    (grouped_gemm_kernel<bf16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, tm_s, tm_lb, p),
-     ::sb::count_launch());
-  } else {
-    SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<f16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES));
-    (grouped_gemm_kernel<f16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, tm_s, tm_lb, p),
-     ::sb::count_launch());
-  }
-  SB_CUDA_CHECK(cudaGetLastError());
-  return STAGEML_OK;
+  if (g.b_fp8)
+    return g.in_bf16 ? launch_kernel<bf16, true>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p)
+                     : launch_kernel<f16, true>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p);
+  return g.in_bf16 ? launch_kernel<bf16, false>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p)
+                   : launch_kernel<f16, false>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p);
 }
 
 }  // namespace sb

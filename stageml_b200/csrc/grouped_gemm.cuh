@@ -23,12 +23,16 @@ namespace sb {
 // SwiGLU mode: B group = [W1 (N rows); W3 (N rows)], S = [s1 | s3] (2*rank
 // columns), Bl rows [0,N) for W1 and [N,2N) for W3; out = silu(g) * u.
 // Plain mode: out = (acc * b_scale[col] + bias[col]) * row_scale[row].
+// FP8 weights (b_fp8): B holds e4m3 codes and b_scale (required) the per-B-row
+// scale; every weight is dequantised to the activation type before the MMA,
+// so the epilogue applies no further scale.
 struct GemmLaunch {
   const void* a = nullptr;       // [a_rows, K] 16-bit
   int64_t a_rows = 0;
   int K = 0;
-  const void* b = nullptr;       // [b_rows_total, K] 16-bit
+  const void* b = nullptr;       // [b_rows_total, K] 16-bit, or e4m3 when b_fp8
   int64_t b_rows_total = 0;
+  bool b_fp8 = false;            // e4m3 weights, dequantised in shared memory with b_scale[row]
   int b_group_rows = 0;          // rows of B per group (N or 2N)
   int N = 0;                     // output columns
   bool swiglu = false;

@@ -121,6 +121,17 @@ Tensor moe_forward(const Tensor& x, const Tensor& gate_up, const Tensor& down, c
                 "moe_forward: tenant_ids must be int32 [T]");
   if (lora_scale.has_value()) TORCH_CHECK(lora_scale->scalar_type() == at::kFloat, "moe_forward: lora_scale fp32");
   if (router_w.has_value()) TORCH_CHECK(router_w->scalar_type() == at::kFloat, "moe_forward: router_w must be fp32");
+  TORCH_CHECK(gate_up.scalar_type() == down.scalar_type(), "moe_forward: gate_up and down must share a dtype");
+  if (gate_up.scalar_type() == at::kFloat8_e4m3fn) {
+    TORCH_CHECK(gate_up_scale.has_value() && down_scale.has_value(),
+                "moe_forward: e4m3 weights need gate_up_scale and down_scale");
+    TORCH_CHECK(gate_up_scale->scalar_type() == at::kFloat && gate_up_scale->numel() == E_tot * 2 * I &&
+                    gate_up_scale->is_contiguous(),
+                "moe_forward: gate_up_scale must be contiguous fp32 [E_tot, 2I]");
+    TORCH_CHECK(down_scale->scalar_type() == at::kFloat && down_scale->numel() == E_tot * H &&
+                    down_scale->is_contiguous(),
+                "moe_forward: down_scale must be contiguous fp32 [E_tot, H]");
+  }
   c10::cuda::CUDAGuard guard(x.device());
   auto out = at::empty({T, H}, x.options());
   stageml_moe_args a{};

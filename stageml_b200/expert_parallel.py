@@ -59,7 +59,7 @@ class EPMoELayer:
         take = lambda t, d: None if t is None else t.index_select(d, idx).contiguous()
         return cls(E=cfg.E, k=cfg.k, n_shared=cfg.n_shared, H=cfg.H, I=cfg.I, rank=rank, world=world,
                    gate_up_local=take(w["gate_up"], 0), down_local=take(w["down"], 0), router_w=w["router_w"],
-                   n_tenants=cfg.n_tenants, lora_rank=cfg.rank, lora_a13=take(w["lora_a13"], 1),
+                   n_tenants=cfg.n_tenants, lora_rank=cfg.bank_rank, lora_a13=take(w["lora_a13"], 1),
                    lora_b13=take(w["lora_b13"], 1), lora_a2=take(w["lora_a2"], 1), lora_b2=take(w["lora_b2"], 1),
                    lora_scale=w["lora_scale"], group=group)
 

@@ -95,6 +95,13 @@ class MoEConfig:
     def E_tot(self) -> int:
         return self.E + self.n_shared
 
+    @property
+    def bank_rank(self) -> int:
+        """Rank of the LoRA banks as stored: the adapter rank zero-padded to 16 or 32."""
+        from ._packing import padded_rank
+
+        return padded_rank(self.rank)
+
     def flops(self, T: int | None = None) -> dict:
         """Algorithmic FLOPs (2 x MACs) of one layer call."""
         T = self.T if T is None else T
@@ -127,7 +134,9 @@ def make_moe_workload(cfg: MoEConfig, *, device="cuda", gen_device: str | None =
     Returned layouts follow the C ABI: gate_up [E_tot, 2I, H] (rows [:I] = w1,
     the SiLU branch), down [E_tot, H, I], router_w [E, H] fp32 (= W_g^T),
     lora_a13 [n_tenants, E_tot, 2r, H], lora_b13 [n_tenants, E_tot, 2I, r],
-    lora_a2 [n_tenants, E_tot, r, I], lora_b2 [n_tenants, E_tot, H, r].
+    lora_a2 [n_tenants, E_tot, r, I], lora_b2 [n_tenants, E_tot, H, r], with
+    r = cfg.bank_rank: factors of rank cfg.rank are drawn, then zero-padded
+    (rows of A, columns of B), which leaves every product unchanged.
     """
     gen_device = gen_device or ("cuda" if torch.device(device).type == "cuda" else "cpu")
     T = cfg.T if T is None else T
@@ -143,6 +152,14 @@ def make_moe_workload(cfg: MoEConfig, *, device="cuda", gen_device: str | None =
     b13 = g.normal_stacked(nT * Et, (2 * I, r), 1.0 / math.sqrt(r), act).view(nT, Et, 2 * I, r)
     a2 = g.normal_stacked(nT * Et, (r, I), 1.0 / math.sqrt(I), act).view(nT, Et, r, I)
     b2 = g.normal_stacked(nT * Et, (H, r), 1.0 / math.sqrt(r), act).view(nT, Et, H, r)
+    rp = cfg.bank_rank
+    if rp != r:
+        pad = lambda t, dim: torch.cat([t, t.new_zeros(t.shape[:dim] + (rp - r,) + t.shape[dim + 1:])], dim)
+        a13 = torch.cat([pad(a13[:, :, :r], 2), pad(a13[:, :, r:], 2)], 2).contiguous()
+        b13 = pad(b13, 3).contiguous()
+        a2 = pad(a2, 2).contiguous()
+        b2 = pad(b2, 3).contiguous()
+        r = rp
     if "w1" not in cfg.lora_on:
         a13[:, :, :r].zero_()
     if "w3" not in cfg.lora_on:

@@ -72,7 +72,14 @@ def test_moe_args_validation_and_workspace_query():
     assert lib.stageml_moe_forward(ctypes.byref(a), None, 0, None) == capi.ERR_INVALID_ARG  # null tensors
     a2 = capi.MoeArgs(T=16, H=64, I=64, E=2, k=1, act_dtype=capi.BF16, weight_dtype=capi.E4M3, topk_ids=1,
                       ids_dtype=capi.I32, x=16, gate_up=16, down=16, out=16)
-    assert lib.stageml_moe_forward(ctypes.byref(a2), None, 0, None) in (capi.ERR_UNSUPPORTED, capi.ERR_WORKSPACE)
+    # e4m3 weights need their per-row scales, and H, I multiples of 16
+    assert lib.stageml_moe_forward(ctypes.byref(a2), None, 0, None) == capi.ERR_INVALID_ARG
+    assert "scale" in lib.stageml_last_error().decode()
+    a2.gate_up_scale = a2.down_scale = 16
+    assert lib.stageml_moe_workspace_bytes(ctypes.byref(a2)) > 0
+    assert lib.stageml_moe_forward(ctypes.byref(a2), None, 0, None) == capi.ERR_WORKSPACE
+    a2.I = 72
+    assert lib.stageml_moe_workspace_bytes(ctypes.byref(a2)) == 0
 
 
 def test_workspace_too_small_is_reported():

@@ -55,7 +55,7 @@ def _worker(rank, world, port, q):
             layer = EPMoELayer.from_full_weights(cfg, w, rank=rank, world=world)
             y_ep = layer(x, ten)
             y_1 = ops.moe_forward(x, w["gate_up"], w["down"], router_w=w["router_w"], k=cfg.k, n_shared=ns,
-                                  tenant_ids=ten, n_tenants=cfg.n_tenants, rank=cfg.rank, lora_a13=w["lora_a13"],
+                                  tenant_ids=ten, n_tenants=cfg.n_tenants, rank=cfg.bank_rank, lora_a13=w["lora_a13"],
                                   lora_b13=w["lora_b13"], lora_a2=w["lora_a2"], lora_b2=w["lora_b2"],
                                   lora_scale=w["lora_scale"])
             torch.cuda.synchronize()

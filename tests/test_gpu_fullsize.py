@@ -22,7 +22,7 @@ def layer():
     w = make_moe_workload(cfg, device=DEV, seed=0)
 
     def call(x, ten, **over):
-        kw = dict(router_w=w["router_w"], k=cfg.k, tenant_ids=ten, n_tenants=cfg.n_tenants, rank=cfg.rank,
+        kw = dict(router_w=w["router_w"], k=cfg.k, tenant_ids=ten, n_tenants=cfg.n_tenants, rank=cfg.bank_rank,
                   lora_a13=w["lora_a13"], lora_b13=w["lora_b13"], lora_a2=w["lora_a2"], lora_b2=w["lora_b2"],
                   lora_scale=w["lora_scale"])
         kw.update(over)
