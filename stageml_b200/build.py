@@ -28,6 +28,7 @@ CU_SOURCES = [
     "permute.cu",
     "shrink.cu",
     "grouped_gemm.cu",
+    "grouped_gemm_pair.cu",
     "combine.cu",
     "fold.cu",
     "gemv.cu",

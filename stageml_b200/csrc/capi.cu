@@ -2,6 +2,7 @@
 // Each entry validates its arguments on the host, carves its scratch from the
 // caller's workspace and launches the kernels of the path on `stream`.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "grouped_gemm.cuh"
@@ -86,9 +87,23 @@ struct MoeBuffers {
   void* s2 = nullptr;    // [rows_cap, r] 16-bit
   int32_t* runs = nullptr;   // [tiles_cap, 128, 5]
   int32_t* nruns = nullptr;  // [tiles_cap]
+  int32_t* pairs = nullptr;      // [tiles_cap, 4] (CTA-pair GEMM)
+  int32_t* num_pairs = nullptr;  // [1]
+  int32_t* pruns = nullptr;      // [tiles_cap, kMaxRunsPerPair, kPairRunInts]
+  int32_t* pnruns = nullptr;     // [tiles_cap]
   int32_t* status = nullptr;
   size_t bytes = 0;
 };
+
+// The grouped GEMMs run on CTA pairs (tcgen05 cta_group::2) unless the
+// environment sets STAGEML_GEMM_PAIRS=0 (one CTA per tile), read once per process.
+bool gemm_pairs_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STAGEML_GEMM_PAIRS");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int moe_validate(const stageml_moe_args* a, bool check_ptrs = true) {
   SB_CHECK_ARG(a, "moe: null args");
@@ -153,12 +168,30 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
     b->spart2 = c.take<float>((size_t)shrink_num_slices(a->I) * rows_cap * a->rank);
     b->s2 = c.take_bytes((size_t)rows_cap * a->rank * es);
   }
-  if (a->rank > 0 && (a->lora_a13 || a->lora_a2)) {
+  const bool lora = a->rank > 0 && (a->lora_a13 || a->lora_a2);
+  if (gemm_pairs_enabled()) {
+    b->pairs = c.take<int32_t>((size_t)(rows_cap / 128) * 4);
+    b->num_pairs = c.take<int32_t>(1);
+    if (lora) {
+      b->pruns = c.take<int32_t>(pair_runs_ints(rows_cap / 128));
+      b->pnruns = c.take<int32_t>((size_t)(rows_cap / 128));
+    }
+  } else if (lora) {
     b->runs = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
     b->nruns = c.take<int32_t>((size_t)(rows_cap / 128));
   }
   b->status = c.take<int32_t>(1);
   b->bytes = c.off;
+}
+
+// Route a GemmLaunch of the MoE layer to the CTA-pair kernel when its pair plan exists.
+void use_pairs(GemmLaunch& g, const MoeBuffers& b, int tiles_cap) {
+  if (!b.pairs) return;
+  g.pairs = b.pairs;
+  g.num_pairs_dev = b.num_pairs;
+  g.pairs_cap = tiles_cap;
+  g.pair_runs = b.pruns;
+  g.pair_nruns = b.pnruns;
 }
 
 int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
@@ -198,7 +231,11 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
                         b.plan, status, scr, st));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
-  if (b.runs)
+  if (b.pairs)
+    SB_STAGE(STAGEML_STAGE_PERMUTE,
+             launch_pair_plan(b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles, tiles_cap, 0,
+                              b.pruns ? b.plan.row_tenant : nullptr, b.pairs, b.num_pairs, b.pruns, b.pnruns, st));
+  else if (b.runs)
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   // gather + R4 shrink of w1|w3
@@ -252,6 +289,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     }
     g.b_scale = a->gate_up_scale;
     g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
+    use_pairs(g, b, tiles_cap);
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
@@ -305,6 +343,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.row_scale = b.plan.row_weight;
     g.b_scale = a->down_scale;
     g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
+    use_pairs(g, b, tiles_cap);
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;

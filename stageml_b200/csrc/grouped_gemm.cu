@@ -581,14 +581,15 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   SB_CHECK_ARG(!g.b_fp8 || g.b_scale, "grouped gemm: FP8 weights need per-row scales");
   SB_CHECK_ARG(g.N > 0, "grouped gemm: N must be positive");
   SB_CHECK_ARG(g.rank == 0 || g.rank == 16 || g.rank == 32, "grouped gemm: LoRA rank %d must be 0, 16 or 32", g.rank);
-  SB_CHECK_ARG(g.rank == 0 || (g.s16 && g.lora_b && g.tile_runs && g.tile_nruns && g.s_rows > 0 &&
-                               g.lora_b_rows_total > 0),
+  SB_CHECK_ARG(g.rank == 0 || (g.s16 && g.lora_b && (g.pairs ? (g.pair_runs && g.pair_nruns) : (g.tile_runs && g.tile_nruns)) &&
+                               g.s_rows > 0 && g.lora_b_rows_total > 0),
                "grouped gemm: LoRA rank > 0 needs S, B, the tile runs and their sizes");
   SB_CHECK_ARG((reinterpret_cast<uintptr_t>(g.a) % 16) == 0 && (reinterpret_cast<uintptr_t>(g.b) % 16) == 0,
                "grouped gemm: operands must be 16-byte aligned");
   SB_CHECK_ARG(g.b_rows_total < (int64_t(1) << 31) && g.a_rows < (int64_t(1) << 31),
                "grouped gemm: operand rows exceed the TMA coordinate range");
   SB_CHECK_ARG(g.lora_b_rows_total < (int64_t(1) << 31), "grouped gemm: LoRA bank exceeds the TMA coordinate range");
+  if (g.pairs) return launch_grouped_gemm_pair(g, stream);
 
   const CUtensorMapDataType dt = g.in_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tm_a, tm_b, tm_s, tm_lb;

@@ -61,6 +61,13 @@ struct GemmLaunch {
   void* out = nullptr;                   // [rows, ldo] 16-bit
   int64_t ldo = 0;
   int32_t* status = nullptr;
+  // CTA-pair kernel (grouped_gemm_pair.cu), used when `pairs` is set: the pair
+  // list and per-pair LoRA runs written by launch_pair_plan.
+  const int32_t* pairs = nullptr;        // [pairs_cap][4]
+  const int32_t* num_pairs_dev = nullptr;
+  int pairs_cap = 0;
+  const int32_t* pair_runs = nullptr;    // [pairs_cap][kMaxRunsPerPair][kPairRunInts]
+  const int32_t* pair_nruns = nullptr;   // [pairs_cap]
 };
 
 int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
@@ -72,5 +79,24 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
                      int32_t* runs, int32_t* nruns, cudaStream_t stream);
 constexpr int kMaxRunsPerTile = 128;
+
+// CTA-pair variant of the grouped GEMM: 256-row tiles made of two 128-row tiles
+// of the same group, computed by a two-CTA cluster (tcgen05 cta_group::2).
+constexpr int kMaxRunsPerPair = 256;
+constexpr int kPairRunInts = 9;  // tenant, 8 row-mask words
+int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream);
+
+// Pair list and per-pair LoRA runs. Grouped rows (tile_group != nullptr): pairs of
+// consecutive tiles of the same group, taken from the group's first tile
+// (group_offsets[g] / 128), a trailing odd tile paired with -1. Direct rows:
+// tiles (2j, 2j+1) of ceil(static_rows / 128). pairs[4p..4p+3] = first tile,
+// second tile or -1, first pair of the group, pairs in the group. pairs_cap =
+// tiles_cap (grouped) or the direct tile count. With row_tenant set, also writes the LoRA runs of every
+// pair: runs[(pair*kMaxRunsPerPair + j)*kPairRunInts + 0] = tenant, [1..8] = mask
+// words over the pair's 256 rows; nruns[pair].
+int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
+                     int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
+                     int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream);
+size_t pair_runs_ints(int64_t pairs_cap);
 
 }  // namespace sb

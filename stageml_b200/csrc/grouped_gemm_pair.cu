@@ -1,0 +1,780 @@
+// Grouped GEMM on CTA pairs: the 256 x 256 tile of a two-CTA cluster computed by
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16, fp32 accumulators in TMEM).
+//
+// Same computation as grouped_gemm.cu (per-group weights, SwiGLU or plain
+// epilogue, per-token-tenant LoRA expand fused as masked MMAs, e4m3 weights
+// dequantised in shared memory), laid out so that each SM moves a third fewer
+// bytes per FLOP: every CTA of the pair stages its own 128 rows of A and only
+// half of the 256 B rows (SwiGLU: the gate half on the even CTA, the up half
+// on the odd one), and the pair MMA issued by the even CTA reads both.
+//
+// A pair covers two 128-row tiles of the same group (consecutive tiles of a
+// padded group segment); a group with an odd tile count ends with a pair whose
+// odd half is idle (its rows are loaded but never stored).
+//
+// Per CTA: warp 0 TMA producer, warp 1 TMEM allocator and -- on the even CTA --
+// MMA issuer; warps 2..5 epilogue over the CTA's own 128 TMEM lanes; warps 6..13
+// e4m3 converters (FP8 weights only). With 16-bit weights both CTAs' copies
+// complete on the even CTA's stage barrier (cta_group::2 copies); with FP8
+// weights each CTA's copies complete locally and its converters signal the even
+// CTA. Every wait is bounded. No load is multicast.
+#include "common.cuh"
+#include "grouped_gemm.cuh"
+#include "host_util.h"
+
+#include <mutex>
+
+namespace sb {
+namespace {
+
+constexpr int BM = 128;                        // rows per CTA (256 per pair)
+constexpr int BN = 256;                        // accumulator columns
+constexpr int BK = 64;                         // one 128 B swizzle row of 16-bit values
+constexpr int A_BYTES = BM * BK * 2;           // 16 KB
+constexpr int B_BYTES = 128 * BK * 2;          // this CTA's half of B: 16 KB
+constexpr int MMA_STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int RAW_BYTES = 128 * BK;            // e4m3 staging of this CTA's half of B: 8 KB
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int LCHUNK = 128 * 32;               // 128 rows x 16 columns, 16-bit (4 KB)
+constexpr int LHALF = 64 * 32;                 // 64 rows x 16 columns, 16-bit (2 KB)
+constexpr int CONVERTER_THREADS = 256;
+
+template <bool FP8B>
+struct Cfg {
+  static constexpr int STAGES = FP8B ? 5 : 7;
+  static constexpr int STAGE_BYTES = FP8B ? MMA_STAGE_BYTES + RAW_BYTES : MMA_STAGE_BYTES;
+  static constexpr int THREADS = FP8B ? 192 + CONVERTER_THREADS : 192;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+  // full: 16-bit weights -- the even CTA's expect_tx (both halves' copies complete on it);
+  // FP8 weights -- one arrival per converter warp of both CTAs
+  static constexpr int FULL_ARRIVALS = FP8B ? 2 * (CONVERTER_THREADS / 32) : 1;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per block");
+  static_assert((3 * STAGES + 5) * 8 + 8 <= 512, "barrier area");
+};
+
+struct PParams {
+  int K;
+  int N;
+  int b_group_rows;
+  int64_t b_rows_total;
+  int num_n_tiles;
+  int swiglu;
+  const int32_t* tile_group;     // null: one group (direct rows)
+  int64_t m_rows;                // direct mode: valid rows
+  const int32_t* pairs;          // [pairs_cap][4]: m-tile of each half (-1: idle half), group's first pair, its pair count
+  const int32_t* num_pairs_dev;
+  int pairs_cap;
+  // LoRA
+  int rank;
+  int lchunks;
+  int s_bytes;
+  int run_bytes;
+  int runs_per_block;
+  int64_t lb_tenant_rows;
+  int64_t lb_group_rows;
+  const int32_t* runs;           // [pairs_cap][kMaxRunsPerPair][9]
+  const int32_t* nruns;          // [pairs_cap]
+  // epilogue
+  const float* row_scale;
+  const void* bias;
+  int64_t bias_group_stride;
+  int bias_group_mod;
+  const float* b_scale;          // 16-bit weights: per-B-row scale in the epilogue (or null)
+  const float* b_row_scale;      // FP8 weights: per-B-row dequantisation scale
+  void* out;
+  int64_t ldo;
+  int32_t* status;
+  unsigned long long timeout_ns;
+};
+
+template <typename T>
+struct IsBf16 {
+  static constexpr int value = 0;
+};
+template <>
+struct IsBf16<bf16> {
+  static constexpr int value = 1;
+};
+
+template <typename T>
+__device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_valid, bool vec_ok) {
+  if (vec_ok && ncols_valid >= 16) {
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lo[i] = v[i];
+      hi[i] = v[8 + i];
+    }
+    reinterpret_cast<uint4*>(dst)[0] = pack8<T>(lo);
+    reinterpret_cast<uint4*>(dst)[1] = pack8<T>(hi);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < ncols_valid) dst[i] = from_f32<T>(v[i]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void dequant16(const uint4& q, float s, uint4& lo, uint4& hi) {
+  const __nv_fp8x2_storage_t* p2 = reinterpret_cast<const __nv_fp8x2_storage_t*>(&q);
+  float a[8], b[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2_raw r0 = __nv_cvt_fp8x2_to_halfraw2(p2[i], __NV_E4M3);
+    const __half2_raw r1 = __nv_cvt_fp8x2_to_halfraw2(p2[4 + i], __NV_E4M3);
+    const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&r0));
+    const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&r1));
+    a[2 * i] = v0.x * s;
+    a[2 * i + 1] = v0.y * s;
+    b[2 * i] = v1.x * s;
+    b[2 * i + 1] = v1.y * s;
+  }
+  lo = pack8<T>(a);
+  hi = pack8<T>(b);
+}
+
+__device__ __forceinline__ int pair_lora_runs(const PParams& p, int pm) {
+  if (p.rank == 0) return 0;
+  const int n = p.nruns[pm];
+  return n < kMaxRunsPerPair ? n : kMaxRunsPerPair;
+}
+
+__device__ __forceinline__ int num_pairs(const PParams& p) {
+  const int n = *p.num_pairs_dev;
+  return n < p.pairs_cap ? n : p.pairs_cap;
+}
+
+// Work unit u -> (pair, n-tile), group-major: every n-tile of a group's pairs (pairs
+// fastest) before the next group, so a weight tile is read by all its row pairs at
+// about the same time and only one group's activations need to stay in L2. The units
+// of group g are [first_pair(g) * n_tiles, (first_pair(g) + pairs(g)) * n_tiles).
+__device__ __forceinline__ void unit_coords(const PParams& p, int u, int& pm, int& n_tile) {
+  const int pstar = u / p.num_n_tiles;
+  const int first = p.pairs[4 * pstar + 2], cnt = p.pairs[4 * pstar + 3];
+  const int local = u - first * p.num_n_tiles;
+  n_tile = local / cnt;
+  pm = first + (local - n_tile * cnt);
+}
+
+template <typename T, bool FP8B>
+__global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                             const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_lb,
+                             const PParams p) {
+  constexpr int STAGES = Cfg<FP8B>::STAGES;
+  constexpr int STAGE_BYTES = Cfg<FP8B>::STAGE_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bars: [0,S) landed (this CTA's TMA), [S,2S) full (both halves ready; used on the
+  // even CTA), [2S,3S) empty, [3S,3S+2) tmem_full, [3S+2,3S+4) tmem_empty (even CTA),
+  // [3S+4] drain
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const uint32_t smem_base = smem_u32(smem);
+  auto landed_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto full_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[2 * STAGES + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[3 * STAGES + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[3 * STAGES + 2 + a]); };
+  const uint32_t drain_bar = smem_u32(&bars[3 * STAGES + 4]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(landed_bar(s), 1);
+      mbar_init(full_bar(s), Cfg<FP8B>::FULL_ARRIVALS);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps of each CTA
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_base_slot), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  const int npairs = num_pairs(p);
+  const int total_units = npairs * p.num_n_tiles;
+  const int num_kb = (p.K + BK - 1) / BK;
+  volatile int never_abort = 0;
+
+  if (threadIdx.x == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+    if (p.rank) {
+      tma_prefetch_desc(&tm_s);
+      tma_prefetch_desc(&tm_lb);
+    }
+    const uint64_t pol_a = l2_policy_evict_last();
+    const uint64_t pol_b = l2_policy_evict_normal();
+    // 16-bit weights: both CTAs' copies complete on the even CTA's full barrier, which the
+    // even CTA arms with the bytes of both halves. FP8 weights: copies complete on this
+    // CTA's landed barrier, the converters then arrive on the even CTA's full barrier.
+    const uint32_t lead_full0 = mapa_shared(full_bar(0), 0);
+    auto arm = [&](int s, uint32_t bytes) {
+      if (FP8B)
+        mbar_arrive_expect_tx(landed_bar(s), bytes);
+      else if (leader)
+        mbar_arrive_expect_tx(full_bar(s), 2 * bytes);
+    };
+    auto load = [&](uint32_t dst, const CUtensorMap* tm, int s, int x, int y, uint64_t pol) {
+      if (FP8B)
+        tma_load_2d(dst, tm, landed_bar(s), x, y, pol);
+      else
+        tma_load_2d_pair(dst, tm, lead_full0 + 8u * (uint32_t)s, x, y, pol);
+    };
+    int last_phase[STAGES];
+    for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = cluster; ok && u < total_units; u += nclusters) {
+      int pm, n_tile;
+      unit_coords(p, u, pm, n_tile);
+      const int m0 = p.pairs[4 * pm];
+      const int mine = p.pairs[4 * pm + rank];
+      const int m_load = mine >= 0 ? mine : m0;  // an idle half loads defined rows it never stores
+      const int group = p.tile_group ? p.tile_group[m0] : 0;
+      const int a_row = m_load * BM;
+      const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
+      const int b_row = group * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait_cluster(empty_bar(s), ph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sa = smem_base + s * STAGE_BYTES;
+        arm(s, FP8B ? A_BYTES + RAW_BYTES : MMA_STAGE_BYTES);
+        load(sa, &tm_a, s, kb * BK, a_row, pol_a);
+        load(FP8B ? sa + MMA_STAGE_BYTES : sa + A_BYTES, &tm_b, s, kb * BK, b_row, pol_b);
+        last_phase[s] = (int)ph;
+      }
+      // LoRA blocks: this CTA's rows of S + its half of the B rows of each tenant run
+      const int nruns = ok ? pair_lora_runs(p, pm) : 0;
+      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
+        const int nr = min(p.runs_per_block, nruns - r0);
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait_cluster(empty_bar(s), ph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const uint32_t base = smem_base + s * STAGE_BYTES;
+        arm(s, p.s_bytes + nr * p.run_bytes);
+        for (int ch = 0; ch < p.lchunks; ++ch) {
+          load(base + ch * LCHUNK, &tm_s, s, ch * 16, a_row, pol_a);
+          if (p.swiglu) load(base + (p.lchunks + ch) * LCHUNK, &tm_s, s, p.rank + ch * 16, a_row, pol_a);
+        }
+        for (int jj = 0; jj < nr; ++jj) {
+          const int tenant = p.runs[((int64_t)pm * kMaxRunsPerPair + r0 + jj) * kPairRunInts];
+          const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
+          const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
+          for (int ch = 0; ch < p.lchunks; ++ch) {
+            if (p.swiglu) {
+              // gate / up MMAs have N = 128: this CTA holds rows [64 * rank, 64 * rank + 64) of each
+              load(rb + ch * LHALF, &tm_lb, s, ch * 16, brow + 64 * (int)rank, pol_b);
+              load(rb + (p.lchunks + ch) * LHALF, &tm_lb, s, ch * 16, brow + p.N + 64 * (int)rank, pol_b);
+            } else {
+              load(rb + ch * LCHUNK, &tm_lb, s, ch * 16, brow + 128 * (int)rank, pol_b);
+              load(rb + ch * LCHUNK + LHALF, &tm_lb, s, ch * 16, brow + 128 * (int)rank + 64, pol_b);
+            }
+          }
+        }
+        last_phase[s] = (int)ph;
+      }
+    }
+    if (!ok) {
+      // Let the copies already in flight land before the CTA pair leaves. The odd CTA's
+      // 16-bit copies complete on the even CTA's barrier; it waits a fixed, ample time.
+      if (FP8B || leader) {
+        for (int s = 0; s < STAGES; ++s)
+          if (last_phase[s] >= 0)
+            mbar_wait(FP8B ? landed_bar(s) : full_bar(s), (uint32_t)last_phase[s], &never_abort, p.status,
+                      200000000ull, kDevTimeoutDrain);
+      } else {
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) {
+        }
+      }
+    }
+  } else if (threadIdx.x == 32 && leader) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    const uint32_t idesc = idesc_f16(2 * BM, BN, IsBf16<T>::value);
+    const uint32_t idesc_n128 = idesc_f16(2 * BM, 128, IsBf16<T>::value);
+    uint32_t it = 0;
+    int tcount = 0;
+    bool ok = true;
+    for (int u = cluster; ok && u < total_units; u += nclusters, ++tcount) {
+      const int acc = tcount & 1;
+      const uint32_t aph = (tcount >> 1) & 1;
+      int pm, n_tile_unused;
+      unit_coords(p, u, pm, n_tile_unused);
+      if (!mbar_wait_cluster(tempty_bar(acc), aph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait_cluster(full_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_base + s * STAGE_BYTES;
+        const uint64_t adesc = smem_desc_sw128(sa);
+        const uint64_t bdesc = smem_desc_sw128(sa + A_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          tc_mma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        tc_commit_pair_both(empty_bar(s), 0x3);
+      }
+      const int nruns = ok ? pair_lora_runs(p, pm) : 0;
+      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
+        const int nr = min(p.runs_per_block, nruns - r0);
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait_cluster(full_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = smem_base + s * STAGE_BYTES;
+        for (int jj = 0; jj < nr; ++jj) {
+          const int32_t* run = p.runs + ((int64_t)pm * kMaxRunsPerPair + r0 + jj) * kPairRunInts;
+          uint32_t dis[8];
+#pragma unroll
+          for (int w = 0; w < 8; ++w) dis[w] = ~(uint32_t)run[1 + w];
+          const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
+          for (int ch = 0; ch < p.lchunks; ++ch) {
+            if (p.swiglu) {
+              tc_mma_f16_pair_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * LHALF),
+                                     idesc_n128, 1u, dis);
+              tc_mma_f16_pair_masked(d_tmem + 128, smem_desc_sw32(base + (p.lchunks + ch) * LCHUNK),
+                                     smem_desc_sw32(rb + (p.lchunks + ch) * LHALF), idesc_n128, 1u, dis);
+            } else {
+              tc_mma_f16_pair_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * LCHUNK),
+                                     idesc, 1u, dis);
+            }
+          }
+        }
+        tc_commit_pair_both(empty_bar(s), 0x3);
+      }
+      if (!ok) break;
+      tc_commit_pair_both(tfull_bar(acc), 0x3);
+    }
+    // Every MMA of this CTA pair has completed (and stopped reading either CTA's
+    // shared memory) before the final cluster barrier.
+    tc_commit_pair(drain_bar);
+    mbar_wait(drain_bar, 0, &never_abort, p.status, 1000000000ull, kDevTimeoutDrain);
+  } else if (warp >= 2 && warp < 6) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const T* bias = reinterpret_cast<const T*>(p.bias);
+    T* out = reinterpret_cast<T*>(p.out);
+    const bool vec_ok = (p.ldo % 8 == 0) && (p.N % 8 == 0);
+    const uint32_t leader_tempty0 = mapa_shared(tempty_bar(0), 0);
+    int tcount = 0;
+    for (int u = cluster; u < total_units; u += nclusters, ++tcount) {
+      const int acc = tcount & 1;
+      const uint32_t aph = (tcount >> 1) & 1;
+      if (!mbar_wait_cluster(tfull_bar(acc), aph, abort_flag, p.status, p.timeout_ns, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      int pm, n_tile;
+      unit_coords(p, u, pm, n_tile);
+      const int mine = p.pairs[4 * pm + rank];
+      const int group = p.tile_group ? p.tile_group[p.pairs[4 * pm]] : 0;
+      const int64_t row = (int64_t)mine * BM + row_in_tile;
+      const bool live = mine >= 0;  // uniform over the CTA: tcgen05.ld below is warp-collective
+      const bool row_ok = live && (p.tile_group ? true : row < p.m_rows);
+      const float rscale = (row_ok && p.row_scale) ? p.row_scale[row] : 1.f;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (p.swiglu) {
+        const int n0 = n_tile * 128;
+        for (int c = 0; c < 128 && live; c += 16) {
+          uint32_t rg[16], ru[16];
+          tmem_ld_x16(t_row + c, rg);
+          tmem_ld_x16(t_row + 128 + c, ru);
+          tmem_wait_ld();
+          const int col = n0 + c;
+          const int nvalid = min(16, p.N - col);
+          float h[16];
+          if (p.b_scale && nvalid > 0) {
+            const float* bsg = p.b_scale + (int64_t)group * p.b_group_rows + col;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float sg = i < nvalid ? bsg[i] : 0.f, su = i < nvalid ? bsg[p.N + i] : 0.f;
+              h[i] = silu_f32(__uint_as_float(rg[i]) * sg) * (__uint_as_float(ru[i]) * su);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) h[i] = silu_f32(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+          }
+          if (row_ok && nvalid > 0) store16<T>(out + row * p.ldo + col, h, nvalid, vec_ok);
+        }
+      } else {
+        const int n0 = n_tile * BN;
+        for (int c = 0; c < BN && live; c += 16) {
+          uint32_t rv[16];
+          tmem_ld_x16(t_row + c, rv);
+          tmem_wait_ld();
+          const int col = n0 + c;
+          const int nvalid = min(16, p.N - col);
+          if (nvalid > 0) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rv[i]);
+            if (p.b_scale) {
+              const float* bs = p.b_scale + (int64_t)group * p.b_group_rows + col;
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (i < nvalid) v[i] *= bs[i];
+            }
+            if (bias) {
+              const int bg = p.bias_group_mod > 0 ? group % p.bias_group_mod : group;
+              const T* bp = bias + bg * p.bias_group_stride + col;
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (i < nvalid) v[i] += to_f32<T>(bp[i]);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] *= rscale;
+            if (row_ok) store16<T>(out + row * p.ldo + col, v, nvalid, vec_ok);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty0 + 8u * (uint32_t)acc);
+    }
+  } else if (FP8B && warp >= 6) {
+    // ------------------------------------------------------------ e4m3 -> 16-bit converters (both CTAs)
+    // Item (r, c): row r of this CTA's 128 B rows, 16-byte chunk c (16 weights) of its 64-byte
+    // e4m3 row; stored as 16-bit logical chunks 2c, 2c+1 of the 128-byte row at physical
+    // chunk (logical ^ (r & 7)), the 128B swizzle of the MMA descriptor.
+    const int ct = threadIdx.x - 192;
+    const uint32_t leader_full0 = mapa_shared(full_bar(0), 0);
+    constexpr int ITEMS = 128 * BK / 16 / CONVERTER_THREADS;  // 2
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = cluster; ok && u < total_units; u += nclusters) {
+      int pm, n_tile;
+      unit_coords(p, u, pm, n_tile);
+      const int group = p.tile_group ? p.tile_group[p.pairs[4 * pm]] : 0;
+      const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
+      const int64_t b_row = (int64_t)group * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
+      float sc[ITEMS];
+      int rr[ITEMS], cc[ITEMS];
+#pragma unroll
+      for (int q = 0; q < ITEMS; ++q) {
+        const int idx = ct + CONVERTER_THREADS * q;
+        rr[q] = idx >> 2;
+        cc[q] = idx & 3;
+        const int64_t grow = b_row + rr[q];
+        sc[q] = grow < p.b_rows_total ? p.b_row_scale[grow] : 0.f;
+      }
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(landed_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        const uint8_t* raw = st + MMA_STAGE_BYTES;
+        uint8_t* bt = st + A_BYTES;
+#pragma unroll
+        for (int q = 0; q < ITEMS; ++q) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + rr[q] * BK + cc[q] * 16);
+          uint4 lo, hi;
+          dequant16<T>(qv, sc[q], lo, hi);
+          uint8_t* row = bt + rr[q] * 128;
+          const int sw = rr[q] & 7;
+          *reinterpret_cast<uint4*>(row + (((2 * cc[q]) ^ sw) << 4)) = lo;
+          *reinterpret_cast<uint4*>(row + (((2 * cc[q] + 1) ^ sw) << 4)) = hi;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(leader_full0 + 8u * (uint32_t)s);
+      }
+      const int nruns = ok ? pair_lora_runs(p, pm) : 0;
+      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(landed_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(leader_full0 + 8u * (uint32_t)s);  // LoRA operands are 16-bit
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // no MMA, TMEM read or remote arrive of either CTA is still outstanding
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------ pair list
+// One CTA: pairs of consecutive 128-row tiles of the same group. Tile t opens a
+// pair when its distance from its group's first tile is even; its partner is
+// t + 1 when that tile exists and belongs to the same group, else -1. Each pair
+// also records its group's first pair and pair count (for the unit order).
+__global__ void __launch_bounds__(1024) pair_tiles_kernel(const int32_t* __restrict__ tile_group,
+                                                          const int32_t* __restrict__ group_offsets,
+                                                          const int32_t* __restrict__ num_tiles_dev, int tiles_cap,
+                                                          int64_t static_rows, int32_t* __restrict__ pairs,
+                                                          int32_t* __restrict__ num_pairs_out) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < ntiles; base += 1024) {
+    const int t = base + tid;
+    int start = 0, partner = -1, in_group = 0, group_pairs = 0;
+    if (t < ntiles) {
+      if (tile_group) {
+        const int g = tile_group[t];
+        const int t0 = group_offsets[g] >> 7;
+        in_group = (t - t0) >> 1;
+        group_pairs = (((group_offsets[g + 1] - group_offsets[g]) >> 7) + 1) >> 1;
+        start = ((t - t0) & 1) == 0;
+        if (start && t + 1 < ntiles && tile_group[t + 1] == g) partner = t + 1;
+      } else {
+        in_group = t >> 1;
+        group_pairs = (ntiles + 1) >> 1;
+        start = (t & 1) == 0;
+        if (start && t + 1 < ntiles) partner = t + 1;
+      }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, start);
+    if (lane == 0) warp_tot[w] = __popc(bal);
+    __syncthreads();
+    int before = carry;
+    for (int i = 0; i < w; ++i) before += warp_tot[i];
+    before += __popc(bal & ((1u << lane) - 1u));
+    if (start) {
+      pairs[4 * before] = t;
+      pairs[4 * before + 1] = partner;
+      pairs[4 * before + 2] = before - in_group;  // the group's first pair
+      pairs[4 * before + 3] = group_pairs;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int tot = 0;
+      for (int i = 0; i < 32; ++i) tot += warp_tot[i];
+      carry += tot;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) *num_pairs_out = carry;
+}
+
+// One warp per pair: distinct tenants of its 256 rows (first-seen order over the
+// 8 row quarters) and the 256-bit mask of the rows each one owns.
+__global__ void __launch_bounds__(64) pair_runs_kernel(const int32_t* __restrict__ row_tenant,
+                                                       const int32_t* __restrict__ pairs,
+                                                       const int32_t* __restrict__ num_pairs_dev, int pairs_cap,
+                                                       int64_t static_rows, int32_t* __restrict__ runs,
+                                                       int32_t* __restrict__ nruns) {
+  __shared__ int32_t s_ten[2][kMaxRunsPerPair];
+  __shared__ uint32_t s_mask[2][kMaxRunsPerPair][8];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pr = blockIdx.x * 2 + w;
+  const int np = min(*num_pairs_dev, pairs_cap);
+  if (pr >= np) return;
+  int count = 0;
+  for (int q = 0; q < 8; ++q) {
+    const int tile = pairs[4 * pr + (q >> 2)];
+    const int64_t row = (int64_t)tile * 128 + (q & 3) * 32 + lane;
+    const int t = (tile >= 0 && (static_rows < 0 || row < static_rows)) ? row_tenant[row] : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, t);
+    const bool lead = (t >= 0) && ((peers & ((1u << lane) - 1u)) == 0u);
+    int found = -1;
+    if (lead)
+      for (int j = 0; j < count; ++j)
+        if (s_ten[w][j] == t) {
+          found = j;
+          break;
+        }
+    const unsigned is_new = __ballot_sync(0xffffffffu, lead && found < 0);
+    if (lead) {
+      int idx = found;
+      if (found < 0) {
+        idx = count + __popc(is_new & ((1u << lane) - 1u));
+        s_ten[w][idx] = t;
+        for (int qq = 0; qq < 8; ++qq) s_mask[w][idx][qq] = 0u;
+      }
+      s_mask[w][idx][q] = peers;
+    }
+    count += __popc(is_new);
+    __syncwarp();
+  }
+  for (int j = lane; j < count; j += 32) {
+    int32_t* r = runs + ((int64_t)pr * kMaxRunsPerPair + j) * kPairRunInts;
+    r[0] = s_ten[w][j];
+#pragma unroll
+    for (int qq = 0; qq < 8; ++qq) r[1 + qq] = (int32_t)s_mask[w][j][qq];
+  }
+  if (lane == 0) nruns[pr] = count;
+}
+
+template <typename T, bool FP8B>
+int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
+                       const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const PParams& p) {
+  auto kern = grouped_gemm_pair_kernel<T, FP8B>;
+  SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<FP8B>::SMEM_BYTES));
+  // Persistent grid: as many CTA pairs as can be resident at once.
+  static std::mutex mu;
+  static int cached[64] = {0};
+  int dev = 0;
+  SB_CUDA_CHECK(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg<FP8B>::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg<FP8B>::SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int max_clusters = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 0 && dev < 64) max_clusters = cached[dev];
+    if (max_clusters == 0) {
+      cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+      if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters <= 0) {
+        cudaGetLastError();
+        max_clusters = sm_count() / 2;
+      }
+      if (dev >= 0 && dev < 64) cached[dev] = max_clusters;
+    }
+  }
+  const int64_t clusters = std::min<int64_t>(units_upper, max_clusters);
+  cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+  SB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tm_a, tm_b, tm_s, tm_lb, p));
+  ::sb::count_launch();
+  return STAGEML_OK;
+}
+
+}  // namespace
+
+size_t pair_runs_ints(int64_t pairs_cap) { return (size_t)pairs_cap * kMaxRunsPerPair * kPairRunInts; }
+
+int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
+                     int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
+                     int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream) {
+  SB_CHECK_ARG(pairs && num_pairs, "pair plan: null output");
+  SB_CHECK_ARG(!tile_group || (group_offsets && num_tiles_dev), "pair plan: grouped tiles need offsets and a count");
+  const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
+  (pair_tiles_kernel<<<1, 1024, 0, stream>>>(tile_group, group_offsets, num_tiles_dev, tiles_cap, static_rows, pairs,
+                                              num_pairs),
+   ::sb::count_launch());
+  SB_CUDA_CHECK(cudaGetLastError());
+  if (row_tenant && tiles > 0) {
+    SB_CHECK_ARG(runs && nruns, "pair plan: LoRA runs need output buffers");
+    const int64_t pairs_cap = tiles;
+    (pair_runs_kernel<<<(unsigned)((pairs_cap + 1) / 2), 64, 0, stream>>>(
+         row_tenant, pairs, num_pairs, (int)pairs_cap, num_tiles_dev ? -1 : static_rows, runs, nruns),
+     ::sb::count_launch());
+    SB_CUDA_CHECK(cudaGetLastError());
+  }
+  return STAGEML_OK;
+}
+
+int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
+  SB_CHECK_ARG(g.pairs && g.num_pairs_dev && g.pairs_cap >= 0, "pair gemm: missing pair list");
+  SB_CHECK_ARG(g.rank == 0 || (g.pair_runs && g.pair_nruns), "pair gemm: LoRA needs the pair runs");
+
+  const CUtensorMapDataType dt = g.in_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tm_a, tm_b, tm_s, tm_lb;
+  SB_TRY(make_tmap_2d(&tm_a, g.a, dt, 2, (uint64_t)g.a_rows, (uint64_t)g.K, (uint64_t)g.K * 2, BM, BK, 128));
+  if (g.b_fp8)
+    SB_TRY(make_tmap_2d(&tm_b, g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.b_rows_total, (uint64_t)g.K,
+                        (uint64_t)g.K, 128, BK, 0));
+  else
+    SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
+  const int lora_cols = g.swiglu ? 2 * g.rank : g.rank;
+  if (g.rank) {
+    SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
+                        16, 32));
+    SB_TRY(make_tmap_2d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.lora_b_rows_total, (uint64_t)g.rank,
+                        (uint64_t)g.rank * 2, 64, 16, 32));
+  } else {
+    tm_s = tm_a;  // unused
+    tm_lb = tm_a;
+  }
+
+  PParams p;
+  p.K = g.K;
+  p.N = g.N;
+  p.b_group_rows = g.b_group_rows;
+  p.b_rows_total = g.b_rows_total;
+  p.swiglu = g.swiglu ? 1 : 0;
+  p.num_n_tiles = g.swiglu ? (g.N + 127) / 128 : (g.N + BN - 1) / BN;
+  p.tile_group = g.tile_group;
+  p.m_rows = g.m_rows;
+  p.pairs = g.pairs;
+  p.num_pairs_dev = g.num_pairs_dev;
+  p.pairs_cap = g.pairs_cap;
+  p.rank = g.rank;
+  p.lchunks = g.rank / 16;
+  p.s_bytes = (g.swiglu ? 2 : 1) * p.lchunks * LCHUNK;
+  p.run_bytes = p.lchunks * LCHUNK;  // this CTA's half: 2 x 64 rows (SwiGLU) or 128 rows per chunk
+  p.runs_per_block = g.rank ? (MMA_STAGE_BYTES - p.s_bytes) / p.run_bytes : 1;
+  p.lb_tenant_rows = g.rank ? g.lora_b_tenant_stride / g.rank : 0;
+  p.lb_group_rows = g.rank ? g.lora_b_group_stride / g.rank : 0;
+  p.runs = g.pair_runs;
+  p.nruns = g.pair_nruns;
+  p.row_scale = g.row_scale;
+  p.bias = g.bias;
+  p.bias_group_stride = g.bias_group_stride;
+  p.bias_group_mod = g.bias_group_mod;
+  p.b_scale = g.b_fp8 ? nullptr : g.b_scale;
+  p.b_row_scale = g.b_fp8 ? g.b_scale : nullptr;
+  p.out = g.out;
+  p.ldo = g.ldo;
+  p.status = g.status;
+  p.timeout_ns = kDefaultWaitNs;
+
+  const int64_t units_upper = (int64_t)g.pairs_cap * p.num_n_tiles;
+  if (units_upper == 0) return STAGEML_OK;
+  if (g.b_fp8)
+    return g.in_bf16 ? launch_pair_kernel<bf16, true>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p)
+                     : launch_pair_kernel<f16, true>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p);
+  return g.in_bf16 ? launch_pair_kernel<bf16, false>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p)
+                   : launch_pair_kernel<f16, false>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p);
+}
+
+}  // namespace sb
