@@ -7,12 +7,15 @@
 // DynamicLoRALinear.forward (stageml/adapter_bank.py:67).
 //
 // The shrink is a GEMM with a tiny N (R <= 64) whose B operand changes with the
-// row's tenant, so it runs on warp-level tensor-core MMAs (m16n8k16, fp32
-// accumulate): one warp owns 16 rows and one 512-wide K slice; rows of the same
-// tenant (contiguous after the (expert, tenant) sort) share one pass over A.
-// K slices write fp32 partials that a second kernel sums in a fixed order and
-// scales, so the result is deterministic. The same CTA copies its rows' K slice
-// from x into the permuted activation buffer with 16-byte accesses.
+// row's tenant; it is bound by reading x and the touched A slices, so the
+// kernel is built for bytes in flight: one warp owns 16 rows and one 512-wide
+// K slice, rows of the same tenant (contiguous after the (expert, tenant) sort)
+// share one pass over A, and the warp's (pass, 64-wide chunk) items stream
+// through a 4-stage cp.async ring in shared memory feeding ldmatrix and
+// warp-level tensor-core MMAs (m16n8k16, fp32 accumulate). K slices write fp32
+// partials that a second kernel sums in a fixed order and scales, so the result
+// is deterministic. The first pass also writes the staged x rows to the
+// permuted activation buffer.
 #include "common.cuh"
 #include "host_util.h"
 #include "kernels.h"
@@ -65,121 +68,183 @@ __device__ __forceinline__ void mma_16816<f16>(float (&c)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint4 ld16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  // src-size 0 fills the 16 bytes with zeros (rows without a source, K past the end)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 
-// One 32-wide K chunk of the shrink for a warp's 16 rows: each lane holds 8
-// consecutive K elements (16 bytes) of rows g and g+8 and of B-row g of every
-// 8-column block. The two m16n8k16 MMAs consume those registers as if lane
-// (g, tig) held logical k = {2tig, 2tig+1, 2tig+8, 2tig+9}; the same
-// logical->physical K permutation is applied to both operands, so the sum over
-// K is unchanged while every global load is a full 16-byte vector.
-struct ShrinkChunk {
-  uint4 xl, xh;
-  uint4 b[8];
+// Shared-memory ring of one warp: each stage holds a 64-wide K chunk of the warp's
+// 16 rows of x and of the R rows of one tenant's A, rows padded to 144 bytes so
+// that the eight 16-byte row segments an ldmatrix reads fall in distinct banks.
+constexpr int kShrinkKC = 64;
+constexpr int kShrinkPitch = kShrinkKC * 2 + 16;
+constexpr int kShrinkStages = 4;
+constexpr int kShrinkMaxPasses = 16;
+
+template <int NBS>
+struct ShrinkRing {
+  static constexpr int R = NBS * 8;
+  static constexpr int X_BYTES = 16 * kShrinkPitch;
+  static constexpr int STAGE = X_BYTES + R * kShrinkPitch;
+  static constexpr int WARP_BYTES = kShrinkStages * STAGE;
+  static constexpr int SMEM = 4 * WARP_BYTES + 4 * kShrinkMaxPasses * 8;
 };
 
-template <typename T>
-__device__ __forceinline__ void shrink_load(ShrinkChunk& c, const T* x_lo, const T* x_hi, const T* A, int K, int nbs,
-                                            int g, int kk) {
-  const bool v = kk < K;
-  const uint4 z = make_uint4(0, 0, 0, 0);
-  c.xl = (v && x_lo) ? ld16(x_lo + kk) : z;
-  c.xh = (v && x_hi) ? ld16(x_hi + kk) : z;
-#pragma unroll
-  for (int nb = 0; nb < 8; ++nb)
-    if (nb < nbs) c.b[nb] = v ? ld16(A + (int64_t)(nb * 8 + g) * K + kk) : z;
-}
-
-template <typename T>
-__device__ __forceinline__ void shrink_mma(float (&acc)[8][4], const ShrinkChunk& c, int nbs) {
-#pragma unroll
-  for (int nb = 0; nb < 8; ++nb) {
-    if (nb < nbs) {
-      mma_16816<T>(acc[nb], c.xl.x, c.xh.x, c.xl.y, c.xh.y, c.b[nb].x, c.b[nb].y);
-      mma_16816<T>(acc[nb], c.xl.z, c.xh.z, c.xl.w, c.xh.w, c.b[nb].z, c.b[nb].w);
-    }
-  }
-}
-
-template <typename T>
+// One warp: 16 consecutive rows, one 512-wide K slice. The distinct tenants of
+// the rows are the warp's passes (rows of one tenant are contiguous after the
+// (expert, tenant) sort, so there are few); the (pass, 64-wide chunk) items
+// stream through a 4-stage cp.async ring so that about three chunks of x and A
+// are in flight per warp. The first pass also copies the staged x rows to the
+// permuted activation buffer.
+template <typename T, int NBS>
 __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p) {
-  const int64_t rows_active = active_rows(p.num_tiles_dev, p.static_rows, p.rows_cap);
+  using Ring = ShrinkRing<NBS>;
+  constexpr int R = Ring::R;
+  extern __shared__ __align__(16) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows_active = active_rows(p.num_tiles_dev, p.static_rows, p.rows_cap);
   const int64_t row0 = (int64_t)blockIdx.y * 64 + warp * 16;
   if (row0 >= rows_active) return;
   const int K = p.K;
   const int k_begin = blockIdx.x * kShrinkKSlice;
   const int k_end = min(K, k_begin + kShrinkKSlice);
+  const int nkc = (k_end - k_begin + kShrinkKC - 1) / kShrinkKC;
   const T* src = static_cast<const T*>(p.src);
+  uint8_t* ring = smem + warp * Ring::WARP_BYTES;
+  int32_t* s_key = reinterpret_cast<int32_t*>(smem + 4 * Ring::WARP_BYTES) + warp * 2 * kShrinkMaxPasses;
+  uint32_t* s_sel = reinterpret_cast<uint32_t*>(s_key + kShrinkMaxPasses);
 
-  if (p.gather_dst) {
-    T* dstb = static_cast<T*>(p.gather_dst);
-#pragma unroll 4
-    for (int r = 0; r < 16; ++r) {
-      const int64_t row = row0 + r;
-      if (row >= rows_active) break;
-      const int64_t srow = p.src_row_of ? (int64_t)p.src_row_of[row] : row;
-      T* dst = dstb + row * K;
-      const T* s = srow >= 0 ? src + srow * K : nullptr;
-      for (int c = k_begin + lane * 8; c < k_end; c += 256) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (s) v = ld16(s + c);
-        *reinterpret_cast<uint4*>(dst + c) = v;
+  // passes: distinct tenants of the 16 rows, first-seen order
+  int np = 0;
+  if (R > 0) {
+    const int my_tenant = (lane < 16 && row0 + lane < rows_active) ? p.row_tenant[row0 + lane] : -1;
+    unsigned pending = __ballot_sync(0xffffffffu, lane < 16 && my_tenant >= 0) & 0xFFFFu;
+    while (pending) {
+      const int leader = __ffs(pending) - 1;
+      const int key = __shfl_sync(0xffffffffu, my_tenant, leader);
+      const unsigned sel = __ballot_sync(0xffffffffu, lane < 16 && my_tenant == key) & pending;
+      pending &= ~sel;
+      if (lane == 0) {
+        s_key[np] = key;
+        s_sel[np] = sel;
       }
+      ++np;
     }
+    __syncwarp();
   }
-  if (p.R == 0) return;
-
-  int my_tenant = -1;
-  if (lane < 16 && row0 + lane < rows_active) my_tenant = p.row_tenant[row0 + lane];
-  unsigned pending = __ballot_sync(0xffffffffu, lane < 16 && my_tenant >= 0) & 0xFFFFu;
-  if (!pending) return;
+  const bool gather = p.gather_dst != nullptr;
+  const int npass = np > 0 ? np : (gather ? 1 : 0);
+  if (npass == 0) return;
+  const int total = npass * nkc;
   const int group = p.tile_group ? p.tile_group[row0 / 128] : 0;
-  const int g = lane >> 2, tig = lane & 3;
-  const int64_t r_lo = row0 + g, r_hi = row0 + g + 8;
-  const T* x_lo = nullptr;
-  const T* x_hi = nullptr;
-  if (r_lo < rows_active) {
-    const int64_t s = p.src_row_of ? (int64_t)p.src_row_of[r_lo] : r_lo;
-    if (s >= 0) x_lo = src + s * K;
-  }
-  if (r_hi < rows_active) {
-    const int64_t s = p.src_row_of ? (int64_t)p.src_row_of[r_hi] : r_hi;
-    if (s >= 0) x_hi = src + s * K;
-  }
-  const int nbs = p.R / 8;
   const T* lora_a = static_cast<const T*>(p.lora_a);
 
-  while (pending) {
-    const int leader = __ffs(pending) - 1;
-    const int key = __shfl_sync(0xffffffffu, my_tenant, leader);
-    const unsigned sel = __ballot_sync(0xffffffffu, lane < 16 && my_tenant == key) & pending;
-    pending &= ~sel;
-    const T* A = lora_a + key * p.a_tenant_stride + group * p.a_group_stride;
-    float acc[8][4];
+  // x pieces of this lane: rows (lane >> 3) + 4q, 16-byte column lane & 7 of the chunk
+  const int xc = lane & 7;
+  const T* xrow[4];
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb)
+  for (int q = 0; q < 4; ++q) {
+    const int64_t row = row0 + (lane >> 3) + 4 * q;
+    int64_t sr = -1;
+    if (row < rows_active) sr = p.src_row_of ? (int64_t)p.src_row_of[row] : row;
+    xrow[q] = sr >= 0 ? src + sr * K : nullptr;
+  }
+
+  auto issue = [&](int i) {
+    if (i < total) {
+      const int pass = i / nkc, kc = i - pass * nkc;
+      const uint32_t st = smem_u32(ring + (i % kShrinkStages) * Ring::STAGE);
+      const int kk = k_begin + kc * kShrinkKC + xc * 8;
+      const bool kv = kk < k_end;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[nb][q] = 0.f;
-    ShrinkChunk cur, nxt;
-    shrink_load<T>(cur, x_lo, x_hi, A, K, nbs, g, k_begin + tig * 8);
-    for (int k0 = k_begin; k0 < k_end; k0 += 32) {
-      const bool more = k0 + 32 < k_end;
-      if (more) shrink_load<T>(nxt, x_lo, x_hi, A, K, nbs, g, k0 + 32 + tig * 8);
-      shrink_mma<T>(acc, cur, nbs);
-      if (more) cur = nxt;
-    }
-    float* sp = p.spart + (int64_t)blockIdx.x * p.rows_cap * p.R;
-    const bool lo_sel = (sel >> g) & 1u, hi_sel = (sel >> (g + 8)) & 1u;
+      for (int q = 0; q < 4; ++q) {
+        const int r = (lane >> 3) + 4 * q;
+        const bool v = kv && xrow[q] != nullptr;
+        cp_async16(st + r * kShrinkPitch + xc * 16, v ? (const void*)(xrow[q] + kk) : p.src, v);
+      }
+      if (R > 0 && pass < np) {
+        const T* A = lora_a + s_key[pass] * p.a_tenant_stride + group * p.a_group_stride;
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      if (nb < nbs) {
-        const int col = nb * 8 + tig * 2;
-        if (lo_sel) *reinterpret_cast<float2*>(sp + r_lo * p.R + col) = make_float2(acc[nb][0], acc[nb][1]);
-        if (hi_sel) *reinterpret_cast<float2*>(sp + r_hi * p.R + col) = make_float2(acc[nb][2], acc[nb][3]);
+        for (int q = 0; q < R / 4; ++q) {
+          const int ar = (lane >> 3) + 4 * q;
+          cp_async16(st + Ring::X_BYTES + ar * kShrinkPitch + xc * 16, kv ? (const void*)(A + (int64_t)ar * K + kk) : p.src,
+                     kv);
+        }
       }
     }
+    cp_async_commit();  // possibly empty: keeps the group count in step
+  };
+
+  float acc[NBS > 0 ? NBS : 1][4];
+  const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int i = 0; i < kShrinkStages - 1; ++i) issue(i);
+  for (int i = 0; i < total; ++i) {
+    issue(i + kShrinkStages - 1);
+    cp_async_wait<kShrinkStages - 1>();
+    __syncwarp();
+    const int pass = i / nkc, kc = i - pass * nkc;
+    const uint8_t* st = ring + (i % kShrinkStages) * Ring::STAGE;
+    if (pass == 0 && gather) {
+      T* dstb = static_cast<T*>(p.gather_dst);
+      const int kk = k_begin + kc * kShrinkKC + xc * 8;
+      if (kk < k_end) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int r = (lane >> 3) + 4 * q;
+          if (row0 + r < rows_active)
+            *reinterpret_cast<uint4*>(dstb + (row0 + r) * K + kk) =
+                *reinterpret_cast<const uint4*>(st + r * kShrinkPitch + xc * 16);
+        }
+      }
+    }
+    if (NBS > 0 && pass < np) {
+      if (kc == 0) {
+#pragma unroll
+        for (int nb = 0; nb < (NBS > 0 ? NBS : 1); ++nb)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[nb][j] = 0.f;
+      }
+      const uint32_t xs = smem_u32(st), as = smem_u32(st + Ring::X_BYTES);
+      const int mi = lane >> 3, mr = lane & 7;
+#pragma unroll
+      for (int k16 = 0; k16 < kShrinkKC / 16; ++k16) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(xs + ((mi & 1) * 8 + mr) * kShrinkPitch + (k16 * 16 + (mi >> 1) * 8) * 2, a0, a1, a2, a3);
+#pragma unroll
+        for (int nb = 0; nb < NBS; nb += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(as + ((nb + (mi >> 1)) * 8 + mr) * kShrinkPitch + (k16 * 16 + (mi & 1) * 8) * 2, b0, b1, b2, b3);
+          mma_16816<T>(acc[nb], a0, a1, a2, a3, b0, b1);
+          mma_16816<T>(acc[nb + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+      if (kc == nkc - 1) {
+        const unsigned sel = s_sel[pass];
+        float* sp = p.spart + (int64_t)blockIdx.x * p.rows_cap * R;
+        const int64_t r_lo = row0 + g, r_hi = row0 + g + 8;
+        const bool lo_sel = (sel >> g) & 1u, hi_sel = (sel >> (g + 8)) & 1u;
+#pragma unroll
+        for (int nb = 0; nb < NBS; ++nb) {
+          const int col = nb * 8 + tig * 2;
+          if (lo_sel) *reinterpret_cast<float2*>(sp + r_lo * R + col) = make_float2(acc[nb][0], acc[nb][1]);
+          if (hi_sel) *reinterpret_cast<float2*>(sp + r_hi * R + col) = make_float2(acc[nb][2], acc[nb][3]);
+        }
+      }
+    }
+    __syncwarp();  // the stage is refilled by a later issue
   }
+  cp_async_wait<0>();
 }
 
 template <typename T>
@@ -200,12 +265,25 @@ __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, in
   s_out[idx] = from_f32<T>(v);
 }
 
+template <int NBS>
+int launch_shrink_variant(bool bf, dim3 grid, const ShrinkParams& p, cudaStream_t stream) {
+  constexpr int smem = ShrinkRing<NBS>::SMEM;
+  if (bf) {
+    SB_CUDA_CHECK(cudaFuncSetAttribute(gather_shrink_kernel<bf16, NBS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    (gather_shrink_kernel<bf16, NBS><<<grid, 128, smem, stream>>>(p), ::sb::count_launch());
+  } else {
+    SB_CUDA_CHECK(cudaFuncSetAttribute(gather_shrink_kernel<f16, NBS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    (gather_shrink_kernel<f16, NBS><<<grid, 128, smem, stream>>>(p), ::sb::count_launch());
+  }
+  return STAGEML_OK;
+}
+
 }  // namespace
 
 int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   SB_CHECK_ARG(s.src, "shrink: null source");
   SB_CHECK_ARG(s.K > 0 && s.K % 8 == 0, "shrink: K=%d must be a positive multiple of 8", s.K);
-  SB_CHECK_ARG(s.R % 8 == 0 && s.R <= 64, "shrink: R=%d must be a multiple of 8 <= 64", s.R);
+  SB_CHECK_ARG(s.R == 0 || s.R == 16 || s.R == 32 || s.R == 64, "shrink: R=%d must be 0, 16, 32 or 64", s.R);
   SB_CHECK_ARG(s.R == 0 || (s.lora_a && s.spart && s.s_out && s.row_tenant), "shrink: missing LoRA buffers");
   SB_CHECK_ARG(reinterpret_cast<uintptr_t>(s.src) % 16 == 0, "shrink: source must be 16-byte aligned");
   if (!s.gather_dst && s.R == 0) return STAGEML_OK;
@@ -229,10 +307,22 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   p.spart = s.spart;
   dim3 grid(KS, (unsigned)((rows_max + 63) / 64));
   SB_CHECK_ARG(grid.y <= 65535u, "shrink: too many rows for one launch");
-  if (s.dtype_bf16)
-    (gather_shrink_kernel<bf16><<<grid, 128, 0, stream>>>(p), ::sb::count_launch());
-  else
-    (gather_shrink_kernel<f16><<<grid, 128, 0, stream>>>(p), ::sb::count_launch());
+  switch (s.R / 8) {
+    case 0:
+      SB_TRY(launch_shrink_variant<0>(s.dtype_bf16, grid, p, stream));
+      break;
+    case 2:
+      SB_TRY(launch_shrink_variant<2>(s.dtype_bf16, grid, p, stream));
+      break;
+    case 4:
+      SB_TRY(launch_shrink_variant<4>(s.dtype_bf16, grid, p, stream));
+      break;
+    case 8:
+      SB_TRY(launch_shrink_variant<8>(s.dtype_bf16, grid, p, stream));
+      break;
+    default:
+      return set_error(STAGEML_ERR_INVALID_ARG, "shrink: R=%d must be 0, 16, 32 or 64", s.R);
+  }
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {
     const int64_t n = rows_max * s.R;
