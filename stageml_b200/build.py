@@ -29,6 +29,7 @@ CU_SOURCES = [
     "shrink.cu",
     "grouped_gemm.cu",
     "grouped_gemm_pair.cu",
+    "skinny.cu",
     "combine.cu",
     "fold.cu",
     "gemv.cu",

@@ -97,6 +97,8 @@ struct MoeBuffers {
 
 // The grouped GEMMs run on CTA pairs (tcgen05 cta_group::2) unless the
 // environment sets STAGEML_GEMM_PAIRS=0 (one CTA per tile), read once per process.
+constexpr int64_t kSkinnyMaxPairs = 16;
+
 bool gemm_pairs_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("STAGEML_GEMM_PAIRS");
@@ -231,11 +233,14 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
                         b.plan, status, scr, st));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
-  if (b.pairs)
+  // Decode-sized batches (at most 16 routed rows in all) stream the weights with the
+  // skinny GEMM; larger ones use the tensor-memory GEMM and its tile / pair plan.
+  const bool skinny = P <= kSkinnyMaxPairs && a->weight_dtype != STAGEML_E4M3;
+  if (!skinny && b.pairs)
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_pair_plan(b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles, tiles_cap, 0,
                               b.pruns ? b.plan.row_tenant : nullptr, b.pairs, b.num_pairs, b.pruns, b.pnruns, st));
-  else if (b.runs)
+  else if (!skinny && b.runs)
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   // gather + R4 shrink of w1|w3
@@ -293,7 +298,9 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, launch_grouped_gemm(g, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP,
+             skinny ? launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st)
+                    : launch_grouped_gemm(g, st));
   }
   // R4 shrink of h for w2
   if (lora2) {
@@ -347,7 +354,9 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, launch_grouped_gemm(g, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN,
+             skinny ? launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st)
+                    : launch_grouped_gemm(g, st));
   }
   // combine
   SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st));

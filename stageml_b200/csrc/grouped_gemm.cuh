@@ -99,4 +99,10 @@ int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, co
                      int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream);
 size_t pair_runs_ints(int64_t pairs_cap);
 
+// Weight-streaming variant for at most 16 valid rows per 128-row tile (decode-sized
+// batches), skinny.cu: same GemmLaunch semantics (16-bit weights; LoRA from s16 /
+// lora_b with the row's tenant), valid rows per tile from the group counts.
+int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int32_t* group_offsets,
+                       const int32_t* group_counts, cudaStream_t stream);
+
 }  // namespace sb

@@ -78,18 +78,24 @@ __device__ __forceinline__ uint32_t pair_key(const PairSrc& a, int64_t p, int32_
   return (uint32_t)(e * a.tkeys + (tn + 1));
 }
 
-__device__ __forceinline__ void bitonic_sort_2048(uint32_t* s) {
-  // 1024 threads, one compare-exchange pair each per stage.
+// Sorts s[0..2048) ascending when s[n..2048) already hold the largest value
+// (the sentinel): only the first next_pow2(n) entries go through the network.
+__device__ __forceinline__ void bitonic_sort_2048(uint32_t* s, int n) {
+  // 1024 threads, at most one compare-exchange pair each per stage.
   const int tid = threadIdx.x;
-  for (int k = 2; k <= kPermChunk; k <<= 1) {
+  int n2 = 1;
+  while (n2 < n) n2 <<= 1;
+  for (int k = 2; k <= n2; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      const int i = 2 * tid - (tid & (j - 1));
-      const int ixj = i + j;
-      const bool up = (i & k) == 0;
-      const uint32_t a = s[i], b = s[ixj];
-      if ((a > b) == up) {
-        s[i] = b;
-        s[ixj] = a;
+      if (tid < (n2 >> 1)) {
+        const int i = 2 * tid - (tid & (j - 1));
+        const int ixj = i + j;
+        const bool up = (i & k) == 0;
+        const uint32_t a = s[i], b = s[ixj];
+        if ((a > b) == up) {
+          s[i] = b;
+          s[ixj] = a;
+        }
       }
       __syncthreads();
     }
@@ -118,7 +124,7 @@ __global__ void __launch_bounds__(1024) perm_count_kernel(PairSrc a, int nkeys, 
     s[i] = (p < a.P) ? ((pair_key(a, p, status) << 11) | (uint32_t)i) : 0xFFFFFFFFu;
   }
   __syncthreads();
-  bitonic_sort_2048(s);
+  bitonic_sort_2048(s, a.P - base < kPermChunk ? (int)(a.P - base) : kPermChunk);
   for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
     const uint32_t v = s[i];
     sorted_out[base + i] = v;

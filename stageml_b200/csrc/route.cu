@@ -3,9 +3,10 @@
 // (benchmarks/real_moe_lora_residual_bench.py:360-386) and
 // normalize_routing_weights (stageml/moe_lora_layers.py:178-183) on the GPU.
 //
-// Logits: one CTA per 32 tokens; x and G are staged through shared memory in
-// 64-wide K chunks so each G element is read once per 32 tokens; each thread
-// accumulates a (token, expert) register block with fp32 FMAs.
+// Logits: for E <= 32 with the gate fitting shared memory, each CTA keeps G
+// resident and warps take whole tokens (a few tokens: one warp per (token,
+// expert) reading G from L2, with the same per-lane sum order); otherwise a
+// register-blocked tiled kernel over (64 tokens x 64 experts) tiles.
 // Top-k: one warp per token, lane j owns experts j, j+32, ...; k rounds of a
 // warp arg-max (larger logit first, ties -> lower expert index).
 #include "common.cuh"
@@ -15,60 +16,82 @@
 namespace sb {
 namespace {
 
-constexpr int RT_TOK = 32;     // tokens per CTA
-constexpr int RT_KC = 64;      // K chunk
+constexpr int RT_TT = 64;      // tokens per CTA
+constexpr int RT_TE = 64;      // experts per CTA
+constexpr int RT_KC = 32;      // K chunk
+constexpr int RT_PAD = RT_TT + 4;
 constexpr int RT_THREADS = 256;
 
+// General case (any E <= 256, gate too large for shared memory): a 64-token x
+// 64-expert output tile per CTA; x and G are staged K-major through shared memory
+// in 32-wide chunks and each thread accumulates a 4 x 4 (token, expert) register
+// block, 16 FMAs per two 16-byte shared-memory reads.
 template <typename T>
 __global__ void __launch_bounds__(RT_THREADS) router_logits_kernel(const T* __restrict__ x,
                                                                    const float* __restrict__ gw, int T_, int H,
                                                                    int E, float* __restrict__ logits) {
-  extern __shared__ float rsm[];
-  float* xs = rsm;                      // [RT_TOK][RT_KC + 1]
-  float* gs = rsm + RT_TOK * (RT_KC + 1);  // [E][RT_KC + 1]
-  const int t0 = blockIdx.x * RT_TOK;
-  const int ntok = min(RT_TOK, T_ - t0);
-  // Thread block of outputs: token index tt = threadIdx.x % 32, experts e = threadIdx.x/32 + 8*i.
-  const int tt = threadIdx.x & 31;
-  const int e0 = threadIdx.x >> 5;      // 0..7
-  constexpr int MAXE = 256;
-  float acc[MAXE / 8];
+  __shared__ __align__(16) float xs[RT_KC][RT_PAD];
+  __shared__ __align__(16) float gs[RT_KC][RT_PAD];
+  const int t0 = blockIdx.x * RT_TT, e0 = blockIdx.y * RT_TE;
+  const int tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  const int lr = tid >> 2, lk = (tid & 3) * 8;  // loader: row lr, 8 K values from lk
+  float acc[4][4];
 #pragma unroll
-  for (int i = 0; i < MAXE / 8; ++i) acc[i] = 0.f;
-
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  const bool xrow_ok = t0 + lr < T_, grow_ok = e0 + lr < E;
+  const T* xr = x + (int64_t)(t0 + lr) * H;
+  const float* gr = gw + (int64_t)(e0 + lr) * H;
   for (int k0 = 0; k0 < H; k0 += RT_KC) {
-    const int kc = min(RT_KC, H - k0);
-    for (int i = threadIdx.x; i < RT_TOK * RT_KC; i += RT_THREADS) {
-      const int r = i / RT_KC, c = i % RT_KC;
-      xs[r * (RT_KC + 1) + c] = (r < ntok && c < kc) ? to_f32<T>(x[(int64_t)(t0 + r) * H + k0 + c]) : 0.f;
-    }
-    for (int i = threadIdx.x; i < E * RT_KC; i += RT_THREADS) {
-      const int r = i / RT_KC, c = i % RT_KC;
-      gs[r * (RT_KC + 1) + c] = (c < kc) ? gw[(int64_t)r * H + k0 + c] : 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int k = k0 + lk + q;
+      xs[lk + q][lr] = (xrow_ok && k < H) ? to_f32<T>(xr[k]) : 0.f;
+      gs[lk + q][lr] = (grow_ok && k < H) ? gr[k] : 0.f;
     }
     __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < RT_KC; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&gs[k][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int i = 0; i < MAXE / 8; ++i) {
-      const int e = e0 + 8 * i;
-      if (e < E) {
-        float a = acc[i];
-        const float* xr = xs + tt * (RT_KC + 1);
-        const float* gr = gs + e * (RT_KC + 1);
-#pragma unroll 16
-        for (int c = 0; c < RT_KC; ++c) a = fmaf(xr[c], gr[c], a);
-        acc[i] = a;
-      }
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
   }
-  if (tt < ntok) {
 #pragma unroll
-    for (int i = 0; i < MAXE / 8; ++i) {
-      const int e = e0 + 8 * i;
-      if (e < E) logits[(int64_t)(t0 + tt) * E + e] = acc[i];
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty * 4 + i;
+    if (t >= T_) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + tx * 4 + j;
+      if (e < E) logits[(int64_t)t * E + e] = acc[i][j];
     }
   }
 }
+
+// Four consecutive values of an x row as fp32 (zeros past the end).
+template <typename T>
+__device__ __forceinline__ void load_x4(const T* xr, int h, int H, float (&xv)[4]) {
+  if (h >= H) {
+    xv[0] = xv[1] = xv[2] = xv[3] = 0.f;
+  } else if (sizeof(T) == 2) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(xr + h));
+    const T* hv = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) xv[q] = to_f32<T>(hv[q]);
+  } else {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(xr + h));
+    xv[0] = f.x, xv[1] = f.y, xv[2] = f.z, xv[3] = f.w;
+  }
+}
+constexpr int RT_XU = 8;
 
 // Gate resident in shared memory (E*H fp32 <= 200 KB): each CTA copies G once,
 // then every warp takes whole tokens; lane l accumulates E partial dot products
@@ -90,25 +113,25 @@ __global__ void __launch_bounds__(256) router_logits_smem_kernel(const T* __rest
     float acc[E_MAX];
 #pragma unroll
     for (int e = 0; e < E_MAX; ++e) acc[e] = 0.f;
-    for (int h = lane * 4; h < H; h += 128) {
-      float xv[4];
-      if (sizeof(T) == 2) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(xr + h));
-        const T* hv = reinterpret_cast<const T*>(&u);
+    // 8 steps of x loaded ahead of their FMAs (the per-lane order of the sums is unchanged)
+    for (int h0 = lane * 4; h0 < H; h0 += 128 * RT_XU) {
+      float xv[RT_XU][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) xv[q] = to_f32<T>(hv[q]);
-      } else {
-        const float4 f = __ldg(reinterpret_cast<const float4*>(xr + h));
-        xv[0] = f.x, xv[1] = f.y, xv[2] = f.z, xv[3] = f.w;
-      }
+      for (int u = 0; u < RT_XU; ++u) load_x4<T>(xr, h0 + 128 * u, H, xv[u]);
 #pragma unroll
-      for (int e = 0; e < E_MAX; ++e) {
-        if (e < E) {
-          const float4 gv = *reinterpret_cast<const float4*>(gsm + e * H + h);
-          acc[e] = fmaf(xv[0], gv.x, acc[e]);
-          acc[e] = fmaf(xv[1], gv.y, acc[e]);
-          acc[e] = fmaf(xv[2], gv.z, acc[e]);
-          acc[e] = fmaf(xv[3], gv.w, acc[e]);
+      for (int u = 0; u < RT_XU; ++u) {
+        const int h = h0 + 128 * u;
+        if (h < H) {
+#pragma unroll
+          for (int e = 0; e < E_MAX; ++e) {
+            if (e < E) {
+              const float4 gv = *reinterpret_cast<const float4*>(gsm + e * H + h);
+              acc[e] = fmaf(xv[u][0], gv.x, acc[e]);
+              acc[e] = fmaf(xv[u][1], gv.y, acc[e]);
+              acc[e] = fmaf(xv[u][2], gv.z, acc[e]);
+              acc[e] = fmaf(xv[u][3], gv.w, acc[e]);
+            }
+          }
         }
       }
     }
@@ -122,6 +145,43 @@ __global__ void __launch_bounds__(256) router_logits_smem_kernel(const T* __rest
       }
     }
   }
+}
+
+// Few tokens: one warp per (token, expert), G read from global / L2 and x with
+// RT_XU steps in flight; the per-lane sum order and the shuffle reduction are
+// those of router_logits_smem_kernel, so both give the same logits.
+template <typename T>
+__global__ void __launch_bounds__(128) router_logits_warp_kernel(const T* __restrict__ x, const float* __restrict__ gw,
+                                                                 int T_, int H, int E, float* __restrict__ logits) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t pairs = (int64_t)T_ * E;
+  const int64_t q = (int64_t)blockIdx.x * 4 + warp;
+  if (q >= pairs) return;
+  const int t = (int)(q / E), e = (int)(q - (int64_t)t * E);
+  const T* xr = x + (int64_t)t * H;
+  const float* gr = gw + (int64_t)e * H;
+  float acc = 0.f;
+  for (int h0 = lane * 4; h0 < H; h0 += 128 * RT_XU) {
+    float xv[RT_XU][4];
+    float4 gv[RT_XU];
+#pragma unroll
+    for (int u = 0; u < RT_XU; ++u) {
+      load_x4<T>(xr, h0 + 128 * u, H, xv[u]);
+      gv[u] = h0 + 128 * u < H ? __ldg(reinterpret_cast<const float4*>(gr + h0 + 128 * u)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < RT_XU; ++u) {
+      if (h0 + 128 * u < H) {
+        acc = fmaf(xv[u][0], gv[u].x, acc);
+        acc = fmaf(xv[u][1], gv[u].y, acc);
+        acc = fmaf(xv[u][2], gv[u].z, acc);
+        acc = fmaf(xv[u][3], gv[u].w, acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) logits[(int64_t)t * E + e] = acc;
 }
 
 // One warp per token.
@@ -217,8 +277,24 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
   SB_CHECK_ARG(x && gate_w && logits, "router: null pointer");
   const size_t gbytes = sizeof(float) * (size_t)E * H;
   const bool aligned = (reinterpret_cast<uintptr_t>(gate_w) % 16 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
-  if (E <= 32 && H % 4 == 0 && gbytes <= 200 * 1024 && aligned &&
-      (x_dtype == STAGEML_BF16 || x_dtype == STAGEML_F16 || x_dtype == STAGEML_F32)) {
+  const bool vec_dtype = x_dtype == STAGEML_BF16 || x_dtype == STAGEML_F16 || x_dtype == STAGEML_F32;
+  if (E <= 32 && H % 4 == 0 && gbytes <= 200 * 1024 && aligned && vec_dtype && T_ <= 32) {
+    // a few tokens: staging G in every CTA would cost more than reading it once from L2
+    const unsigned grid = (unsigned)(((int64_t)T_ * E + 3) / 4);
+    if (x_dtype == STAGEML_BF16)
+      (router_logits_warp_kernel<bf16><<<grid, 128, 0, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E, logits),
+       ::sb::count_launch());
+    else if (x_dtype == STAGEML_F16)
+      (router_logits_warp_kernel<f16><<<grid, 128, 0, stream>>>(static_cast<const f16*>(x), gate_w, T_, H, E, logits),
+       ::sb::count_launch());
+    else
+      (router_logits_warp_kernel<float><<<grid, 128, 0, stream>>>(static_cast<const float*>(x), gate_w, T_, H, E,
+                                                                  logits),
+       ::sb::count_launch());
+    SB_CUDA_CHECK(cudaGetLastError());
+    return STAGEML_OK;
+  }
+  if (E <= 32 && H % 4 == 0 && gbytes <= 200 * 1024 && aligned && vec_dtype) {
     const int grid = std::min<int>(sm_count(), (T_ + 7) / 8);
     auto launch = [&](auto kern, const auto* xp) -> int {
       SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gbytes));
@@ -243,26 +319,19 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
     if (E <= 16) return launch(router_logits_smem_kernel<float, 16>, xp);
     return launch(router_logits_smem_kernel<float, 32>, xp);
   }
-  const size_t smem = sizeof(float) * (size_t)(RT_TOK + E) * (RT_KC + 1);
-  const int grid = (T_ + RT_TOK - 1) / RT_TOK;
-  if (x_dtype == STAGEML_BF16) {
-    SB_CUDA_CHECK(cudaFuncSetAttribute(router_logits_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem));
-    (router_logits_kernel<bf16><<<grid, RT_THREADS, smem, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E,
-                                                                    logits), ::sb::count_launch());
-  } else if (x_dtype == STAGEML_F16) {
-    SB_CUDA_CHECK(cudaFuncSetAttribute(router_logits_kernel<f16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem));
-    (router_logits_kernel<f16><<<grid, RT_THREADS, smem, stream>>>(static_cast<const f16*>(x), gate_w, T_, H, E,
-                                                                   logits), ::sb::count_launch());
-  } else if (x_dtype == STAGEML_F32) {
-    SB_CUDA_CHECK(cudaFuncSetAttribute(router_logits_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem));
-    (router_logits_kernel<float><<<grid, RT_THREADS, smem, stream>>>(static_cast<const float*>(x), gate_w, T_, H,
-                                                                     E, logits), ::sb::count_launch());
-  } else {
+  const dim3 grid((unsigned)((T_ + RT_TT - 1) / RT_TT), (unsigned)((E + RT_TE - 1) / RT_TE));
+  if (x_dtype == STAGEML_BF16)
+    (router_logits_kernel<bf16><<<grid, RT_THREADS, 0, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E, logits),
+     ::sb::count_launch());
+  else if (x_dtype == STAGEML_F16)
+    (router_logits_kernel<f16><<<grid, RT_THREADS, 0, stream>>>(static_cast<const f16*>(x), gate_w, T_, H, E, logits),
+     ::sb::count_launch());
+  else if (x_dtype == STAGEML_F32)
+    (router_logits_kernel<float><<<grid, RT_THREADS, 0, stream>>>(static_cast<const float*>(x), gate_w, T_, H, E,
+                                                                  logits),
+     ::sb::count_launch());
+  else
     return set_error(STAGEML_ERR_INVALID_ARG, "router: unsupported x dtype %d", x_dtype);
-  }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }

@@ -1,0 +1,257 @@
+// Grouped GEMM for a handful of rows per group (decode-sized batches): at most
+// 16 valid rows in every 128-row tile, so the work is streaming the weights.
+//
+// One CTA computes 8 output columns of one tile: the eight warps split K, each
+// streams its K range of the 8 weight rows (SwiGLU: 8 gate + 8 up rows) with
+// 16-byte loads, eight 32-wide chunks in flight per lane, and multiplies by the
+// tile's rows on warp-level tensor cores (m16n8k16, rows past the valid count
+// are zeros). Partial sums meet in shared memory; the epilogue adds the
+// per-tenant LoRA expand S . B^T (S = the pre-scaled shrink output), then SwiGLU
+// or the plain scale / bias / routing weight, and stores 16-bit rows. The same
+// computation as the grouped tcgen05 GEMM (grouped_gemm.cu) for the
+// per-(slot, expert) body of RequestExecutor.dynamic_one
+// (benchmarks/multitenant_bta_system_bench.py:408-413).
+#include "common.cuh"
+#include "grouped_gemm.cuh"
+#include "host_util.h"
+
+namespace sb {
+namespace {
+
+constexpr int kSkNB = 8;        // output columns per CTA
+constexpr int kSkWarps = 8;
+constexpr int kSkUnroll = 8;
+
+struct SkParams {
+  const void* a;
+  int K;
+  const void* b;
+  int64_t b_rows_total;
+  int b_group_rows;
+  int N;
+  const int32_t* num_tiles_dev;
+  int tiles_cap;
+  const int32_t* tile_group;
+  const int32_t* group_offsets;
+  const int32_t* group_counts;
+  int64_t m_rows;
+  const int32_t* row_tenant;
+  int rank;
+  int lora_cols;
+  const void* s16;
+  const void* lora_b;
+  int64_t lb_tenant_stride;
+  int64_t lb_group_stride;
+  const float* row_scale;
+  const void* bias;
+  int64_t bias_group_stride;
+  int bias_group_mod;
+  const float* b_scale;
+  void* out;
+  int64_t ldo;
+};
+
+template <typename T>
+__device__ __forceinline__ void sk_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1);
+template <>
+__device__ __forceinline__ void sk_mma<bf16>(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void sk_mma<f16>(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+// Lane (g, tig) holds 8 consecutive K values (16 bytes) of rows g, g+8 and of
+// weight row g; the two MMAs read them as logical k = {2tig, 2tig+1, 2tig+8,
+// 2tig+9}, the same permutation on both operands, so the dot products are exact.
+template <typename T, int NBLK>
+__device__ __forceinline__ void sk_chunk(float (&acc)[NBLK][4], const uint4& xl, const uint4& xh, const uint4 (&w)[NBLK]) {
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    sk_mma<T>(acc[b], xl.x, xh.x, xl.y, xh.y, w[b].x, w[b].y);
+    sk_mma<T>(acc[b], xl.z, xh.z, xl.w, xh.w, w[b].z, w[b].w);
+  }
+}
+
+template <typename T, bool SWIGLU>
+__global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkParams p) {
+  constexpr int NBLK = SWIGLU ? 2 : 1;
+  __shared__ float red[kSkWarps][NBLK][32][4];
+  __shared__ float tile[NBLK][16][kSkNB];
+  const int m = blockIdx.y;
+  const int ntiles = p.tile_group ? min(*p.num_tiles_dev, p.tiles_cap) : (int)((p.m_rows + 127) / 128);
+  if (m >= ntiles) return;
+  const int group = p.tile_group ? p.tile_group[m] : 0;
+  int64_t valid;
+  if (p.tile_group)
+    valid = (int64_t)p.group_counts[group] - ((int64_t)m * 128 - p.group_offsets[group]);
+  else
+    valid = p.m_rows - (int64_t)m * 128;
+  valid = valid < 0 ? 0 : (valid > 16 ? 16 : valid);
+  if (valid == 0) return;
+  const int n0 = blockIdx.x * kSkNB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int K = p.K;
+  const T* A = static_cast<const T*>(p.a);
+  const T* W = static_cast<const T*>(p.b);
+  const int64_t row0 = (int64_t)m * 128;
+  const T* x_lo = g < valid ? A + (row0 + g) * K : nullptr;
+  const T* x_hi = g + 8 < valid ? A + (row0 + g + 8) * K : nullptr;
+  const T* wrow[NBLK];
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    const int64_t r = (int64_t)group * p.b_group_rows + n0 + g + (b ? p.N : 0);
+    wrow[b] = (n0 + g < p.N && r < p.b_rows_total) ? W + r * K : nullptr;
+  }
+  // this warp's K range, a multiple of 32 wide
+  const int kw = ((K + kSkWarps * 32 - 1) / (kSkWarps * 32)) * 32;
+  const int kb = warp * kw, ke = min(K, kb + kw);
+  float acc[NBLK][4];
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[b][j] = 0.f;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int k0 = kb; k0 < ke; k0 += 32 * kSkUnroll) {
+    uint4 xl[kSkUnroll], xh[kSkUnroll], w[kSkUnroll][NBLK];
+#pragma unroll
+    for (int u = 0; u < kSkUnroll; ++u) {
+      const int kk = k0 + u * 32 + tig * 8;
+      const bool v = kk < ke;
+      xl[u] = (v && x_lo) ? ldg16(x_lo + kk) : z;
+      xh[u] = (v && x_hi) ? ldg16(x_hi + kk) : z;
+#pragma unroll
+      for (int b = 0; b < NBLK; ++b) w[u][b] = (v && wrow[b]) ? ldg16(wrow[b] + kk) : z;
+    }
+#pragma unroll
+    for (int u = 0; u < kSkUnroll; ++u) sk_chunk<T, NBLK>(acc, xl[u], xh[u], w[u]);
+  }
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[warp][b][lane][j] = acc[b][j];
+  __syncthreads();
+  if (threadIdx.x < NBLK * 128) {
+    const int b = threadIdx.x >> 7, e = threadIdx.x & 127;
+    const int l = e >> 2, j = e & 3;
+    float s = 0.f;
+#pragma unroll
+    for (int wv = 0; wv < kSkWarps; ++wv) s += red[wv][b][l][j];
+    const int r = (l >> 2) + (j >= 2 ? 8 : 0), c = (l & 3) * 2 + (j & 1);
+    tile[b][r][c] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x >= 128) return;
+  const int r = threadIdx.x >> 3, c = threadIdx.x & 7;
+  const int col = n0 + c;
+  if (r >= valid || col >= p.N) return;
+  const int64_t row = row0 + r;
+  float v0 = tile[0][r][c];
+  float v1 = SWIGLU ? tile[NBLK - 1][r][c] : 0.f;
+  if (p.rank > 0) {
+    const int t = p.row_tenant[row];
+    if (t >= 0) {
+      const T* S = static_cast<const T*>(p.s16) + row * p.lora_cols;
+      const T* Bl = static_cast<const T*>(p.lora_b) + t * p.lb_tenant_stride + group * p.lb_group_stride;
+      const T* b0 = Bl + (int64_t)col * p.rank;
+      float d0 = 0.f, d1 = 0.f;
+      for (int j = 0; j < p.rank; ++j) d0 += to_f32<T>(S[j]) * to_f32<T>(b0[j]);
+      if (SWIGLU) {
+        const T* b1 = Bl + (int64_t)(p.N + col) * p.rank;
+        for (int j = 0; j < p.rank; ++j) d1 += to_f32<T>(S[p.rank + j]) * to_f32<T>(b1[j]);
+      }
+      v0 += d0;
+      v1 += d1;
+    }
+  }
+  T* out = static_cast<T*>(p.out);
+  if (SWIGLU) {
+    if (p.b_scale) {
+      const float* bs = p.b_scale + (int64_t)group * p.b_group_rows;
+      v0 *= bs[col];
+      v1 *= bs[p.N + col];
+    }
+    out[row * p.ldo + col] = from_f32<T>(silu_f32(v0) * v1);
+  } else {
+    if (p.b_scale) v0 *= p.b_scale[(int64_t)group * p.b_group_rows + col];
+    if (p.bias) {
+      const int bg = p.bias_group_mod > 0 ? group % p.bias_group_mod : group;
+      v0 += to_f32<T>(static_cast<const T*>(p.bias)[bg * p.bias_group_stride + col]);
+    }
+    if (p.row_scale) v0 *= p.row_scale[row];
+    out[row * p.ldo + col] = from_f32<T>(v0);
+  }
+}
+
+}  // namespace
+
+int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int32_t* group_offsets,
+                       const int32_t* group_counts, cudaStream_t stream) {
+  SB_CHECK_ARG(g.a && g.b && g.out, "skinny gemm: null operand");
+  SB_CHECK_ARG(!g.b_fp8, "skinny gemm: 16-bit weights only");
+  SB_CHECK_ARG(g.K > 0 && g.K % 8 == 0 && g.N > 0, "skinny gemm: K=%d must be a positive multiple of 8", g.K);
+  SB_CHECK_ARG(!g.tile_group || (g.num_tiles_dev && group_offsets && group_counts),
+               "skinny gemm: grouped rows need the tile count, group offsets and counts");
+  SB_CHECK_ARG(g.rank == 0 || (g.s16 && g.lora_b && row_tenant), "skinny gemm: LoRA needs S, B and the row tenants");
+  SB_CHECK_ARG((reinterpret_cast<uintptr_t>(g.a) % 16) == 0 && (reinterpret_cast<uintptr_t>(g.b) % 16) == 0,
+               "skinny gemm: operands must be 16-byte aligned");
+  SkParams p;
+  p.a = g.a;
+  p.K = g.K;
+  p.b = g.b;
+  p.b_rows_total = g.b_rows_total;
+  p.b_group_rows = g.b_group_rows;
+  p.N = g.N;
+  p.num_tiles_dev = g.num_tiles_dev;
+  p.tiles_cap = g.tiles_cap;
+  p.tile_group = g.tile_group;
+  p.group_offsets = group_offsets;
+  p.group_counts = group_counts;
+  p.m_rows = g.m_rows;
+  p.row_tenant = row_tenant;
+  p.rank = g.rank;
+  p.lora_cols = g.swiglu ? 2 * g.rank : g.rank;
+  p.s16 = g.s16;
+  p.lora_b = g.lora_b;
+  p.lb_tenant_stride = g.lora_b_tenant_stride;
+  p.lb_group_stride = g.lora_b_group_stride;
+  p.row_scale = g.row_scale;
+  p.bias = g.bias;
+  p.bias_group_stride = g.bias_group_stride;
+  p.bias_group_mod = g.bias_group_mod;
+  p.b_scale = g.b_scale;
+  p.out = g.out;
+  p.ldo = g.ldo;
+  const int64_t tiles = g.tile_group ? (int64_t)g.tiles_cap : (g.m_rows + 127) / 128;
+  if (tiles == 0) return STAGEML_OK;
+  SB_CHECK_ARG(tiles <= 65535, "skinny gemm: too many row tiles");
+  const dim3 grid((unsigned)((g.N + kSkNB - 1) / kSkNB), (unsigned)tiles);
+  if (g.in_bf16) {
+    if (g.swiglu)
+      (skinny_gemm_kernel<bf16, true><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
+    else
+      (skinny_gemm_kernel<bf16, false><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
+  } else {
+    if (g.swiglu)
+      (skinny_gemm_kernel<f16, true><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
+    else
+      (skinny_gemm_kernel<f16, false><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
+  }
+  SB_CUDA_CHECK(cudaGetLastError());
+  return STAGEML_OK;
+}
+
+}  // namespace sb
