@@ -2,8 +2,8 @@
 // tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16, fp32 accumulators in TMEM).
 //
 // Same computation as grouped_gemm.cu (per-group weights, SwiGLU or plain
-// epilogue, per-token-tenant LoRA expand fused as masked MMAs, e4m3 weights
-// dequantised in shared memory), laid out so that each SM moves a third fewer
+// epilogue, per-token-tenant LoRA expand fused as masked MMAs; 16-bit weights —
+// e4m3 weights use grouped_gemm.cu), laid out so that each SM moves a third fewer
 // bytes per FLOP: every CTA of the pair stages its own 128 rows of A and only
 // half of the 256 B rows (SwiGLU: the gate half on the even CTA, the up half
 // on the odd one), and the pair MMA issued by the even CTA reads both.
@@ -13,11 +13,10 @@
 // odd half is idle (its rows are loaded but never stored).
 //
 // Per CTA: warp 0 TMA producer, warp 1 TMEM allocator and -- on the even CTA --
-// MMA issuer; warps 2..5 epilogue over the CTA's own 128 TMEM lanes; warps 6..13
-// e4m3 converters (FP8 weights only). With 16-bit weights both CTAs' copies
-// complete on the even CTA's stage barrier (cta_group::2 copies); with FP8
-// weights each CTA's copies complete locally and its converters signal the even
-// CTA. Every wait is bounded. No load is multicast.
+// MMA issuer; warps 2..5 epilogue over the CTA's own 128 TMEM lanes. Both CTAs'
+// copies complete on the even CTA's stage barrier (cta_group::2 copies), which
+// the even CTA arms with both halves' bytes; stage and accumulator releases go
+// to both CTAs in one commit. Every wait is bounded. No load is multicast.
 #include "common.cuh"
 #include "grouped_gemm.cuh"
 #include "host_util.h"
@@ -33,24 +32,16 @@ constexpr int BK = 64;                         // one 128 B swizzle row of 16-bi
 constexpr int A_BYTES = BM * BK * 2;           // 16 KB
 constexpr int B_BYTES = 128 * BK * 2;          // this CTA's half of B: 16 KB
 constexpr int MMA_STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int RAW_BYTES = 128 * BK;            // e4m3 staging of this CTA's half of B: 8 KB
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int LCHUNK = 128 * 32;               // 128 rows x 16 columns, 16-bit (4 KB)
 constexpr int LHALF = 64 * 32;                 // 64 rows x 16 columns, 16-bit (2 KB)
-constexpr int CONVERTER_THREADS = 256;
 
-template <bool FP8B>
-struct Cfg {
-  static constexpr int STAGES = FP8B ? 5 : 7;
-  static constexpr int STAGE_BYTES = FP8B ? MMA_STAGE_BYTES + RAW_BYTES : MMA_STAGE_BYTES;
-  static constexpr int THREADS = FP8B ? 192 + CONVERTER_THREADS : 192;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
-  // full: 16-bit weights -- the even CTA's expect_tx (both halves' copies complete on it);
-  // FP8 weights -- one arrival per converter warp of both CTAs
-  static constexpr int FULL_ARRIVALS = FP8B ? 2 * (CONVERTER_THREADS / 32) : 1;
-  static_assert(SMEM_BYTES <= 232448, "shared memory per block");
-  static_assert((3 * STAGES + 5) * 8 + 8 <= 512, "barrier area");
-};
+constexpr int STAGES = 7;
+constexpr int STAGE_BYTES = MMA_STAGE_BYTES;
+constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+static_assert(SMEM_BYTES <= 232448, "shared memory per block");
+static_assert((3 * STAGES + 5) * 8 + 8 <= 512, "barrier area");
 
 struct PParams {
   int K;
@@ -79,8 +70,7 @@ struct PParams {
   const void* bias;
   int64_t bias_group_stride;
   int bias_group_mod;
-  const float* b_scale;          // 16-bit weights: per-B-row scale in the epilogue (or null)
-  const float* b_row_scale;      // FP8 weights: per-B-row dequantisation scale
+  const float* b_scale;          // per-B-row scale in the epilogue (or null)
   void* out;
   int64_t ldo;
   int32_t* status;
@@ -114,25 +104,6 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
   }
 }
 
-template <typename T>
-__device__ __forceinline__ void dequant16(const uint4& q, float s, uint4& lo, uint4& hi) {
-  const __nv_fp8x2_storage_t* p2 = reinterpret_cast<const __nv_fp8x2_storage_t*>(&q);
-  float a[8], b[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2_raw r0 = __nv_cvt_fp8x2_to_halfraw2(p2[i], __NV_E4M3);
-    const __half2_raw r1 = __nv_cvt_fp8x2_to_halfraw2(p2[4 + i], __NV_E4M3);
-    const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&r0));
-    const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&r1));
-    a[2 * i] = v0.x * s;
-    a[2 * i + 1] = v0.y * s;
-    b[2 * i] = v1.x * s;
-    b[2 * i + 1] = v1.y * s;
-  }
-  lo = pack8<T>(a);
-  hi = pack8<T>(b);
-}
-
 __device__ __forceinline__ int pair_lora_runs(const PParams& p, int pm) {
   if (p.rank == 0) return 0;
   const int n = p.nruns[pm];
@@ -156,20 +127,17 @@ __device__ __forceinline__ void unit_coords(const PParams& p, int u, int& pm, in
   pm = first + (local - n_tile * cnt);
 }
 
-template <typename T, bool FP8B>
-__global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
+template <typename T>
+__global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                              const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_lb,
                              const PParams p) {
-  constexpr int STAGES = Cfg<FP8B>::STAGES;
-  constexpr int STAGE_BYTES = Cfg<FP8B>::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  // bars: [0,S) landed (this CTA's TMA), [S,2S) full (both halves ready; used on the
-  // even CTA), [2S,3S) empty, [3S,3S+2) tmem_full, [3S+2,3S+4) tmem_empty (even CTA),
-  // [3S+4] drain
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
+  // bars: [0,S) full (both halves landed; used on the even CTA), [S,2S) empty,
+  // [2S,2S+2) tmem_full, [2S+2,2S+4) tmem_empty (even CTA), [2S+4] drain
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -179,17 +147,15 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   const int cluster = blockIdx.x >> 1;
   const int nclusters = gridDim.x >> 1;
   const uint32_t smem_base = smem_u32(smem);
-  auto landed_bar = [&](int s) { return smem_u32(&bars[s]); };
-  auto full_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
-  auto empty_bar = [&](int s) { return smem_u32(&bars[2 * STAGES + s]); };
-  auto tfull_bar = [&](int a) { return smem_u32(&bars[3 * STAGES + a]); };
-  auto tempty_bar = [&](int a) { return smem_u32(&bars[3 * STAGES + 2 + a]); };
-  const uint32_t drain_bar = smem_u32(&bars[3 * STAGES + 4]);
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+  auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + a]); };
+  auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + 2 + a]); };
+  const uint32_t drain_bar = smem_u32(&bars[2 * STAGES + 4]);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(landed_bar(s), 1);
-      mbar_init(full_bar(s), Cfg<FP8B>::FULL_ARRIVALS);
+      mbar_init(full_bar(s), 1);  // the even CTA's expect_tx
       mbar_init(empty_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -224,21 +190,14 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     }
     const uint64_t pol_a = l2_policy_evict_last();
     const uint64_t pol_b = l2_policy_evict_normal();
-    // 16-bit weights: both CTAs' copies complete on the even CTA's full barrier, which the
-    // even CTA arms with the bytes of both halves. FP8 weights: copies complete on this
-    // CTA's landed barrier, the converters then arrive on the even CTA's full barrier.
+    // Both CTAs' copies complete on the even CTA's full barrier, which the even CTA
+    // arms with the bytes of both halves (the halves are the same size).
     const uint32_t lead_full0 = mapa_shared(full_bar(0), 0);
     auto arm = [&](int s, uint32_t bytes) {
-      if (FP8B)
-        mbar_arrive_expect_tx(landed_bar(s), bytes);
-      else if (leader)
-        mbar_arrive_expect_tx(full_bar(s), 2 * bytes);
+      if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * bytes);
     };
     auto load = [&](uint32_t dst, const CUtensorMap* tm, int s, int x, int y, uint64_t pol) {
-      if (FP8B)
-        tma_load_2d(dst, tm, landed_bar(s), x, y, pol);
-      else
-        tma_load_2d_pair(dst, tm, lead_full0 + 8u * (uint32_t)s, x, y, pol);
+      tma_load_2d_pair(dst, tm, lead_full0 + 8u * (uint32_t)s, x, y, pol);
     };
     int last_phase[STAGES];
     for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
@@ -262,9 +221,9 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           break;
         }
         const uint32_t sa = smem_base + s * STAGE_BYTES;
-        arm(s, FP8B ? A_BYTES + RAW_BYTES : MMA_STAGE_BYTES);
+        arm(s, MMA_STAGE_BYTES);
         load(sa, &tm_a, s, kb * BK, a_row, pol_a);
-        load(FP8B ? sa + MMA_STAGE_BYTES : sa + A_BYTES, &tm_b, s, kb * BK, b_row, pol_b);
+        load(sa + A_BYTES, &tm_b, s, kb * BK, b_row, pol_b);
         last_phase[s] = (int)ph;
       }
       // LoRA blocks: this CTA's rows of S + its half of the B rows of each tenant run
@@ -303,12 +262,11 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     }
     if (!ok) {
       // Let the copies already in flight land before the CTA pair leaves. The odd CTA's
-      // 16-bit copies complete on the even CTA's barrier; it waits a fixed, ample time.
-      if (FP8B || leader) {
+      // copies complete on the even CTA's barrier; it waits a fixed, ample time.
+      if (leader) {
         for (int s = 0; s < STAGES; ++s)
           if (last_phase[s] >= 0)
-            mbar_wait(FP8B ? landed_bar(s) : full_bar(s), (uint32_t)last_phase[s], &never_abort, p.status,
-                      200000000ull, kDevTimeoutDrain);
+            mbar_wait(full_bar(s), (uint32_t)last_phase[s], &never_abort, p.status, 200000000ull, kDevTimeoutDrain);
       } else {
         const unsigned long long t0 = globaltimer_ns();
         while (globaltimer_ns() - t0 < 200000ull) {
@@ -468,68 +426,6 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty0 + 8u * (uint32_t)acc);
     }
-  } else if (FP8B && warp >= 6) {
-    // ------------------------------------------------------------ e4m3 -> 16-bit converters (both CTAs)
-    // Item (r, c): row r of this CTA's 128 B rows, 16-byte chunk c (16 weights) of its 64-byte
-    // e4m3 row; stored as 16-bit logical chunks 2c, 2c+1 of the 128-byte row at physical
-    // chunk (logical ^ (r & 7)), the 128B swizzle of the MMA descriptor.
-    const int ct = threadIdx.x - 192;
-    const uint32_t leader_full0 = mapa_shared(full_bar(0), 0);
-    constexpr int ITEMS = 128 * BK / 16 / CONVERTER_THREADS;  // 2
-    uint32_t it = 0;
-    bool ok = true;
-    for (int u = cluster; ok && u < total_units; u += nclusters) {
-      int pm, n_tile;
-      unit_coords(p, u, pm, n_tile);
-      const int group = p.tile_group ? p.tile_group[p.pairs[4 * pm]] : 0;
-      const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
-      const int64_t b_row = (int64_t)group * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
-      float sc[ITEMS];
-      int rr[ITEMS], cc[ITEMS];
-#pragma unroll
-      for (int q = 0; q < ITEMS; ++q) {
-        const int idx = ct + CONVERTER_THREADS * q;
-        rr[q] = idx >> 2;
-        cc[q] = idx & 3;
-        const int64_t grow = b_row + rr[q];
-        sc[q] = grow < p.b_rows_total ? p.b_row_scale[grow] : 0.f;
-      }
-      for (int kb = 0; kb < num_kb; ++kb, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(landed_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        uint8_t* st = smem + s * STAGE_BYTES;
-        const uint8_t* raw = st + MMA_STAGE_BYTES;
-        uint8_t* bt = st + A_BYTES;
-#pragma unroll
-        for (int q = 0; q < ITEMS; ++q) {
-          const uint4 qv = *reinterpret_cast<const uint4*>(raw + rr[q] * BK + cc[q] * 16);
-          uint4 lo, hi;
-          dequant16<T>(qv, sc[q], lo, hi);
-          uint8_t* row = bt + rr[q] * 128;
-          const int sw = rr[q] & 7;
-          *reinterpret_cast<uint4*>(row + (((2 * cc[q]) ^ sw) << 4)) = lo;
-          *reinterpret_cast<uint4*>(row + (((2 * cc[q] + 1) ^ sw) << 4)) = hi;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(leader_full0 + 8u * (uint32_t)s);
-      }
-      const int nruns = ok ? pair_lora_runs(p, pm) : 0;
-      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(landed_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(leader_full0 + 8u * (uint32_t)s);  // LoRA operands are 16-bit
-      }
-    }
   }
 
   __syncwarp();
@@ -647,11 +543,11 @@ __global__ void __launch_bounds__(64) pair_runs_kernel(const int32_t* __restrict
   if (lane == 0) nruns[pr] = count;
 }
 
-template <typename T, bool FP8B>
+template <typename T>
 int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
                        const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const PParams& p) {
-  auto kern = grouped_gemm_pair_kernel<T, FP8B>;
-  SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<FP8B>::SMEM_BYTES));
+  auto kern = grouped_gemm_pair_kernel<T>;
+  SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   // Persistent grid: as many CTA pairs as can be resident at once.
   static std::mutex mu;
   static int cached[64] = {0};
@@ -663,8 +559,8 @@ int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorM
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(Cfg<FP8B>::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = Cfg<FP8B>::SMEM_BYTES;
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -715,16 +611,13 @@ int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, co
 
 int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
   SB_CHECK_ARG(g.pairs && g.num_pairs_dev && g.pairs_cap >= 0, "pair gemm: missing pair list");
+  SB_CHECK_ARG(!g.b_fp8, "pair gemm: e4m3 weights run on the one-CTA grouped GEMM");
   SB_CHECK_ARG(g.rank == 0 || (g.pair_runs && g.pair_nruns), "pair gemm: LoRA needs the pair runs");
 
   const CUtensorMapDataType dt = g.in_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tm_a, tm_b, tm_s, tm_lb;
   SB_TRY(make_tmap_2d(&tm_a, g.a, dt, 2, (uint64_t)g.a_rows, (uint64_t)g.K, (uint64_t)g.K * 2, BM, BK, 128));
-  if (g.b_fp8)
-    SB_TRY(make_tmap_2d(&tm_b, g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)g.b_rows_total, (uint64_t)g.K,
-                        (uint64_t)g.K, 128, BK, 0));
-  else
-    SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
+  SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
   const int lora_cols = g.swiglu ? 2 * g.rank : g.rank;
   if (g.rank) {
     SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
@@ -761,8 +654,7 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
   p.bias = g.bias;
   p.bias_group_stride = g.bias_group_stride;
   p.bias_group_mod = g.bias_group_mod;
-  p.b_scale = g.b_fp8 ? nullptr : g.b_scale;
-  p.b_row_scale = g.b_fp8 ? g.b_scale : nullptr;
+  p.b_scale = g.b_scale;
   p.out = g.out;
   p.ldo = g.ldo;
   p.status = g.status;
@@ -770,11 +662,8 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
 
   const int64_t units_upper = (int64_t)g.pairs_cap * p.num_n_tiles;
   if (units_upper == 0) return STAGEML_OK;
-  if (g.b_fp8)
-    return g.in_bf16 ? launch_pair_kernel<bf16, true>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p)
-                     : launch_pair_kernel<f16, true>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p);
-  return g.in_bf16 ? launch_pair_kernel<bf16, false>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p)
-                   : launch_pair_kernel<f16, false>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p);
+  return g.in_bf16 ? launch_pair_kernel<bf16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p)
+                   : launch_pair_kernel<f16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p);
 }
 
 }  // namespace sb
