@@ -241,6 +241,7 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
     peaks = load_peaks()
     T = args.tokens or cfg.T
     t_gen = time.time()
+    layer = None
     if world > 1:
         from stageml_b200.expert_parallel import EPMoELayer
 
@@ -343,6 +344,10 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
         batch1 = {"p50_us": round(lat[len(lat) // 2], 2), "p95_us": round(lat[int(len(lat) * 0.95)], 2),
                   "samples": len(lat)}
 
+    ep_status = None
+    if layer is not None:  # collective: every rank releases the exchange buffers
+        ep_status = layer.take_status()
+        layer.close()
     if rank != 0:
         return
     fl = cfg.flops(T)
@@ -383,6 +388,7 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
                    "intermediate": cfg.I, "experts": cfg.E, "top_k": cfg.k, "lora_rank": cfg.rank,
                    "tenants": cfg.n_tenants, "lora_on": "w1,w3,w2", "router": "in-layer (fp32 logits, softmax, top-2)",
                    "parallelism": f"ep{world}" if world > 1 else "single",
+                   "ep_transport": layer.transport if layer is not None else None,
                    "l2": f"inputs larger than L2 ({by['weights'] / 1e9:.2f} GB expert weights per step)"},
         "roofline": {"bound": "tensor", "kernel": "grouped gate/up GEMM (tcgen05) + LoRA expand + SwiGLU",
                      "achieved": None if achieved is None else round(achieved, 1), "peak": peak_tf,
@@ -400,6 +406,8 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
         "batch1_latency": batch1,
         "cpu_baseline": cpu,
     }
+    if layer is not None:
+        line["ep_status"] = ep_status
     print(json.dumps(line), flush=True)
 
 

@@ -59,7 +59,8 @@ enum {
 enum {
   STAGEML_DEV_OK = 0,
   STAGEML_DEV_TIMEOUT = 101,   /* 101..104: a bounded wait in a pipelined kernel expired */
-  STAGEML_DEV_BAD_INDEX = 110  /* an expert / tenant / group id was out of range; that item was skipped */
+  STAGEML_DEV_BAD_INDEX = 110, /* an expert / tenant / group id was out of range; that item was skipped */
+  STAGEML_DEV_PEER_TIMEOUT = 105 /* expert parallel: another GPU did not signal within the bound */
 };
 
 /* Text of the last error reported on this thread ("" if none). */
@@ -210,6 +211,9 @@ typedef struct stageml_moe_args {
   void* out;             /* [T,H] act_dtype */
   int32_t* status;       /* device status word, may be NULL */
   const stageml_moe_plan* plan_out; /* optional: keep the permutation in caller memory */
+  const int32_t* T_dev;  /* optional device int: only tokens [0, *T_dev) are valid (<= T); the rest
+                            are skipped and their output rows left untouched. Used when the token
+                            count is known only on the device (rows received from other GPUs). */
 } stageml_moe_args;
 
 size_t stageml_moe_workspace_bytes(const stageml_moe_args* args);
@@ -332,6 +336,70 @@ int stageml_lora_gemv_f32_noalloc(const float* x, const float* W, const float* A
  * with round-to-nearest-even and saturation to +-448. Input F32/BF16/F16. */
 int stageml_quantize_e4m3_rows(const void* w, int dtype, int64_t rows, int64_t cols, uint8_t* q_out,
                                float* scale_out, stageml_stream_t stream);
+
+/* ------------------------------------------------------- expert parallel over peer memory
+ * No counterpart in the reference, which has no distributed code: this is the
+ * expert-parallel layout of the MoE-LoRA layer (experts and their adapter-bank
+ * slices sharded over `world` GPUs, one process per GPU). Instead of NCCL
+ * all-to-alls with host-side split sizes, rows move with plain stores into the
+ * other GPUs' memory (CUDA IPC mappings over NVLink / NVSwitch) and epoch flags;
+ * the host never waits for counts.
+ *
+ * Every rank allocates one workspace with stageml_ep_workspace_alloc (layout from
+ * stageml_ep_get_layout, identical on all ranks; zero-filled), exchanges the IPC
+ * handles out of band (e.g. torch.distributed.all_gather_object), opens the
+ * others' with stageml_ep_workspace_open and keeps a device array peers[world]
+ * of all workspace bases (its own at index rank). A layer call with a new epoch
+ * (1, 2, 3, ... per workspace) is:
+ *   stageml_ep_dispatch  route this rank's pairs to the owners of their experts;
+ *                        afterwards the receive region holds recv_tokens dense rows
+ *                        (x, local expert, tenant, routing weight, source);
+ *   (local expert computation on those rows, e.g. stageml_moe_forward with k = 1,
+ *    T = world * tokens_cap * k and T_dev = the recv_tokens word)
+ *   stageml_ep_return    send each result row back to its source;
+ *   stageml_ep_combine   out[t] = sum_j result(t, j) (+ add[t]).
+ * All three calls of an epoch go on one stream, and every rank makes them in the
+ * same order. Waits on other GPUs are bounded (timeout_ns, default 5 s); on
+ * expiry the status word gets STAGEML_DEV_PEER_TIMEOUT. world <= 8. */
+typedef struct stageml_ep_layout {
+  size_t count_matrix;  /* int32 [world][world]: row s = pairs rank s sends to each rank */
+  size_t flags_count, flags_rows, flags_return; /* int32 [world] epoch flags, one per source */
+  size_t counters;      /* int32 [4] */
+  size_t recv_tokens;   /* int32: rows received in the current epoch */
+  size_t recv_expert;   /* int32 [world*tokens_cap*k]: local expert of each received row */
+  size_t recv_weight;   /* f32   [..]: routing weight */
+  size_t recv_tenant;   /* int32 [..]: tenant (-1 = none) */
+  size_t recv_source;   /* int32 [..]: source pair * world + source rank */
+  size_t recv_x;        /* 16-bit [world*tokens_cap*k][H] */
+  size_t ret_y;         /* 16-bit [tokens_cap*k][H]: result rows, by this rank's pair index */
+  size_t total;
+} stageml_ep_layout;
+
+typedef struct stageml_ep_args {
+  int world, rank;
+  int T, k, H, E_loc;     /* this rank's tokens, slots, hidden size, experts per rank */
+  int act_dtype;          /* BF16 or F16 */
+  int epoch;              /* > 0, one more than the previous call on this workspace */
+  int64_t tokens_cap;     /* T <= tokens_cap on every rank (sizes the buffers) */
+  uint64_t timeout_ns;    /* 0 = 5 s */
+  const uint64_t* peers;  /* device [world]: workspace base of every rank */
+  void* self;             /* this rank's workspace */
+  const int32_t* topk_ids;    /* [T,k] global expert ids (owner = id / E_loc) */
+  const float* topk_weights;  /* [T,k] */
+  const int32_t* tenant_ids;  /* [T] or NULL */
+  const void* x;              /* [T,H] act_dtype */
+  int32_t* pos;               /* [T*k] scratch */
+  int32_t* status;            /* device status word or NULL */
+} stageml_ep_args;
+
+int stageml_ep_get_layout(int world, int64_t tokens_cap, int k, int H, int act_dtype, stageml_ep_layout* out);
+int stageml_ep_workspace_alloc(size_t bytes, void** ptr, void* ipc_handle_64);
+int stageml_ep_workspace_free(void* ptr);
+int stageml_ep_workspace_open(const void* ipc_handle_64, void** ptr);
+int stageml_ep_workspace_close(void* ptr);
+int stageml_ep_dispatch(const stageml_ep_args* args, stageml_stream_t stream);
+int stageml_ep_return(const stageml_ep_args* args, const void* y_local, stageml_stream_t stream);
+int stageml_ep_combine(const stageml_ep_args* args, const void* add, void* out, stageml_stream_t stream);
 
 #ifdef __cplusplus
 }

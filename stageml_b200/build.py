@@ -30,6 +30,7 @@ CU_SOURCES = [
     "grouped_gemm.cu",
     "grouped_gemm_pair.cu",
     "skinny.cu",
+    "ep.cu",
     "combine.cu",
     "fold.cu",
     "gemv.cu",

@@ -21,7 +21,7 @@ ERR_UNSUPPORTED = 3
 ERR_WORKSPACE = 4
 
 F32, BF16, F16, E4M3, I32, I64 = 0, 1, 2, 3, 4, 5
-DEV_OK, DEV_TIMEOUT, DEV_BAD_INDEX = 0, 101, 110
+DEV_OK, DEV_TIMEOUT, DEV_PEER_TIMEOUT, DEV_BAD_INDEX = 0, 101, 105, 110
 
 
 class MoePlan(ctypes.Structure):
@@ -71,6 +71,7 @@ class MoeArgs(ctypes.Structure):
         ("out", c_void_p),
         ("status", c_void_p),
         ("plan_out", c_void_p),
+        ("T_dev", c_void_p),
     ]
 
 
@@ -92,6 +93,35 @@ class LoraLinearArgs(ctypes.Structure):
         ("lora_b", c_void_p),
         ("lora_scale", c_void_p),
         ("y", c_void_p),
+        ("status", c_void_p),
+    ]
+
+
+class EpLayout(ctypes.Structure):
+    _fields_ = [(n, c_size_t) for n in ("count_matrix", "flags_count", "flags_rows", "flags_return", "counters",
+                                         "recv_tokens", "recv_expert", "recv_weight", "recv_tenant", "recv_source",
+                                         "recv_x", "ret_y", "total")]
+
+
+class EpArgs(ctypes.Structure):
+    _fields_ = [
+        ("world", c_int),
+        ("rank", c_int),
+        ("T", c_int),
+        ("k", c_int),
+        ("H", c_int),
+        ("E_loc", c_int),
+        ("act_dtype", c_int),
+        ("epoch", c_int),
+        ("tokens_cap", c_int64),
+        ("timeout_ns", ctypes.c_uint64),
+        ("peers", c_void_p),
+        ("self", c_void_p),
+        ("topk_ids", c_void_p),
+        ("topk_weights", c_void_p),
+        ("tenant_ids", c_void_p),
+        ("x", c_void_p),
+        ("pos", c_void_p),
         ("status", c_void_p),
     ]
 
@@ -131,12 +161,20 @@ SIGNATURES = {
     "stageml_stage_timer_enable": (c_int, [c_int]),
     "stageml_stage_timer_read": (c_int, [c_float_p, c_int32_p, c_int]),
     "stageml_launch_count": (ctypes.c_ulonglong, []),
+    "stageml_ep_get_layout": (c_int, [c_int, c_int64, c_int, c_int, c_int, POINTER(EpLayout)]),
+    "stageml_ep_workspace_alloc": (c_int, [c_size_t, POINTER(c_void_p), c_void_p]),
+    "stageml_ep_workspace_free": (c_int, [c_void_p]),
+    "stageml_ep_workspace_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "stageml_ep_workspace_close": (c_int, [c_void_p]),
+    "stageml_ep_dispatch": (c_int, [POINTER(EpArgs), c_void_p]),
+    "stageml_ep_return": (c_int, [POINTER(EpArgs), c_void_p, c_void_p]),
+    "stageml_ep_combine": (c_int, [POINTER(EpArgs), c_void_p, c_void_p, c_void_p]),
 }
 
 STAGE_NAMES = ("route", "permute", "gather_shrink", "gemm_gate_up", "shrink_h", "gemm_down", "combine", "gemm",
                "fold", "gemv")
 
-STRUCTS = {0: MoePlan, 1: MoeArgs, 2: LoraLinearArgs}
+STRUCTS = {0: MoePlan, 1: MoeArgs, 2: LoraLinearArgs, 3: EpLayout, 4: EpArgs}
 
 
 def declare(lib: ctypes.CDLL) -> None:
@@ -164,5 +202,5 @@ def stream_handle(stream=None) -> int:
     return s.cuda_stream
 
 
-__all__ = ["MoePlan", "MoeArgs", "LoraLinearArgs", "SIGNATURES", "STRUCTS", "declare", "check", "ptr",
+__all__ = ["MoePlan", "MoeArgs", "LoraLinearArgs", "EpLayout", "EpArgs", "SIGNATURES", "STRUCTS", "declare", "check", "ptr",
            "stream_handle", "F32", "BF16", "F16", "E4M3", "I32", "I64", "OK"]

@@ -234,7 +234,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   const int64_t nkeys = permute_num_keys(0, a->n_tenants, 0, E_tot);
   permute_carve(b.perm_scratch, P, nkeys, &scr);
   SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
-                        b.plan, status, scr, st));
+                        b.plan, status, scr, st, a->T_dev));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
   // Decode-sized batches (at most 16 routed rows in all) stream the weights with the
   // skinny GEMM; larger ones use the tensor-memory GEMM and its tile / pair plan.
@@ -362,7 +362,8 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
                     : launch_grouped_gemm(g, st));
   }
   // combine
-  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st));
+  SB_STAGE(STAGEML_STAGE_COMBINE,
+           launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st, a->T_dev));
   return STAGEML_OK;
 }
 
@@ -428,6 +429,10 @@ size_t stageml_struct_size(int which) {
       return sizeof(stageml_moe_args);
     case 2:
       return sizeof(stageml_lora_linear_args);
+    case 3:
+      return sizeof(stageml_ep_layout);
+    case 4:
+      return sizeof(stageml_ep_args);
     default:
       return 0;
   }

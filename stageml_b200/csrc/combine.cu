@@ -12,10 +12,11 @@ namespace {
 
 template <typename T>
 __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ pair_row, int T_, int kk, int H,
-                               T* __restrict__ out) {
+                               T* __restrict__ out, const int32_t* __restrict__ T_dev, int t_base) {
   const int t = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (t >= T_ || c >= H) return;
+  if (T_dev && t_base + t >= *T_dev) return;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -46,7 +47,7 @@ __global__ void validate_tenants_kernel(const int32_t* __restrict__ in, int64_t 
 }  // namespace
 
 int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H, int dtype_bf16, void* out,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const int32_t* T_dev) {
   SB_CHECK_ARG(H % 8 == 0, "combine: H=%d must be a multiple of 8", H);
   if (T_ == 0 || H == 0) return STAGEML_OK;
   dim3 block(128);
@@ -59,17 +60,19 @@ int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H
       dim3 g2(grid.x, (unsigned)nt);
       if (dtype_bf16)
         (combine_kernel<bf16><<<g2, block, 0, stream>>>(static_cast<const bf16*>(y), pair_row + (int64_t)t0 * kk, nt,
-                                                        kk, H, static_cast<bf16*>(out) + (int64_t)t0 * H), ::sb::count_launch());
+                                                        kk, H, static_cast<bf16*>(out) + (int64_t)t0 * H, T_dev, t0),
+         ::sb::count_launch());
       else
         (combine_kernel<f16><<<g2, block, 0, stream>>>(static_cast<const f16*>(y), pair_row + (int64_t)t0 * kk, nt,
-                                                       kk, H, static_cast<f16*>(out) + (int64_t)t0 * H), ::sb::count_launch());
+                                                       kk, H, static_cast<f16*>(out) + (int64_t)t0 * H, T_dev, t0),
+         ::sb::count_launch());
     }
   } else if (dtype_bf16) {
     (combine_kernel<bf16><<<grid, block, 0, stream>>>(static_cast<const bf16*>(y), pair_row, T_, kk, H,
-                                                      static_cast<bf16*>(out)), ::sb::count_launch());
+                                                      static_cast<bf16*>(out), T_dev, 0), ::sb::count_launch());
   } else {
     (combine_kernel<f16><<<grid, block, 0, stream>>>(static_cast<const f16*>(y), pair_row, T_, kk, H,
-                                                     static_cast<f16*>(out)), ::sb::count_launch());
+                                                     static_cast<f16*>(out), T_dev, 0), ::sb::count_launch());
   }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;

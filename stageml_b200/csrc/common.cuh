@@ -27,6 +27,7 @@ enum DeviceError : int {
   kDevTimeoutMma = 102,        // MMA issuer gave up waiting for a loaded stage / free accumulator
   kDevTimeoutEpilogue = 103,   // epilogue gave up waiting for a finished accumulator
   kDevTimeoutDrain = 104,      // abort path: in-flight copies / MMAs did not drain
+  kDevTimeoutPeer = 105,       // expert parallel: another GPU did not signal within the bound
   kDevBadIndex = 110,          // an index input was out of range (expert id, tenant id, ...)
 };
 

@@ -25,7 +25,8 @@ size_t permute_scratch_bytes(int64_t num_pairs, int64_t nkeys);
 void permute_carve(void* base, int64_t num_pairs, int64_t nkeys, PermuteScratch* out);
 int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
                    int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
-                   const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream);
+                   const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream,
+                   const int32_t* T_dev = nullptr);  // T_dev: optional device count of valid tokens
 
 // shrink.cu: gather rows and/or LoRA shrink partials (split-K), then reduce.
 struct ShrinkLaunch {
@@ -53,7 +54,7 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream);
 
 // combine.cu: out[t] = sum_j Y[pair_row[t*kk + j]]
 int launch_combine(const void* y, const int32_t* pair_row, int T, int kk, int H, int dtype_bf16, void* out,
-                   cudaStream_t stream);
+                   cudaStream_t stream, const int32_t* T_dev = nullptr);  // rows >= *T_dev left untouched
 // clamp caller tenant ids into [-1, n_tenants) (invalid -> -1 + status)
 int launch_validate_tenants(const int32_t* in, int64_t n, int n_tenants, int32_t* out, int32_t* status,
                             cudaStream_t stream);

@@ -31,7 +31,15 @@ struct PairSrc {
   const int32_t* tenant_ids;
   int T, k, kk, E_routed, E_tot, n_tenants, group_by_tenant, tkeys;
   int64_t P;
+  const int32_t* T_dev;  // optional: tokens >= *T_dev are not routed (no error)
 };
+
+// Pairs that exist: all P, or those of the first *T_dev tokens.
+__device__ __forceinline__ int64_t live_pairs(const PairSrc& a) {
+  if (!a.T_dev) return a.P;
+  const int64_t n = (int64_t)(*a.T_dev) * a.kk;
+  return n < a.P ? (n < 0 ? 0 : n) : a.P;
+}
 
 __device__ __forceinline__ int pair_expert(const PairSrc& a, int t, int j, bool* bad) {
   if (j >= a.k) return a.E_routed + (j - a.k);
@@ -119,12 +127,14 @@ __global__ void __launch_bounds__(1024) perm_count_kernel(PairSrc a, int nkeys, 
                                                            int32_t* hist, int32_t* status) {
   __shared__ uint32_t s[kPermChunk];
   const int64_t base = (int64_t)blockIdx.x * kPermChunk;
+  const int64_t live = live_pairs(a);
   for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
     const int64_t p = base + i;
-    s[i] = (p < a.P) ? ((pair_key(a, p, status) << 11) | (uint32_t)i) : 0xFFFFFFFFu;
+    s[i] = (p < live) ? ((pair_key(a, p, status) << 11) | (uint32_t)i) : 0xFFFFFFFFu;
   }
   __syncthreads();
-  bitonic_sort_2048(s, a.P - base < kPermChunk ? (int)(a.P - base) : kPermChunk);
+  const int64_t n_live = live - base;
+  bitonic_sort_2048(s, n_live <= 0 ? 0 : (n_live < kPermChunk ? (int)n_live : kPermChunk));
   for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
     const uint32_t v = s[i];
     sorted_out[base + i] = v;
@@ -285,7 +295,8 @@ void permute_carve(void* base, int64_t P, int64_t nkeys, PermuteScratch* out) {
 
 int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
                    int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
-                   const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream) {
+                   const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream,
+                   const int32_t* T_dev) {
   SB_CHECK_ARG(T >= 0 && k >= 0 && n_shared >= 0, "permute: negative size");
   SB_CHECK_ARG(k + n_shared >= 1, "permute: need at least one slot per token");
   SB_CHECK_ARG(n_experts_total > n_shared || (k == 0 && n_experts_total == n_shared),
@@ -324,6 +335,7 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
   a.group_by_tenant = group_by_tenant;
   a.tkeys = group_by_tenant ? 1 : n_tenants + 1;
   a.P = P;
+  a.T_dev = T_dev;
 
   const int64_t nch = nchunks_of(P);
   if (nch > 0) {

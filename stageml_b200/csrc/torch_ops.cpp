@@ -105,8 +105,11 @@ Tensor moe_forward(const Tensor& x, const Tensor& gate_up, const Tensor& down, c
                    int64_t rank, const c10::optional<Tensor>& lora_a13, const c10::optional<Tensor>& lora_b13,
                    const c10::optional<Tensor>& lora_a2, const c10::optional<Tensor>& lora_b2,
                    const c10::optional<Tensor>& lora_scale, const c10::optional<Tensor>& gate_up_scale,
-                   const c10::optional<Tensor>& down_scale) {
+                   const c10::optional<Tensor>& down_scale, const c10::optional<Tensor>& T_dev) {
   TORCH_CHECK(x.dim() == 2 && gate_up.dim() == 3 && down.dim() == 3, "moe_forward: bad ranks");
+  if (T_dev.has_value())
+    TORCH_CHECK(T_dev->is_cuda() && T_dev->scalar_type() == at::kInt && T_dev->numel() >= 1,
+                "moe_forward: T_dev must be a CUDA int32 tensor");
   const int64_t T = x.size(0), H = x.size(1), E_tot = gate_up.size(0), I = gate_up.size(1) / 2;
   TORCH_CHECK(gate_up.size(2) == H && down.size(0) == E_tot && down.size(1) == H && down.size(2) == I,
               "moe_forward: weight shapes do not match x");
@@ -164,6 +167,7 @@ Tensor moe_forward(const Tensor& x, const Tensor& gate_up, const Tensor& down, c
   a.lora_scale = static_cast<const float*>(opt_ptr(lora_scale));
   a.out = out.data_ptr();
   a.status = status_word(x);
+  a.T_dev = static_cast<const int32_t*>(opt_ptr(T_dev));
   const size_t ws = stageml_moe_workspace_bytes(&a);
   TORCH_CHECK(ws > 0 || T == 0, "moe_forward: invalid arguments: ", stageml_last_error());
   auto w = workspace(ws, x);
@@ -412,7 +416,7 @@ TORCH_LIBRARY(stageml, m) {
       "moe_forward(Tensor x, Tensor gate_up, Tensor down, Tensor? topk_weights, Tensor? topk_ids, Tensor? router_w, "
       "int k, int n_shared, bool renormalize, Tensor? tenant_ids, int n_tenants, int rank, Tensor? lora_a13, "
       "Tensor? lora_b13, Tensor? lora_a2, Tensor? lora_b2, Tensor? lora_scale, Tensor? gate_up_scale, "
-      "Tensor? down_scale) -> Tensor");
+      "Tensor? down_scale, Tensor? T_dev=None) -> Tensor");
   m.def("route_topk(Tensor x, Tensor gate_w, int k, bool renormalize) -> (Tensor, Tensor, Tensor)");
   m.def("topk_from_logits(Tensor logits, int k, bool renormalize) -> (Tensor, Tensor)");
   m.def(

@@ -148,24 +148,27 @@ def make_moe_workload(cfg: MoEConfig, *, device="cuda", gen_device: str | None =
     w["router_w"] = g.normal((H, E), 1.0 / math.sqrt(H), torch.float32).t().contiguous()
     w["gate_up"] = g.normal_stacked(Et, (2 * I, H), 1.0 / math.sqrt(H), act)
     w["down"] = g.normal_stacked(Et, (H, I), 1.0 / math.sqrt(I), act)
-    a13 = g.normal_stacked(nT * Et, (2 * r, H), 1.0 / math.sqrt(H), act).view(nT, Et, 2 * r, H)
-    b13 = g.normal_stacked(nT * Et, (2 * I, r), 1.0 / math.sqrt(r), act).view(nT, Et, 2 * I, r)
-    a2 = g.normal_stacked(nT * Et, (r, I), 1.0 / math.sqrt(I), act).view(nT, Et, r, I)
-    b2 = g.normal_stacked(nT * Et, (H, r), 1.0 / math.sqrt(r), act).view(nT, Et, H, r)
-    rp = cfg.bank_rank
-    if rp != r:
-        pad = lambda t, dim: torch.cat([t, t.new_zeros(t.shape[:dim] + (rp - r,) + t.shape[dim + 1:])], dim)
-        a13 = torch.cat([pad(a13[:, :, :r], 2), pad(a13[:, :, r:], 2)], 2).contiguous()
-        b13 = pad(b13, 3).contiguous()
-        a2 = pad(a2, 2).contiguous()
-        b2 = pad(b2, 3).contiguous()
-        r = rp
-    if "w1" not in cfg.lora_on:
-        a13[:, :, :r].zero_()
-    if "w3" not in cfg.lora_on:
-        a13[:, :, r:].zero_()
-    w["lora_a13"], w["lora_b13"] = a13, b13
-    w["lora_a2"], w["lora_b2"] = (a2, b2) if "w2" in cfg.lora_on else (None, None)
+    if r == 0:  # no adapters
+        w["lora_a13"] = w["lora_b13"] = w["lora_a2"] = w["lora_b2"] = None
+    else:
+        a13 = g.normal_stacked(nT * Et, (2 * r, H), 1.0 / math.sqrt(H), act).view(nT, Et, 2 * r, H)
+        b13 = g.normal_stacked(nT * Et, (2 * I, r), 1.0 / math.sqrt(r), act).view(nT, Et, 2 * I, r)
+        a2 = g.normal_stacked(nT * Et, (r, I), 1.0 / math.sqrt(I), act).view(nT, Et, r, I)
+        b2 = g.normal_stacked(nT * Et, (H, r), 1.0 / math.sqrt(r), act).view(nT, Et, H, r)
+        rp = cfg.bank_rank
+        if rp != r:
+            pad = lambda t, dim: torch.cat([t, t.new_zeros(t.shape[:dim] + (rp - r,) + t.shape[dim + 1:])], dim)
+            a13 = torch.cat([pad(a13[:, :, :r], 2), pad(a13[:, :, r:], 2)], 2).contiguous()
+            b13 = pad(b13, 3).contiguous()
+            a2 = pad(a2, 2).contiguous()
+            b2 = pad(b2, 3).contiguous()
+            r = rp
+        if "w1" not in cfg.lora_on:
+            a13[:, :, :r].zero_()
+        if "w3" not in cfg.lora_on:
+            a13[:, :, r:].zero_()
+        w["lora_a13"], w["lora_b13"] = a13, b13
+        w["lora_a2"], w["lora_b2"] = (a2, b2) if "w2" in cfg.lora_on else (None, None)
     w["lora_scale"] = torch.full((nT,), cfg.lora_scale, dtype=torch.float32, device=device)
     ten = sample_tenants(T, nT, cfg.tenant_dist, cfg.alpha, seed=seed)
     w["tenant_ids"] = torch.tensor(ten, dtype=torch.int32, device=device)
