@@ -91,6 +91,10 @@ struct MoeBuffers {
   int32_t* num_pairs = nullptr;  // [1]
   int32_t* pruns = nullptr;      // [tiles_cap, kMaxRunsPerPair, kPairRunInts]
   int32_t* pnruns = nullptr;     // [tiles_cap]
+  int32_t* singles = nullptr;    // [tiles_cap]: trailing odd tiles, run on the one-CTA kernel
+  int32_t* num_singles = nullptr;
+  int32_t* sruns = nullptr;      // [tiles_cap, kMaxRunsPerTile, 5]: tenant runs of the singles
+  int32_t* snruns = nullptr;
   int32_t* status = nullptr;
   size_t bytes = 0;
 };
@@ -174,9 +178,13 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
   if (gemm_pairs_enabled() && a->weight_dtype != STAGEML_E4M3) {
     b->pairs = c.take<int32_t>((size_t)(rows_cap / 128) * 4);
     b->num_pairs = c.take<int32_t>(1);
+    b->singles = c.take<int32_t>((size_t)(rows_cap / 128));
+    b->num_singles = c.take<int32_t>(1);
     if (lora) {
       b->pruns = c.take<int32_t>(pair_runs_ints(rows_cap / 128));
       b->pnruns = c.take<int32_t>((size_t)(rows_cap / 128));
+      b->sruns = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
+      b->snruns = c.take<int32_t>((size_t)(rows_cap / 128));
     }
   } else if (lora) {
     b->runs = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
@@ -184,6 +192,27 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
   }
   b->status = c.take<int32_t>(1);
   b->bytes = c.off;
+}
+
+// Per host thread and device: a side stream and two events for running the odd tiles
+// of a grouped GEMM next to the CTA-pair kernel.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+int side_stream(SideStream** out) {
+  thread_local SideStream per_dev[64];
+  int dev = 0;
+  SB_CUDA_CHECK(cudaGetDevice(&dev));
+  SB_CHECK_ARG(dev >= 0 && dev < 64, "side stream: device %d", dev);
+  SideStream& ss = per_dev[dev];
+  if (!ss.s) {
+    SB_CUDA_CHECK(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking));
+    SB_CUDA_CHECK(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
+    SB_CUDA_CHECK(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
+  }
+  *out = &ss;
+  return STAGEML_OK;
 }
 
 // Route a GemmLaunch of the MoE layer to the CTA-pair kernel when its pair plan exists.
@@ -197,6 +226,34 @@ void use_pairs(GemmLaunch& g, const MoeBuffers& b, int tiles_cap) {
   g.pairs_cap = tiles_cap;
   g.pair_runs = b.pruns;
   g.pair_nruns = b.pnruns;
+}
+
+// One expert projection of the MoE layer. Decode-sized batches: the skinny GEMM.
+// With a pair plan: full tile pairs on the CTA-pair kernel and the groups' trailing
+// odd tiles on the one-CTA kernel from a side stream, launched right after it so its
+// CTAs take the SMs the persistent pair kernel frees in its last wave (an odd tile
+// in a pair would leave half the pair idle). Otherwise: the one-CTA kernel.
+int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, int tiles_cap, bool skinny, cudaStream_t st) {
+  if (skinny) return launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st);
+  if (!g.pairs || !b.singles) return launch_grouped_gemm(g, st);
+  SideStream* ss = nullptr;
+  SB_TRY(side_stream(&ss));
+  SB_CUDA_CHECK(cudaEventRecord(ss->fork, st));
+  SB_TRY(launch_grouped_gemm(g, st));
+  SB_CUDA_CHECK(cudaStreamWaitEvent(ss->s, ss->fork, 0));
+  GemmLaunch s1 = g;
+  s1.pairs = nullptr;
+  s1.num_pairs_dev = nullptr;
+  s1.pair_runs = s1.pair_nruns = nullptr;
+  s1.tile_list = b.singles;
+  s1.num_tiles_dev = b.num_singles;
+  s1.tiles_cap = tiles_cap;
+  s1.tile_runs = b.sruns;
+  s1.tile_nruns = b.snruns;
+  SB_TRY(launch_grouped_gemm(s1, ss->s));
+  SB_CUDA_CHECK(cudaEventRecord(ss->join, ss->s));
+  SB_CUDA_CHECK(cudaStreamWaitEvent(st, ss->join, 0));
+  return STAGEML_OK;
 }
 
 int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
@@ -239,13 +296,18 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   // Decode-sized batches (at most 16 routed rows in all) stream the weights with the
   // skinny GEMM; larger ones use the tensor-memory GEMM and its tile / pair plan.
   const bool skinny = P <= kSkinnyMaxPairs && a->weight_dtype != STAGEML_E4M3;
-  if (!skinny && b.pairs)
+  if (!skinny && b.pairs) {
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_pair_plan(b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles, tiles_cap, 0,
-                              b.pruns ? b.plan.row_tenant : nullptr, b.pairs, b.num_pairs, b.pruns, b.pnruns, st));
-  else if (!skinny && b.runs)
+                              b.pruns ? b.plan.row_tenant : nullptr, b.pairs, b.num_pairs, b.pruns, b.pnruns, st,
+                              b.singles, b.num_singles));
+    if (b.sruns)
+      SB_STAGE(STAGEML_STAGE_PERMUTE, launch_tile_runs(b.plan.row_tenant, b.num_singles, 0, tiles_cap, b.sruns,
+                                                       b.snruns, st, b.singles));
+  } else if (!skinny && b.runs) {
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
+  }
   // gather + R4 shrink of w1|w3
   {
     ShrinkLaunch s;
@@ -301,9 +363,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP,
-             skinny ? launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st)
-                    : launch_grouped_gemm(g, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, tiles_cap, skinny, st));
   }
   // R4 shrink of h for w2
   if (lora2) {
@@ -357,9 +417,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_DOWN,
-             skinny ? launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st)
-                    : launch_grouped_gemm(g, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, tiles_cap, skinny, st));
   }
   // combine
   SB_STAGE(STAGEML_STAGE_COMBINE,

@@ -59,6 +59,7 @@ struct KParams {
   const int32_t* num_tiles_dev;
   int tiles_cap;
   const int32_t* tile_group;
+  const int32_t* tile_list;   // optional: m-tile i is tile_list[i] (LoRA runs stay indexed by i)
   int64_t m_rows;
   // LoRA
   int rank;
@@ -110,9 +111,9 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
   }
 }
 
-__device__ __forceinline__ int tile_lora_runs(const KParams& p, int m_tile) {
+__device__ __forceinline__ int tile_lora_runs(const KParams& p, int m_pos) {
   if (p.rank == 0) return 0;
-  const int n = p.tile_nruns[m_tile];
+  const int n = p.tile_nruns[m_pos];
   return n < kMaxRunsPerTile ? n : kMaxRunsPerTile;
 }
 
@@ -209,7 +210,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-      const int m_tile = tile % num_m_tiles;
+      const int m_pos = tile % num_m_tiles;
+      const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
       const int n_tile = tile / num_m_tiles;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int a_row = m_tile * BM;
@@ -240,7 +242,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         last_phase[s] = (int)ph;
       }
       // LoRA blocks: S of the tile + B rows of each tenant run
-      const int nruns = ok ? tile_lora_runs(p, m_tile) : 0;
+      const int nruns = ok ? tile_lora_runs(p, m_pos) : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -257,7 +259,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           if (p.swiglu) tma_load_2d(base + (p.lchunks + ch) * LCHUNK, &tm_s, bar, p.rank + ch * 16, a_row, pol_a);
         }
         for (int jj = 0; jj < nr; ++jj) {
-          const int tenant = p.tile_runs[((int64_t)m_tile * kMaxRunsPerTile + r0 + jj) * 5];
+          const int tenant = p.tile_runs[((int64_t)m_pos * kMaxRunsPerTile + r0 + jj) * 5];
           const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
@@ -290,7 +292,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
-      const int m_tile = tile % num_m_tiles;
+      const int m_pos = tile % num_m_tiles;
       if (!mbar_wait(tempty_bar(acc), aph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
         ok = false;
         break;
@@ -314,7 +316,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         tc_commit(empty_bar(s));
         issued_any = true;
       }
-      const int nruns = ok ? tile_lora_runs(p, m_tile) : 0;
+      const int nruns = ok ? tile_lora_runs(p, m_pos) : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         tc_fence_after();
         const uint32_t base = smem_base + s * STAGE_BYTES;
         for (int jj = 0; jj < nr; ++jj) {
-          const int32_t* run = p.tile_runs + ((int64_t)m_tile * kMaxRunsPerTile + r0 + jj) * 5;
+          const int32_t* run = p.tile_runs + ((int64_t)m_pos * kMaxRunsPerTile + r0 + jj) * 5;
           const uint32_t d0 = ~(uint32_t)run[1], d1 = ~(uint32_t)run[2], d2 = ~(uint32_t)run[3],
                          d3 = ~(uint32_t)run[4];
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
@@ -364,7 +366,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       const uint32_t aph = (tcount >> 1) & 1;
       if (!mbar_wait(tfull_bar(acc), aph, abort_flag, p.status, p.timeout_ns, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const int m_tile = tile % num_m_tiles;
+      const int m_pos = tile % num_m_tiles;
+      const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
       const int n_tile = tile / num_m_tiles;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int64_t row = (int64_t)m_tile * BM + row_in_tile;
@@ -438,7 +441,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     const int ct = threadIdx.x - 192;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-      const int m_tile = tile % num_m_tiles;
+      const int m_pos = tile % num_m_tiles;
+      const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
       const int n_tile = tile / num_m_tiles;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
@@ -478,7 +482,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         fence_proxy_async_smem();
         mbar_arrive(full_bar(s));
       }
-      const int nruns = ok ? tile_lora_runs(p, m_tile) : 0;
+      const int nruns = ok ? tile_lora_runs(p, m_pos) : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -504,17 +508,19 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
 __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restrict__ row_tenant,
                                                         const int32_t* __restrict__ num_tiles_dev,
                                                         int64_t static_rows, int tiles_cap, int32_t* __restrict__ runs,
-                                                        int32_t* __restrict__ nruns) {
+                                                        int32_t* __restrict__ nruns,
+                                                        const int32_t* __restrict__ tile_list) {
   __shared__ int32_t s_ten[4][kMaxRunsPerTile];
   __shared__ uint32_t s_mask[4][kMaxRunsPerTile][4];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x * 4 + w;
+  const int tile = blockIdx.x * 4 + w;  // entry of the output (and of tile_list)
   const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
   if (tile >= ntiles) return;
-  const int64_t rows_active = num_tiles_dev ? (int64_t)ntiles * 128 : static_rows;
+  const int64_t src_tile = tile_list ? tile_list[tile] : tile;
+  const int64_t rows_active = tile_list ? INT64_MAX : (num_tiles_dev ? (int64_t)ntiles * 128 : static_rows);
   int count = 0;
   for (int q = 0; q < 4; ++q) {
-    const int64_t row = (int64_t)tile * 128 + q * 32 + lane;
+    const int64_t row = src_tile * 128 + q * 32 + lane;
     const int t = row < rows_active ? row_tenant[row] : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, t);
     const bool leader = (t >= 0) && ((peers & ((1u << lane) - 1u)) == 0u);
@@ -563,12 +569,13 @@ int launch_kernel(int grid, cudaStream_t stream, const CUtensorMap& tm_a, const 
 }  // namespace
 
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
-                     int32_t* runs, int32_t* nruns, cudaStream_t stream) {
+                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list) {
   SB_CHECK_ARG(row_tenant && runs && nruns, "tile_runs: null pointer");
+  SB_CHECK_ARG(!tile_list || num_tiles_dev, "tile_runs: a tile list needs its device count");
   const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
   if (tiles == 0) return STAGEML_OK;
   (tile_runs_kernel<<<(unsigned)((tiles + 3) / 4), 128, 0, stream>>>(row_tenant, num_tiles_dev, static_rows,
-                                                                     tiles_cap, runs, nruns),
+                                                                     tiles_cap, runs, nruns, tile_list),
    ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
@@ -620,6 +627,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.num_tiles_dev = g.num_tiles_dev;
   p.tiles_cap = g.tiles_cap;
   p.tile_group = g.tile_group;
+  p.tile_list = g.tile_list;
   p.m_rows = g.m_rows;
   p.rank = g.rank;
   p.lchunks = g.rank / 16;

@@ -41,6 +41,7 @@ struct GemmLaunch {
   const int32_t* num_tiles_dev = nullptr;
   int tiles_cap = 0;
   const int32_t* tile_group = nullptr;
+  const int32_t* tile_list = nullptr;  // one-CTA kernel: process tiles tile_list[0 .. *num_tiles_dev)
   int64_t m_rows = 0;            // direct mode row count
   // LoRA (tensor-core expand)
   int rank = 0;                          // 0, 16 or 32
@@ -77,7 +78,9 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 // Rows with tenant < 0 belong to no run. Active rows: 128 * (*num_tiles_dev)
 // (capped at tiles_cap tiles) or static_rows when num_tiles_dev is null.
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
-                     int32_t* runs, int32_t* nruns, cudaStream_t stream);
+                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list = nullptr);
+// With tile_list, entry i covers tile tile_list[i] (i < *num_tiles_dev) and runs / nruns
+// are indexed by i.
 constexpr int kMaxRunsPerTile = 128;
 
 // CTA-pair variant of the grouped GEMM: 256-row tiles made of two 128-row tiles
@@ -96,7 +99,11 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream);
 // words over the pair's 256 rows; nruns[pair].
 int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
-                     int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream);
+                     int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream,
+                     int32_t* singles = nullptr, int32_t* num_singles = nullptr);
+// With `singles`, a group's trailing odd tile is listed there (count in *num_singles)
+// instead of forming a pair with an idle half; the one-CTA kernel runs those tiles
+// (GemmLaunch::tile_list).
 size_t pair_runs_ints(int64_t pairs_cap);
 
 // Weight-streaming variant for at most 16 valid rows per 128-row tile (decode-sized

@@ -440,58 +440,76 @@ __global__ void __launch_bounds__(THREADS, 1)
 // ------------------------------------------------------------ pair list
 // One CTA: pairs of consecutive 128-row tiles of the same group. Tile t opens a
 // pair when its distance from its group's first tile is even; its partner is
-// t + 1 when that tile exists and belongs to the same group, else -1. Each pair
-// also records its group's first pair and pair count (for the unit order).
+// t + 1 when that tile exists and belongs to the same group. A group's trailing
+// odd tile goes to `singles` when that list is given (for the one-CTA kernel),
+// else it forms a pair with an idle half (-1). Each pair also records its
+// group's first pair and pair count (for the unit order).
 __global__ void __launch_bounds__(1024) pair_tiles_kernel(const int32_t* __restrict__ tile_group,
                                                           const int32_t* __restrict__ group_offsets,
                                                           const int32_t* __restrict__ num_tiles_dev, int tiles_cap,
                                                           int64_t static_rows, int32_t* __restrict__ pairs,
-                                                          int32_t* __restrict__ num_pairs_out) {
-  __shared__ int32_t warp_tot[32];
-  __shared__ int32_t carry;
+                                                          int32_t* __restrict__ num_pairs_out,
+                                                          int32_t* __restrict__ singles,
+                                                          int32_t* __restrict__ num_singles_out) {
+  __shared__ int32_t warp_tot[2][32];
+  __shared__ int32_t carry[2];
   const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  if (tid == 0) carry = 0;
+  const bool split = singles != nullptr;
+  if (tid < 2) carry[tid] = 0;
   __syncthreads();
   for (int base = 0; base < ntiles; base += 1024) {
     const int t = base + tid;
-    int start = 0, partner = -1, in_group = 0, group_pairs = 0;
+    int start = 0, partner = -1, in_group = 0, group_tiles = 0;
     if (t < ntiles) {
       if (tile_group) {
         const int g = tile_group[t];
         const int t0 = group_offsets[g] >> 7;
         in_group = (t - t0) >> 1;
-        group_pairs = (((group_offsets[g + 1] - group_offsets[g]) >> 7) + 1) >> 1;
+        group_tiles = (group_offsets[g + 1] - group_offsets[g]) >> 7;
         start = ((t - t0) & 1) == 0;
         if (start && t + 1 < ntiles && tile_group[t + 1] == g) partner = t + 1;
       } else {
         in_group = t >> 1;
-        group_pairs = (ntiles + 1) >> 1;
+        group_tiles = ntiles;
         start = (t & 1) == 0;
         if (start && t + 1 < ntiles) partner = t + 1;
       }
     }
-    const unsigned bal = __ballot_sync(0xffffffffu, start);
-    if (lane == 0) warp_tot[w] = __popc(bal);
+    const bool as_single = split && start && partner < 0;
+    const bool as_pair = start && !as_single;
+    const unsigned bp = __ballot_sync(0xffffffffu, as_pair), bs = __ballot_sync(0xffffffffu, as_single);
+    if (lane == 0) {
+      warp_tot[0][w] = __popc(bp);
+      warp_tot[1][w] = __popc(bs);
+    }
     __syncthreads();
-    int before = carry;
-    for (int i = 0; i < w; ++i) before += warp_tot[i];
-    before += __popc(bal & ((1u << lane) - 1u));
-    if (start) {
+    const unsigned lt = (1u << lane) - 1u;
+    if (as_pair) {
+      int before = carry[0] + __popc(bp & lt);
+      for (int i = 0; i < w; ++i) before += warp_tot[0][i];
       pairs[4 * before] = t;
       pairs[4 * before + 1] = partner;
       pairs[4 * before + 2] = before - in_group;  // the group's first pair
-      pairs[4 * before + 3] = group_pairs;
+      pairs[4 * before + 3] = split ? group_tiles >> 1 : (group_tiles + 1) >> 1;
+    }
+    if (as_single) {
+      int before = carry[1] + __popc(bs & lt);
+      for (int i = 0; i < w; ++i) before += warp_tot[1][i];
+      singles[before] = t;
     }
     __syncthreads();
-    if (tid == 0) {
+    if (tid < 2) {
       int tot = 0;
-      for (int i = 0; i < 32; ++i) tot += warp_tot[i];
-      carry += tot;
+      for (int i = 0; i < 32; ++i) tot += warp_tot[tid][i];
+      carry[tid] += tot;
     }
     __syncthreads();
   }
-  if (tid == 0) *num_pairs_out = carry;
+  if (tid == 0) {
+    *num_pairs_out = carry[0];
+    if (num_singles_out) *num_singles_out = carry[1];
+  }
 }
 
 // One warp per pair: distinct tenants of its 256 rows (first-seen order over the
@@ -590,12 +608,14 @@ size_t pair_runs_ints(int64_t pairs_cap) { return (size_t)pairs_cap * kMaxRunsPe
 
 int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
-                     int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream) {
+                     int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream, int32_t* singles,
+                     int32_t* num_singles) {
   SB_CHECK_ARG(pairs && num_pairs, "pair plan: null output");
+  SB_CHECK_ARG(!singles == !num_singles, "pair plan: singles need their count");
   SB_CHECK_ARG(!tile_group || (group_offsets && num_tiles_dev), "pair plan: grouped tiles need offsets and a count");
   const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
   (pair_tiles_kernel<<<1, 1024, 0, stream>>>(tile_group, group_offsets, num_tiles_dev, tiles_cap, static_rows, pairs,
-                                              num_pairs),
+                                              num_pairs, singles, num_singles),
    ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   if (row_tenant && tiles > 0) {
