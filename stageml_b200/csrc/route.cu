@@ -16,53 +16,92 @@
 namespace sb {
 namespace {
 
-constexpr int RT_TT = 64;      // tokens per CTA
+constexpr int RT_TT = 32;      // tokens per CTA
 constexpr int RT_TE = 64;      // experts per CTA
 constexpr int RT_KC = 32;      // K chunk
-constexpr int RT_PAD = RT_TT + 4;
-constexpr int RT_THREADS = 256;
+constexpr int RT_PAD = RT_TE + 4;
+constexpr int RT_THREADS = 128;
 
-// General case (any E <= 256, gate too large for shared memory): a 64-token x
+// General case (any E <= 256, gate too large for shared memory): a 32-token x
 // 64-expert output tile per CTA; x and G are staged K-major through shared memory
-// in 32-wide chunks and each thread accumulates a 4 x 4 (token, expert) register
-// block, 16 FMAs per two 16-byte shared-memory reads.
-template <typename T>
+// in 32-wide chunks (16-byte global loads when rows are 16-byte aligned) and each
+// thread accumulates a 4 x 4 (token, expert) register block, 16 FMAs per two
+// 16-byte shared-memory reads.
+// Loader of one K chunk: x 32 tokens x 32 K (8 values per thread), G 64 experts x 32 K
+// (16 values per thread), 16-byte global loads when VEC.
+template <typename T, bool VEC>
+__device__ __forceinline__ void router_chunk_load(const T* __restrict__ x, const float* __restrict__ gw, int T_, int H,
+                                                  int E, int t0, int e0, int k0, float (&vx)[8], float (&vg)[2][8]) {
+  const int tid = threadIdx.x;
+  const int r = tid >> 2, kk = (tid & 3) * 8;
+  {
+    const int t = t0 + r, k = k0 + kk;
+    if (VEC && t < T_ && k + 8 <= H) {
+      if (sizeof(T) == 2) {
+        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)t * H + k)), vx);
+      } else {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(x + (int64_t)t * H + k));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(x + (int64_t)t * H + k + 4));
+        vx[0] = a.x, vx[1] = a.y, vx[2] = a.z, vx[3] = a.w, vx[4] = b.x, vx[5] = b.y, vx[6] = b.z, vx[7] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) vx[q] = (t < T_ && k + q < H) ? to_f32<T>(x[(int64_t)t * H + k + q]) : 0.f;
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int e = e0 + r + 32 * h, k = k0 + kk;
+    if (VEC && e < E && k + 8 <= H) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(gw + (int64_t)e * H + k));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(gw + (int64_t)e * H + k + 4));
+      vg[h][0] = a.x, vg[h][1] = a.y, vg[h][2] = a.z, vg[h][3] = a.w;
+      vg[h][4] = b.x, vg[h][5] = b.y, vg[h][6] = b.z, vg[h][7] = b.w;
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) vg[h][q] = (e < E && k + q < H) ? gw[(int64_t)e * H + k + q] : 0.f;
+    }
+  }
+}
+
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(RT_THREADS) router_logits_kernel(const T* __restrict__ x,
                                                                    const float* __restrict__ gw, int T_, int H,
                                                                    int E, float* __restrict__ logits) {
-  __shared__ __align__(16) float xs[RT_KC][RT_PAD];
-  __shared__ __align__(16) float gs[RT_KC][RT_PAD];
+  __shared__ __align__(16) float xs[2][RT_KC][RT_PAD];
+  __shared__ __align__(16) float gs[2][RT_KC][RT_PAD];
   const int t0 = blockIdx.x * RT_TT, e0 = blockIdx.y * RT_TE;
   const int tid = threadIdx.x;
-  const int ty = tid >> 4, tx = tid & 15;
-  const int lr = tid >> 2, lk = (tid & 3) * 8;  // loader: row lr, 8 K values from lk
+  const int ty = tid >> 4, tx = tid & 15;  // tokens ty*4.., experts tx*4..
+  const int r = tid >> 2, kk = (tid & 3) * 8;
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  const bool xrow_ok = t0 + lr < T_, grow_ok = e0 + lr < E;
-  const T* xr = x + (int64_t)(t0 + lr) * H;
-  const float* gr = gw + (int64_t)(e0 + lr) * H;
-  for (int k0 = 0; k0 < H; k0 += RT_KC) {
+  float vx[8], vg[2][8];
+  router_chunk_load<T, VEC>(x, gw, T_, H, E, t0, e0, 0, vx, vg);
+  int buf = 0;
+  for (int k0 = 0; k0 < H; k0 += RT_KC, buf ^= 1) {
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const int k = k0 + lk + q;
-      xs[lk + q][lr] = (xrow_ok && k < H) ? to_f32<T>(xr[k]) : 0.f;
-      gs[lk + q][lr] = (grow_ok && k < H) ? gr[k] : 0.f;
+      xs[buf][kk + q][r] = vx[q];
+      gs[buf][kk + q][r] = vg[0][q];
+      gs[buf][kk + q][r + 32] = vg[1][q];
     }
     __syncthreads();
+    // the next chunk's loads are in flight while this one is multiplied
+    if (k0 + RT_KC < H) router_chunk_load<T, VEC>(x, gw, T_, H, E, t0, e0, k0 + RT_KC, vx, vg);
 #pragma unroll 8
     for (int k = 0; k < RT_KC; ++k) {
-      const float4 a = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&gs[k][tx * 4]);
+      const float4 a = *reinterpret_cast<const float4*>(&xs[buf][k][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&gs[buf][k][tx * 4]);
       const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
-    __syncthreads();
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -320,18 +359,20 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
     return launch(router_logits_smem_kernel<float, 32>, xp);
   }
   const dim3 grid((unsigned)((T_ + RT_TT - 1) / RT_TT), (unsigned)((E + RT_TE - 1) / RT_TE));
-  if (x_dtype == STAGEML_BF16)
-    (router_logits_kernel<bf16><<<grid, RT_THREADS, 0, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E, logits),
-     ::sb::count_launch());
-  else if (x_dtype == STAGEML_F16)
-    (router_logits_kernel<f16><<<grid, RT_THREADS, 0, stream>>>(static_cast<const f16*>(x), gate_w, T_, H, E, logits),
-     ::sb::count_launch());
-  else if (x_dtype == STAGEML_F32)
-    (router_logits_kernel<float><<<grid, RT_THREADS, 0, stream>>>(static_cast<const float*>(x), gate_w, T_, H, E,
-                                                                  logits),
-     ::sb::count_launch());
-  else
+  const bool vec = H % 8 == 0 && aligned;
+  auto launch = [&](auto kern, const auto* xp) { (kern<<<grid, RT_THREADS, 0, stream>>>(xp, gate_w, T_, H, E, logits), ::sb::count_launch()); };
+  if (x_dtype == STAGEML_BF16) {
+    const bf16* xp = static_cast<const bf16*>(x);
+    vec ? launch(router_logits_kernel<bf16, true>, xp) : launch(router_logits_kernel<bf16, false>, xp);
+  } else if (x_dtype == STAGEML_F16) {
+    const f16* xp = static_cast<const f16*>(x);
+    vec ? launch(router_logits_kernel<f16, true>, xp) : launch(router_logits_kernel<f16, false>, xp);
+  } else if (x_dtype == STAGEML_F32) {
+    const float* xp = static_cast<const float*>(x);
+    vec ? launch(router_logits_kernel<float, true>, xp) : launch(router_logits_kernel<float, false>, xp);
+  } else {
     return set_error(STAGEML_ERR_INVALID_ARG, "router: unsupported x dtype %d", x_dtype);
+  }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }

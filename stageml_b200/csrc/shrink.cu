@@ -70,7 +70,8 @@ __device__ __forceinline__ void mma_16816<f16>(float (&c)[4], uint32_t a0, uint3
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   // src-size 0 fills the 16 bytes with zeros (rows without a source, K past the end)
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>

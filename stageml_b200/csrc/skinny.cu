@@ -1,11 +1,13 @@
 // Grouped GEMM for a handful of rows per group (decode-sized batches): at most
 // 16 valid rows in every 128-row tile, so the work is streaming the weights.
 //
-// One CTA computes 8 output columns of one tile: the eight warps split K, each
-// streams its K range of the 8 weight rows (SwiGLU: 8 gate + 8 up rows) with
-// 16-byte loads, eight 32-wide chunks in flight per lane, and multiplies by the
-// tile's rows on warp-level tensor cores (m16n8k16, rows past the valid count
-// are zeros). Partial sums meet in shared memory; the epilogue adds the
+// A work item is 8 output columns of one tile, computed by 1-8 warps that split
+// K; each warp streams its K range of the item's 8 weight rows (SwiGLU: 8 gate +
+// 8 up rows) with 16-byte loads, eight 32-wide chunks in flight per lane, and
+// multiplies by the tile's rows on warp-level tensor cores (m16n8k16, rows past
+// the valid count are zeros). The warps per item follow from K only, so a row's
+// result does not depend on the rest of the batch. Partial sums meet in shared
+// memory; the epilogue adds the
 // per-tenant LoRA expand S . B^T (S = the pre-scaled shrink output), then SwiGLU
 // or the plain scale / bias / routing weight, and stores 16-bit rows. The same
 // computation as the grouped tcgen05 GEMM (grouped_gemm.cu) for the
@@ -72,6 +74,15 @@ __device__ __forceinline__ void sk_mma<f16>(float (&c)[4], uint32_t a0, uint32_t
 }
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// Weight stream: read-only, and L2 fetches the surrounding 256 bytes (a warp load
+// touches 64 contiguous bytes of each of 8 rows; the next chunks follow right after).
+__device__ __forceinline__ uint4 ldg16_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
 
 // Lane (g, tig) holds 8 consecutive K values (16 bytes) of rows g, g+8 and of
 // weight row g; the two MMAs read them as logical k = {2tig, 2tig+1, 2tig+8,
@@ -85,114 +96,141 @@ __device__ __forceinline__ void sk_chunk(float (&acc)[NBLK][4], const uint4& xl,
   }
 }
 
-template <typename T, bool SWIGLU>
-__global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkParams p) {
+// Item = (tile, 8 output columns), computed by WPI warps that split K; the partial sums of
+// an item meet in shared memory and its first warp runs the epilogue from the
+// MMA fragment: lane (g, tig) owns rows g, g+8 and columns 2tig, 2tig+1.
+template <typename T, bool SWIGLU, int WPI>
+__global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkParams p, int n_items) {
   constexpr int NBLK = SWIGLU ? 2 : 1;
-  __shared__ float red[kSkWarps][NBLK][32][4];
-  __shared__ float tile[NBLK][16][kSkNB];
-  const int m = blockIdx.y;
-  const int ntiles = p.tile_group ? min(*p.num_tiles_dev, p.tiles_cap) : (int)((p.m_rows + 127) / 128);
-  if (m >= ntiles) return;
-  const int group = p.tile_group ? p.tile_group[m] : 0;
-  int64_t valid;
-  if (p.tile_group)
-    valid = (int64_t)p.group_counts[group] - ((int64_t)m * 128 - p.group_offsets[group]);
-  else
-    valid = p.m_rows - (int64_t)m * 128;
-  valid = valid < 0 ? 0 : (valid > 16 ? 16 : valid);
-  if (valid == 0) return;
-  const int n0 = blockIdx.x * kSkNB;
+  constexpr int IPC = kSkWarps / WPI;  // items per CTA
+  __shared__ float red[WPI > 1 ? kSkWarps : 1][NBLK][32][4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = warp / WPI, part = warp - slot * WPI;
   const int g = lane >> 2, tig = lane & 3;
+  const int nblocks = (p.N + kSkNB - 1) / kSkNB;
+  const int item = blockIdx.x * IPC + slot;
+  const int m = item / nblocks, n0 = (item - m * nblocks) * kSkNB;
+  const int ntiles = p.tile_group ? min(*p.num_tiles_dev, p.tiles_cap) : (int)((p.m_rows + 127) / 128);
+  int group = 0;
+  int64_t valid = 0;
+  if (item < n_items && m < ntiles) {
+    group = p.tile_group ? p.tile_group[m] : 0;
+    valid = p.tile_group ? (int64_t)p.group_counts[group] - ((int64_t)m * 128 - p.group_offsets[group])
+                         : p.m_rows - (int64_t)m * 128;
+    valid = valid < 0 ? 0 : (valid > 16 ? 16 : valid);
+  }
   const int K = p.K;
   const T* A = static_cast<const T*>(p.a);
   const T* W = static_cast<const T*>(p.b);
   const int64_t row0 = (int64_t)m * 128;
-  const T* x_lo = g < valid ? A + (row0 + g) * K : nullptr;
-  const T* x_hi = g + 8 < valid ? A + (row0 + g + 8) * K : nullptr;
-  const T* wrow[NBLK];
-#pragma unroll
-  for (int b = 0; b < NBLK; ++b) {
-    const int64_t r = (int64_t)group * p.b_group_rows + n0 + g + (b ? p.N : 0);
-    wrow[b] = (n0 + g < p.N && r < p.b_rows_total) ? W + r * K : nullptr;
-  }
-  // this warp's K range, a multiple of 32 wide
-  const int kw = ((K + kSkWarps * 32 - 1) / (kSkWarps * 32)) * 32;
-  const int kb = warp * kw, ke = min(K, kb + kw);
   float acc[NBLK][4];
 #pragma unroll
   for (int b = 0; b < NBLK; ++b)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[b][j] = 0.f;
-  const uint4 z = make_uint4(0, 0, 0, 0);
-  for (int k0 = kb; k0 < ke; k0 += 32 * kSkUnroll) {
-    uint4 xl[kSkUnroll], xh[kSkUnroll], w[kSkUnroll][NBLK];
+  if (valid > 0) {  // warp-uniform
+    const T* x_lo = g < valid ? A + (row0 + g) * K : nullptr;
+    const T* x_hi = g + 8 < valid ? A + (row0 + g + 8) * K : nullptr;
+    const T* wrow[NBLK];
 #pragma unroll
-    for (int u = 0; u < kSkUnroll; ++u) {
-      const int kk = k0 + u * 32 + tig * 8;
-      const bool v = kk < ke;
-      xl[u] = (v && x_lo) ? ldg16(x_lo + kk) : z;
-      xh[u] = (v && x_hi) ? ldg16(x_hi + kk) : z;
-#pragma unroll
-      for (int b = 0; b < NBLK; ++b) w[u][b] = (v && wrow[b]) ? ldg16(wrow[b] + kk) : z;
+    for (int b = 0; b < NBLK; ++b) {
+      const int64_t r = (int64_t)group * p.b_group_rows + n0 + g + (b ? p.N : 0);
+      wrow[b] = (n0 + g < p.N && r < p.b_rows_total) ? W + r * K : nullptr;
     }
+    const int kw = ((K + WPI * 32 - 1) / (WPI * 32)) * 32;
+    const int kb = part * kw, ke = min(K, kb + kw);
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int k0 = kb; k0 < ke; k0 += 32 * kSkUnroll) {
+      uint4 xl[kSkUnroll], xh[kSkUnroll], w[kSkUnroll][NBLK];
 #pragma unroll
-    for (int u = 0; u < kSkUnroll; ++u) sk_chunk<T, NBLK>(acc, xl[u], xh[u], w[u]);
-  }
+      for (int u = 0; u < kSkUnroll; ++u) {
+        const int kk = k0 + u * 32 + tig * 8;
+        const bool v = kk < ke;
+        xl[u] = (v && x_lo) ? ldg16(x_lo + kk) : z;
+        xh[u] = (v && x_hi) ? ldg16(x_hi + kk) : z;
 #pragma unroll
-  for (int b = 0; b < NBLK; ++b)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) red[warp][b][lane][j] = acc[b][j];
-  __syncthreads();
-  if (threadIdx.x < NBLK * 128) {
-    const int b = threadIdx.x >> 7, e = threadIdx.x & 127;
-    const int l = e >> 2, j = e & 3;
-    float s = 0.f;
-#pragma unroll
-    for (int wv = 0; wv < kSkWarps; ++wv) s += red[wv][b][l][j];
-    const int r = (l >> 2) + (j >= 2 ? 8 : 0), c = (l & 3) * 2 + (j & 1);
-    tile[b][r][c] = s;
-  }
-  __syncthreads();
-  if (threadIdx.x >= 128) return;
-  const int r = threadIdx.x >> 3, c = threadIdx.x & 7;
-  const int col = n0 + c;
-  if (r >= valid || col >= p.N) return;
-  const int64_t row = row0 + r;
-  float v0 = tile[0][r][c];
-  float v1 = SWIGLU ? tile[NBLK - 1][r][c] : 0.f;
-  if (p.rank > 0) {
-    const int t = p.row_tenant[row];
-    if (t >= 0) {
-      const T* S = static_cast<const T*>(p.s16) + row * p.lora_cols;
-      const T* Bl = static_cast<const T*>(p.lora_b) + t * p.lb_tenant_stride + group * p.lb_group_stride;
-      const T* b0 = Bl + (int64_t)col * p.rank;
-      float d0 = 0.f, d1 = 0.f;
-      for (int j = 0; j < p.rank; ++j) d0 += to_f32<T>(S[j]) * to_f32<T>(b0[j]);
-      if (SWIGLU) {
-        const T* b1 = Bl + (int64_t)(p.N + col) * p.rank;
-        for (int j = 0; j < p.rank; ++j) d1 += to_f32<T>(S[p.rank + j]) * to_f32<T>(b1[j]);
+        for (int b = 0; b < NBLK; ++b) w[u][b] = (v && wrow[b]) ? ldg16_stream(wrow[b] + kk) : z;
       }
-      v0 += d0;
-      v1 += d1;
+#pragma unroll
+      for (int u = 0; u < kSkUnroll; ++u) sk_chunk<T, NBLK>(acc, xl[u], xh[u], w[u]);
     }
   }
+  if (WPI > 1) {
+#pragma unroll
+    for (int b = 0; b < NBLK; ++b)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red[WPI > 1 ? warp : 0][b][lane][j] = acc[b][j];
+    __syncthreads();
+    if (part == 0) {
+#pragma unroll
+      for (int q = 1; q < WPI; ++q)
+#pragma unroll
+        for (int b = 0; b < NBLK; ++b)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[b][j] += red[WPI > 1 ? warp + q : 0][b][lane][j];
+    }
+  }
+  if (part != 0 || valid == 0) return;
   T* out = static_cast<T*>(p.out);
-  if (SWIGLU) {
-    if (p.b_scale) {
-      const float* bs = p.b_scale + (int64_t)group * p.b_group_rows;
-      v0 *= bs[col];
-      v1 *= bs[p.N + col];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = g + (j >= 2 ? 8 : 0), c = tig * 2 + (j & 1);
+    const int col = n0 + c;
+    if (r >= valid || col >= p.N) continue;
+    const int64_t row = row0 + r;
+    float v0 = acc[0][j];
+    float v1 = SWIGLU ? acc[NBLK - 1][j] : 0.f;
+    if (p.rank > 0) {
+      const int t = p.row_tenant[row];
+      if (t >= 0) {
+        const T* S = static_cast<const T*>(p.s16) + row * p.lora_cols;
+        const T* Bl = static_cast<const T*>(p.lora_b) + t * p.lb_tenant_stride + group * p.lb_group_stride;
+        const T* b0 = Bl + (int64_t)col * p.rank;
+        float d0 = 0.f, d1 = 0.f;
+        for (int q = 0; q < p.rank; ++q) d0 += to_f32<T>(S[q]) * to_f32<T>(b0[q]);
+        if (SWIGLU) {
+          const T* b1 = Bl + (int64_t)(p.N + col) * p.rank;
+          for (int q = 0; q < p.rank; ++q) d1 += to_f32<T>(S[p.rank + q]) * to_f32<T>(b1[q]);
+        }
+        v0 += d0;
+        v1 += d1;
+      }
     }
-    out[row * p.ldo + col] = from_f32<T>(silu_f32(v0) * v1);
-  } else {
-    if (p.b_scale) v0 *= p.b_scale[(int64_t)group * p.b_group_rows + col];
-    if (p.bias) {
-      const int bg = p.bias_group_mod > 0 ? group % p.bias_group_mod : group;
-      v0 += to_f32<T>(static_cast<const T*>(p.bias)[bg * p.bias_group_stride + col]);
+    if (SWIGLU) {
+      if (p.b_scale) {
+        const float* bs = p.b_scale + (int64_t)group * p.b_group_rows;
+        v0 *= bs[col];
+        v1 *= bs[p.N + col];
+      }
+      out[row * p.ldo + col] = from_f32<T>(silu_f32(v0) * v1);
+    } else {
+      if (p.b_scale) v0 *= p.b_scale[(int64_t)group * p.b_group_rows + col];
+      if (p.bias) {
+        const int bg = p.bias_group_mod > 0 ? group % p.bias_group_mod : group;
+        v0 += to_f32<T>(static_cast<const T*>(p.bias)[bg * p.bias_group_stride + col]);
+      }
+      if (p.row_scale) v0 *= p.row_scale[row];
+      out[row * p.ldo + col] = from_f32<T>(v0);
     }
-    if (p.row_scale) v0 *= p.row_scale[row];
-    out[row * p.ldo + col] = from_f32<T>(v0);
+  }
+}
+
+template <typename T, bool SWIGLU>
+void launch_sk(int wpi, int n_items, const SkParams& p, cudaStream_t stream) {
+  const unsigned grid = (unsigned)(((int64_t)n_items * wpi + kSkWarps - 1) / kSkWarps);
+  switch (wpi) {
+    case 1:
+      (skinny_gemm_kernel<T, SWIGLU, 1><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      break;
+    case 2:
+      (skinny_gemm_kernel<T, SWIGLU, 2><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      break;
+    case 4:
+      (skinny_gemm_kernel<T, SWIGLU, 4><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      break;
+    default:
+      (skinny_gemm_kernel<T, SWIGLU, 8><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      break;
   }
 }
 
@@ -237,19 +275,16 @@ int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int
   p.ldo = g.ldo;
   const int64_t tiles = g.tile_group ? (int64_t)g.tiles_cap : (g.m_rows + 127) / 128;
   if (tiles == 0) return STAGEML_OK;
-  SB_CHECK_ARG(tiles <= 65535, "skinny gemm: too many row tiles");
-  const dim3 grid((unsigned)((g.N + kSkNB - 1) / kSkNB), (unsigned)tiles);
-  if (g.in_bf16) {
-    if (g.swiglu)
-      (skinny_gemm_kernel<bf16, true><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
-    else
-      (skinny_gemm_kernel<bf16, false><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
-  } else {
-    if (g.swiglu)
-      (skinny_gemm_kernel<f16, true><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
-    else
-      (skinny_gemm_kernel<f16, false><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
-  }
+  const int64_t items = tiles * ((g.N + kSkNB - 1) / kSkNB);
+  SB_CHECK_ARG(items * 8 < (int64_t(1) << 31), "skinny gemm: too many output blocks");
+  // Warps per item from K alone (so a row's sums do not depend on the batch): one
+  // warp per ~3-6K of K, at most 8.
+  int wpi = 1;
+  while (wpi < 8 && g.K >= wpi * 2 * 3072) wpi *= 2;
+  if (g.in_bf16)
+    g.swiglu ? launch_sk<bf16, true>(wpi, (int)items, p, stream) : launch_sk<bf16, false>(wpi, (int)items, p, stream);
+  else
+    g.swiglu ? launch_sk<f16, true>(wpi, (int)items, p, stream) : launch_sk<f16, false>(wpi, (int)items, p, stream);
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
