@@ -72,6 +72,116 @@ void carve_plan(Carver& c, int64_t P, int n_groups, stageml_moe_plan* plan) {
   plan->num_tiles = c.take<int32_t>(1);
 }
 
+// ------------------------------------------------------------------ CTA-pair GEMM plan
+// Pairs of 128-row tiles for the CTA-pair grouped GEMM, the groups' trailing odd
+// tiles for the one-CTA kernel, and the tenant runs of both, for one row layout
+// (shared by every GEMM over those rows).
+struct PairPlan {
+  int32_t* pairs = nullptr;      // [tiles_cap, 4]
+  int32_t* num_pairs = nullptr;  // [1]
+  int32_t* pruns = nullptr;      // [tiles_cap, kMaxRunsPerPair, kPairRunInts]
+  int32_t* pnruns = nullptr;     // [tiles_cap]
+  int32_t* singles = nullptr;    // [tiles_cap]
+  int32_t* num_singles = nullptr;
+  int32_t* sruns = nullptr;      // [tiles_cap, kMaxRunsPerTile, 5]
+  int32_t* snruns = nullptr;
+  int tiles_cap = 0;
+  bool on() const { return pairs != nullptr; }
+};
+
+// The grouped GEMMs run on CTA pairs (tcgen05 cta_group::2) unless the
+// environment sets STAGEML_GEMM_PAIRS=0 (one CTA per tile), read once per process.
+bool gemm_pairs_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STAGEML_GEMM_PAIRS");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Pairs pay off once the groups average two tiles: with fewer rows most groups are a
+// single tile, which the plan would route to the one-CTA kernel anyway.
+bool pairs_pay(int64_t rows, int n_groups) { return rows >= 256 * (int64_t)n_groups; }
+
+void carve_pair_plan(Carver& c, int64_t tiles_cap, bool lora, PairPlan* pp) {
+  *pp = PairPlan{};
+  if (!gemm_pairs_enabled() || tiles_cap <= 0) return;
+  pp->tiles_cap = (int)tiles_cap;
+  pp->pairs = c.take<int32_t>((size_t)tiles_cap * 4);
+  pp->num_pairs = c.take<int32_t>(1);
+  pp->singles = c.take<int32_t>((size_t)tiles_cap);
+  pp->num_singles = c.take<int32_t>(1);
+  if (lora) {
+    pp->pruns = c.take<int32_t>(pair_runs_ints(tiles_cap));
+    pp->pnruns = c.take<int32_t>((size_t)tiles_cap);
+    pp->sruns = c.take<int32_t>((size_t)tiles_cap * kMaxRunsPerTile * 5);
+    pp->snruns = c.take<int32_t>((size_t)tiles_cap);
+  }
+}
+
+// Grouped rows (tile_group, group_offsets, num_tiles_dev from a plan) or direct
+// rows (static_rows); row_tenant only when the GEMMs carry LoRA.
+int build_pair_plan(const PairPlan& pp, const int32_t* tile_group, const int32_t* group_offsets,
+                    const int32_t* num_tiles_dev, int64_t static_rows, const int32_t* row_tenant, cudaStream_t st) {
+  SB_TRY(launch_pair_plan(tile_group, group_offsets, num_tiles_dev, pp.tiles_cap, static_rows,
+                          pp.pruns ? row_tenant : nullptr, pp.pairs, pp.num_pairs, pp.pruns, pp.pnruns, st,
+                          pp.singles, pp.num_singles));
+  if (pp.sruns)
+    SB_TRY(launch_tile_runs(row_tenant, pp.num_singles, num_tiles_dev ? 0 : static_rows, pp.tiles_cap, pp.sruns,
+                            pp.snruns, st, pp.singles));
+  return STAGEML_OK;
+}
+
+// Per host thread and device: a side stream and two events for running the odd tiles
+// of a grouped GEMM next to the CTA-pair kernel.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+int side_stream(SideStream** out) {
+  thread_local SideStream per_dev[64];
+  int dev = 0;
+  SB_CUDA_CHECK(cudaGetDevice(&dev));
+  SB_CHECK_ARG(dev >= 0 && dev < 64, "side stream: device %d", dev);
+  SideStream& ss = per_dev[dev];
+  if (!ss.s) {
+    SB_CUDA_CHECK(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking));
+    SB_CUDA_CHECK(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
+    SB_CUDA_CHECK(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
+  }
+  *out = &ss;
+  return STAGEML_OK;
+}
+
+// A grouped GEMM with a pair plan: full tile pairs on the CTA-pair kernel, the
+// trailing odd tiles on the one-CTA kernel from a side stream launched right after
+// it, so their CTAs take the SMs the persistent pair kernel frees in its last wave
+// (an odd tile in a pair would leave half the pair idle). Without a plan (or with
+// e4m3 weights): the one-CTA kernel over all tiles (g.tile_runs set by the caller).
+int run_grouped_gemm(GemmLaunch g, const PairPlan& pp, cudaStream_t st) {
+  if (!pp.on() || g.b_fp8) return launch_grouped_gemm(g, st);
+  GemmLaunch s1 = g;
+  g.pairs = pp.pairs;
+  g.num_pairs_dev = pp.num_pairs;
+  g.pairs_cap = pp.tiles_cap;
+  g.pair_runs = pp.pruns;
+  g.pair_nruns = pp.pnruns;
+  SideStream* ss = nullptr;
+  SB_TRY(side_stream(&ss));
+  SB_CUDA_CHECK(cudaEventRecord(ss->fork, st));
+  SB_TRY(launch_grouped_gemm(g, st));
+  SB_CUDA_CHECK(cudaStreamWaitEvent(ss->s, ss->fork, 0));
+  s1.tile_list = pp.singles;
+  s1.num_tiles_dev = pp.num_singles;
+  s1.tiles_cap = pp.tiles_cap;
+  s1.tile_runs = pp.sruns;
+  s1.tile_nruns = pp.snruns;
+  SB_TRY(launch_grouped_gemm(s1, ss->s));
+  SB_CUDA_CHECK(cudaEventRecord(ss->join, ss->s));
+  SB_CUDA_CHECK(cudaStreamWaitEvent(st, ss->join, 0));
+  return STAGEML_OK;
+}
+
 // ------------------------------------------------------------------ MoE layer
 struct MoeBuffers {
   stageml_moe_plan plan;
@@ -87,14 +197,7 @@ struct MoeBuffers {
   void* s2 = nullptr;    // [rows_cap, r] 16-bit
   int32_t* runs = nullptr;   // [tiles_cap, 128, 5]
   int32_t* nruns = nullptr;  // [tiles_cap]
-  int32_t* pairs = nullptr;      // [tiles_cap, 4] (CTA-pair GEMM)
-  int32_t* num_pairs = nullptr;  // [1]
-  int32_t* pruns = nullptr;      // [tiles_cap, kMaxRunsPerPair, kPairRunInts]
-  int32_t* pnruns = nullptr;     // [tiles_cap]
-  int32_t* singles = nullptr;    // [tiles_cap]: trailing odd tiles, run on the one-CTA kernel
-  int32_t* num_singles = nullptr;
-  int32_t* sruns = nullptr;      // [tiles_cap, kMaxRunsPerTile, 5]: tenant runs of the singles
-  int32_t* snruns = nullptr;
+  PairPlan pp;                   // CTA-pair GEMM plan (16-bit weights)
   int32_t* status = nullptr;
   size_t bytes = 0;
 };
@@ -102,14 +205,6 @@ struct MoeBuffers {
 // The grouped GEMMs run on CTA pairs (tcgen05 cta_group::2) unless the
 // environment sets STAGEML_GEMM_PAIRS=0 (one CTA per tile), read once per process.
 constexpr int64_t kSkinnyMaxPairs = 16;
-
-bool gemm_pairs_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("STAGEML_GEMM_PAIRS");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
 
 int moe_validate(const stageml_moe_args* a, bool check_ptrs = true) {
   SB_CHECK_ARG(a, "moe: null args");
@@ -175,18 +270,8 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
     b->s2 = c.take_bytes((size_t)rows_cap * a->rank * es);
   }
   const bool lora = a->rank > 0 && (a->lora_a13 || a->lora_a2);
-  if (gemm_pairs_enabled() && a->weight_dtype != STAGEML_E4M3) {
-    b->pairs = c.take<int32_t>((size_t)(rows_cap / 128) * 4);
-    b->num_pairs = c.take<int32_t>(1);
-    b->singles = c.take<int32_t>((size_t)(rows_cap / 128));
-    b->num_singles = c.take<int32_t>(1);
-    if (lora) {
-      b->pruns = c.take<int32_t>(pair_runs_ints(rows_cap / 128));
-      b->pnruns = c.take<int32_t>((size_t)(rows_cap / 128));
-      b->sruns = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
-      b->snruns = c.take<int32_t>((size_t)(rows_cap / 128));
-    }
-  } else if (lora) {
+  if (a->weight_dtype != STAGEML_E4M3 && pairs_pay(P, E_tot)) carve_pair_plan(c, rows_cap / 128, lora, &b->pp);
+  if (!b->pp.on() && lora) {
     b->runs = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
     b->nruns = c.take<int32_t>((size_t)(rows_cap / 128));
   }
@@ -194,66 +279,11 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
   b->bytes = c.off;
 }
 
-// Per host thread and device: a side stream and two events for running the odd tiles
-// of a grouped GEMM next to the CTA-pair kernel.
-struct SideStream {
-  cudaStream_t s = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
-};
-int side_stream(SideStream** out) {
-  thread_local SideStream per_dev[64];
-  int dev = 0;
-  SB_CUDA_CHECK(cudaGetDevice(&dev));
-  SB_CHECK_ARG(dev >= 0 && dev < 64, "side stream: device %d", dev);
-  SideStream& ss = per_dev[dev];
-  if (!ss.s) {
-    SB_CUDA_CHECK(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking));
-    SB_CUDA_CHECK(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
-    SB_CUDA_CHECK(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
-  }
-  *out = &ss;
-  return STAGEML_OK;
-}
-
-// Route a GemmLaunch of the MoE layer to the CTA-pair kernel when its pair plan exists.
-// FP8 weights stay on the one-CTA kernel: in a pair, the odd CTA's converter warps
-// would have to signal the even CTA's MMA issuer across the cluster for every stage,
-// which measured 2.15 ms for the fine-grained gate/up GEMM against 1.4 ms on one CTA.
-void use_pairs(GemmLaunch& g, const MoeBuffers& b, int tiles_cap) {
-  if (!b.pairs || g.b_fp8) return;
-  g.pairs = b.pairs;
-  g.num_pairs_dev = b.num_pairs;
-  g.pairs_cap = tiles_cap;
-  g.pair_runs = b.pruns;
-  g.pair_nruns = b.pnruns;
-}
-
-// One expert projection of the MoE layer. Decode-sized batches: the skinny GEMM.
-// With a pair plan: full tile pairs on the CTA-pair kernel and the groups' trailing
-// odd tiles on the one-CTA kernel from a side stream, launched right after it so its
-// CTAs take the SMs the persistent pair kernel frees in its last wave (an odd tile
-// in a pair would leave half the pair idle). Otherwise: the one-CTA kernel.
-int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, int tiles_cap, bool skinny, cudaStream_t st) {
+// One expert projection of the MoE layer: decode-sized batches on the skinny GEMM,
+// otherwise the grouped GEMM with the layer's pair plan.
+int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, bool skinny, cudaStream_t st) {
   if (skinny) return launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st);
-  if (!g.pairs || !b.singles) return launch_grouped_gemm(g, st);
-  SideStream* ss = nullptr;
-  SB_TRY(side_stream(&ss));
-  SB_CUDA_CHECK(cudaEventRecord(ss->fork, st));
-  SB_TRY(launch_grouped_gemm(g, st));
-  SB_CUDA_CHECK(cudaStreamWaitEvent(ss->s, ss->fork, 0));
-  GemmLaunch s1 = g;
-  s1.pairs = nullptr;
-  s1.num_pairs_dev = nullptr;
-  s1.pair_runs = s1.pair_nruns = nullptr;
-  s1.tile_list = b.singles;
-  s1.num_tiles_dev = b.num_singles;
-  s1.tiles_cap = tiles_cap;
-  s1.tile_runs = b.sruns;
-  s1.tile_nruns = b.snruns;
-  SB_TRY(launch_grouped_gemm(s1, ss->s));
-  SB_CUDA_CHECK(cudaEventRecord(ss->join, ss->s));
-  SB_CUDA_CHECK(cudaStreamWaitEvent(st, ss->join, 0));
-  return STAGEML_OK;
+  return run_grouped_gemm(g, b.pp, st);
 }
 
 int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
@@ -296,14 +326,9 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   // Decode-sized batches (at most 16 routed rows in all) stream the weights with the
   // skinny GEMM; larger ones use the tensor-memory GEMM and its tile / pair plan.
   const bool skinny = P <= kSkinnyMaxPairs && a->weight_dtype != STAGEML_E4M3;
-  if (!skinny && b.pairs) {
-    SB_STAGE(STAGEML_STAGE_PERMUTE,
-             launch_pair_plan(b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles, tiles_cap, 0,
-                              b.pruns ? b.plan.row_tenant : nullptr, b.pairs, b.num_pairs, b.pruns, b.pnruns, st,
-                              b.singles, b.num_singles));
-    if (b.sruns)
-      SB_STAGE(STAGEML_STAGE_PERMUTE, launch_tile_runs(b.plan.row_tenant, b.num_singles, 0, tiles_cap, b.sruns,
-                                                       b.snruns, st, b.singles));
+  if (!skinny && b.pp.on()) {
+    SB_STAGE(STAGEML_STAGE_PERMUTE, build_pair_plan(b.pp, b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles,
+                                                    0, b.plan.row_tenant, st));
   } else if (!skinny && b.runs) {
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
@@ -359,11 +384,10 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     }
     g.b_scale = a->gate_up_scale;
     g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
-    use_pairs(g, b, tiles_cap);
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, tiles_cap, skinny, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, skinny, st));
   }
   // R4 shrink of h for w2
   if (lora2) {
@@ -413,11 +437,10 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.row_scale = b.plan.row_weight;
     g.b_scale = a->down_scale;
     g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
-    use_pairs(g, b, tiles_cap);
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, tiles_cap, skinny, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, skinny, st));
   }
   // combine
   SB_STAGE(STAGEML_STAGE_COMBINE,
@@ -436,6 +459,7 @@ struct LinBuffers {
   void* yp = nullptr;     // permuted output rows [rows_cap, N]
   int32_t* runs = nullptr;
   int32_t* nruns = nullptr;
+  PairPlan pp;
   int32_t* tenants = nullptr;  // direct mode: validated row tenants
   int32_t* status = nullptr;
   size_t bytes = 0;
@@ -457,12 +481,15 @@ void lin_carve(bool permuted, int64_t P_or_M, int n_groups, int n_tenants, int g
     rows = P_or_M;
     b->tenants = c.take<int32_t>((size_t)std::max<int64_t>(rows, 1));
   }
+  const int64_t tiles = (rows + 127) / 128;
+  if (pairs_pay(P_or_M, permuted ? n_groups : 1)) carve_pair_plan(c, tiles, rank > 0, &b->pp);
   if (rank > 0) {
     b->spart = c.take<float>((size_t)shrink_num_slices(K) * rows * rank);
     b->s = c.take_bytes((size_t)rows * rank * es);
-    const int64_t tiles = (rows + 127) / 128;
-    b->runs = c.take<int32_t>((size_t)tiles * kMaxRunsPerTile * 5);
-    b->nruns = c.take<int32_t>((size_t)tiles);
+    if (!b->pp.on()) {
+      b->runs = c.take<int32_t>((size_t)tiles * kMaxRunsPerTile * 5);
+      b->nruns = c.take<int32_t>((size_t)tiles);
+    }
   }
   b->status = c.take<int32_t>(1);
   b->bytes = c.off;
@@ -649,7 +676,10 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
            launch_permute(topk_ids, ids_dtype, topk_weights, weights_dtype, tenant_ids, T, k, 0, E,
                           group_by_tenant || lora ? n_tenants : 0, group_by_tenant, b.plan, stat, scr, st));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
-  if (lora)
+  if (b.pp.on())
+    SB_STAGE(STAGEML_STAGE_PERMUTE, build_pair_plan(b.pp, b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles,
+                                                    0, lora ? b.plan.row_tenant : nullptr, st));
+  else if (lora)
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   ShrinkLaunch sh;
@@ -702,7 +732,7 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
   g.out = b.yp;
   g.ldo = N;
   g.status = stat;
-  SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
+  SB_STAGE(STAGEML_STAGE_GEMM, run_grouped_gemm(g, b.pp, st));
   SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.yp, b.plan.pair_row, T, k, N, bf, out, st));
   return STAGEML_OK;
 }
@@ -790,8 +820,9 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
     if (lora) {
       SB_STAGE(STAGEML_STAGE_GATHER_SHRINK,
                launch_validate_tenants(a->row_tenant, a->M, n_ten, b.tenants, stat, st));
-      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK,
-               launch_tile_runs(b.tenants, nullptr, a->M, (int)((a->M + 127) / 128), b.runs, b.nruns, st));
+      if (!b.pp.on())
+        SB_STAGE(STAGEML_STAGE_GATHER_SHRINK,
+                 launch_tile_runs(b.tenants, nullptr, a->M, (int)((a->M + 127) / 128), b.runs, b.nruns, st));
       sh.src = a->x;
       sh.static_rows = a->M;
       sh.rows_cap = a->M;
@@ -799,12 +830,15 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
       SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
       g.s_rows = a->M;
     }
+    if (b.pp.on())
+      SB_STAGE(STAGEML_STAGE_PERMUTE,
+               build_pair_plan(b.pp, nullptr, nullptr, nullptr, a->M, lora ? b.tenants : nullptr, st));
     g.a = a->x;
     g.a_rows = a->M;
     g.m_rows = a->M;
     g.out = a->y;
     g.ldo = a->N;
-    SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
+    SB_STAGE(STAGEML_STAGE_GEMM, run_grouped_gemm(g, b.pp, st));
     return STAGEML_OK;
   }
   PermuteScratch scr;
@@ -813,7 +847,10 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
            launch_permute(a->row_group, STAGEML_I32, nullptr, STAGEML_F32, lora ? a->row_tenant : nullptr, a->M, 1, 0,
                           a->n_groups, n_ten, 0, b.plan, stat, scr, st));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
-  if (lora)
+  if (b.pp.on())
+    SB_STAGE(STAGEML_STAGE_PERMUTE, build_pair_plan(b.pp, b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles,
+                                                    0, lora ? b.plan.row_tenant : nullptr, st));
+  else if (lora)
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   sh.src = a->x;
@@ -832,7 +869,7 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   g.s_rows = b.plan.rows_cap;
   g.out = b.yp;
   g.ldo = a->N;
-  SB_STAGE(STAGEML_STAGE_GEMM, launch_grouped_gemm(g, st));
+  SB_STAGE(STAGEML_STAGE_GEMM, run_grouped_gemm(g, b.pp, st));
   SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.yp, b.plan.pair_row, a->M, 1, a->N, bf, a->y, st));
   return STAGEML_OK;
 }

@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
-  const int num_m_tiles = p.tile_group ? min(*p.num_tiles_dev, p.tiles_cap) : (int)((p.m_rows + BM - 1) / BM);
+  const int num_m_tiles = (p.tile_group || p.tile_list) ? min(*p.num_tiles_dev, p.tiles_cap)
+                                                        : (int)((p.m_rows + BM - 1) / BM);
   const int total_tiles = num_m_tiles * p.num_n_tiles;
   const int num_kb = (p.K + BK - 1) / BK;
   volatile int never_abort = 0;  // the drain waits below ignore the abort flag
@@ -517,7 +518,8 @@ __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restric
   const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
   if (tile >= ntiles) return;
   const int64_t src_tile = tile_list ? tile_list[tile] : tile;
-  const int64_t rows_active = tile_list ? INT64_MAX : (num_tiles_dev ? (int64_t)ntiles * 128 : static_rows);
+  const int64_t rows_active = tile_list ? (static_rows > 0 ? static_rows : INT64_MAX)
+                                        : (num_tiles_dev ? (int64_t)ntiles * 128 : static_rows);
   int count = 0;
   for (int q = 0; q < 4; ++q) {
     const int64_t row = src_tile * 128 + q * 32 + lane;
@@ -649,7 +651,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.status = g.status;
   p.timeout_ns = kDefaultWaitNs;
 
-  int64_t tiles_upper = g.tile_group ? (int64_t)g.tiles_cap : (g.m_rows + BM - 1) / BM;
+  int64_t tiles_upper = (g.tile_group || g.tile_list) ? (int64_t)g.tiles_cap : (g.m_rows + BM - 1) / BM;
   tiles_upper *= p.num_n_tiles;
   if (tiles_upper == 0) return STAGEML_OK;
   const int grid = (int)std::min<int64_t>(tiles_upper, sm_count());

@@ -80,7 +80,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
                      int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list = nullptr);
 // With tile_list, entry i covers tile tile_list[i] (i < *num_tiles_dev) and runs / nruns
-// are indexed by i.
+// are indexed by i; static_rows > 0 then bounds the rows read (direct rows).
 constexpr int kMaxRunsPerTile = 128;
 
 // CTA-pair variant of the grouped GEMM: 256-row tiles made of two 128-row tiles
