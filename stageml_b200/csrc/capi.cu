@@ -309,8 +309,8 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   const void* wts = a->topk_weights;
   int wts_dtype = a->weights_dtype;
   if (!ids && a->k > 0) {
-    SB_STAGE(STAGEML_STAGE_ROUTE, launch_router_logits(a->x, a->act_dtype, a->router_w, a->T, a->H, a->E, b.logits, st));
-    SB_STAGE(STAGEML_STAGE_ROUTE, launch_topk(b.logits, a->T, a->E, a->k, a->renormalize, b.ids, b.weights, st));
+    SB_STAGE(STAGEML_STAGE_ROUTE, launch_route(a->x, a->act_dtype, a->router_w, a->T, a->H, a->E, a->k,
+                                               a->renormalize, b.logits, b.ids, b.weights, st));
     ids = b.ids;
     ids_dtype = STAGEML_I32;
     wts = b.weights;
@@ -528,8 +528,7 @@ int stageml_route_topk(const void* x, int x_dtype, const float* gate_w, int T, i
   clear_error();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   SB_CHECK_ARG(logits_out, "route_topk: logits_out is required as scratch ([T, E] fp32)");
-  SB_TRY(launch_router_logits(x, x_dtype, gate_w, T, H, E, logits_out, st));
-  return launch_topk(logits_out, T, E, k, renormalize, ids_out, weights_out, st);
+  return launch_route(x, x_dtype, gate_w, T, H, E, k, renormalize, logits_out, ids_out, weights_out, st);
 }
 
 int stageml_topk_from_logits(const float* logits, int T, int E, int k, int renormalize, int32_t* ids_out,

@@ -12,6 +12,11 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T,
                          cudaStream_t stream);
 int launch_topk(const float* logits, int T, int E, int k, int renorm, int32_t* ids, float* weights,
                 cudaStream_t stream);
+// Router logits + top-k; a few tokens (at most 64, gate and 8 rows per CTA in
+// shared memory) take one fused kernel, otherwise launch_router_logits then
+// launch_topk.
+int launch_route(const void* x, int x_dtype, const float* gate_w, int T, int H, int E, int k, int renorm,
+                 float* logits, int32_t* ids, float* weights, cudaStream_t stream);
 
 // permute.cu
 struct PermuteScratch {

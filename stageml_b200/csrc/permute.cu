@@ -4,7 +4,7 @@
 //
 // The reference groups rows with one torch.nonzero per (slot, expert) and a
 // host sync each (benchmarks/multitenant_bta_system_bench.py:401-406); here the
-// whole grouping is three kernels with no host round trip:
+// whole grouping is three kernels (one when P <= 2048) with no host round trip:
 //   count   one CTA per 2048-pair chunk: bitonic sort of (key << 11 | index)
 //           in shared memory, per-key counts of the chunk -> hist[chunk][key]
 //   scan    one CTA: per-key totals, per-group counts, padded group offsets,
@@ -147,19 +147,12 @@ __global__ void __launch_bounds__(1024) perm_count_kernel(PairSrc a, int nkeys, 
   }
 }
 
-__global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restrict__ hist, int32_t* __restrict__ off,
-                                                          int nkeys, int nchunks, int tkeys, int n_groups,
-                                                          stageml_moe_plan plan) {
-  extern __shared__ int32_t tot[];  // [nkeys]
-  __shared__ int32_t warp_part[32];
+// From the per-key totals tot[nkeys] (in shared memory, 1024 threads): per-group
+// counts, padded group offsets, tile -> group map and padding rows of the plan;
+// tot is left holding each key's first row.
+__device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_groups, const stageml_moe_plan& plan,
+                                            int32_t* warp_part) {
   const int tid = threadIdx.x;
-  // 1. per-key totals (coalesced over keys)
-  for (int key = tid; key < nkeys; key += 1024) {
-    int s = 0;
-    for (int c = 0; c < nchunks; ++c) s += hist[(int64_t)c * nkeys + key];
-    tot[key] = s;
-  }
-  __syncthreads();
   // 2. per-group real counts; padded sizes parked in group_offsets[g]
   for (int g = tid; g < n_groups; g += 1024) {
     int cnt = 0;
@@ -224,6 +217,22 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
     }
   }
   __syncthreads();
+}
+
+__global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restrict__ hist, int32_t* __restrict__ off,
+                                                          int nkeys, int nchunks, int tkeys, int n_groups,
+                                                          stageml_moe_plan plan) {
+  extern __shared__ int32_t tot[];  // [nkeys]
+  __shared__ int32_t warp_part[32];
+  const int tid = threadIdx.x;
+  // 1. per-key totals (coalesced over keys)
+  for (int key = tid; key < nkeys; key += 1024) {
+    int s = 0;
+    for (int c = 0; c < nchunks; ++c) s += hist[(int64_t)c * nkeys + key];
+    tot[key] = s;
+  }
+  __syncthreads();
+  plan_groups(tot, tkeys, n_groups, plan, warp_part);
   // 5. per-(chunk, key) destination offsets
   for (int key = tid; key < nkeys; key += 1024) {
     int b = tot[key];
@@ -233,6 +242,19 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
       b += v;
     }
   }
+}
+
+// Pair p lands in plan row `row`.
+__device__ __forceinline__ void place_pair(const PairSrc& a, const stageml_moe_plan& plan, int64_t p, int row) {
+  const int t = (int)(p / a.kk);
+  const int j = (int)(p - (int64_t)t * a.kk);
+  bool dummy = false;
+  const int tn = pair_tenant(a, t, &dummy);
+  plan.row_token[row] = t;
+  plan.row_tenant[row] = a.group_by_tenant ? -1 : tn;
+  plan.row_weight[row] = pair_weight(a, t, j);
+  plan.row_pair[row] = (int32_t)p;
+  plan.pair_row[p] = row;
 }
 
 __global__ void __launch_bounds__(1024) perm_scatter_kernel(PairSrc a, int nkeys, const uint32_t* __restrict__ sorted,
@@ -251,16 +273,40 @@ __global__ void __launch_bounds__(1024) perm_scatter_kernel(PairSrc a, int nkeys
       continue;
     }
     const int start = lower_bound_key(s, i, key);
-    const int row = off[(int64_t)blockIdx.x * nkeys + key] + (i - start);
-    const int t = (int)(p / a.kk);
-    const int j = (int)(p - (int64_t)t * a.kk);
-    bool dummy = false;
-    const int tn = pair_tenant(a, t, &dummy);
-    plan.row_token[row] = t;
-    plan.row_tenant[row] = a.group_by_tenant ? -1 : tn;
-    plan.row_weight[row] = pair_weight(a, t, j);
-    plan.row_pair[row] = (int32_t)p;
-    plan.pair_row[p] = row;
+    place_pair(a, plan, p, off[(int64_t)blockIdx.x * nkeys + key] + (i - start));
+  }
+}
+
+// P <= 2048 (one chunk): count, scan and scatter in one CTA, the per-key counts
+// in shared memory; the same plan as the three kernels.
+__global__ void __launch_bounds__(1024) perm_fused_kernel(PairSrc a, int nkeys, int n_groups, stageml_moe_plan plan,
+                                                           int32_t* status) {
+  extern __shared__ int32_t tot[];  // [nkeys]
+  __shared__ uint32_t s[kPermChunk];
+  __shared__ int32_t warp_part[32];
+  const int64_t live = live_pairs(a);
+  for (int key = threadIdx.x; key < nkeys; key += 1024) tot[key] = 0;
+  for (int i = threadIdx.x; i < kPermChunk; i += 1024)
+    s[i] = (i < live) ? ((pair_key(a, i, status) << 11) | (uint32_t)i) : 0xFFFFFFFFu;
+  __syncthreads();
+  bitonic_sort_2048(s, live < kPermChunk ? (int)live : kPermChunk);
+  for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
+    const uint32_t key = s[i] >> 11;
+    if (key == kSentKey) continue;
+    if (i == kPermChunk - 1 || (s[i + 1] >> 11) != key) tot[key] = i - lower_bound_key(s, i + 1, key) + 1;
+  }
+  __syncthreads();
+  plan_groups(tot, a.tkeys, n_groups, plan, warp_part);
+  for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
+    const uint32_t v = s[i];
+    const int64_t p = v & 2047u;
+    if (p >= a.P) continue;
+    const uint32_t key = v >> 11;
+    if (key == kSentKey) {
+      plan.pair_row[p] = -1;
+      continue;
+    }
+    place_pair(a, plan, p, tot[key] + (i - lower_bound_key(s, i, key)));
   }
 }
 
@@ -338,12 +384,18 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
   a.T_dev = T_dev;
 
   const int64_t nch = nchunks_of(P);
+  const size_t smem = (size_t)nkeys * 4;
+  if (nch == 1) {
+    SB_CUDA_CHECK(cudaFuncSetAttribute(perm_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    (perm_fused_kernel<<<1, 1024, smem, stream>>>(a, (int)nkeys, n_groups, plan, status), ::sb::count_launch());
+    SB_CUDA_CHECK(cudaGetLastError());
+    return STAGEML_OK;
+  }
   if (nch > 0) {
     SB_CUDA_CHECK(cudaMemsetAsync(scr.hist, 0, (size_t)nkeys * nch * 4, stream));
     (perm_count_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.hist, status), ::sb::count_launch());
     SB_CUDA_CHECK(cudaGetLastError());
   }
-  const size_t smem = (size_t)nkeys * 4;
   SB_CUDA_CHECK(cudaFuncSetAttribute(perm_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   (perm_scan_kernel<<<1, 1024, smem, stream>>>(scr.hist, scr.off, (int)nkeys, (int)nch, a.tkeys, n_groups, plan), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());

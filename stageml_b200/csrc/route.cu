@@ -132,7 +132,31 @@ __device__ __forceinline__ void load_x4(const T* xr, int h, int H, float (&xv)[4
 }
 constexpr int RT_XU = 8;
 
-// Gate resident in shared memory (E*H fp32 <= 200 KB): each CTA copies G once,
+// Bulk-copies `a_bytes` from `a` (and `b_bytes` from `b`) into shared memory at
+// `dst` (b right after a), all in flight at once; every thread of the CTA returns
+// once they landed (false if the bounded wait gave up). Sizes and addresses are
+// multiples of 16 bytes.
+__device__ __forceinline__ bool stage_to_smem(uint32_t dst, const void* a, uint32_t a_bytes, const void* b,
+                                              uint32_t b_bytes, uint64_t* bar, volatile int* abort_flag) {
+  constexpr uint32_t kChunk = 16384;
+  const uint32_t mb = smem_u32(bar);
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    mbar_init(mb, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(mb, a_bytes + b_bytes);
+    for (uint32_t off = 0; off < a_bytes; off += kChunk)
+      bulk_load_1d(dst + off, static_cast<const char*>(a) + off, min(kChunk, a_bytes - off), mb);
+    for (uint32_t off = 0; off < b_bytes; off += kChunk)
+      bulk_load_1d(dst + a_bytes + off, static_cast<const char*>(b) + off, min(kChunk, b_bytes - off), mb);
+  }
+  return mbar_wait(mb, 0, abort_flag, nullptr, kDefaultWaitNs, 0);
+}
+
+// Gate resident in shared memory (E*H fp32 <= 200 KB): each CTA bulk-copies G once,
 // then every warp takes whole tokens; lane l accumulates E partial dot products
 // over columns 4l + 128i with float4 reads of G and 8-byte reads of x, and the
 // warp reduces them with shuffles. E <= 32.
@@ -141,10 +165,9 @@ __global__ void __launch_bounds__(256) router_logits_smem_kernel(const T* __rest
                                                                  int T_, int H, int E, float* __restrict__ logits) {
   extern __shared__ float4 gsm4[];
   float* gsm = reinterpret_cast<float*>(gsm4);
-  const int n = E * H;
-  for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
-    *reinterpret_cast<float4*>(gsm + i) = __ldg(reinterpret_cast<const float4*>(gw + i));
-  __syncthreads();
+  __shared__ uint64_t bar;
+  __shared__ volatile int abort_flag;
+  const bool staged = stage_to_smem(smem_u32(gsm), gw, (uint32_t)(sizeof(float) * E * H), nullptr, 0, &bar, &abort_flag);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   for (int t = blockIdx.x * wpb + warp; t < T_; t += gridDim.x * wpb) {
@@ -180,59 +203,18 @@ __global__ void __launch_bounds__(256) router_logits_smem_kernel(const T* __rest
         float v = acc[e];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) logits[(int64_t)t * E + e] = v;
+        if (lane == 0) logits[(int64_t)t * E + e] = staged ? v : __int_as_float(0x7fc00000);
       }
     }
   }
 }
 
-// Few tokens: one warp per (token, expert), G read from global / L2 and x with
-// RT_XU steps in flight; the per-lane sum order and the shuffle reduction are
-// those of router_logits_smem_kernel, so both give the same logits.
-template <typename T>
-__global__ void __launch_bounds__(128) router_logits_warp_kernel(const T* __restrict__ x, const float* __restrict__ gw,
-                                                                 int T_, int H, int E, float* __restrict__ logits) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t pairs = (int64_t)T_ * E;
-  const int64_t q = (int64_t)blockIdx.x * 4 + warp;
-  if (q >= pairs) return;
-  const int t = (int)(q / E), e = (int)(q - (int64_t)t * E);
-  const T* xr = x + (int64_t)t * H;
-  const float* gr = gw + (int64_t)e * H;
-  float acc = 0.f;
-  for (int h0 = lane * 4; h0 < H; h0 += 128 * RT_XU) {
-    float xv[RT_XU][4];
-    float4 gv[RT_XU];
-#pragma unroll
-    for (int u = 0; u < RT_XU; ++u) {
-      load_x4<T>(xr, h0 + 128 * u, H, xv[u]);
-      gv[u] = h0 + 128 * u < H ? __ldg(reinterpret_cast<const float4*>(gr + h0 + 128 * u)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < RT_XU; ++u) {
-      if (h0 + 128 * u < H) {
-        acc = fmaf(xv[u][0], gv[u].x, acc);
-        acc = fmaf(xv[u][1], gv[u].y, acc);
-        acc = fmaf(xv[u][2], gv[u].z, acc);
-        acc = fmaf(xv[u][3], gv[u].w, acc);
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) logits[(int64_t)t * E + e] = acc;
-}
-
-// One warp per token.
-__global__ void topk_kernel(const float* __restrict__ logits, int T_, int E, int k, int renorm,
-                            int32_t* __restrict__ ids, float* __restrict__ weights) {
-  const int warps_per_block = blockDim.x >> 5;
-  const int t = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T_) return;
+// Softmax over one token's E logits, top-k (ties -> lower expert index) and the
+// optional renormalisation of the k weights; one warp, results written by lane 0.
+__device__ __forceinline__ void topk_row(const float* lrow, int E, int k, int renorm, int lane,
+                                         int32_t* __restrict__ ids_row, float* __restrict__ w_row) {
   constexpr int PER = 8;  // E <= 256
   float v[PER];
-  const float* lrow = logits + (int64_t)t * E;
   float mx = -INFINITY;
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
@@ -288,10 +270,82 @@ __global__ void topk_kernel(const float* __restrict__ logits, int T_, int E, int
     for (int r = 0; r < k; ++r) wsum += sel_w[r];
     const float denom = fmaxf(wsum, 1e-12f);
     for (int r = 0; r < k; ++r) {
-      ids[(int64_t)t * k + r] = sel_e[r];
-      weights[(int64_t)t * k + r] = renorm ? sel_w[r] / denom : sel_w[r];
+      ids_row[r] = sel_e[r];
+      w_row[r] = renorm ? sel_w[r] / denom : sel_w[r];
     }
   }
+}
+
+// One warp per token.
+__global__ void topk_kernel(const float* __restrict__ logits, int T_, int E, int k, int renorm,
+                            int32_t* __restrict__ ids, float* __restrict__ weights) {
+  const int warps_per_block = blockDim.x >> 5;
+  const int t = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T_) return;
+  topk_row(logits + (int64_t)t * E, E, k, renorm, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
+}
+
+constexpr int kRouteSmallT = 8;    // tokens per CTA of router_small_kernel
+constexpr int kRouteSmallMaxT = 64;
+
+// Up to 8 tokens per CTA: G and the CTA's token rows arrive in shared memory by
+// bulk copies, and warp w takes the (token, expert) dot products w, w + 8, ...; each
+// lane's sum over columns 4l + 128i and the shuffle reduction are those of
+// router_logits_smem_kernel, so both kernels give the same logits for a token.
+// The top-k of topk_kernel follows in the same CTA.
+template <typename T>
+__global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__ x, const float* __restrict__ gw,
+                                                           int T_, int H, int E, int k, int renorm,
+                                                           float* __restrict__ logits, int32_t* __restrict__ ids,
+                                                           float* __restrict__ weights) {
+  extern __shared__ float4 sm4[];
+  float* gsm = reinterpret_cast<float*>(sm4);                   // [E, H]
+  const T* xsm = reinterpret_cast<const T*>(gsm + (size_t)E * H);  // [T_, H]
+  __shared__ uint64_t bar;
+  __shared__ volatile int abort_flag;
+  __shared__ float lsm[kRouteSmallT * 32];
+  const int t0 = blockIdx.x * kRouteSmallT;
+  const int nt = min(kRouteSmallT, T_ - t0);
+  const bool staged = stage_to_smem(smem_u32(gsm), gw, (uint32_t)(sizeof(float) * E * H), x + (size_t)t0 * H,
+                                    (uint32_t)(sizeof(T) * nt * H), &bar, &abort_flag);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  logits += (int64_t)t0 * E;
+  ids += (int64_t)t0 * k;
+  weights += (int64_t)t0 * k;
+  for (int u = warp; u < nt * E; u += 8) {
+    const int t = u / E, e = u - t * E;
+    const T* xr = xsm + (size_t)t * H;
+    const float* gr = gsm + (size_t)e * H;
+    float acc = 0.f;
+    for (int h = lane * 4; h < H; h += 128) {
+      float xv[4];
+      if (sizeof(T) == 2) {
+        const uint2 w = *reinterpret_cast<const uint2*>(xr + h);
+        const T* hv = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xv[q] = to_f32<T>(hv[q]);
+      } else {
+        const float4 f = *reinterpret_cast<const float4*>(xr + h);
+        xv[0] = f.x, xv[1] = f.y, xv[2] = f.z, xv[3] = f.w;
+      }
+      const float4 gv = *reinterpret_cast<const float4*>(gr + h);
+      acc = fmaf(xv[0], gv.x, acc);
+      acc = fmaf(xv[1], gv.y, acc);
+      acc = fmaf(xv[2], gv.z, acc);
+      acc = fmaf(xv[3], gv.w, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      const float v = staged ? acc : __int_as_float(0x7fc00000);
+      lsm[u] = v;
+      logits[(int64_t)t * E + e] = v;
+    }
+  }
+  __syncthreads();
+  for (int t = warp; t < nt; t += 8)
+    topk_row(lsm + t * E, E, k, renorm, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
 }
 
 }  // namespace
@@ -317,22 +371,6 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
   const size_t gbytes = sizeof(float) * (size_t)E * H;
   const bool aligned = (reinterpret_cast<uintptr_t>(gate_w) % 16 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
   const bool vec_dtype = x_dtype == STAGEML_BF16 || x_dtype == STAGEML_F16 || x_dtype == STAGEML_F32;
-  if (E <= 32 && H % 4 == 0 && gbytes <= 200 * 1024 && aligned && vec_dtype && T_ <= 32) {
-    // a few tokens: staging G in every CTA would cost more than reading it once from L2
-    const unsigned grid = (unsigned)(((int64_t)T_ * E + 3) / 4);
-    if (x_dtype == STAGEML_BF16)
-      (router_logits_warp_kernel<bf16><<<grid, 128, 0, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E, logits),
-       ::sb::count_launch());
-    else if (x_dtype == STAGEML_F16)
-      (router_logits_warp_kernel<f16><<<grid, 128, 0, stream>>>(static_cast<const f16*>(x), gate_w, T_, H, E, logits),
-       ::sb::count_launch());
-    else
-      (router_logits_warp_kernel<float><<<grid, 128, 0, stream>>>(static_cast<const float*>(x), gate_w, T_, H, E,
-                                                                  logits),
-       ::sb::count_launch());
-    SB_CUDA_CHECK(cudaGetLastError());
-    return STAGEML_OK;
-  }
   if (E <= 32 && H % 4 == 0 && gbytes <= 200 * 1024 && aligned && vec_dtype) {
     const int grid = std::min<int>(sm_count(), (T_ + 7) / 8);
     auto launch = [&](auto kern, const auto* xp) -> int {
@@ -375,6 +413,35 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
   }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
+}
+
+int launch_route(const void* x, int x_dtype, const float* gate_w, int T_, int H, int E, int k, int renorm,
+                 float* logits, int32_t* ids, float* weights, cudaStream_t stream) {
+  SB_CHECK_ARG(E >= 1 && E <= 256, "router: E=%d must be in [1, 256]", E);
+  SB_CHECK_ARG(k >= 1 && k <= 8 && k <= E, "top-k: k=%d must be in [1, min(8, E)]", k);
+  SB_CHECK_ARG(H >= 1, "router: H must be positive");
+  if (T_ == 0) return STAGEML_OK;
+  SB_CHECK_ARG(x && gate_w && logits && ids && weights, "router: null pointer");
+  const size_t es = x_dtype == STAGEML_F32 ? 4 : 2;
+  const size_t gbytes = sizeof(float) * (size_t)E * H, xbytes = es * (size_t)std::min(T_, kRouteSmallT) * H;
+  const bool aligned = (reinterpret_cast<uintptr_t>(gate_w) % 16 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+  const bool vec_dtype = x_dtype == STAGEML_BF16 || x_dtype == STAGEML_F16 || x_dtype == STAGEML_F32;
+  if (T_ <= kRouteSmallMaxT && E <= 32 && H % 4 == 0 && (es * H) % 16 == 0 && gbytes + xbytes <= 220 * 1024 &&
+      aligned && vec_dtype) {
+    auto launch = [&](auto kern, const auto* xp) -> int {
+      SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(gbytes + xbytes)));
+      (kern<<<(T_ + kRouteSmallT - 1) / kRouteSmallT, 256, gbytes + xbytes, stream>>>(xp, gate_w, T_, H, E, k, renorm,
+                                                                                      logits, ids, weights),
+       ::sb::count_launch());
+      SB_CUDA_CHECK(cudaGetLastError());
+      return STAGEML_OK;
+    };
+    if (x_dtype == STAGEML_BF16) return launch(router_small_kernel<bf16>, static_cast<const bf16*>(x));
+    if (x_dtype == STAGEML_F16) return launch(router_small_kernel<f16>, static_cast<const f16*>(x));
+    return launch(router_small_kernel<float>, static_cast<const float*>(x));
+  }
+  SB_TRY(launch_router_logits(x, x_dtype, gate_w, T_, H, E, logits, stream));
+  return launch_topk(logits, T_, E, k, renorm, ids, weights, stream);
 }
 
 }  // namespace sb

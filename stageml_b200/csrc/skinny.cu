@@ -100,7 +100,7 @@ __device__ __forceinline__ void sk_chunk(float (&acc)[NBLK][4], const uint4& xl,
 // an item meet in shared memory and its first warp runs the epilogue from the
 // MMA fragment: lane (g, tig) owns rows g, g+8 and columns 2tig, 2tig+1.
 template <typename T, bool SWIGLU, int WPI>
-__global__ void __launch_bounds__(256) skinny_gemm_kernel(const SkParams p, int n_items) {
+__global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, int n_items) {
   constexpr int NBLK = SWIGLU ? 2 : 1;
   constexpr int IPC = kSkWarps / WPI;  // items per CTA
   __shared__ float red[WPI > 1 ? kSkWarps : 1][NBLK][32][4];

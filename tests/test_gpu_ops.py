@@ -55,6 +55,22 @@ def test_route_topk(ops, T, H, E, k, renorm):
     np.testing.assert_allclose(w.cpu().numpy(), ref_w, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("H,E", [(4096, 8), (2048, 32), (512, 3)])
+def test_route_batch_invariant(ops, dtype, H, E):
+    """A token's logits, ids and weights do not depend on the batch around it: the
+    fused few-token kernel (T <= 8) and the shared-memory kernel (more tokens) sum
+    in the same order."""
+    x = rand((300, H), dtype=dtype, seed=5)
+    G = rand((E, H), 1 / H ** 0.5, torch.float32, seed=6)
+    k = min(2, E)
+    ids_all, w_all, l_all = ops.route_topk(x, G, k, True)
+    for T in (1, 3, 8, 9, 40):
+        ids, w, logits = ops.route_topk(x[:T].contiguous(), G, k, True)
+        assert torch.equal(logits, l_all[:T]), f"T={T}"
+        assert torch.equal(ids, ids_all[:T]) and torch.equal(w, w_all[:T]), f"T={T}"
+
+
 def test_route_matches_reference_make_routing(ops, golden):
     g = golden("routing")
     x = torch.from_numpy(g["hidden"]).to(DEV)
