@@ -333,8 +333,9 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     SB_STAGE(STAGEML_STAGE_PERMUTE,
              launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
   }
-  // gather + R4 shrink of w1|w3
-  {
+  // gather + R4 shrink of w1|w3 (decode-sized batches: no gather, the skinny GEMM
+  // reads the token rows in place, and the per-pair shrink)
+  if (!skinny || lora13) {
     ShrinkLaunch s;
     s.src = a->x;
     s.src_row_of = b.plan.row_token;
@@ -354,13 +355,17 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       s.s_out = b.s13;
       s.lora_scale = a->lora_scale;
     }
-    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(s, st));
+    if (skinny)
+      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(s, b.plan.pair_row, P, st));
+    else
+      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(s, st));
   }
   // R3 + R5: gate/up GEMM, LoRA expand, SwiGLU
   {
     GemmLaunch g;
-    g.a = b.xp;
-    g.a_rows = b.plan.rows_cap;
+    g.a = skinny ? a->x : b.xp;
+    g.a_rows = skinny ? a->T : b.plan.rows_cap;
+    g.a_row_of = skinny ? b.plan.row_token : nullptr;
     g.K = a->H;
     g.b = a->gate_up;
     g.b_rows_total = (int64_t)E_tot * 2 * a->I;
@@ -406,7 +411,10 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     s.spart = b.spart2;
     s.s_out = b.s2;
     s.lora_scale = a->lora_scale;
-    SB_STAGE(STAGEML_STAGE_SHRINK_H, launch_gather_shrink(s, st));
+    if (skinny)
+      SB_STAGE(STAGEML_STAGE_SHRINK_H, launch_pair_shrink(s, b.plan.pair_row, P, st));
+    else
+      SB_STAGE(STAGEML_STAGE_SHRINK_H, launch_gather_shrink(s, st));
   }
   // R3 + R5: down GEMM, LoRA expand, routing weight
   {

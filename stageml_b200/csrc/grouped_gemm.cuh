@@ -29,6 +29,7 @@ namespace sb {
 struct GemmLaunch {
   const void* a = nullptr;       // [a_rows, K] 16-bit
   int64_t a_rows = 0;
+  const int32_t* a_row_of = nullptr;  // skinny GEMM only: output row r reads A row a_row_of[r]
   int K = 0;
   const void* b = nullptr;       // [b_rows_total, K] 16-bit, or e4m3 when b_fp8
   int64_t b_rows_total = 0;

@@ -56,6 +56,11 @@ struct ShrinkLaunch {
 constexpr int kShrinkKSlice = 512;
 inline int shrink_num_slices(int K) { return (K + kShrinkKSlice - 1) / kShrinkKSlice; }
 int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream);
+// The shrink for decode-sized batches: pairs p < P (pair_row[p] = their plan row),
+// one CTA per (pair, 8 output columns) whose 8 warps split K in a fixed order;
+// writes the scaled 16-bit S rows (zeros for rows without a tenant) and reads the
+// source rows in place (src_row_of, if given, maps a plan row to its source row).
+int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream);
 
 // combine.cu: out[t] = sum_j Y[pair_row[t*kk + j]]
 int launch_combine(const void* y, const int32_t* pair_row, int T, int kk, int H, int dtype_bf16, void* out,

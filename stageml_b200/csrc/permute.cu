@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(1024) perm_fused_kernel(PairSrc a, int nkeys, 
   }
   __syncthreads();
   plan_groups(tot, a.tkeys, n_groups, plan, warp_part);
+  for (int64_t p = live + threadIdx.x; p < a.P; p += 1024) plan.pair_row[p] = -1;  // pairs of tokens past *T_dev
   for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
     const uint32_t v = s[i];
     const int64_t p = v & 2047u;

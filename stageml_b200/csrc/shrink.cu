@@ -279,7 +279,135 @@ int launch_shrink_variant(bool bf, dim3 grid, const ShrinkParams& p, cudaStream_
   return STAGEML_OK;
 }
 
+// Decode-sized batches: CTA (pair, nb) computes S[row, 8nb .. 8nb+8) for the pair's
+// plan row; warp w sums its K range [w kw, (w+1) kw) with 16-byte loads, all of
+// them in flight, and the 8 warp sums are added in warp order.
+struct PairShrinkParams {
+  const void* src;
+  const int32_t* src_row_of;
+  int K;
+  const int32_t* pair_row;
+  const int32_t* row_tenant;
+  const int32_t* tile_group;
+  const void* lora_a;
+  int64_t a_tenant_stride;
+  int64_t a_group_stride;
+  int R;
+  const float* lora_scale;
+  void* s_out;
+};
+
+__device__ __forceinline__ uint4 ldg16_nc(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f32<T>(h[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1) pair_shrink_kernel(const PairShrinkParams p) {
+  constexpr int U = 4;
+  __shared__ float red[8][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = p.pair_row[blockIdx.x];
+  if (row < 0) return;  // dropped pair
+  const int tn = p.row_tenant[row];
+  T* s_out = static_cast<T*>(p.s_out) + (int64_t)row * p.R + blockIdx.y * 8;
+  if (tn < 0) {
+    if (threadIdx.x < 8) s_out[threadIdx.x] = from_f32<T>(0.f);
+    return;
+  }
+  const int K = p.K;
+  const int group = p.tile_group ? p.tile_group[row / 128] : 0;
+  const T* x = static_cast<const T*>(p.src) + (p.src_row_of ? (int64_t)p.src_row_of[row] : (int64_t)row) * K;
+  const T* A = static_cast<const T*>(p.lora_a) + tn * p.a_tenant_stride + group * p.a_group_stride +
+               (int64_t)(blockIdx.y * 8) * K;
+  const int kw = ((K + 63) / 64) * 8;
+  const int kb = warp * kw, ke = min(K, kb + kw);
+  float acc[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int k0 = kb + lane * 8; k0 < ke; k0 += 256 * U) {
+    uint4 xv[U], av[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + 256 * u;
+      const bool v = k < ke;
+      xv[u] = v ? __ldg(reinterpret_cast<const uint4*>(x + k)) : z;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) av[u][r] = v ? ldg16_nc(A + (int64_t)r * K + k) : z;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float xf[8];
+      unpack8<T>(xv[u], xf);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        float af[8];
+        unpack8<T>(av[u][r], af);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[r] = fmaf(xf[q], af[q], acc[r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < 8; ++r) red[warp][r] = acc[r];
+  }
+  __syncthreads();
+  if (threadIdx.x < 8) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) v += red[w][threadIdx.x];
+    s_out[threadIdx.x] = from_f32<T>(v * (p.lora_scale ? p.lora_scale[tn] : 1.f));
+  }
+}
+
 }  // namespace
+
+int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream) {
+  SB_CHECK_ARG(s.src && pair_row && s.lora_a && s.s_out && s.row_tenant, "pair shrink: missing buffers");
+  SB_CHECK_ARG(s.K > 0 && s.K % 8 == 0, "pair shrink: K=%d must be a positive multiple of 8", s.K);
+  SB_CHECK_ARG(s.R > 0 && s.R % 8 == 0 && s.R <= 64, "pair shrink: R=%d must be a multiple of 8 up to 64", s.R);
+  SB_CHECK_ARG(P >= 0 && P <= 65535, "pair shrink: %lld pairs", (long long)P);
+  SB_CHECK_ARG(reinterpret_cast<uintptr_t>(s.src) % 16 == 0 && reinterpret_cast<uintptr_t>(s.lora_a) % 16 == 0,
+               "pair shrink: operands must be 16-byte aligned");
+  if (P == 0) return STAGEML_OK;
+  PairShrinkParams p;
+  p.src = s.src;
+  p.src_row_of = s.src_row_of;
+  p.K = s.K;
+  p.pair_row = pair_row;
+  p.row_tenant = s.row_tenant;
+  p.tile_group = s.tile_group;
+  p.lora_a = s.lora_a;
+  p.a_tenant_stride = s.a_tenant_stride;
+  p.a_group_stride = s.a_group_stride;
+  p.R = s.R;
+  p.lora_scale = s.lora_scale;
+  p.s_out = s.s_out;
+  const dim3 grid((unsigned)P, (unsigned)(s.R / 8));
+  if (s.dtype_bf16)
+    (pair_shrink_kernel<bf16><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
+  else
+    (pair_shrink_kernel<f16><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
+  SB_CUDA_CHECK(cudaGetLastError());
+  return STAGEML_OK;
+}
 
 int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   SB_CHECK_ARG(s.src, "shrink: null source");

@@ -26,6 +26,7 @@ constexpr int kSkUnroll = 8;
 
 struct SkParams {
   const void* a;
+  const int32_t* a_row_of;
   int K;
   const void* b;
   int64_t b_rows_total;
@@ -129,8 +130,9 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[b][j] = 0.f;
   if (valid > 0) {  // warp-uniform
-    const T* x_lo = g < valid ? A + (row0 + g) * K : nullptr;
-    const T* x_hi = g + 8 < valid ? A + (row0 + g + 8) * K : nullptr;
+    const int64_t r_lo = row0 + g, r_hi = row0 + g + 8;
+    const T* x_lo = g < valid ? A + (p.a_row_of ? (int64_t)p.a_row_of[r_lo] : r_lo) * K : nullptr;
+    const T* x_hi = g + 8 < valid ? A + (p.a_row_of ? (int64_t)p.a_row_of[r_hi] : r_hi) * K : nullptr;
     const T* wrow[NBLK];
 #pragma unroll
     for (int b = 0; b < NBLK; ++b) {
@@ -248,6 +250,7 @@ int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int
                "skinny gemm: operands must be 16-byte aligned");
   SkParams p;
   p.a = g.a;
+  p.a_row_of = g.a_row_of;
   p.K = g.K;
   p.b = g.b;
   p.b_rows_total = g.b_rows_total;
