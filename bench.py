@@ -341,8 +341,17 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
             b.synchronize()
             lat.append(a.elapsed_time(b) * 1000.0)
         lat.sort()
-        batch1 = {"p50_us": round(lat[len(lat) // 2], 2), "p95_us": round(lat[int(len(lat) * 0.95)], 2),
-                  "samples": len(lat)}
+        # HBM roofline of the call: the touched experts' weights (distinct top-k ids of
+        # the token, plus shared experts), their adapter slices and the row in / out
+        ids_b = ops.route_topk(xb, w["router_w"], cfg.k, True)[0]
+        n_exp = len(set(ids_b.flatten().tolist())) + cfg.n_shared
+        esz = 1 if cfg.weight_dtype == "e4m3" else 2
+        b1_bytes = n_exp * 3 * cfg.H * cfg.I * esz + (cfg.k + cfg.n_shared) * moe_bytes(cfg, w, 1)["adapter_per_pair"] + 2 * cfg.H * 2
+        t_b1 = b1_bytes / (float(peaks.get("hbm_gbs", 6650.0)) * 1e9) * 1e6
+        p50 = lat[len(lat) // 2]
+        batch1 = {"p50_us": round(p50, 2), "p95_us": round(lat[int(len(lat) * 0.95)], 2), "samples": len(lat),
+                  "roofline": {"bound": "hbm", "bytes": b1_bytes, "experts_touched": n_exp,
+                               "t_roof_us": round(t_b1, 2), "frac": round(t_b1 / p50, 4)}}
 
     ep_status = None
     if layer is not None:  # collective: every rank releases the exchange buffers
