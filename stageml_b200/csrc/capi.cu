@@ -160,6 +160,10 @@ int side_stream(SideStream** out) {
 // e4m3 weights): the one-CTA kernel over all tiles (g.tile_runs set by the caller).
 int run_grouped_gemm(GemmLaunch g, const PairPlan& pp, cudaStream_t st) {
   if (!pp.on() || g.b_fp8) return launch_grouped_gemm(g, st);
+  g.split_pairs_dev = pp.num_pairs;
+  g.split_singles_dev = pp.num_singles;
+  g.split_cap = pp.tiles_cap;
+  g.split_sms = 2 * (sm_count() / 2);
   GemmLaunch s1 = g;
   g.pairs = pp.pairs;
   g.num_pairs_dev = pp.num_pairs;

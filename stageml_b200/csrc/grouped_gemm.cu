@@ -81,6 +81,11 @@ struct KParams {
   void* out;
   int64_t ldo;
   int32_t* status;
+  // beside the pair kernel (split_sms > 0): only the odd-tile share of the SMs
+  const int32_t* split_pairs_dev;
+  const int32_t* split_singles_dev;
+  int split_cap;
+  int split_sms;
   unsigned long long timeout_ns;
 };
 
@@ -167,6 +172,12 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   // the barrier TMA completes on: the MMA's own for 16-bit weights, the converters' for FP8
   auto land_bar = [&](int s) { return FP8B ? raw_bar(s) : full_bar(s); };
 
+  // Beside the pair kernel only the first `nctas` CTAs work; the others leave at once.
+  int nctas = gridDim.x;
+  if (p.split_sms > 0) {
+    nctas = min(nctas, split_single_ctas(p.split_pairs_dev, p.split_singles_dev, p.split_cap, p.split_sms));
+    if ((int)blockIdx.x >= nctas) return;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), FP8B ? CONVERTER_THREADS : 1);
@@ -210,7 +221,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
     uint32_t it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += nctas) {
       const int m_pos = tile % num_m_tiles;
       const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
       const int n_tile = tile / num_m_tiles;
@@ -290,7 +301,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     int tcount = 0;
     bool ok = true;
     bool issued_any = false;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++tcount) {
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += nctas, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
       const int m_pos = tile % num_m_tiles;
@@ -362,7 +373,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     T* out = reinterpret_cast<T*>(p.out);
     const bool vec_ok = (p.ldo % 8 == 0) && (p.N % 8 == 0);
     int tcount = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tcount) {
+    for (int tile = blockIdx.x; tile < total_tiles; tile += nctas, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
       if (!mbar_wait(tfull_bar(acc), aph, abort_flag, p.status, p.timeout_ns, kDevTimeoutEpilogue)) break;
@@ -441,7 +452,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     // physical chunk (logical ^ (r & 7)) -- the 128B swizzle the MMA descriptor expects.
     const int ct = threadIdx.x - 192;
     uint32_t it = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < total_tiles; tile += nctas) {
       const int m_pos = tile % num_m_tiles;
       const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
       const int n_tile = tile / num_m_tiles;
@@ -650,6 +661,10 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.ldo = g.ldo;
   p.status = g.status;
   p.timeout_ns = kDefaultWaitNs;
+  p.split_pairs_dev = g.split_pairs_dev;
+  p.split_singles_dev = g.split_singles_dev;
+  p.split_cap = g.split_cap;
+  p.split_sms = (g.split_pairs_dev && g.split_singles_dev) ? g.split_sms : 0;
 
   int64_t tiles_upper = (g.tile_group || g.tile_list) ? (int64_t)g.tiles_cap : (g.m_rows + BM - 1) / BM;
   tiles_upper *= p.num_n_tiles;

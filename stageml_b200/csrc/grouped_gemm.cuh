@@ -70,7 +70,29 @@ struct GemmLaunch {
   int pairs_cap = 0;
   const int32_t* pair_runs = nullptr;    // [pairs_cap][kMaxRunsPerPair][kPairRunInts]
   const int32_t* pair_nruns = nullptr;   // [pairs_cap]
+  // The pair kernel and the odd-tile kernel side by side (split_sms > 0): each
+  // reads the pair and odd-tile counts and keeps only its share of the split_sms
+  // SMs busy (split_single_ctas); the CTAs past its share exit at once.
+  const int32_t* split_pairs_dev = nullptr;
+  const int32_t* split_singles_dev = nullptr;
+  int split_cap = 0;
+  int split_sms = 0;
 };
+
+// CTAs of the odd-tile kernel next to the pair kernel on `sms` SMs: its share of
+// the work (a pair unit keeps two SMs busy about as long as an odd-tile unit keeps
+// one), at least one, leaving the pair kernel an even count of at least two.
+__device__ __forceinline__ int split_single_ctas(const int32_t* n_pairs_dev, const int32_t* n_singles_dev, int cap,
+                                                 int sms) {
+  const int np = min(*n_pairs_dev, cap), ns = min(*n_singles_dev, cap);
+  if (ns <= 0) return 0;
+  if (np <= 0) return sms;
+  const int64_t den = 2LL * np + ns;
+  int s = (int)(((int64_t)sms * ns + den / 2) / den);
+  s = max(1, min(s, sms - 2));
+  if ((sms - s) & 1) s = min(s + 1, sms - 2);
+  return s;
+}
 
 int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 

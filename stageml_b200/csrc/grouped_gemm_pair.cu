@@ -75,6 +75,9 @@ struct PParams {
   int64_t ldo;
   int32_t* status;
   unsigned long long timeout_ns;
+  // side by side with the odd-tile kernel (split_sms > 0)
+  const int32_t* split_singles_dev;
+  int split_sms;
 };
 
 template <typename T>
@@ -132,6 +135,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                              const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_lb,
                              const PParams p) {
+  // Beside the odd-tile kernel only the first `nclusters` clusters work; the others
+  // leave their SMs to it (both CTAs of a cluster decide alike, before any barrier).
+  int nclusters = gridDim.x >> 1;
+  if (p.split_sms > 0) {
+    const int budget =
+        (p.split_sms - split_single_ctas(p.num_pairs_dev, p.split_singles_dev, p.pairs_cap, p.split_sms)) >> 1;
+    nclusters = min(nclusters, max(budget, 1));
+    if ((int)(blockIdx.x >> 1) >= nclusters) return;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -145,7 +157,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int cluster = blockIdx.x >> 1;
-  const int nclusters = gridDim.x >> 1;
   const uint32_t smem_base = smem_u32(smem);
   auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
   auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
@@ -679,6 +690,8 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
   p.ldo = g.ldo;
   p.status = g.status;
   p.timeout_ns = kDefaultWaitNs;
+  p.split_singles_dev = g.split_singles_dev;
+  p.split_sms = g.split_singles_dev ? g.split_sms : 0;
 
   const int64_t units_upper = (int64_t)g.pairs_cap * p.num_n_tiles;
   if (units_upper == 0) return STAGEML_OK;
