@@ -196,24 +196,26 @@ __device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_group
     plan.num_tiles[0] = run / 128;
   }
   __syncthreads();
-  // 4. key bases (in place in tot), tile -> group, padding rows
-  for (int g = tid; g < n_groups; g += 1024) {
+  // 4. key bases (in place in tot), tile -> group, padding rows: one warp per group
+  for (int g = wid; g < n_groups; g += 32) {
     const int o = plan.group_offsets[g];
     const int cnt = plan.group_counts[g];
     const int end = o + ((cnt + 127) & ~127);
-    for (int t = o / 128; t < end / 128; ++t) plan.tile_group[t] = g;
-    for (int r = o + cnt; r < end; ++r) {
+    for (int t = o / 128 + lane; t < end / 128; t += 32) plan.tile_group[t] = g;
+    for (int r = o + cnt + lane; r < end; r += 32) {
       plan.row_token[r] = -1;
       plan.row_tenant[r] = -1;
       plan.row_weight[r] = 0.f;
       plan.row_pair[r] = -1;
     }
-    int b = o;
-    for (int tk = 0; tk < tkeys; ++tk) {
-      const int key = g * tkeys + tk;
-      const int v = tot[key];
-      tot[key] = b;
-      b += v;
+    if (lane == 0) {
+      int b = o;
+      for (int tk = 0; tk < tkeys; ++tk) {
+        const int key = g * tkeys + tk;
+        const int v = tot[key];
+        tot[key] = b;
+        b += v;
+      }
     }
   }
   __syncthreads();
