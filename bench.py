@@ -612,14 +612,14 @@ def dense_arm(args):
                         "frac": round(fl / (ms / 1e3) / 1e12 / peak_tf, 4), "traffic": None})
     elif name == "fine_grained_moe_lora_bf16":
         cfg = wl.MoEConfig("fine_grained_moe_lora_bf16", T=8192, H=2048, I=1408, E=64, k=6, n_shared=2,
-                           n_tenants=128, rank=16, tenant_dist="zipf")  # rank 8 zero-padded to 16
+                           n_tenants=128, rank=8, tenant_dist="zipf")
         w = wl.make_moe_workload(cfg, device=dev, seed=0)
         ms, st, n = _timed(lambda i: layer_call(ops, cfg, w, w["x"], w["tenant_ids"]), args.steps, args.warmup, lib)
         fl = cfg.flops()
         _line("fine-grained MoE-LoRA layer tokens/s (bf16 weights)", round(cfg.T / (ms / 1e3), 1), "tokens/s",
               args.steps, args.warmup, ms, True, "bf16",
               {"workload": cfg.name, "tokens": cfg.T, "hidden": 2048, "intermediate": 1408, "experts": 64, "top_k": 6,
-               "shared_experts": 2, "tenants": 128, "lora_rank": "16 (the cost of rank 8 zero-padded to 16)",
+               "shared_experts": 2, "tenants": 128, "lora_rank": 8,
                "weights": "bf16"},
               stages_ms_per_step={k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in st.items()},
               gpu_launches=n, clocks=sampler.stop(),

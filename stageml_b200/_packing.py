@@ -1,7 +1,8 @@
 """Stage-0 packing of weights and adapter factors for the sm_100a kernels.
 
 The kernels want 16-byte row pitches (feature sizes that are multiples of 8)
-and LoRA ranks of 16 or 32 (one or two K=16 tensor-core steps). Zero padding
+and LoRA ranks of 8, 16 or 32 (one or two K=16 tensor-core steps; rank 8 fills
+the other half of its step with zeros in shared memory). Zero padding
 gives identical results: padded input columns meet zero weight columns, padded
 output rows are sliced away, and padded rank columns of A / B multiply zeros.
 """
@@ -20,6 +21,8 @@ def round_up(n: int, m: int) -> int:
 def padded_rank(r: int) -> int:
     if r <= 0:
         return 0
+    if r <= 8:
+        return 8
     if r <= 16:
         return 16
     if r <= 32:

@@ -226,8 +226,8 @@ int moe_validate(const stageml_moe_args* a, bool check_ptrs = true) {
     SB_CHECK_ARG(!check_ptrs || a->T == 0 || (a->gate_up_scale && a->down_scale),
                  "moe: E4M3 weights need gate_up_scale and down_scale");
   }
-  SB_CHECK_ARG(a->rank == 0 || a->rank == 16 || a->rank == 32,
-               "moe: rank=%d must be 0, 16 or 32 (zero-pad smaller ranks)", a->rank);
+  SB_CHECK_ARG(a->rank == 0 || a->rank == 8 || a->rank == 16 || a->rank == 32,
+               "moe: rank=%d must be 0, 8, 16 or 32 (zero-pad other ranks)", a->rank);
   const bool lora13 = a->rank > 0 && a->lora_a13;
   const bool lora2 = a->rank > 0 && a->lora_a2;
   SB_CHECK_ARG(!lora13 || a->lora_b13, "moe: lora_a13 without lora_b13");
@@ -663,7 +663,7 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
   SB_CHECK_ARG(K % 8 == 0 && N % 8 == 0, "moe_linear: K=%d and N=%d must be multiples of 8", K, N);
   SB_CHECK_ARG(is16(dtype), "moe_linear: dtype must be BF16 or F16");
   SB_CHECK_ARG(ids_dtype == STAGEML_I32 || ids_dtype == STAGEML_I64, "moe_linear: ids dtype");
-  SB_CHECK_ARG(rank == 0 || rank == 16 || rank == 32, "moe_linear: rank=%d must be 0, 16 or 32", rank);
+  SB_CHECK_ARG(rank == 0 || rank == 8 || rank == 16 || rank == 32, "moe_linear: rank=%d must be 0, 8, 16 or 32", rank);
   const bool lora = rank > 0 && lora_a && !group_by_tenant;
   SB_CHECK_ARG(!lora || (lora_b && lora_scale && tenant_ids && n_tenants > 0), "moe_linear: incomplete LoRA inputs");
   SB_CHECK_ARG(!group_by_tenant || (tenant_ids && n_tenants > 0), "moe_linear: group_by_tenant needs tenant ids");
@@ -780,7 +780,8 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   SB_CHECK_ARG(a->M >= 0 && a->K > 0 && a->N > 0 && a->n_groups >= 1, "lora_linear: bad sizes");
   SB_CHECK_ARG(a->K % 8 == 0 && a->N % 8 == 0, "lora_linear: K=%d and N=%d must be multiples of 8", a->K, a->N);
   SB_CHECK_ARG(is16(a->dtype), "lora_linear: dtype must be BF16 or F16");
-  SB_CHECK_ARG(a->rank == 0 || a->rank == 16 || a->rank == 32, "lora_linear: rank=%d must be 0, 16 or 32", a->rank);
+  SB_CHECK_ARG(a->rank == 0 || a->rank == 8 || a->rank == 16 || a->rank == 32,
+               "lora_linear: rank=%d must be 0, 8, 16 or 32", a->rank);
   const bool lora = a->rank > 0 && a->lora_a && a->row_tenant;
   SB_CHECK_ARG(!lora || (a->lora_b && a->lora_scale && a->n_tenants > 0), "lora_linear: incomplete LoRA inputs");
   SB_CHECK_ARG(a->n_groups == 1 || a->row_group, "lora_linear: n_groups > 1 needs row_group");

@@ -600,7 +600,8 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   SB_CHECK_ARG(!g.b_fp8 || g.K % 16 == 0, "grouped gemm: FP8 weights need K=%d to be a multiple of 16", g.K);
   SB_CHECK_ARG(!g.b_fp8 || g.b_scale, "grouped gemm: FP8 weights need per-row scales");
   SB_CHECK_ARG(g.N > 0, "grouped gemm: N must be positive");
-  SB_CHECK_ARG(g.rank == 0 || g.rank == 16 || g.rank == 32, "grouped gemm: LoRA rank %d must be 0, 16 or 32", g.rank);
+  SB_CHECK_ARG(g.rank == 0 || g.rank == 8 || g.rank == 16 || g.rank == 32,
+               "grouped gemm: LoRA rank %d must be 0, 8, 16 or 32", g.rank);
   SB_CHECK_ARG(g.rank == 0 || (g.s16 && g.lora_b && (g.pairs ? (g.pair_runs && g.pair_nruns) : (g.tile_runs && g.tile_nruns)) &&
                                g.s_rows > 0 && g.lora_b_rows_total > 0),
                "grouped gemm: LoRA rank > 0 needs S, B, the tile runs and their sizes");
@@ -623,6 +624,8 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   if (g.rank) {
     SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
                         16, 32));
+    // rank 8: the 16-wide box reads past the 8 bank columns, which TMA fills with
+    // zeros, so the K=16 MMA adds nothing for the other 8 columns of its S operand
     SB_TRY(make_tmap_2d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.lora_b_rows_total, (uint64_t)g.rank,
                         (uint64_t)g.rank * 2, 128, 16, 32));
   } else {
@@ -643,7 +646,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.tile_list = g.tile_list;
   p.m_rows = g.m_rows;
   p.rank = g.rank;
-  p.lchunks = g.rank / 16;
+  p.lchunks = (g.rank + 15) / 16;
   p.s_bytes = (g.swiglu ? 2 : 1) * p.lchunks * LCHUNK;
   p.run_bytes = 2 * p.lchunks * LCHUNK;
   p.runs_per_block = g.rank ? (MMA_STAGE_BYTES - p.s_bytes) / p.run_bytes : 1;

@@ -673,7 +673,7 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
   p.num_pairs_dev = g.num_pairs_dev;
   p.pairs_cap = g.pairs_cap;
   p.rank = g.rank;
-  p.lchunks = g.rank / 16;
+  p.lchunks = (g.rank + 15) / 16;
   p.s_bytes = (g.swiglu ? 2 : 1) * p.lchunks * LCHUNK;
   p.run_bytes = p.lchunks * LCHUNK;  // this CTA's half: 2 x 64 rows (SwiGLU) or 128 rows per chunk
   p.runs_per_block = g.rank ? (MMA_STAGE_BYTES - p.s_bytes) / p.run_bytes : 1;

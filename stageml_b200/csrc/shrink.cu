@@ -78,6 +78,9 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -223,11 +226,16 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
         uint32_t a0, a1, a2, a3;
         ldsm_x4(xs + ((mi & 1) * 8 + mr) * kShrinkPitch + (k16 * 16 + (mi >> 1) * 8) * 2, a0, a1, a2, a3);
 #pragma unroll
-        for (int nb = 0; nb < NBS; nb += 2) {
+        for (int nb = 0; nb + 1 < NBS; nb += 2) {
           uint32_t b0, b1, b2, b3;
           ldsm_x4(as + ((nb + (mi >> 1)) * 8 + mr) * kShrinkPitch + (k16 * 16 + (mi & 1) * 8) * 2, b0, b1, b2, b3);
           mma_16816<T>(acc[nb], a0, a1, a2, a3, b0, b1);
           mma_16816<T>(acc[nb + 1], a0, a1, a2, a3, b2, b3);
+        }
+        if constexpr ((NBS & 1) != 0) {  // a last single block of 8 output columns
+          uint32_t b0, b1;
+          ldsm_x2(as + ((NBS - 1) * 8 + mr) * kShrinkPitch + (k16 * 16 + (mi & 1) * 8) * 2, b0, b1);
+          mma_16816<T>(acc[NBS - 1], a0, a1, a2, a3, b0, b1);
         }
       }
       if (kc == nkc - 1) {
@@ -412,7 +420,8 @@ int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P
 int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   SB_CHECK_ARG(s.src, "shrink: null source");
   SB_CHECK_ARG(s.K > 0 && s.K % 8 == 0, "shrink: K=%d must be a positive multiple of 8", s.K);
-  SB_CHECK_ARG(s.R == 0 || s.R == 16 || s.R == 32 || s.R == 64, "shrink: R=%d must be 0, 16, 32 or 64", s.R);
+  SB_CHECK_ARG(s.R == 0 || s.R == 8 || s.R == 16 || s.R == 32 || s.R == 64, "shrink: R=%d must be 0, 8, 16, 32 or 64",
+               s.R);
   SB_CHECK_ARG(s.R == 0 || (s.lora_a && s.spart && s.s_out && s.row_tenant), "shrink: missing LoRA buffers");
   SB_CHECK_ARG(reinterpret_cast<uintptr_t>(s.src) % 16 == 0, "shrink: source must be 16-byte aligned");
   if (!s.gather_dst && s.R == 0) return STAGEML_OK;
@@ -440,6 +449,9 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
     case 0:
       SB_TRY(launch_shrink_variant<0>(s.dtype_bf16, grid, p, stream));
       break;
+    case 1:
+      SB_TRY(launch_shrink_variant<1>(s.dtype_bf16, grid, p, stream));
+      break;
     case 2:
       SB_TRY(launch_shrink_variant<2>(s.dtype_bf16, grid, p, stream));
       break;
@@ -450,7 +462,7 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
       SB_TRY(launch_shrink_variant<8>(s.dtype_bf16, grid, p, stream));
       break;
     default:
-      return set_error(STAGEML_ERR_INVALID_ARG, "shrink: R=%d must be 0, 16, 32 or 64", s.R);
+      return set_error(STAGEML_ERR_INVALID_ARG, "shrink: R=%d must be 0, 8, 16, 32 or 64", s.R);
   }
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {

@@ -97,7 +97,7 @@ class MoEConfig:
 
     @property
     def bank_rank(self) -> int:
-        """Rank of the LoRA banks as stored: the adapter rank zero-padded to 16 or 32."""
+        """Rank of the LoRA banks as stored: the adapter rank zero-padded to 8, 16 or 32."""
         from ._packing import padded_rank
 
         return padded_rank(self.rank)

@@ -63,8 +63,10 @@ def test_moe_args_validation_and_workspace_query():
     a.T = 2048
     need = lib.stageml_moe_workspace_bytes(ctypes.byref(a))
     assert need > 2048 * 2 * 14336 * 2  # holds the SwiGLU intermediate of the padded rows
-    a.rank = 8  # ranks are 16 or 32 after zero padding
+    a.rank = 12  # ranks are 8, 16 or 32 after zero padding
     assert lib.stageml_moe_workspace_bytes(ctypes.byref(a)) == 0
+    a.rank = 8
+    assert lib.stageml_moe_workspace_bytes(ctypes.byref(a)) > 0
     a.rank = 16
     a.H = 4100  # not a multiple of 8
     assert lib.stageml_moe_forward(ctypes.byref(a), None, 0, None) == capi.ERR_INVALID_ARG

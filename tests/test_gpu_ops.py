@@ -168,6 +168,8 @@ def _oracle_moe(c, ids, w, ns=0):
     dict(T=64, H=128, I=128, E=4, k=2, nT=3, r=16, lora=("w13",)),
     dict(T=1, H=256, I=256, E=8, k=2, nT=2, r=16),
     dict(T=130, H=136, I=200, E=3, k=3, nT=0, r=0),
+    dict(T=600, H=256, I=384, E=6, k=2, nT=9, r=8, ns=1, ten_dist="zipf"),  # rank 8 on tile pairs
+    dict(T=3, H=256, I=256, E=4, k=2, nT=2, r=8),  # rank 8, decode-sized batch
 ])
 def test_moe_forward_vs_oracle(ops, case):
     ns = case.get("ns", 0)
@@ -271,6 +273,8 @@ def test_moe_linear_dynamic_and_materialized(ops):
                                                 (300, 128, 256, 9, 32, 1, torch.bfloat16),
                                                 (400, 256, 256, 4, 16, 3, torch.bfloat16),
                                                 (256, 512, 512, 64, 16, 9, torch.bfloat16),
+                                                (333, 256, 384, 6, 8, 1, torch.bfloat16),
+                                                (400, 256, 256, 5, 8, 3, torch.float16),
                                                 (7, 72, 24, 0, 0, 1, torch.bfloat16)])
 def test_lora_linear(ops, M, K, N, nT, r, G, dtype):
     rng = np.random.default_rng(M + N)
@@ -393,6 +397,7 @@ def _fp8_weights(c, ops):
     dict(T=1000, H=256, I=128, E=16, k=4, nT=40, r=16, ns=2, ten_dist="zipf"),
     dict(T=130, H=128, I=176, E=3, k=3, nT=0, r=0),
     dict(T=1, H=256, I=256, E=8, k=2, nT=2, r=16),
+    dict(T=700, H=256, I=192, E=8, k=3, nT=20, r=8, ns=1, ten_dist="zipf"),
 ])
 def test_moe_forward_fp8_weights(ops, case):
     """e4m3 weights, fp32 per-output-channel scales (weight-only FP8: dequantised before the MMA).

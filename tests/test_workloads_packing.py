@@ -33,7 +33,8 @@ def test_single_lora_config():
 
 
 def test_padding_helpers_are_exact():
-    assert _packing.padded_rank(2) == 16 and _packing.padded_rank(17) == 32 and _packing.padded_rank(0) == 0
+    assert _packing.padded_rank(2) == 8 and _packing.padded_rank(8) == 8 and _packing.padded_rank(9) == 16
+    assert _packing.padded_rank(17) == 32 and _packing.padded_rank(0) == 0
     A = [torch.randn(3, 10, 6), torch.randn(3, 2, 6)]
     B = [torch.randn(3, 5, 10), torch.randn(3, 5, 2)]
     a, b = _packing.pack_lora_bank([x.transpose(1, 2) for x in [torch.randn(3, 6, 10)]] * 0 + [A[0].transpose(1, 2)
