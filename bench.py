@@ -625,11 +625,51 @@ def dense_arm(args):
               gpu_launches=n, clocks=sampler.stop(),
               layer_roofline={"flops": fl["total"], "t_roof_ms": round(fl["total"] / (peak_tf * 1e12) * 1e3, 4),
                               "frac": round(fl["total"] / (peak_tf * 1e12) * 1e3 / ms, 4)})
+    elif name == "request_stream":
+        # the reference system benchmark's request stream (128 requests x 16 tokens over 512
+        # token rows, 16 Zipf(1.2) tenants in bursts of 8 on 8 rank-16 w1 adapters, memory-budget
+        # materialization) on Mixtral-shape experts: the whole stream as one layer call
+        from stageml_b200.executor import RequestExecutor, make_workload_plan, run_sequence
+        from stageml_b200.moe_lora_layers import MoEAdapterSpec
+
+        H, I, E, k, nA, r, Tav = 4096, 14336, 8, 2, 8, 16, 512
+        g = wl._Gen(0, "cuda", dev)
+        hidden = g.normal((Tav, H), 1.0, torch.bfloat16)
+        gate_up = g.normal_stacked(E, (2 * I, H), H ** -0.5, torch.bfloat16)
+        down = g.normal_stacked(E, (H, I), I ** -0.5, torch.bfloat16)
+        router_w = g.normal((E, H), H ** -0.5, torch.float32)
+        ids, wts, _ = ops.route_topk(hidden, router_w, k, True)
+        ads = [MoEAdapterSpec(f"adapter_{i}", g.normal_stacked(E, (r, H), H ** -0.5, torch.bfloat16),
+                              g.normal_stacked(E, (I, r), r ** -0.5, torch.bfloat16), 2.0) for i in range(nA)]
+        folded_bytes = E * I * H * 2
+        plan = make_workload_plan(num_requests=128, num_tenants=16, num_adapters=nA, tokens_available=Tav,
+                                  tokens_per_request=16, distribution="zipf", zipf_alpha=1.2, burst_size=8,
+                                  materialization_policy="memory_budget", materialize_top_k=4,
+                                  materialize_min_requests=2, memory_budget_mb=2048.0,
+                                  memory_per_adapter_bytes=folded_bytes, seed=17)
+        ex = RequestExecutor(gate_up, down, ads, plan.materialized_adapter_ids)
+        toks = sum(q.end - q.start for q in plan.requests)
+        ms, st, n = _timed(lambda i: run_sequence(ex, plan, hidden, ids, wts, "batched"), args.steps, args.warmup,
+                           lib)
+        per = {}
+        for mode in ("dynamic", "bta"):
+            ms_m, _, n_m = _timed(lambda i: run_sequence(ex, plan, hidden, ids, wts, mode), max(3, args.steps // 10),
+                                  2, lib)
+            per[mode] = {"ms_per_stream": round(ms_m, 4), "tokens_per_s": round(toks / (ms_m / 1e3), 1),
+                         "gpu_launches": n_m}
+        _line("request stream tokens/s (128 requests x 16 tokens, Mixtral experts, w1 adapters)",
+              round(toks / (ms / 1e3), 1), "tokens/s", args.steps, args.warmup, ms, True, "bf16",
+              {"workload": "request_stream", "requests": len(plan.requests), "tokens_per_request": 16,
+               "tokens": toks, "token_rows": Tav, "hidden": H, "intermediate": I, "experts": E, "top_k": k,
+               "tenants": 16, "adapters": nA, "rank": r, "materialized": sorted(plan.materialized_adapter_ids),
+               "mode": "batched: the whole stream as one layer call"},
+              per_request_modes=per, stage0_fold_ms=round(ex.compile_time_ms, 3), gpu_launches=n,
+              clocks=sampler.stop())
     else:
         raise SystemExit(f"unknown workload {name}")
 
 
-DENSE_WORKLOADS = ("single_lora", "adapter_bank", "llama_block", "fine_grained_moe_lora_bf16")
+DENSE_WORKLOADS = ("single_lora", "adapter_bank", "llama_block", "fine_grained_moe_lora_bf16", "request_stream")
 
 
 def make_moe_workload_tokens(cfg, dev, seed: int, T: int):

@@ -21,6 +21,10 @@ Cases (reference file the outputs come from):
   single_lora.npz        trace_and_annotate -> optimize_evaluation_order -> specialize on the config-1
                          LoRA expression y = x W + s (x A) B (stageml/tracer.py, rewrite.py, evaluator.py)
   router_split.npz       route_fused_experts with fake backends (stageml/vllm_stage_router.py)
+  workload_plan.npz      make_workload_plan (benchmarks/multitenant_bta_system_bench.py), every
+                         materialization policy
+
+    python tests/golden/make_golden.py --only workload_plan   # that case alone
 """
 
 from __future__ import annotations
@@ -39,14 +43,40 @@ def np32(t):
     return t.detach().cpu().to(dtype=__import__("torch").float32).numpy()
 
 
+PLAN_CASES = [  # (policy, distribution, seed)
+    ("none", "zipf", 5), ("all", "uniform", 6), ("top_k", "zipf", 7), ("memory_budget", "bursty", 8),
+    ("top_k", "round_robin", 9),
+]
+PLAN_ARGS = dict(num_requests=40, num_tenants=12, num_adapters=5, tokens_available=256, tokens_per_request=16,
+                 zipf_alpha=1.1, burst_size=3, materialize_top_k=3, materialize_min_requests=2, memory_budget_mb=1.0,
+                 memory_per_adapter_bytes=300000)
+
+
+def workload_plan() -> None:
+    import multitenant_bta_system_bench as mb
+
+    out = {}
+    for i, (policy, dist, seed) in enumerate(PLAN_CASES):
+        plan = mb.make_workload_plan(distribution=dist, materialization_policy=policy, seed=seed, **PLAN_ARGS)
+        out[f"c{i}_requests"] = np.array([[r.request_id, r.tenant_id, r.adapter_id, r.start, r.end]
+                                          for r in plan.requests])
+        out[f"c{i}_materialized"] = np.array(sorted(plan.materialized_adapter_ids), dtype=np.int64)
+        out[f"c{i}_selected_bytes"] = np.array(plan.selected_materialized_memory_bytes)
+    np.savez(HERE / "workload_plan.npz", **out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", default=None, help="generate one case (workload_plan)")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.dont_write_bytecode = True
     sys.path.insert(0, str(ref))
     sys.path.insert(0, str(ref / "benchmarks"))
+    if args.only == "workload_plan":
+        workload_plan()
+        return
     import torch
     import torch.nn as nn
 
@@ -246,6 +276,7 @@ def main() -> None:
                             tenant_ids=tenant_ids, router=router, vllm_fused_experts=fv, stageml_op=fs)
     np.savez(HERE / "router_split.npz", hidden=np32(hidden), tenant_ids=tenant_ids.numpy(),
              materialized=np.array([0, 3]), out=np32(y))
+    workload_plan()
     print("golden vectors written to", HERE)
 
 
