@@ -23,8 +23,11 @@ Cases (reference file the outputs come from):
   router_split.npz       route_fused_experts with fake backends (stageml/vllm_stage_router.py)
   workload_plan.npz      make_workload_plan (benchmarks/multitenant_bta_system_bench.py), every
                          materialization policy
+  expert_lora_adapter.npz  load_expert_lora_adapter (benchmarks/real_moe_lora_residual_bench.py) on
+                         a seeded PEFT-style checkpoint (the state dict is stored too)
 
-    python tests/golden/make_golden.py --only workload_plan   # that case alone
+    python tests/golden/make_golden.py --only workload_plan         # that case alone
+    python tests/golden/make_golden.py --only expert_lora_adapter
 """
 
 from __future__ import annotations
@@ -65,6 +68,48 @@ def workload_plan() -> None:
     np.savez(HERE / "workload_plan.npz", **out)
 
 
+def adapter_state_dict(seed: int = 21):
+    """A PEFT-style Mixtral expert LoRA state dict: 4 experts x (w1, w3, w2) x (A, B) at
+    rank 4, one expert at rank 2, one without its w1 B, plus attention LoRA keys."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    E, H, I = 4, 16, 24
+    sd = {}
+    pre = "base_model.model.model.layers.0.block_sparse_moe.experts"
+    for e in range(E):
+        r = 2 if e == 3 else 4
+        for proj, (din, dout) in (("w1", (H, I)), ("w3", (H, I)), ("w2", (I, H))):
+            sd[f"{pre}.{e}.{proj}.lora_A.default.weight"] = torch.randn(r, din, generator=g)
+            if not (e == 2 and proj == "w1"):
+                sd[f"{pre}.{e}.{proj}.lora_B.default.weight"] = torch.randn(dout, r, generator=g)
+    sd["base_model.model.model.layers.0.self_attn.q_proj.lora_A.default.weight"] = torch.randn(4, H, generator=g)
+    sd["base_model.model.model.layers.0.self_attn.q_proj.lora_B.default.weight"] = torch.randn(H, 4, generator=g)
+    return sd, E, H, I
+
+
+def expert_lora_adapter() -> None:
+    import tempfile
+
+    import real_moe_lora_residual_bench as rb
+    from safetensors.torch import save_file
+
+    sd, E, H, I = adapter_state_dict()
+    out = {"keys": np.array(sorted(sd)), "E": np.array(E), "H": np.array(H), "I": np.array(I)}
+    for i, k in enumerate(sorted(sd)):
+        out[f"t{i}"] = sd[k].numpy()
+    with tempfile.TemporaryDirectory() as d:
+        save_file(sd, os.path.join(d, "adapter_model.safetensors"))
+        for proj, (din, dout) in (("w1", (H, I)), ("w3", (H, I)), ("w2", (I, H))):
+            os.environ["LORA_PROJECTION"] = proj
+            spec = rb.load_expert_lora_adapter(Path(d), num_experts=E, in_features=din, out_features=dout)
+            out[f"{proj}_A"] = spec.A.numpy()
+            out[f"{proj}_B"] = spec.B.numpy()
+            out[f"{proj}_scaling"] = np.array(spec.scaling)
+        os.environ.pop("LORA_PROJECTION", None)
+    np.savez(HERE / "expert_lora_adapter.npz", **out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -76,6 +121,9 @@ def main() -> None:
     sys.path.insert(0, str(ref / "benchmarks"))
     if args.only == "workload_plan":
         workload_plan()
+        return
+    if args.only == "expert_lora_adapter":
+        expert_lora_adapter()
         return
     import torch
     import torch.nn as nn
@@ -277,6 +325,7 @@ def main() -> None:
     np.savez(HERE / "router_split.npz", hidden=np32(hidden), tenant_ids=tenant_ids.numpy(),
              materialized=np.array([0, 3]), out=np32(y))
     workload_plan()
+    expert_lora_adapter()
     print("golden vectors written to", HERE)
 
 
