@@ -23,11 +23,14 @@ Cases (reference file the outputs come from):
   router_split.npz       route_fused_experts with fake backends (stageml/vllm_stage_router.py)
   workload_plan.npz      make_workload_plan (benchmarks/multitenant_bta_system_bench.py), every
                          materialization policy
+  residual_plan.json     choose_residual_plan + plan_to_json (stageml/residual_planner.py,
+                         stageml/moe_plan_export.py) for a seeded set of adapters
   expert_lora_adapter.npz  load_expert_lora_adapter (benchmarks/real_moe_lora_residual_bench.py) on
                          a seeded PEFT-style checkpoint (the state dict is stored too)
 
     python tests/golden/make_golden.py --only workload_plan         # that case alone
     python tests/golden/make_golden.py --only expert_lora_adapter
+    python tests/golden/make_golden.py --only residual_plan
 """
 
 from __future__ import annotations
@@ -110,6 +113,21 @@ def expert_lora_adapter() -> None:
     np.savez(HERE / "expert_lora_adapter.npz", **out)
 
 
+def residual_plan() -> None:
+    from stageml.moe_ir import MoEAdapterMeta
+    from stageml.moe_plan_export import plan_to_json
+    from stageml.residual_planner import AdapterQuantInfo, PlannerConfig, choose_residual_plan
+
+    metas = [MoEAdapterMeta(f"adapter_{i}", rank=r, num_experts=8, in_features=4096, out_features=14336,
+                            dtype="bf16", request_count=c)
+             for i, (r, c) in enumerate([(16, 900), (16, 450), (8, 120), (32, 600), (64, 700), (16, 40), (16, 300)])]
+    cfg = PlannerConfig(memory_budget_mb=2000.0, dtype="bf16", hot_request_threshold=200,
+                        disaggregate_request_threshold=500, rank_specialization_threshold=16)
+    quant = {"adapter_6": AdapterQuantInfo(epsilon=0.5, safe=True)}
+    (HERE / "residual_plan.json").write_text(plan_to_json(choose_residual_plan(metas, config=cfg,
+                                                                               quant_info=quant)) + "\n")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -124,6 +142,9 @@ def main() -> None:
         return
     if args.only == "expert_lora_adapter":
         expert_lora_adapter()
+        return
+    if args.only == "residual_plan":
+        residual_plan()
         return
     import torch
     import torch.nn as nn
@@ -326,6 +347,7 @@ def main() -> None:
              materialized=np.array([0, 3]), out=np32(y))
     workload_plan()
     expert_lora_adapter()
+    residual_plan()
     print("golden vectors written to", HERE)
 
 
