@@ -285,8 +285,9 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
 
 // One expert projection of the MoE layer: decode-sized batches on the skinny GEMM,
 // otherwise the grouped GEMM with the layer's pair plan.
-int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, bool skinny, cudaStream_t st) {
-  if (skinny) return launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st);
+int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, bool skinny, cudaStream_t st, int64_t max_rows) {
+  if (skinny)
+    return launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st, max_rows);
   return run_grouped_gemm(g, b.pp, st);
 }
 
@@ -396,7 +397,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, skinny, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, skinny, st, P));
   }
   // R4 shrink of h for w2
   if (lora2) {
@@ -452,7 +453,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, skinny, st));
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, skinny, st, P));
   }
   // combine
   SB_STAGE(STAGEML_STAGE_COMBINE,

@@ -131,8 +131,9 @@ size_t pair_runs_ints(int64_t pairs_cap);
 
 // Weight-streaming variant for at most 16 valid rows per 128-row tile (decode-sized
 // batches), skinny.cu: same GemmLaunch semantics (16-bit weights; LoRA from s16 /
-// lora_b with the row's tenant), valid rows per tile from the group counts.
+// lora_b with the row's tenant), valid rows per tile from the group counts; max_rows
+// bounds the valid rows of any tile (at most 8 selects the one-m8-block variant).
 int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int32_t* group_offsets,
-                       const int32_t* group_counts, cudaStream_t stream);
+                       const int32_t* group_counts, cudaStream_t stream, int64_t max_rows = 16);
 
 }  // namespace sb

@@ -100,7 +100,9 @@ __device__ __forceinline__ void sk_chunk(float (&acc)[NBLK][4], const uint4& xl,
 // Item = (tile, 8 output columns), computed by WPI warps that split K; the partial sums of
 // an item meet in shared memory and its first warp runs the epilogue from the
 // MMA fragment: lane (g, tig) owns rows g, g+8 and columns 2tig, 2tig+1.
-template <typename T, bool SWIGLU, int WPI>
+// HI: rows 8-15 of a tile may be valid (more than 8 routed rows in all); without it
+// the second m16 half of the MMA reads constant zeros and its x rows are never loaded.
+template <typename T, bool SWIGLU, int WPI, bool HI>
 __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, int n_items) {
   constexpr int NBLK = SWIGLU ? 2 : 1;
   constexpr int IPC = kSkWarps / WPI;  // items per CTA
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
   if (valid > 0) {  // warp-uniform
     const int64_t r_lo = row0 + g, r_hi = row0 + g + 8;
     const T* x_lo = g < valid ? A + (p.a_row_of ? (int64_t)p.a_row_of[r_lo] : r_lo) * K : nullptr;
-    const T* x_hi = g + 8 < valid ? A + (p.a_row_of ? (int64_t)p.a_row_of[r_hi] : r_hi) * K : nullptr;
+    const T* x_hi = (HI && g + 8 < valid) ? A + (p.a_row_of ? (int64_t)p.a_row_of[r_hi] : r_hi) * K : nullptr;
     const T* wrow[NBLK];
 #pragma unroll
     for (int b = 0; b < NBLK; ++b) {
@@ -149,7 +151,10 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
         const int kk = k0 + u * 32 + tig * 8;
         const bool v = kk < ke;
         xl[u] = (v && x_lo) ? ldg16(x_lo + kk) : z;
-        xh[u] = (v && x_hi) ? ldg16(x_hi + kk) : z;
+        if constexpr (HI)
+          xh[u] = (v && x_hi) ? ldg16(x_hi + kk) : z;
+        else
+          xh[u] = z;
 #pragma unroll
         for (int b = 0; b < NBLK; ++b) w[u][b] = (v && wrow[b]) ? ldg16_stream(wrow[b] + kk) : z;
       }
@@ -217,29 +222,34 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
   }
 }
 
-template <typename T, bool SWIGLU>
-void launch_sk(int wpi, int n_items, const SkParams& p, cudaStream_t stream) {
+template <typename T, bool SWIGLU, bool HI>
+void launch_sk_hi(int wpi, int n_items, const SkParams& p, cudaStream_t stream) {
   const unsigned grid = (unsigned)(((int64_t)n_items * wpi + kSkWarps - 1) / kSkWarps);
   switch (wpi) {
     case 1:
-      (skinny_gemm_kernel<T, SWIGLU, 1><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      (skinny_gemm_kernel<T, SWIGLU, 1, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
       break;
     case 2:
-      (skinny_gemm_kernel<T, SWIGLU, 2><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      (skinny_gemm_kernel<T, SWIGLU, 2, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
       break;
     case 4:
-      (skinny_gemm_kernel<T, SWIGLU, 4><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      (skinny_gemm_kernel<T, SWIGLU, 4, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
       break;
     default:
-      (skinny_gemm_kernel<T, SWIGLU, 8><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
+      (skinny_gemm_kernel<T, SWIGLU, 8, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
       break;
   }
+}
+
+template <typename T, bool SWIGLU>
+void launch_sk(int wpi, int n_items, bool hi, const SkParams& p, cudaStream_t stream) {
+  hi ? launch_sk_hi<T, SWIGLU, true>(wpi, n_items, p, stream) : launch_sk_hi<T, SWIGLU, false>(wpi, n_items, p, stream);
 }
 
 }  // namespace
 
 int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int32_t* group_offsets,
-                       const int32_t* group_counts, cudaStream_t stream) {
+                       const int32_t* group_counts, cudaStream_t stream, int64_t max_rows) {
   SB_CHECK_ARG(g.a && g.b && g.out, "skinny gemm: null operand");
   SB_CHECK_ARG(!g.b_fp8, "skinny gemm: 16-bit weights only");
   SB_CHECK_ARG(g.K > 0 && g.K % 8 == 0 && g.N > 0, "skinny gemm: K=%d must be a positive multiple of 8", g.K);
@@ -284,10 +294,13 @@ int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int
   // warp per ~3-6K of K, at most 8.
   int wpi = 1;
   while (wpi < 8 && g.K >= wpi * 2 * 3072) wpi *= 2;
+  const bool hi = max_rows > 8;  // a tile holds at most max_rows valid rows
   if (g.in_bf16)
-    g.swiglu ? launch_sk<bf16, true>(wpi, (int)items, p, stream) : launch_sk<bf16, false>(wpi, (int)items, p, stream);
+    g.swiglu ? launch_sk<bf16, true>(wpi, (int)items, hi, p, stream)
+             : launch_sk<bf16, false>(wpi, (int)items, hi, p, stream);
   else
-    g.swiglu ? launch_sk<f16, true>(wpi, (int)items, p, stream) : launch_sk<f16, false>(wpi, (int)items, p, stream);
+    g.swiglu ? launch_sk<f16, true>(wpi, (int)items, hi, p, stream)
+             : launch_sk<f16, false>(wpi, (int)items, hi, p, stream);
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
