@@ -453,9 +453,10 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) of one full-size gate/up GEMM launch, from one ncu
-# capture of this build (profiles/grouped_gemm_pair_mixtral.md).
-GATE_UP_DRAM_BYTES: dict = {"mixtral_moe_lora": 2.373079e9 + 0.132927e9}
+# DRAM bytes (read + write) of one full-size gate/up GEMM (the pair kernel plus the
+# odd-tile kernel beside it), from one ncu capture of this build
+# (profiles/grouped_gemm_pair_mixtral.md).
+GATE_UP_DRAM_BYTES: dict = {"mixtral_moe_lora": (2.146935e9 + 0.114305e9) + (1.186184e9 + 0.016355e9)}
 
 
 # ------------------------------------------------------------------ other configurations
