@@ -123,13 +123,9 @@ void carve_pair_plan(Carver& c, int64_t tiles_cap, bool lora, PairPlan* pp) {
 // rows (static_rows); row_tenant only when the GEMMs carry LoRA.
 int build_pair_plan(const PairPlan& pp, const int32_t* tile_group, const int32_t* group_offsets,
                     const int32_t* num_tiles_dev, int64_t static_rows, const int32_t* row_tenant, cudaStream_t st) {
-  SB_TRY(launch_pair_plan(tile_group, group_offsets, num_tiles_dev, pp.tiles_cap, static_rows,
+  return launch_pair_plan(tile_group, group_offsets, num_tiles_dev, pp.tiles_cap, static_rows,
                           pp.pruns ? row_tenant : nullptr, pp.pairs, pp.num_pairs, pp.pruns, pp.pnruns, st,
-                          pp.singles, pp.num_singles));
-  if (pp.sruns)
-    SB_TRY(launch_tile_runs(row_tenant, pp.num_singles, num_tiles_dev ? 0 : static_rows, pp.tiles_cap, pp.sruns,
-                            pp.snruns, st, pp.singles));
-  return STAGEML_OK;
+                          pp.singles, pp.num_singles, pp.sruns, pp.snruns);
 }
 
 // Per host thread and device: a side stream and two events for running the odd tiles

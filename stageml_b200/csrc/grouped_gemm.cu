@@ -59,7 +59,7 @@ struct KParams {
   const int32_t* num_tiles_dev;
   int tiles_cap;
   const int32_t* tile_group;
-  const int32_t* tile_list;   // optional: m-tile i is tile_list[i] (LoRA runs stay indexed by i)
+  const int32_t* tile_list;   // optional: m-tile i is tile_list[i] (LoRA runs indexed by the tile id)
   int64_t m_rows;
   // LoRA
   int rank;
@@ -116,10 +116,17 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
   }
 }
 
+// LoRA runs of m-tile m_pos are stored at its tile id (tile_list[m_pos] with a list).
+__device__ __forceinline__ int run_slot(const KParams& p, int m_pos) { return p.tile_list ? p.tile_list[m_pos] : m_pos; }
+
 __device__ __forceinline__ int tile_lora_runs(const KParams& p, int m_pos) {
   if (p.rank == 0) return 0;
-  const int n = p.tile_nruns[m_pos];
+  const int n = p.tile_nruns[run_slot(p, m_pos)];
   return n < kMaxRunsPerTile ? n : kMaxRunsPerTile;
+}
+// Run r of the tile whose runs are in slot `slot`.
+__device__ __forceinline__ const int32_t* tile_run(const KParams& p, int slot, int r) {
+  return p.tile_runs + ((int64_t)slot * kMaxRunsPerTile + min(r, kMaxRunsPerTile - 1)) * 5;
 }
 
 // 16 e4m3 values (one 16-byte chunk) -> 16 x 16-bit, scaled.
@@ -271,8 +278,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           if (p.swiglu) tma_load_2d(base + (p.lchunks + ch) * LCHUNK, &tm_s, bar, p.rank + ch * 16, a_row, pol_a);
         }
         for (int jj = 0; jj < nr; ++jj) {
-          const int tenant = p.tile_runs[((int64_t)m_pos * kMaxRunsPerTile + r0 + jj) * 5];
-          const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
+          const int brow = (int)(tile_run(p, m_tile, r0 + jj)[0] * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
             if (p.swiglu) {
@@ -328,6 +334,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         tc_commit(empty_bar(s));
         issued_any = true;
       }
+      const int slot = run_slot(p, m_pos);
       const int nruns = ok ? tile_lora_runs(p, m_pos) : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
@@ -340,7 +347,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         tc_fence_after();
         const uint32_t base = smem_base + s * STAGE_BYTES;
         for (int jj = 0; jj < nr; ++jj) {
-          const int32_t* run = p.tile_runs + ((int64_t)m_pos * kMaxRunsPerTile + r0 + jj) * 5;
+          const int32_t* run = tile_run(p, slot, r0 + jj);
           const uint32_t d0 = ~(uint32_t)run[1], d1 = ~(uint32_t)run[2], d2 = ~(uint32_t)run[3],
                          d3 = ~(uint32_t)run[4];
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
@@ -460,6 +467,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
       const int64_t b_row0 = (int64_t)group * p.b_group_rows + n0;
       const int64_t b_row1 = p.swiglu ? b_row0 + p.N : b_row0 + 128;
+      const int tile_nruns = tile_lora_runs(p, m_pos);  // used after the K loop
       float sc[4];
       int rr[4], cc[4];
 #pragma unroll
@@ -494,7 +502,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         fence_proxy_async_smem();
         mbar_arrive(full_bar(s));
       }
-      const int nruns = ok ? tile_lora_runs(p, m_pos) : 0;
+      const int nruns = ok ? tile_nruns : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -558,14 +566,14 @@ __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restric
     __syncwarp();
   }
   for (int j = lane; j < count; j += 32) {
-    int32_t* r = runs + ((int64_t)tile * kMaxRunsPerTile + j) * 5;
+    int32_t* r = runs + ((int64_t)src_tile * kMaxRunsPerTile + j) * 5;
     r[0] = s_ten[w][j];
     r[1] = (int32_t)s_mask[w][j][0];
     r[2] = (int32_t)s_mask[w][j][1];
     r[3] = (int32_t)s_mask[w][j][2];
     r[4] = (int32_t)s_mask[w][j][3];
   }
-  if (lane == 0) nruns[tile] = count;
+  if (lane == 0) nruns[src_tile] = count;
 }
 
 template <typename T, bool FP8B>

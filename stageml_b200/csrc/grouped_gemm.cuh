@@ -68,7 +68,7 @@ struct GemmLaunch {
   const int32_t* pairs = nullptr;        // [pairs_cap][4]
   const int32_t* num_pairs_dev = nullptr;
   int pairs_cap = 0;
-  const int32_t* pair_runs = nullptr;    // [pairs_cap][kMaxRunsPerPair][kPairRunInts]
+  const int32_t* pair_runs = nullptr;    // [tiles][kMaxRunsPerPair][kPairRunInts], at each pair's first tile
   const int32_t* pair_nruns = nullptr;   // [pairs_cap]
   // The pair kernel and the odd-tile kernel side by side (split_sms > 0): each
   // reads the pair and odd-tile counts and keeps only its share of the split_sms
@@ -103,7 +103,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
                      int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list = nullptr);
 // With tile_list, entry i covers tile tile_list[i] (i < *num_tiles_dev) and runs / nruns
-// are indexed by i; static_rows > 0 then bounds the rows read (direct rows).
+// are indexed by that tile id; static_rows > 0 then bounds the rows read (direct rows).
 constexpr int kMaxRunsPerTile = 128;
 
 // CTA-pair variant of the grouped GEMM: 256-row tiles made of two 128-row tiles
@@ -117,16 +117,18 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream);
 // (group_offsets[g] / 128), a trailing odd tile paired with -1. Direct rows:
 // tiles (2j, 2j+1) of ceil(static_rows / 128). pairs[4p..4p+3] = first tile,
 // second tile or -1, first pair of the group, pairs in the group. pairs_cap =
-// tiles_cap (grouped) or the direct tile count. With row_tenant set, also writes the LoRA runs of every
-// pair: runs[(pair*kMaxRunsPerPair + j)*kPairRunInts + 0] = tenant, [1..8] = mask
-// words over the pair's 256 rows; nruns[pair].
+// tiles_cap (grouped) or the direct tile count. With row_tenant set, also writes the
+// LoRA runs of every pair at its first tile t: runs[(t*kMaxRunsPerPair + j)*kPairRunInts
+// + 0] = tenant, [1..8] = mask words over the pair's 256 rows; nruns[t].
+// With `singles`, a group's trailing odd tile is listed there (count in *num_singles)
+// instead of forming a pair with an idle half; the one-CTA kernel runs those tiles
+// (GemmLaunch::tile_list), and with row_tenant and sruns / snruns their runs are
+// written as launch_tile_runs does (at the tile id). One launch.
 int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
                      int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream,
-                     int32_t* singles = nullptr, int32_t* num_singles = nullptr);
-// With `singles`, a group's trailing odd tile is listed there (count in *num_singles)
-// instead of forming a pair with an idle half; the one-CTA kernel runs those tiles
-// (GemmLaunch::tile_list).
+                     int32_t* singles = nullptr, int32_t* num_singles = nullptr, int32_t* sruns = nullptr,
+                     int32_t* snruns = nullptr);
 size_t pair_runs_ints(int64_t pairs_cap);
 
 // Weight-streaming variant for at most 16 valid rows per 128-row tile (decode-sized

@@ -63,8 +63,8 @@ struct PParams {
   int runs_per_block;
   int64_t lb_tenant_rows;
   int64_t lb_group_rows;
-  const int32_t* runs;           // [pairs_cap][kMaxRunsPerPair][9]
-  const int32_t* nruns;          // [pairs_cap]
+  const int32_t* runs;           // [tiles][kMaxRunsPerPair][9], at each pair's first tile
+  const int32_t* nruns;          // [tiles]
   // epilogue
   const float* row_scale;
   const void* bias;
@@ -107,10 +107,14 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
   }
 }
 
-__device__ __forceinline__ int pair_lora_runs(const PParams& p, int pm) {
+// LoRA runs of a pair are stored at its first tile m0.
+__device__ __forceinline__ int pair_lora_runs(const PParams& p, int m0) {
   if (p.rank == 0) return 0;
-  const int n = p.nruns[pm];
+  const int n = p.nruns[m0];
   return n < kMaxRunsPerPair ? n : kMaxRunsPerPair;
+}
+__device__ __forceinline__ const int32_t* pair_run(const PParams& p, int m0, int r) {
+  return p.runs + ((int64_t)m0 * kMaxRunsPerPair + min(r, kMaxRunsPerPair - 1)) * kPairRunInts;
 }
 
 __device__ __forceinline__ int num_pairs(const PParams& p) {
@@ -224,6 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int a_row = m_load * BM;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
       const int b_row = group * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
+      const int nruns = pair_lora_runs(p, m0);
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -238,7 +243,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         last_phase[s] = (int)ph;
       }
       // LoRA blocks: this CTA's rows of S + its half of the B rows of each tenant run
-      const int nruns = ok ? pair_lora_runs(p, pm) : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -254,8 +258,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (p.swiglu) load(base + (p.lchunks + ch) * LCHUNK, &tm_s, s, p.rank + ch * 16, a_row, pol_a);
         }
         for (int jj = 0; jj < nr; ++jj) {
-          const int tenant = p.runs[((int64_t)pm * kMaxRunsPerPair + r0 + jj) * kPairRunInts];
-          const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
+          const int brow = (int)(pair_run(p, m0, r0 + jj)[0] * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
             if (p.swiglu) {
@@ -296,6 +299,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t aph = (tcount >> 1) & 1;
       int pm, n_tile_unused;
       unit_coords(p, u, pm, n_tile_unused);
+      const int m0 = p.pairs[4 * pm];
       if (!mbar_wait_cluster(tempty_bar(acc), aph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
         ok = false;
         break;
@@ -318,7 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_mma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
         tc_commit_pair_both(empty_bar(s), 0x3);
       }
-      const int nruns = ok ? pair_lora_runs(p, pm) : 0;
+      const int nruns = ok ? pair_lora_runs(p, m0) : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t base = smem_base + s * STAGE_BYTES;
         for (int jj = 0; jj < nr; ++jj) {
-          const int32_t* run = p.runs + ((int64_t)pm * kMaxRunsPerPair + r0 + jj) * kPairRunInts;
+          const int32_t* run = pair_run(p, m0, r0 + jj);
           uint32_t dis[8];
 #pragma unroll
           for (int w = 0; w < 8; ++w) dis[w] = ~(uint32_t)run[1 + w];
@@ -448,47 +452,140 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-// ------------------------------------------------------------ pair list
-// One CTA: pairs of consecutive 128-row tiles of the same group. Tile t opens a
-// pair when its distance from its group's first tile is even; its partner is
-// t + 1 when that tile exists and belongs to the same group. A group's trailing
-// odd tile goes to `singles` when that list is given (for the one-CTA kernel),
-// else it forms a pair with an idle half (-1). Each pair also records its
-// group's first pair and pair count (for the unit order).
-__global__ void __launch_bounds__(1024) pair_tiles_kernel(const int32_t* __restrict__ tile_group,
-                                                          const int32_t* __restrict__ group_offsets,
-                                                          const int32_t* __restrict__ num_tiles_dev, int tiles_cap,
-                                                          int64_t static_rows, int32_t* __restrict__ pairs,
-                                                          int32_t* __restrict__ num_pairs_out,
-                                                          int32_t* __restrict__ singles,
-                                                          int32_t* __restrict__ num_singles_out) {
-  __shared__ int32_t warp_tot[2][32];
-  __shared__ int32_t carry[2];
+// ------------------------------------------------------------ pair list and LoRA runs
+// Tile t opens a pair when its distance from its group's first tile is even; its
+// partner is t + 1 when that tile exists and belongs to the same group. A group's
+// trailing odd tile is a single when singles are listed (for the one-CTA kernel),
+// else it forms a pair with an idle half (-1).
+struct TileRole {
+  int start, partner, in_group, group_tiles;
+};
+
+__device__ __forceinline__ TileRole tile_role(const int32_t* tile_group, const int32_t* group_offsets, int ntiles,
+                                              int t) {
+  TileRole r{0, -1, 0, 0};
+  if (t >= ntiles) return r;
+  if (tile_group) {
+    const int g = tile_group[t];
+    const int t0 = group_offsets[g] >> 7;
+    r.in_group = (t - t0) >> 1;
+    r.group_tiles = (group_offsets[g + 1] - group_offsets[g]) >> 7;
+    r.start = ((t - t0) & 1) == 0;
+    if (r.start && t + 1 < ntiles && tile_group[t + 1] == g) r.partner = t + 1;
+  } else {
+    r.in_group = t >> 1;
+    r.group_tiles = ntiles;
+    r.start = (t & 1) == 0;
+    if (r.start && t + 1 < ntiles) r.partner = t + 1;
+  }
+  return r;
+}
+
+constexpr int kPlanThreads = 128;
+constexpr int kPlanWarps = kPlanThreads / 32;
+
+// Distinct tenants (>= 0) of NQ row quarters of 32 (first-seen order) and the
+// rows each one owns, one warp; every quarter's tenant is loaded before the
+// first match so the loads overlap. Writes runs[j * ints + 0] = tenant,
+// [1 .. NQ] = mask words, and *nruns.
+template <int NQ>
+__device__ __forceinline__ void quarter_runs(const int32_t* row_tenant, const int64_t (&qrow)[NQ], int64_t row_bound,
+                                             int32_t* s_ten, uint32_t (*s_mask)[8], int32_t* runs, int32_t* nruns,
+                                             int max_runs) {
+  const int lane = threadIdx.x & 31;
+  int ten[NQ];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int64_t row = qrow[q] < 0 ? -1 : qrow[q] + lane;
+    ten[q] = (row >= 0 && row < row_bound) ? row_tenant[row] : -1;
+  }
+  int count = 0;
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int t = ten[q];
+    const unsigned peers = __match_any_sync(0xffffffffu, t);
+    const bool lead = (t >= 0) && ((peers & ((1u << lane) - 1u)) == 0u);
+    int found = -1;
+    if (lead)
+      for (int j = 0; j < count; ++j)
+        if (s_ten[j] == t) {
+          found = j;
+          break;
+        }
+    const unsigned is_new = __ballot_sync(0xffffffffu, lead && found < 0);
+    if (lead) {
+      int idx = found;
+      if (found < 0) {
+        idx = count + __popc(is_new & ((1u << lane) - 1u));
+        if (idx < max_runs) {
+          s_ten[idx] = t;
+#pragma unroll
+          for (int qq = 0; qq < NQ; ++qq) s_mask[idx][qq] = 0u;
+        }
+      }
+      if (idx < max_runs) s_mask[idx][q] = peers;
+    }
+    count += __popc(is_new);
+    __syncwarp();
+  }
+  count = min(count, max_runs);
+  for (int j = lane; j < count; j += 32) {
+    int32_t* r = runs + (int64_t)j * (1 + NQ);
+    r[0] = s_ten[j];
+#pragma unroll
+    for (int qq = 0; qq < NQ; ++qq) r[1 + qq] = (int32_t)s_mask[j][qq];
+  }
+  if (lane == 0) *nruns = count;
+}
+
+// One launch for the whole plan. Block 0 lists the pairs (and the singles) in tile
+// order, each with its group's first pair and pair count (for the unit order).
+// Blocks 1.. (with row_tenant): one warp per tile t, which writes the LoRA runs of
+// the pair t opens at pruns[t] / pnruns[t] (256 rows, 8 mask words), or of the single
+// t at sruns[t] / snruns[t] (128 rows, 4 mask words): runs are indexed by the first
+// tile, so no block waits for the list.
+__global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
+    const int32_t* __restrict__ tile_group, const int32_t* __restrict__ group_offsets,
+    const int32_t* __restrict__ num_tiles_dev, int tiles_cap, int64_t static_rows, const int32_t* __restrict__ row_tenant,
+    int32_t* __restrict__ pairs, int32_t* __restrict__ num_pairs_out, int32_t* __restrict__ singles,
+    int32_t* __restrict__ num_singles_out, int32_t* __restrict__ pruns, int32_t* __restrict__ pnruns,
+    int32_t* __restrict__ sruns, int32_t* __restrict__ snruns) {
   const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const bool split = singles != nullptr;
+  if (blockIdx.x > 0) {
+    __shared__ int32_t s_ten[kPlanWarps][kMaxRunsPerPair];
+    __shared__ uint32_t s_mask[kPlanWarps][kMaxRunsPerPair][8];
+    const int t = (blockIdx.x - 1) * kPlanWarps + w;
+    const TileRole r = tile_role(tile_group, group_offsets, ntiles, t);
+    if (!r.start) return;
+    const int64_t bound = num_tiles_dev ? INT64_MAX : static_rows;
+    if (split && r.partner < 0) {
+      if (!sruns) return;
+      const int64_t q4[4] = {(int64_t)t * 128, (int64_t)t * 128 + 32, (int64_t)t * 128 + 64, (int64_t)t * 128 + 96};
+      quarter_runs<4>(row_tenant, q4, bound, s_ten[w], s_mask[w], sruns + (int64_t)t * kMaxRunsPerTile * 5,
+                      snruns + t, kMaxRunsPerTile);
+    } else {
+      int64_t q8[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int tile = q < 4 ? t : r.partner;
+        q8[q] = tile < 0 ? -1 : (int64_t)tile * 128 + (q & 3) * 32;
+      }
+      quarter_runs<8>(row_tenant, q8, bound, s_ten[w], s_mask[w],
+                      pruns + (int64_t)t * kMaxRunsPerPair * kPairRunInts, pnruns + t, kMaxRunsPerPair);
+    }
+    return;
+  }
+  __shared__ int32_t warp_tot[2][kPlanWarps];
+  __shared__ int32_t carry[2];
   if (tid < 2) carry[tid] = 0;
   __syncthreads();
-  for (int base = 0; base < ntiles; base += 1024) {
+  for (int base = 0; base < ntiles; base += kPlanThreads) {
     const int t = base + tid;
-    int start = 0, partner = -1, in_group = 0, group_tiles = 0;
-    if (t < ntiles) {
-      if (tile_group) {
-        const int g = tile_group[t];
-        const int t0 = group_offsets[g] >> 7;
-        in_group = (t - t0) >> 1;
-        group_tiles = (group_offsets[g + 1] - group_offsets[g]) >> 7;
-        start = ((t - t0) & 1) == 0;
-        if (start && t + 1 < ntiles && tile_group[t + 1] == g) partner = t + 1;
-      } else {
-        in_group = t >> 1;
-        group_tiles = ntiles;
-        start = (t & 1) == 0;
-        if (start && t + 1 < ntiles) partner = t + 1;
-      }
-    }
-    const bool as_single = split && start && partner < 0;
-    const bool as_pair = start && !as_single;
+    const TileRole r = tile_role(tile_group, group_offsets, ntiles, t);
+    const bool as_single = split && r.start && r.partner < 0;
+    const bool as_pair = r.start && !as_single;
     const unsigned bp = __ballot_sync(0xffffffffu, as_pair), bs = __ballot_sync(0xffffffffu, as_single);
     if (lane == 0) {
       warp_tot[0][w] = __popc(bp);
@@ -500,9 +597,9 @@ __global__ void __launch_bounds__(1024) pair_tiles_kernel(const int32_t* __restr
       int before = carry[0] + __popc(bp & lt);
       for (int i = 0; i < w; ++i) before += warp_tot[0][i];
       pairs[4 * before] = t;
-      pairs[4 * before + 1] = partner;
-      pairs[4 * before + 2] = before - in_group;  // the group's first pair
-      pairs[4 * before + 3] = split ? group_tiles >> 1 : (group_tiles + 1) >> 1;
+      pairs[4 * before + 1] = r.partner;
+      pairs[4 * before + 2] = before - r.in_group;  // the group's first pair
+      pairs[4 * before + 3] = split ? r.group_tiles >> 1 : (r.group_tiles + 1) >> 1;
     }
     if (as_single) {
       int before = carry[1] + __popc(bs & lt);
@@ -512,7 +609,7 @@ __global__ void __launch_bounds__(1024) pair_tiles_kernel(const int32_t* __restr
     __syncthreads();
     if (tid < 2) {
       int tot = 0;
-      for (int i = 0; i < 32; ++i) tot += warp_tot[tid][i];
+      for (int i = 0; i < kPlanWarps; ++i) tot += warp_tot[tid][i];
       carry[tid] += tot;
     }
     __syncthreads();
@@ -521,55 +618,6 @@ __global__ void __launch_bounds__(1024) pair_tiles_kernel(const int32_t* __restr
     *num_pairs_out = carry[0];
     if (num_singles_out) *num_singles_out = carry[1];
   }
-}
-
-// One warp per pair: distinct tenants of its 256 rows (first-seen order over the
-// 8 row quarters) and the 256-bit mask of the rows each one owns.
-__global__ void __launch_bounds__(64) pair_runs_kernel(const int32_t* __restrict__ row_tenant,
-                                                       const int32_t* __restrict__ pairs,
-                                                       const int32_t* __restrict__ num_pairs_dev, int pairs_cap,
-                                                       int64_t static_rows, int32_t* __restrict__ runs,
-                                                       int32_t* __restrict__ nruns) {
-  __shared__ int32_t s_ten[2][kMaxRunsPerPair];
-  __shared__ uint32_t s_mask[2][kMaxRunsPerPair][8];
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pr = blockIdx.x * 2 + w;
-  const int np = min(*num_pairs_dev, pairs_cap);
-  if (pr >= np) return;
-  int count = 0;
-  for (int q = 0; q < 8; ++q) {
-    const int tile = pairs[4 * pr + (q >> 2)];
-    const int64_t row = (int64_t)tile * 128 + (q & 3) * 32 + lane;
-    const int t = (tile >= 0 && (static_rows < 0 || row < static_rows)) ? row_tenant[row] : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, t);
-    const bool lead = (t >= 0) && ((peers & ((1u << lane) - 1u)) == 0u);
-    int found = -1;
-    if (lead)
-      for (int j = 0; j < count; ++j)
-        if (s_ten[w][j] == t) {
-          found = j;
-          break;
-        }
-    const unsigned is_new = __ballot_sync(0xffffffffu, lead && found < 0);
-    if (lead) {
-      int idx = found;
-      if (found < 0) {
-        idx = count + __popc(is_new & ((1u << lane) - 1u));
-        s_ten[w][idx] = t;
-        for (int qq = 0; qq < 8; ++qq) s_mask[w][idx][qq] = 0u;
-      }
-      s_mask[w][idx][q] = peers;
-    }
-    count += __popc(is_new);
-    __syncwarp();
-  }
-  for (int j = lane; j < count; j += 32) {
-    int32_t* r = runs + ((int64_t)pr * kMaxRunsPerPair + j) * kPairRunInts;
-    r[0] = s_ten[w][j];
-#pragma unroll
-    for (int qq = 0; qq < 8; ++qq) r[1 + qq] = (int32_t)s_mask[w][j][qq];
-  }
-  if (lane == 0) nruns[pr] = count;
 }
 
 template <typename T>
@@ -620,23 +668,20 @@ size_t pair_runs_ints(int64_t pairs_cap) { return (size_t)pairs_cap * kMaxRunsPe
 int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
                      int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream, int32_t* singles,
-                     int32_t* num_singles) {
+                     int32_t* num_singles, int32_t* sruns, int32_t* snruns) {
   SB_CHECK_ARG(pairs && num_pairs, "pair plan: null output");
   SB_CHECK_ARG(!singles == !num_singles, "pair plan: singles need their count");
   SB_CHECK_ARG(!tile_group || (group_offsets && num_tiles_dev), "pair plan: grouped tiles need offsets and a count");
+  SB_CHECK_ARG(!row_tenant || (runs && nruns), "pair plan: LoRA runs need output buffers");
+  SB_CHECK_ARG(!sruns == !snruns, "pair plan: single-tile runs need their counts");
   const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
-  (pair_tiles_kernel<<<1, 1024, 0, stream>>>(tile_group, group_offsets, num_tiles_dev, tiles_cap, static_rows, pairs,
-                                              num_pairs, singles, num_singles),
+  const int64_t run_blocks = (row_tenant && tiles > 0) ? (tiles + kPlanWarps - 1) / kPlanWarps : 0;
+  SB_CHECK_ARG(run_blocks < 65535 * 1024LL, "pair plan: too many tiles");
+  (pair_plan_kernel<<<(unsigned)(1 + run_blocks), kPlanThreads, 0, stream>>>(
+       tile_group, group_offsets, num_tiles_dev, tiles_cap, static_rows, row_tenant, pairs, num_pairs, singles,
+       num_singles, row_tenant ? runs : nullptr, nruns, row_tenant ? sruns : nullptr, snruns),
    ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
-  if (row_tenant && tiles > 0) {
-    SB_CHECK_ARG(runs && nruns, "pair plan: LoRA runs need output buffers");
-    const int64_t pairs_cap = tiles;
-    (pair_runs_kernel<<<(unsigned)((pairs_cap + 1) / 2), 64, 0, stream>>>(
-         row_tenant, pairs, num_pairs, (int)pairs_cap, num_tiles_dev ? -1 : static_rows, runs, nruns),
-     ::sb::count_launch());
-    SB_CUDA_CHECK(cudaGetLastError());
-  }
   return STAGEML_OK;
 }
 

@@ -23,6 +23,7 @@ struct PermuteScratch {
   uint32_t* sorted;  // [nchunks * 2048]
   int32_t* hist;     // [nkeys * nchunks]
   int32_t* off;      // [nchunks * nkeys] destination offsets
+  int32_t* ticket;   // [1] chunks finished (multi-chunk rank kernel); zeroed by launch_permute
 };
 constexpr int kPermChunk = 2048;
 int64_t permute_num_keys(int n_groups_total, int n_tenants, int group_by_tenant, int n_experts_total);

@@ -4,7 +4,11 @@
 //
 // The reference groups rows with one torch.nonzero per (slot, expert) and a
 // host sync each (benchmarks/multitenant_bta_system_bench.py:401-406); here the
-// whole grouping is three kernels (one when P <= 2048) with no host round trip:
+// whole grouping runs on the device with no host round trip. Up to 1024 keys
+// (every MoE-LoRA shape here) one kernel ranks the pairs of each 2048-pair chunk
+// by warp matching and its last CTA builds the plan (perm_rank_kernel; a second
+// kernel places the pairs beyond 8 chunks). Beyond 1024 keys it is three
+// kernels (one when P <= 2048):
 //   count   one CTA per 2048-pair chunk: bitonic sort of (key << 11 | index)
 //           in shared memory, per-key counts of the chunk -> hist[chunk][key]
 //   scan    one CTA: per-key totals, per-group counts, padded group offsets,
@@ -313,6 +317,120 @@ __global__ void __launch_bounds__(1024) perm_fused_kernel(PairSrc a, int nkeys, 
   }
 }
 
+// Up to kRankMaxKeys keys: ranks by warp matching instead of a sort. One CTA per
+// 2048-pair chunk; warp w owns chunk entries [64 w, 64 w + 64) in two rounds of 32.
+// Within a round __match_any_sync finds the lanes of each key, so an entry's rank
+// among the chunk's entries of its key is (earlier warps' count of the key) +
+// (this warp's count from its earlier round) + (lower lanes of the same key) --
+// chunk order, i.e. the stable order. Each entry is written as key << 11 | rank.
+// The last CTA to finish (ticket) turns the per-chunk counts into the plan
+// (plan_groups) and the per-(chunk, key) first rows; with few chunks it also
+// places every pair, else perm_place_kernel does.
+constexpr int kRankMaxKeys = 1024;
+constexpr int kLastPlacesChunks = 8;
+
+__global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, int n_groups, stageml_moe_plan plan,
+                                                          uint32_t* __restrict__ rank_key, int32_t* __restrict__ hist,
+                                                          int32_t* __restrict__ off, int32_t* __restrict__ ticket,
+                                                          int32_t* status) {
+  extern __shared__ int32_t sm[];  // [32][nkeys] per-warp counts; in the last CTA tot[nkeys] + offsets
+  __shared__ int32_t warp_part[32];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int nch = (int)gridDim.x;
+  const int64_t base = (int64_t)blockIdx.x * kPermChunk;
+  const int64_t live = live_pairs(a);
+  for (int i = tid; i < 32 * nkeys; i += 1024) sm[i] = 0;
+  __syncthreads();
+  const unsigned below = (1u << lane) - 1u;
+  uint32_t key[2];
+  int rnk[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int64_t p = base + w * 64 + r * 32 + lane;
+    const uint32_t k = p < live ? pair_key(a, p, status) : kSentKey;
+    const unsigned peers = __match_any_sync(0xffffffffu, k);
+    const int before = k != kSentKey ? sm[w * nkeys + (int)k] : 0;
+    __syncwarp();
+    if (k != kSentKey && (peers & below) == 0u) sm[w * nkeys + (int)k] = before + __popc(peers);
+    __syncwarp();
+    key[r] = k;
+    rnk[r] = before + __popc(peers & below);
+  }
+  __syncthreads();
+  for (int k = tid; k < nkeys; k += 1024) {  // exclusive prefix over warps, chunk total
+    int run = 0;
+    for (int ww = 0; ww < 32; ++ww) {
+      const int c = sm[ww * nkeys + k];
+      sm[ww * nkeys + k] = run;
+      run += c;
+    }
+    hist[(int64_t)blockIdx.x * nkeys + k] = run;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int64_t p = base + w * 64 + r * 32 + lane;
+    if (p < a.P)
+      rank_key[p] = key[r] == kSentKey ? 0xFFFFFFFFu : ((key[r] << 11) | (uint32_t)(sm[w * nkeys + (int)key[r]] + rnk[r]));
+  }
+  // Classic last-block pattern: every thread's writes are fenced before the ticket.
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int t = nch == 1 ? 0 : atomicAdd(ticket, 1);
+    s_last = t == nch - 1;
+    if (s_last && nch > 1) *ticket = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  int32_t* tot = sm;  // [nkeys]
+  for (int k = tid; k < nkeys; k += 1024) {
+    int s = 0;
+#pragma unroll 4
+    for (int c = 0; c < nch; ++c) s += __ldcg(hist + (int64_t)c * nkeys + k);
+    tot[k] = s;
+  }
+  __syncthreads();
+  plan_groups(tot, a.tkeys, n_groups, plan, warp_part);
+  const bool place_here = nch <= kLastPlacesChunks;
+  int32_t* offs = place_here ? sm + nkeys : off;  // [nch][nkeys]
+  for (int k = tid; k < nkeys; k += 1024) {
+    int b = tot[k];
+#pragma unroll 4
+    for (int c = 0; c < nch; ++c) {
+      const int v = __ldcg(hist + (int64_t)c * nkeys + k);
+      offs[(int64_t)c * nkeys + k] = b;
+      b += v;
+    }
+  }
+  if (!place_here) return;
+  __syncthreads();
+  for (int64_t p = tid; p < a.P; p += 1024) {
+    const uint32_t v = __ldcg(rank_key + p);
+    const uint32_t k = v >> 11;
+    if (k == kSentKey) {
+      plan.pair_row[p] = -1;
+      continue;
+    }
+    place_pair(a, plan, p, offs[(p / kPermChunk) * nkeys + k] + (int)(v & 2047u));
+  }
+}
+
+__global__ void __launch_bounds__(256) perm_place_kernel(PairSrc a, int nkeys, const uint32_t* __restrict__ rank_key,
+                                                          const int32_t* __restrict__ off, stageml_moe_plan plan) {
+  const int64_t p = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (p >= a.P) return;
+  const uint32_t v = rank_key[p];
+  const uint32_t k = v >> 11;
+  if (k == kSentKey) {
+    plan.pair_row[p] = -1;
+    return;
+  }
+  place_pair(a, plan, p, off[(p / kPermChunk) * nkeys + k] + (int)(v & 2047u));
+}
+
 }  // namespace
 
 int64_t permute_num_keys(int n_groups_total, int n_tenants, int group_by_tenant, int n_experts_total) {
@@ -321,7 +439,7 @@ int64_t permute_num_keys(int n_groups_total, int n_tenants, int group_by_tenant,
   return (int64_t)n_experts_total * (n_tenants + 1);
 }
 
-static int64_t nchunks_of(int64_t P) { return (P + kPermChunk - 1) / kPermChunk; }
+static int64_t nchunks_of(int64_t P) { return P > 0 ? (P + kPermChunk - 1) / kPermChunk : 1; }
 
 size_t permute_scratch_bytes(int64_t P, int64_t nkeys) {
   const int64_t nch = nchunks_of(P);
@@ -329,6 +447,7 @@ size_t permute_scratch_bytes(int64_t P, int64_t nkeys) {
   b += ((size_t)nch * kPermChunk * 4 + 255) & ~size_t(255);
   b += ((size_t)nkeys * nch * 4 + 255) & ~size_t(255);
   b += ((size_t)nkeys * nch * 4 + 255) & ~size_t(255);
+  b += 256;  // ticket
   return b;
 }
 
@@ -340,6 +459,8 @@ void permute_carve(void* base, int64_t P, int64_t nkeys, PermuteScratch* out) {
   out->hist = reinterpret_cast<int32_t*>(p);
   p += ((size_t)nkeys * nch * 4 + 255) & ~size_t(255);
   out->off = reinterpret_cast<int32_t*>(p);
+  p += ((size_t)nkeys * nch * 4 + 255) & ~size_t(255);
+  out->ticket = reinterpret_cast<int32_t*>(p);
 }
 
 int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
@@ -387,6 +508,22 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
   a.T_dev = T_dev;
 
   const int64_t nch = nchunks_of(P);
+  if (nkeys <= kRankMaxKeys) {
+    const size_t smem_r = (size_t)32 * nkeys * 4;
+    SB_CHECK_ARG(nch <= 65535, "permute: too many pairs");
+    if (nch > 1) SB_CUDA_CHECK(cudaMemsetAsync(scr.ticket, 0, sizeof(int32_t), stream));
+    SB_CUDA_CHECK(cudaFuncSetAttribute(perm_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_r));
+    (perm_rank_kernel<<<(unsigned)nch, 1024, smem_r, stream>>>(a, (int)nkeys, n_groups, plan, scr.sorted, scr.hist,
+                                                               scr.off, scr.ticket, status),
+     ::sb::count_launch());
+    SB_CUDA_CHECK(cudaGetLastError());
+    if (nch > kLastPlacesChunks) {
+      (perm_place_kernel<<<(unsigned)((P + 255) / 256), 256, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.off, plan),
+       ::sb::count_launch());
+      SB_CUDA_CHECK(cudaGetLastError());
+    }
+    return STAGEML_OK;
+  }
   const size_t smem = (size_t)nkeys * 4;
   if (nch == 1) {
     SB_CUDA_CHECK(cudaFuncSetAttribute(perm_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
