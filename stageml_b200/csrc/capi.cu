@@ -281,9 +281,11 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
 
 // One expert projection of the MoE layer: decode-sized batches on the skinny GEMM,
 // otherwise the grouped GEMM with the layer's pair plan.
-int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, bool skinny, cudaStream_t st, int64_t max_rows) {
+int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, bool skinny, cudaStream_t st, int64_t max_rows,
+                 int pdl_mode = 0) {
   if (skinny)
-    return launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st, max_rows);
+    return launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st, max_rows,
+                              pdl_mode);
   return run_grouped_gemm(g, b.pp, st);
 }
 
@@ -303,6 +305,13 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   const int bf = a->act_dtype == STAGEML_BF16;
   const bool lora13 = a->rank > 0 && a->lora_a13;
   const bool lora2 = a->rank > 0 && a->lora_a2;
+  // Decode-sized batches (at most 16 routed rows in all) stream the weights with the
+  // skinny GEMM; larger ones use the tensor-memory GEMM and its tile / pair plan.
+  const bool skinny = P <= kSkinnyMaxPairs && a->weight_dtype != STAGEML_E4M3;
+  // Their chain of small kernels runs as programmatic dependent launches: each one is
+  // scheduled while the previous one finishes, and each skinny GEMM streams its
+  // weights while the shrink before it runs.
+  const bool pdl = skinny && pdl_enabled();
 
   // R1: routing
   const void* ids = a->topk_ids;
@@ -311,7 +320,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   int wts_dtype = a->weights_dtype;
   if (!ids && a->k > 0) {
     SB_STAGE(STAGEML_STAGE_ROUTE, launch_route(a->x, a->act_dtype, a->router_w, a->T, a->H, a->E, a->k,
-                                               a->renormalize, b.logits, b.ids, b.weights, st));
+                                               a->renormalize, b.logits, b.ids, b.weights, st, pdl));
     ids = b.ids;
     ids_dtype = STAGEML_I32;
     wts = b.weights;
@@ -322,11 +331,8 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   const int64_t nkeys = permute_num_keys(0, a->n_tenants, 0, E_tot);
   permute_carve(b.perm_scratch, P, nkeys, &scr);
   SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
-                        b.plan, status, scr, st, a->T_dev));
+                        b.plan, status, scr, st, a->T_dev, pdl));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
-  // Decode-sized batches (at most 16 routed rows in all) stream the weights with the
-  // skinny GEMM; larger ones use the tensor-memory GEMM and its tile / pair plan.
-  const bool skinny = P <= kSkinnyMaxPairs && a->weight_dtype != STAGEML_E4M3;
   if (!skinny && b.pp.on()) {
     SB_STAGE(STAGEML_STAGE_PERMUTE, build_pair_plan(b.pp, b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles,
                                                     0, b.plan.row_tenant, st));
@@ -357,7 +363,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       s.lora_scale = a->lora_scale;
     }
     if (skinny)
-      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(s, b.plan.pair_row, P, st));
+      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(s, b.plan.pair_row, P, st, pdl));
     else
       SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(s, st));
   }
@@ -393,7 +399,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, skinny, st, P));
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, skinny, st, P, pdl ? (lora13 ? 2 : 1) : 0));
   }
   // R4 shrink of h for w2
   if (lora2) {
@@ -413,7 +419,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     s.s_out = b.s2;
     s.lora_scale = a->lora_scale;
     if (skinny)
-      SB_STAGE(STAGEML_STAGE_SHRINK_H, launch_pair_shrink(s, b.plan.pair_row, P, st));
+      SB_STAGE(STAGEML_STAGE_SHRINK_H, launch_pair_shrink(s, b.plan.pair_row, P, st, pdl));
     else
       SB_STAGE(STAGEML_STAGE_SHRINK_H, launch_gather_shrink(s, st));
   }
@@ -449,11 +455,11 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, skinny, st, P));
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, skinny, st, P, pdl ? (lora2 ? 2 : 1) : 0));
   }
   // combine
   SB_STAGE(STAGEML_STAGE_COMBINE,
-           launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st, a->T_dev));
+           launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st, a->T_dev, pdl));
   return STAGEML_OK;
 }
 

@@ -13,6 +13,7 @@ namespace {
 template <typename T>
 __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ pair_row, int T_, int kk, int H,
                                T* __restrict__ out, const int32_t* __restrict__ T_dev, int t_base) {
+  pdl_wait();  // y comes from the previous kernel
   const int t = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (t >= T_ || c >= H) return;
@@ -47,7 +48,7 @@ __global__ void validate_tenants_kernel(const int32_t* __restrict__ in, int64_t 
 }  // namespace
 
 int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H, int dtype_bf16, void* out,
-                   cudaStream_t stream, const int32_t* T_dev) {
+                   cudaStream_t stream, const int32_t* T_dev, bool pdl) {
   SB_CHECK_ARG(H % 8 == 0, "combine: H=%d must be a multiple of 8", H);
   if (T_ == 0 || H == 0) return STAGEML_OK;
   dim3 block(128);
@@ -68,11 +69,13 @@ int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H
          ::sb::count_launch());
     }
   } else if (dtype_bf16) {
-    (combine_kernel<bf16><<<grid, block, 0, stream>>>(static_cast<const bf16*>(y), pair_row, T_, kk, H,
-                                                      static_cast<bf16*>(out), T_dev, 0), ::sb::count_launch());
+    SB_CUDA_CHECK(launch_kernel(combine_kernel<bf16>, grid, block, 0, stream, pdl, static_cast<const bf16*>(y), pair_row,
+                                T_, kk, H, static_cast<bf16*>(out), T_dev, 0));
+    ::sb::count_launch();
   } else {
-    (combine_kernel<f16><<<grid, block, 0, stream>>>(static_cast<const f16*>(y), pair_row, T_, kk, H,
-                                                     static_cast<f16*>(out), T_dev, 0), ::sb::count_launch());
+    SB_CUDA_CHECK(launch_kernel(combine_kernel<f16>, grid, block, 0, stream, pdl, static_cast<const f16*>(y), pair_row,
+                                T_, kk, H, static_cast<f16*>(out), T_dev, 0));
+    ::sb::count_launch();
   }
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;

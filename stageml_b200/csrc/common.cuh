@@ -39,6 +39,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch. pdl_wait(): returns once the previous kernel in the
+// stream has completed and its writes are visible (immediately for a kernel launched
+// without PDL). pdl_trigger(): lets the next kernel, if it is a PDL launch, start once
+// every CTA of this grid has triggered or exited. A kernel triggers only after its own
+// pdl_wait(), so a PDL kernel may read, before its wait, what the kernel two back wrote.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

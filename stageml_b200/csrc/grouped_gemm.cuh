@@ -135,7 +135,11 @@ size_t pair_runs_ints(int64_t pairs_cap);
 // batches), skinny.cu: same GemmLaunch semantics (16-bit weights; LoRA from s16 /
 // lora_b with the row's tenant), valid rows per tile from the group counts; max_rows
 // bounds the valid rows of any tile (at most 8 selects the one-m8-block variant).
+// pdl_mode 0: ordinary launch; 1: programmatic dependent launch that waits at the
+// start; 2: PDL launch right after a kernel that writes only S (the shrink), which
+// streams the weights before it waits -- everything else it reads must come from
+// kernels before that one.
 int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int32_t* group_offsets,
-                       const int32_t* group_counts, cudaStream_t stream, int64_t max_rows = 16);
+                       const int32_t* group_counts, cudaStream_t stream, int64_t max_rows = 16, int pdl_mode = 0);
 
 }  // namespace sb

@@ -5,6 +5,8 @@
 
 #include "host_util.h"
 
+#include <cstdlib>
+
 namespace sb {
 
 static thread_local char g_last_error[1024] = "";
@@ -30,6 +32,14 @@ void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 extern "C" unsigned long long stageml_launch_count(void) { return sb::g_launches.load(std::memory_order_relaxed); }
 
 namespace sb {
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STAGEML_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int sm_count() {
   static int cached[64] = {0};

@@ -29,6 +29,30 @@ int sm_count();
 int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
                  uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
 
+// Programmatic dependent launch (PDL) of the decode-sized layer's kernel chain:
+// on by default, STAGEML_PDL=0 turns it off.
+bool pdl_enabled();
+
+// Launch `kernel` on `stream`. With `pdl` it is a programmatic dependent launch:
+// its CTAs may start while the previous kernel in the stream is still running, so
+// the kernel must call pdl_wait() (common.cuh) before it reads anything that
+// kernel writes. Without `pdl` it is an ordinary launch.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 }  // namespace sb
 
 #define SB_CUDA_CHECK(expr)                                                                     \

@@ -14,9 +14,9 @@ int launch_topk(const float* logits, int T, int E, int k, int renorm, int32_t* i
                 cudaStream_t stream);
 // Router logits + top-k; a few tokens (at most 64, gate and 8 rows per CTA in
 // shared memory) take one fused kernel, otherwise launch_router_logits then
-// launch_topk.
+// launch_topk. pdl: the fused kernel as a programmatic dependent launch (host_util.h).
 int launch_route(const void* x, int x_dtype, const float* gate_w, int T, int H, int E, int k, int renorm,
-                 float* logits, int32_t* ids, float* weights, cudaStream_t stream);
+                 float* logits, int32_t* ids, float* weights, cudaStream_t stream, bool pdl = false);
 
 // permute.cu
 struct PermuteScratch {
@@ -32,7 +32,8 @@ void permute_carve(void* base, int64_t num_pairs, int64_t nkeys, PermuteScratch*
 int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
                    int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
                    const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream,
-                   const int32_t* T_dev = nullptr);  // T_dev: optional device count of valid tokens
+                   const int32_t* T_dev = nullptr,  // T_dev: optional device count of valid tokens
+                   bool pdl = false);               // pdl: single-kernel plans as PDL launches
 
 // shrink.cu: gather rows and/or LoRA shrink partials (split-K), then reduce.
 struct ShrinkLaunch {
@@ -61,11 +62,14 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream);
 // one CTA per (pair, 8 output columns) whose 8 warps split K in a fixed order;
 // writes the scaled 16-bit S rows (zeros for rows without a tenant) and reads the
 // source rows in place (src_row_of, if given, maps a plan row to its source row).
-int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream);
+// pdl: as a programmatic dependent launch that lets the next kernel start at once.
+int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream,
+                       bool pdl = false);
 
 // combine.cu: out[t] = sum_j Y[pair_row[t*kk + j]]
 int launch_combine(const void* y, const int32_t* pair_row, int T, int kk, int H, int dtype_bf16, void* out,
-                   cudaStream_t stream, const int32_t* T_dev = nullptr);  // rows >= *T_dev left untouched
+                   cudaStream_t stream, const int32_t* T_dev = nullptr,  // rows >= *T_dev left untouched
+                   bool pdl = false);
 // clamp caller tenant ids into [-1, n_tenants) (invalid -> -1 + status)
 int launch_validate_tenants(const int32_t* in, int64_t n, int n_tenants, int32_t* out, int32_t* status,
                             cudaStream_t stream);

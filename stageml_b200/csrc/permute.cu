@@ -336,6 +336,8 @@ __global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, i
   extern __shared__ int32_t sm[];  // [32][nkeys] per-warp counts; in the last CTA tot[nkeys] + offsets
   __shared__ int32_t warp_part[32];
   __shared__ int s_last;
+  pdl_wait();  // ids / weights may come from the previous kernel
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int nch = (int)gridDim.x;
   const int64_t base = (int64_t)blockIdx.x * kPermChunk;
@@ -466,7 +468,7 @@ void permute_carve(void* base, int64_t P, int64_t nkeys, PermuteScratch* out) {
 int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
                    int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
                    const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream,
-                   const int32_t* T_dev) {
+                   const int32_t* T_dev, bool pdl) {
   SB_CHECK_ARG(T >= 0 && k >= 0 && n_shared >= 0, "permute: negative size");
   SB_CHECK_ARG(k + n_shared >= 1, "permute: need at least one slot per token");
   SB_CHECK_ARG(n_experts_total > n_shared || (k == 0 && n_experts_total == n_shared),
@@ -513,10 +515,9 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
     SB_CHECK_ARG(nch <= 65535, "permute: too many pairs");
     if (nch > 1) SB_CUDA_CHECK(cudaMemsetAsync(scr.ticket, 0, sizeof(int32_t), stream));
     SB_CUDA_CHECK(cudaFuncSetAttribute(perm_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_r));
-    (perm_rank_kernel<<<(unsigned)nch, 1024, smem_r, stream>>>(a, (int)nkeys, n_groups, plan, scr.sorted, scr.hist,
-                                                               scr.off, scr.ticket, status),
-     ::sb::count_launch());
-    SB_CUDA_CHECK(cudaGetLastError());
+    SB_CUDA_CHECK(launch_kernel(perm_rank_kernel, dim3((unsigned)nch), dim3(1024), smem_r, stream, pdl && nch == 1, a,
+                                (int)nkeys, n_groups, plan, scr.sorted, scr.hist, scr.off, scr.ticket, status));
+    ::sb::count_launch();
     if (nch > kLastPlacesChunks) {
       (perm_place_kernel<<<(unsigned)((P + 255) / 256), 256, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.off, plan),
        ::sb::count_launch());

@@ -305,6 +305,8 @@ __global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__
   __shared__ uint64_t bar;
   __shared__ volatile int abort_flag;
   __shared__ float lsm[kRouteSmallT * 32];
+  pdl_wait();  // x may come from the previous kernel
+  pdl_trigger();
   const int t0 = blockIdx.x * kRouteSmallT;
   const int nt = min(kRouteSmallT, T_ - t0);
   const bool staged = stage_to_smem(smem_u32(gsm), gw, (uint32_t)(sizeof(float) * E * H), x + (size_t)t0 * H,
@@ -416,7 +418,7 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
 }
 
 int launch_route(const void* x, int x_dtype, const float* gate_w, int T_, int H, int E, int k, int renorm,
-                 float* logits, int32_t* ids, float* weights, cudaStream_t stream) {
+                 float* logits, int32_t* ids, float* weights, cudaStream_t stream, bool pdl) {
   SB_CHECK_ARG(E >= 1 && E <= 256, "router: E=%d must be in [1, 256]", E);
   SB_CHECK_ARG(k >= 1 && k <= 8 && k <= E, "top-k: k=%d must be in [1, min(8, E)]", k);
   SB_CHECK_ARG(H >= 1, "router: H must be positive");
@@ -430,10 +432,9 @@ int launch_route(const void* x, int x_dtype, const float* gate_w, int T_, int H,
       aligned && vec_dtype) {
     auto launch = [&](auto kern, const auto* xp) -> int {
       SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(gbytes + xbytes)));
-      (kern<<<(T_ + kRouteSmallT - 1) / kRouteSmallT, 256, gbytes + xbytes, stream>>>(xp, gate_w, T_, H, E, k, renorm,
-                                                                                      logits, ids, weights),
-       ::sb::count_launch());
-      SB_CUDA_CHECK(cudaGetLastError());
+      SB_CUDA_CHECK(launch_kernel(kern, dim3((T_ + kRouteSmallT - 1) / kRouteSmallT), dim3(256), gbytes + xbytes, stream,
+                                  pdl, xp, gate_w, T_, H, E, k, renorm, logits, ids, weights));
+      ::sb::count_launch();
       return STAGEML_OK;
     };
     if (x_dtype == STAGEML_BF16) return launch(router_small_kernel<bf16>, static_cast<const bf16*>(x));

@@ -324,6 +324,8 @@ template <typename T>
 __global__ void __launch_bounds__(256, 1) pair_shrink_kernel(const PairShrinkParams p) {
   constexpr int U = 4;
   __shared__ float red[8][8];
+  pdl_wait();  // the plan and the source rows may come from the previous kernels
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = p.pair_row[blockIdx.x];
   if (row < 0) return;  // dropped pair
@@ -387,7 +389,7 @@ __global__ void __launch_bounds__(256, 1) pair_shrink_kernel(const PairShrinkPar
 
 }  // namespace
 
-int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream) {
+int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream, bool pdl) {
   SB_CHECK_ARG(s.src && pair_row && s.lora_a && s.s_out && s.row_tenant, "pair shrink: missing buffers");
   SB_CHECK_ARG(s.K > 0 && s.K % 8 == 0, "pair shrink: K=%d must be a positive multiple of 8", s.K);
   SB_CHECK_ARG(s.R > 0 && s.R % 8 == 0 && s.R <= 64, "pair shrink: R=%d must be a multiple of 8 up to 64", s.R);
@@ -410,10 +412,10 @@ int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P
   p.s_out = s.s_out;
   const dim3 grid((unsigned)P, (unsigned)(s.R / 8));
   if (s.dtype_bf16)
-    (pair_shrink_kernel<bf16><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
+    SB_CUDA_CHECK(launch_kernel(pair_shrink_kernel<bf16>, grid, dim3(256), 0, stream, pdl, p));
   else
-    (pair_shrink_kernel<f16><<<grid, 256, 0, stream>>>(p), ::sb::count_launch());
-  SB_CUDA_CHECK(cudaGetLastError());
+    SB_CUDA_CHECK(launch_kernel(pair_shrink_kernel<f16>, grid, dim3(256), 0, stream, pdl, p));
+  ::sb::count_launch();
   return STAGEML_OK;
 }
 

@@ -52,6 +52,7 @@ struct SkParams {
   const float* b_scale;
   void* out;
   int64_t ldo;
+  int wait_late;  // PDL launch after a kernel that writes only S: wait before the epilogue (else at the start)
 };
 
 template <typename T>
@@ -107,6 +108,9 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
   constexpr int NBLK = SWIGLU ? 2 : 1;
   constexpr int IPC = kSkWarps / WPI;  // items per CTA
   __shared__ float red[WPI > 1 ? kSkWarps : 1][NBLK][32][4];
+  // Weight streaming does not depend on the shrink that precedes this kernel: with
+  // wait_late the partial sums are formed while it runs, and only S waits.
+  if (!p.wait_late) pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = warp / WPI, part = warp - slot * WPI;
   const int g = lane >> 2, tig = lane & 3;
@@ -177,6 +181,8 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
           for (int j = 0; j < 4; ++j) acc[b][j] += red[WPI > 1 ? warp + q : 0][b][lane][j];
     }
   }
+  // Every thread waits, so this grid completes only after the kernel before it.
+  if (p.wait_late) pdl_wait();
   if (part != 0 || valid == 0) return;
   T* out = static_cast<T*>(p.out);
 #pragma unroll
@@ -223,33 +229,31 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
 }
 
 template <typename T, bool SWIGLU, bool HI>
-void launch_sk_hi(int wpi, int n_items, const SkParams& p, cudaStream_t stream) {
-  const unsigned grid = (unsigned)(((int64_t)n_items * wpi + kSkWarps - 1) / kSkWarps);
+cudaError_t launch_sk_hi(int wpi, int n_items, const SkParams& p, cudaStream_t stream, bool pdl) {
+  const dim3 grid((unsigned)(((int64_t)n_items * wpi + kSkWarps - 1) / kSkWarps)), block(256);
+  ::sb::count_launch();
   switch (wpi) {
     case 1:
-      (skinny_gemm_kernel<T, SWIGLU, 1, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
-      break;
+      return launch_kernel(skinny_gemm_kernel<T, SWIGLU, 1, HI>, grid, block, 0, stream, pdl, p, n_items);
     case 2:
-      (skinny_gemm_kernel<T, SWIGLU, 2, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
-      break;
+      return launch_kernel(skinny_gemm_kernel<T, SWIGLU, 2, HI>, grid, block, 0, stream, pdl, p, n_items);
     case 4:
-      (skinny_gemm_kernel<T, SWIGLU, 4, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
-      break;
+      return launch_kernel(skinny_gemm_kernel<T, SWIGLU, 4, HI>, grid, block, 0, stream, pdl, p, n_items);
     default:
-      (skinny_gemm_kernel<T, SWIGLU, 8, HI><<<grid, 256, 0, stream>>>(p, n_items), ::sb::count_launch());
-      break;
+      return launch_kernel(skinny_gemm_kernel<T, SWIGLU, 8, HI>, grid, block, 0, stream, pdl, p, n_items);
   }
 }
 
 template <typename T, bool SWIGLU>
-void launch_sk(int wpi, int n_items, bool hi, const SkParams& p, cudaStream_t stream) {
-  hi ? launch_sk_hi<T, SWIGLU, true>(wpi, n_items, p, stream) : launch_sk_hi<T, SWIGLU, false>(wpi, n_items, p, stream);
+cudaError_t launch_sk(int wpi, int n_items, bool hi, const SkParams& p, cudaStream_t stream, bool pdl) {
+  return hi ? launch_sk_hi<T, SWIGLU, true>(wpi, n_items, p, stream, pdl)
+            : launch_sk_hi<T, SWIGLU, false>(wpi, n_items, p, stream, pdl);
 }
 
 }  // namespace
 
 int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int32_t* group_offsets,
-                       const int32_t* group_counts, cudaStream_t stream, int64_t max_rows) {
+                       const int32_t* group_counts, cudaStream_t stream, int64_t max_rows, int pdl_mode) {
   SB_CHECK_ARG(g.a && g.b && g.out, "skinny gemm: null operand");
   SB_CHECK_ARG(!g.b_fp8, "skinny gemm: 16-bit weights only");
   SB_CHECK_ARG(g.K > 0 && g.K % 8 == 0 && g.N > 0, "skinny gemm: K=%d must be a positive multiple of 8", g.K);
@@ -286,6 +290,7 @@ int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int
   p.b_scale = g.b_scale;
   p.out = g.out;
   p.ldo = g.ldo;
+  p.wait_late = pdl_mode == 2;
   const int64_t tiles = g.tile_group ? (int64_t)g.tiles_cap : (g.m_rows + 127) / 128;
   if (tiles == 0) return STAGEML_OK;
   const int64_t items = tiles * ((g.N + kSkNB - 1) / kSkNB);
@@ -295,13 +300,15 @@ int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int
   int wpi = 1;
   while (wpi < 8 && g.K >= wpi * 2 * 3072) wpi *= 2;
   const bool hi = max_rows > 8;  // a tile holds at most max_rows valid rows
+  const bool pdl = pdl_mode != 0;
+  cudaError_t e;
   if (g.in_bf16)
-    g.swiglu ? launch_sk<bf16, true>(wpi, (int)items, hi, p, stream)
-             : launch_sk<bf16, false>(wpi, (int)items, hi, p, stream);
+    e = g.swiglu ? launch_sk<bf16, true>(wpi, (int)items, hi, p, stream, pdl)
+                 : launch_sk<bf16, false>(wpi, (int)items, hi, p, stream, pdl);
   else
-    g.swiglu ? launch_sk<f16, true>(wpi, (int)items, hi, p, stream)
-             : launch_sk<f16, false>(wpi, (int)items, hi, p, stream);
-  SB_CUDA_CHECK(cudaGetLastError());
+    e = g.swiglu ? launch_sk<f16, true>(wpi, (int)items, hi, p, stream, pdl)
+                 : launch_sk<f16, false>(wpi, (int)items, hi, p, stream, pdl);
+  SB_CUDA_CHECK(e);
   return STAGEML_OK;
 }
 

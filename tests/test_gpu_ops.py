@@ -237,6 +237,35 @@ def test_moe_forward_zero_lora_scale_equals_no_lora(ops):
     assert torch.equal(y0, y1)
 
 
+def test_decode_calls_back_to_back_match_synchronized_calls(ops):
+    """Decode-sized calls (at most 16 routed rows) run their kernel chain as
+    programmatic dependent launches; issued back to back on one stream, with LoRA on
+    w1/w3/w2, on w1/w3 only and off, they give the same bits as the same calls with a
+    device synchronization after each."""
+    full = _moe_case(T=48, H=256, I=256, E=8, k=2, nT=3, r=16, seed=13)
+    w13 = _moe_case(T=48, H=256, I=256, E=8, k=2, nT=3, r=16, seed=13, lora=("w13",))
+
+    def call(i):
+        c = (full, w13, full)[i % 3]
+        x = c["x"][2 * i:2 * i + 2]
+        kw = dict(router_w=c["router_w"], k=2)
+        if i % 3 != 2:
+            kw.update(tenant_ids=c["tenant_ids"][2 * i:2 * i + 2], n_tenants=3, rank=16, lora_a13=c["lora_a13"],
+                      lora_b13=c["lora_b13"], lora_a2=c.get("lora_a2"), lora_b2=c.get("lora_b2"),
+                      lora_scale=c["lora_scale"])
+        return ops.moe_forward(x, c["gate_up"], c["down"], **kw)
+
+    ref = []
+    for i in range(24):
+        ref.append(call(i))
+        torch.cuda.synchronize()
+    out = [call(i) for i in range(24)]
+    torch.cuda.synchronize()
+    for i in range(24):
+        assert torch.equal(out[i], ref[i]), f"call {i}"
+    check_status(ops)
+
+
 def test_moe_forward_empty_batch(ops):
     c = _moe_case(T=1, H=128, I=128, E=4, k=2, nT=0, r=0)
     y = ops.moe_forward(c["x"][:0], c["gate_up"], c["down"], router_w=c["router_w"], k=2)
