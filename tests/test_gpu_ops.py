@@ -266,6 +266,22 @@ def test_decode_calls_back_to_back_match_synchronized_calls(ops):
     check_status(ops)
 
 
+def test_decode_rows_do_not_depend_on_the_batch(ops):
+    """A token's output from a decode-sized call has the same bits alone as inside a
+    batch of 8: the skinny GEMMs' per-row sums do not depend on the batch (the
+    batch also takes the kernel variant for more than 8 rows per tile)."""
+    c = _moe_case(T=8, H=512, I=14336, E=2, k=2, nT=2, r=16, seed=17)
+    kw = dict(router_w=c["router_w"], k=2, n_tenants=2, rank=16, lora_a13=c["lora_a13"], lora_b13=c["lora_b13"],
+              lora_a2=c["lora_a2"], lora_b2=c["lora_b2"], lora_scale=c["lora_scale"])
+    y = ops.moe_forward(c["x"], c["gate_up"], c["down"], tenant_ids=c["tenant_ids"], **kw)
+    for t in range(8):
+        yt = ops.moe_forward(c["x"][t:t + 1], c["gate_up"], c["down"], tenant_ids=c["tenant_ids"][t:t + 1], **kw)
+        assert torch.equal(yt[0], y[t]), f"token {t}"
+    ids, w, _ = ops.route_topk(c["x"], c["router_w"], 2, True)
+    assert rel_l2(f64(y), _oracle_moe(c, ids.cpu().numpy(), w.cpu().numpy())) < TOL16
+    check_status(ops)
+
+
 def test_moe_forward_empty_batch(ops):
     c = _moe_case(T=1, H=128, I=128, E=4, k=2, nT=0, r=0)
     y = ops.moe_forward(c["x"][:0], c["gate_up"], c["down"], router_w=c["router_w"], k=2)
