@@ -333,7 +333,8 @@ __global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, i
                                                           uint32_t* __restrict__ rank_key, int32_t* __restrict__ hist,
                                                           int32_t* __restrict__ off, int32_t* __restrict__ ticket,
                                                           int32_t* status) {
-  extern __shared__ int32_t sm[];  // [32][nkeys] per-warp counts; in the last CTA tot[nkeys] + offsets
+  extern __shared__ int32_t sm[];  // [32][nkeys] per-warp counts (+ [nkeys] totals for one chunk); in the
+                                   // last CTA of several: tot[nkeys] + offsets
   __shared__ int32_t warp_part[32];
   __shared__ int s_last;
   pdl_wait();  // ids / weights may come from the previous kernel
@@ -360,6 +361,32 @@ __global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, i
     rnk[r] = before + __popc(peers & below);
   }
   __syncthreads();
+  if (nch == 1) {
+    // One chunk: the key totals and the ranks stay on chip; the plan is built and
+    // every pair placed here (no global round trip).
+    int32_t* tot = sm + 32 * nkeys;  // [nkeys]
+    for (int k = tid; k < nkeys; k += 1024) {
+      int run = 0;
+      for (int ww = 0; ww < 32; ++ww) {
+        const int c = sm[ww * nkeys + k];
+        sm[ww * nkeys + k] = run;
+        run += c;
+      }
+      tot[k] = run;
+    }
+    __syncthreads();
+    plan_groups(tot, a.tkeys, n_groups, plan, warp_part);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int64_t p = w * 64 + r * 32 + lane;
+      if (p >= a.P) continue;
+      if (key[r] == kSentKey)
+        plan.pair_row[p] = -1;
+      else
+        place_pair(a, plan, p, tot[key[r]] + sm[w * nkeys + (int)key[r]] + rnk[r]);
+    }
+    return;
+  }
   for (int k = tid; k < nkeys; k += 1024) {  // exclusive prefix over warps, chunk total
     int run = 0;
     for (int ww = 0; ww < 32; ++ww) {
@@ -511,7 +538,7 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
 
   const int64_t nch = nchunks_of(P);
   if (nkeys <= kRankMaxKeys) {
-    const size_t smem_r = (size_t)32 * nkeys * 4;
+    const size_t smem_r = (size_t)33 * nkeys * 4;
     SB_CHECK_ARG(nch <= 65535, "permute: too many pairs");
     if (nch > 1) SB_CUDA_CHECK(cudaMemsetAsync(scr.ticket, 0, sizeof(int32_t), stream));
     SB_CUDA_CHECK(cudaFuncSetAttribute(perm_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_r));
