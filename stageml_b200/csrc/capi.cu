@@ -383,6 +383,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.num_tiles_dev = b.plan.num_tiles;
     g.tiles_cap = (int)(b.plan.rows_cap / 128);
     g.tile_group = b.plan.tile_group;
+    g.group_offsets = b.plan.group_offsets;
     if (lora13) {
       g.s16 = b.s13;
       g.s_rows = b.plan.rows_cap;
@@ -438,6 +439,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.num_tiles_dev = b.plan.num_tiles;
     g.tiles_cap = (int)(b.plan.rows_cap / 128);
     g.tile_group = b.plan.tile_group;
+    g.group_offsets = b.plan.group_offsets;
     if (lora2) {
       g.s16 = b.s2;
       g.s_rows = b.plan.rows_cap;

@@ -60,6 +60,7 @@ struct KParams {
   int tiles_cap;
   const int32_t* tile_group;
   const int32_t* tile_list;   // optional: m-tile i is tile_list[i] (LoRA runs indexed by the tile id)
+  const int32_t* group_offsets;  // grouped rows without a list: group-major unit order
   int64_t m_rows;
   // LoRA
   int rank;
@@ -113,6 +114,25 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
 #pragma unroll
     for (int i = 0; i < 16; ++i)
       if (i < ncols_valid) dst[i] = from_f32<T>(v[i]);
+  }
+}
+
+// Unit u -> (m-tile position, n-tile). With group offsets (grouped rows, no list) the
+// order is group-major: every n-tile of a group's m-tiles (m-tiles fastest) before
+// the next group, so a weight tile is read by all of its group's m-tiles at about
+// the same time and only one group's activation rows need to stay in L2. The units
+// of group g are [first_tile(g) * n_tiles, (first_tile(g) + tiles(g)) * n_tiles).
+// Otherwise m-tiles fastest.
+__device__ __forceinline__ void unit_mn(const KParams& p, int u, int num_m_tiles, int& m_pos, int& n_tile) {
+  if (p.group_offsets) {
+    const int g = p.tile_group[u / p.num_n_tiles];
+    const int first = p.group_offsets[g] >> 7, cnt = (p.group_offsets[g + 1] >> 7) - first;
+    const int local = u - first * p.num_n_tiles;
+    n_tile = local / cnt;
+    m_pos = first + (local - n_tile * cnt);
+  } else {
+    m_pos = u % num_m_tiles;
+    n_tile = u / num_m_tiles;
   }
 }
 
@@ -229,9 +249,9 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += nctas) {
-      const int m_pos = tile % num_m_tiles;
+      int m_pos, n_tile;
+      unit_mn(p, tile, num_m_tiles, m_pos, n_tile);
       const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
-      const int n_tile = tile / num_m_tiles;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int a_row = m_tile * BM;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
@@ -310,7 +330,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += nctas, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
-      const int m_pos = tile % num_m_tiles;
+      int m_pos, n_tile_unused;
+      unit_mn(p, tile, num_m_tiles, m_pos, n_tile_unused);
       if (!mbar_wait(tempty_bar(acc), aph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
         ok = false;
         break;
@@ -385,9 +406,9 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       const uint32_t aph = (tcount >> 1) & 1;
       if (!mbar_wait(tfull_bar(acc), aph, abort_flag, p.status, p.timeout_ns, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const int m_pos = tile % num_m_tiles;
+      int m_pos, n_tile;
+      unit_mn(p, tile, num_m_tiles, m_pos, n_tile);
       const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
-      const int n_tile = tile / num_m_tiles;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int64_t row = (int64_t)m_tile * BM + row_in_tile;
       const bool row_ok = p.tile_group ? true : (row < p.m_rows);
@@ -460,9 +481,9 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     const int ct = threadIdx.x - 192;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += nctas) {
-      const int m_pos = tile % num_m_tiles;
+      int m_pos, n_tile;
+      unit_mn(p, tile, num_m_tiles, m_pos, n_tile);
       const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
-      const int n_tile = tile / num_m_tiles;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
       const int64_t b_row0 = (int64_t)group * p.b_group_rows + n0;
@@ -652,6 +673,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.tiles_cap = g.tiles_cap;
   p.tile_group = g.tile_group;
   p.tile_list = g.tile_list;
+  p.group_offsets = (g.tile_group && !g.tile_list) ? g.group_offsets : nullptr;
   p.m_rows = g.m_rows;
   p.rank = g.rank;
   p.lchunks = (g.rank + 15) / 16;

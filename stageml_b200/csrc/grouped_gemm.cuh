@@ -43,6 +43,8 @@ struct GemmLaunch {
   int tiles_cap = 0;
   const int32_t* tile_group = nullptr;
   const int32_t* tile_list = nullptr;  // one-CTA kernel: process tiles tile_list[0 .. *num_tiles_dev)
+  const int32_t* group_offsets = nullptr;  // one-CTA kernel, grouped rows: [groups + 1] padded row offsets
+                                           // (group-major unit order; null: m-tile fastest)
   int64_t m_rows = 0;            // direct mode row count
   // LoRA (tensor-core expand)
   int rank = 0;                          // 0, 16 or 32
