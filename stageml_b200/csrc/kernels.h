@@ -13,7 +13,8 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T,
 int launch_topk(const float* logits, int T, int E, int k, int renorm, int32_t* ids, float* weights,
                 cudaStream_t stream);
 // Router logits + top-k; a few tokens (at most 64, gate and 8 rows per CTA in
-// shared memory) take one fused kernel, otherwise launch_router_logits then
+// shared memory) take one fused kernel, more tokens with E <= 32 another (gate in
+// shared memory, two tokens per warp), otherwise launch_router_logits then
 // launch_topk. pdl: the fused kernel as a programmatic dependent launch (host_util.h).
 int launch_route(const void* x, int x_dtype, const float* gate_w, int T, int H, int E, int k, int renorm,
                  float* logits, int32_t* ids, float* weights, cudaStream_t stream, bool pdl = false);

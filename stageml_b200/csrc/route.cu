@@ -13,6 +13,8 @@
 #include "host_util.h"
 #include "kernels.h"
 
+#include <type_traits>
+
 namespace sb {
 namespace {
 
@@ -350,6 +352,81 @@ __global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__
     topk_row(lsm + t * E, E, k, renorm, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
 }
 
+// Logits + top-k in one kernel for E <= 32 with the gate resident in shared memory:
+// as router_logits_smem_kernel, but each warp takes two tokens at a time (every G
+// read from shared memory serves both) and runs topk_row on their logits right
+// away. Each token's per-lane sums are those of router_logits_smem_kernel (same
+// columns, same order), so the logits are the same bits.
+constexpr int RT_TPW = 2;
+template <typename T, int E_MAX>
+__global__ void __launch_bounds__(256) router_route_smem_kernel(const T* __restrict__ x, const float* __restrict__ gw,
+                                                                int T_, int H, int E, int k, int renorm,
+                                                                float* __restrict__ logits, int32_t* __restrict__ ids,
+                                                                float* __restrict__ weights) {
+  constexpr int XU = 4;
+  extern __shared__ float4 gsm4[];
+  float* gsm = reinterpret_cast<float*>(gsm4);
+  __shared__ uint64_t bar;
+  __shared__ volatile int abort_flag;
+  __shared__ float lsm[8][RT_TPW][E_MAX];
+  const bool staged = stage_to_smem(smem_u32(gsm), gw, (uint32_t)(sizeof(float) * E * H), nullptr, 0, &bar, &abort_flag);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t0 = (blockIdx.x * 8 + warp) * RT_TPW; t0 < T_; t0 += gridDim.x * 8 * RT_TPW) {
+    const int nt = min(RT_TPW, T_ - t0);
+    float acc[RT_TPW][E_MAX];
+#pragma unroll
+    for (int j = 0; j < RT_TPW; ++j)
+#pragma unroll
+      for (int e = 0; e < E_MAX; ++e) acc[j][e] = 0.f;
+    for (int h0 = lane * 4; h0 < H; h0 += 128 * XU) {
+      float xv[RT_TPW][XU][4];
+#pragma unroll
+      for (int j = 0; j < RT_TPW; ++j)
+#pragma unroll
+        for (int u = 0; u < XU; ++u) load_x4<T>(x + (int64_t)(t0 + min(j, nt - 1)) * H, h0 + 128 * u, H, xv[j][u]);
+#pragma unroll
+      for (int u = 0; u < XU; ++u) {
+        const int h = h0 + 128 * u;
+        if (h < H) {
+#pragma unroll
+          for (int e = 0; e < E_MAX; ++e) {
+            if (e < E) {
+              const float4 gv = *reinterpret_cast<const float4*>(gsm + e * H + h);
+#pragma unroll
+              for (int j = 0; j < RT_TPW; ++j) {
+                acc[j][e] = fmaf(xv[j][u][0], gv.x, acc[j][e]);
+                acc[j][e] = fmaf(xv[j][u][1], gv.y, acc[j][e]);
+                acc[j][e] = fmaf(xv[j][u][2], gv.z, acc[j][e]);
+                acc[j][e] = fmaf(xv[j][u][3], gv.w, acc[j][e]);
+              }
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < RT_TPW; ++j) {
+#pragma unroll
+      for (int e = 0; e < E_MAX; ++e) {
+        if (e < E && j < nt) {
+          float v = acc[j][e];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) {
+            const float lv = staged ? v : __int_as_float(0x7fc00000);
+            lsm[warp][j][e] = lv;
+            logits[(int64_t)(t0 + j) * E + e] = lv;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    for (int j = 0; j < nt; ++j)
+      topk_row(&lsm[warp][j][0], E, k, renorm, lane, ids + (int64_t)(t0 + j) * k, weights + (int64_t)(t0 + j) * k);
+    __syncwarp();
+  }
+}
+
 }  // namespace
 
 int launch_topk(const float* logits, int T_, int E, int k, int renorm, int32_t* ids, float* weights,
@@ -440,6 +517,24 @@ int launch_route(const void* x, int x_dtype, const float* gate_w, int T_, int H,
     if (x_dtype == STAGEML_BF16) return launch(router_small_kernel<bf16>, static_cast<const bf16*>(x));
     if (x_dtype == STAGEML_F16) return launch(router_small_kernel<f16>, static_cast<const f16*>(x));
     return launch(router_small_kernel<float>, static_cast<const float*>(x));
+  }
+  if (E <= 32 && H % 4 == 0 && gbytes <= 200 * 1024 && aligned && vec_dtype) {
+    const int grid = (int)std::min<int64_t>(sm_count(), ((int64_t)T_ + 8 * RT_TPW - 1) / (8 * RT_TPW));
+    auto launch = [&](auto kern, const auto* xp) -> int {
+      SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gbytes));
+      (kern<<<grid, 256, gbytes, stream>>>(xp, gate_w, T_, H, E, k, renorm, logits, ids, weights), ::sb::count_launch());
+      SB_CUDA_CHECK(cudaGetLastError());
+      return STAGEML_OK;
+    };
+    auto pick = [&](const auto* xp) -> int {
+      using TT = std::remove_cv_t<std::remove_pointer_t<decltype(xp)>>;
+      if (E <= 8) return launch(router_route_smem_kernel<TT, 8>, xp);
+      if (E <= 16) return launch(router_route_smem_kernel<TT, 16>, xp);
+      return launch(router_route_smem_kernel<TT, 32>, xp);
+    };
+    if (x_dtype == STAGEML_BF16) return pick(static_cast<const bf16*>(x));
+    if (x_dtype == STAGEML_F16) return pick(static_cast<const f16*>(x));
+    return pick(static_cast<const float*>(x));
   }
   SB_TRY(launch_router_logits(x, x_dtype, gate_w, T_, H, E, logits, stream));
   return launch_topk(logits, T_, E, k, renorm, ids, weights, stream);
