@@ -80,7 +80,7 @@ struct PairPlan {
   int32_t* pairs = nullptr;      // [tiles_cap, 4]
   int32_t* num_pairs = nullptr;  // [1]
   int32_t* pruns = nullptr;      // [tiles_cap, kMaxRunsPerPair, kPairRunInts]
-  int32_t* pnruns = nullptr;     // [tiles_cap]
+  int32_t* pnruns = nullptr;     // [tiles_cap, kRunHdrInts] run headers
   int32_t* singles = nullptr;    // [tiles_cap]
   int32_t* num_singles = nullptr;
   int32_t* sruns = nullptr;      // [tiles_cap, kMaxRunsPerTile, 5]
@@ -113,7 +113,7 @@ void carve_pair_plan(Carver& c, int64_t tiles_cap, bool lora, PairPlan* pp) {
   pp->num_singles = c.take<int32_t>(1);
   if (lora) {
     pp->pruns = c.take<int32_t>(pair_runs_ints(tiles_cap));
-    pp->pnruns = c.take<int32_t>((size_t)tiles_cap);
+    pp->pnruns = c.take<int32_t>((size_t)tiles_cap * kRunHdrInts);
     pp->sruns = c.take<int32_t>((size_t)tiles_cap * kMaxRunsPerTile * 5);
     pp->snruns = c.take<int32_t>((size_t)tiles_cap);
   }

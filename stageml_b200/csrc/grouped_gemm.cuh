@@ -71,7 +71,7 @@ struct GemmLaunch {
   const int32_t* num_pairs_dev = nullptr;
   int pairs_cap = 0;
   const int32_t* pair_runs = nullptr;    // [tiles][kMaxRunsPerPair][kPairRunInts], at each pair's first tile
-  const int32_t* pair_nruns = nullptr;   // [pairs_cap]
+  const int32_t* pair_nruns = nullptr;   // [tiles][kRunHdrInts] run headers, at each pair's first tile
   // The pair kernel and the odd-tile kernel side by side (split_sms > 0): each
   // reads the pair and odd-tile counts and keeps only its share of the split_sms
   // SMs busy (split_single_ctas); the CTAs past its share exit at once.
@@ -112,6 +112,10 @@ constexpr int kMaxRunsPerTile = 128;
 // of the same group, computed by a two-CTA cluster (tcgen05 cta_group::2).
 constexpr int kMaxRunsPerPair = 256;
 constexpr int kPairRunInts = 9;  // tenant, 8 row-mask words
+// Run header of a pair (at its first tile t): nruns[t * kRunHdrInts] = run count,
+// [1 + j] = tenant of run j for j < kRunHdrInts - 1 (one 128-byte block the pair
+// kernel's producer bulk-copies at the start of each unit).
+constexpr int kRunHdrInts = 32;
 int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream);
 
 // Pair list and per-pair LoRA runs. Grouped rows (tile_group != nullptr): pairs of

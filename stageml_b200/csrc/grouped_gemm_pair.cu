@@ -41,7 +41,9 @@ constexpr int STAGE_BYTES = MMA_STAGE_BYTES;
 constexpr int THREADS = 192;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 static_assert(SMEM_BYTES <= 232448, "shared memory per block");
-static_assert((3 * STAGES + 5) * 8 + 8 <= 512, "barrier area");
+// barrier area (512 B): the barriers, the TMEM address and abort flag (< 160 B), the
+// producer's header barrier at byte 160 and its 128-byte run header at byte 256
+static_assert((2 * STAGES + 5) * 8 + 8 <= 160, "barrier area");
 
 struct PParams {
   int K;
@@ -64,7 +66,7 @@ struct PParams {
   int64_t lb_tenant_rows;
   int64_t lb_group_rows;
   const int32_t* runs;           // [tiles][kMaxRunsPerPair][9], at each pair's first tile
-  const int32_t* nruns;          // [tiles]
+  const int32_t* nruns;          // [tiles][kRunHdrInts] run headers
   // epilogue
   const float* row_scale;
   const void* bias;
@@ -110,7 +112,7 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
 // LoRA runs of a pair are stored at its first tile m0.
 __device__ __forceinline__ int pair_lora_runs(const PParams& p, int m0) {
   if (p.rank == 0) return 0;
-  const int n = p.nruns[m0];
+  const int n = p.nruns[(int64_t)m0 * kRunHdrInts];
   return n < kMaxRunsPerPair ? n : kMaxRunsPerPair;
 }
 __device__ __forceinline__ const int32_t* pair_run(const PParams& p, int m0, int r) {
@@ -155,6 +157,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // [2S,2S+2) tmem_full, [2S+2,2S+4) tmem_empty (even CTA), [2S+4] drain
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  // the producer's copy of the current unit's run header (LoRA), and its barrier
+  uint64_t* hdr_bar_p = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 160);
+  const int32_t* hdr_smem = reinterpret_cast<const int32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -178,6 +183,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(tempty_bar(a), 8);  // 4 epilogue warps of each CTA
     }
     mbar_init(drain_bar, 1);
+    mbar_init(smem_u32(hdr_bar_p), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -216,8 +222,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     int last_phase[STAGES];
     for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
-    uint32_t it = 0;
+    uint32_t it = 0, hdr_uses = 0;
     bool ok = true;
+    const uint32_t hdr_bar = smem_u32(hdr_bar_p);
+    bool hdr_inflight = false;
     for (int u = cluster; ok && u < total_units; u += nclusters) {
       int pm, n_tile;
       unit_coords(p, u, pm, n_tile);
@@ -228,7 +236,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int a_row = m_load * BM;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
       const int b_row = group * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
-      const int nruns = pair_lora_runs(p, m0);
+      if (p.rank) {  // the run header arrives while the K loop's copies are issued
+        mbar_arrive_expect_tx(hdr_bar, kRunHdrInts * 4);
+        bulk_load_1d(smem_u32(hdr_smem), p.nruns + (int64_t)m0 * kRunHdrInts, kRunHdrInts * 4, hdr_bar);
+        hdr_inflight = true;
+      }
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -243,6 +255,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         last_phase[s] = (int)ph;
       }
       // LoRA blocks: this CTA's rows of S + its half of the B rows of each tenant run
+      int nruns = 0;
+      if (p.rank && ok) {
+        ok = mbar_wait(hdr_bar, hdr_uses & 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutProducer);
+        ++hdr_uses;
+        hdr_inflight = !ok;
+        nruns = ok ? min(hdr_smem[0], kMaxRunsPerPair) : 0;
+      }
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -258,7 +277,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (p.swiglu) load(base + (p.lchunks + ch) * LCHUNK, &tm_s, s, p.rank + ch * 16, a_row, pol_a);
         }
         for (int jj = 0; jj < nr; ++jj) {
-          const int brow = (int)(pair_run(p, m0, r0 + jj)[0] * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
+          const int r = r0 + jj;
+          const int tenant = r < kRunHdrInts - 1 ? hdr_smem[1 + r] : pair_run(p, m0, r)[0];
+          const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
             if (p.swiglu) {
@@ -277,6 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (!ok) {
       // Let the copies already in flight land before the CTA pair leaves. The odd CTA's
       // copies complete on the even CTA's barrier; it waits a fixed, ample time.
+      if (hdr_inflight) mbar_wait(hdr_bar, hdr_uses & 1, &never_abort, p.status, 200000000ull, kDevTimeoutDrain);
       if (leader) {
         for (int s = 0; s < STAGES; ++s)
           if (last_phase[s] >= 0)
@@ -535,7 +557,11 @@ __device__ __forceinline__ void quarter_runs(const int32_t* row_tenant, const in
 #pragma unroll
     for (int qq = 0; qq < NQ; ++qq) r[1 + qq] = (int32_t)s_mask[j][qq];
   }
-  if (lane == 0) *nruns = count;
+  if (NQ == 8) {  // pair: run header (count, then the first kRunHdrInts - 1 tenants)
+    nruns[lane] = lane == 0 ? count : (lane - 1 < count ? s_ten[lane - 1] : -1);
+  } else if (lane == 0) {
+    *nruns = count;
+  }
 }
 
 // One launch for the whole plan. Block 0 lists the pairs (and the singles) in tile
@@ -573,7 +599,8 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
         q8[q] = tile < 0 ? -1 : (int64_t)tile * 128 + (q & 3) * 32;
       }
       quarter_runs<8>(row_tenant, q8, bound, s_ten[w], s_mask[w],
-                      pruns + (int64_t)t * kMaxRunsPerPair * kPairRunInts, pnruns + t, kMaxRunsPerPair);
+                      pruns + (int64_t)t * kMaxRunsPerPair * kPairRunInts, pnruns + (int64_t)t * kRunHdrInts,
+                      kMaxRunsPerPair);
     }
     return;
   }
