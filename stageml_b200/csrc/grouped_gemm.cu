@@ -46,8 +46,13 @@ struct Cfg {
   static constexpr int STAGES = FP8B ? 3 : 4;
   static constexpr int STAGE_BYTES = FP8B ? MMA_STAGE_BYTES + RAW_B_BYTES : MMA_STAGE_BYTES;
   static constexpr int THREADS = FP8B ? 192 + CONVERTER_THREADS : 192;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 1024 /*barriers, run header*/;
 };
+// The producer bulk-copies the first kHdrRuns runs (tenant + 4 mask words each) of a
+// unit's tile at the unit's start: area after the stages = barriers (< 192 B), the
+// copy's barrier at byte 192, the runs at byte 256.
+constexpr int kHdrRuns = 32;
+static_assert(256 + kHdrRuns * 5 * 4 <= 1024 && (kHdrRuns * 5 * 4) % 16 == 0, "run header area");
 
 struct KParams {
   int K;
@@ -186,6 +191,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   // [2S+2,2S+4) tmem_empty, [2S+4] drain, [2S+5,3S+5) raw (TMA landed; FP8 weights only)
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  uint64_t* hdr_bar_p = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 192);
+  const int32_t* hdr_smem = reinterpret_cast<const int32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -216,6 +223,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       mbar_init(tempty_bar(a), 4);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(smem_u32(hdr_bar_p), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -246,12 +254,22 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     const uint64_t pol_b = l2_policy_evict_normal();
     int last_phase[STAGES];
     for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
-    uint32_t it = 0;
+    uint32_t it = 0, hdr_uses = 0;
     bool ok = true;
+    const uint32_t hdr_bar = smem_u32(hdr_bar_p);
+    bool hdr_inflight = false;
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += nctas) {
       int m_pos, n_tile;
       unit_mn(p, tile, num_m_tiles, m_pos, n_tile);
       const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
+      int nruns = 0;
+      if (p.rank) {  // the tile's first runs arrive while the K loop's copies are issued
+        mbar_arrive_expect_tx(hdr_bar, kHdrRuns * 5 * 4);
+        bulk_load_1d(smem_u32(hdr_smem), p.tile_runs + (int64_t)m_tile * kMaxRunsPerTile * 5, kHdrRuns * 5 * 4,
+                     hdr_bar);
+        hdr_inflight = true;
+        nruns = tile_lora_runs(p, m_pos);  // used after the K loop
+      }
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int a_row = m_tile * BM;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
@@ -281,7 +299,12 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         last_phase[s] = (int)ph;
       }
       // LoRA blocks: S of the tile + B rows of each tenant run
-      const int nruns = ok ? tile_lora_runs(p, m_pos) : 0;
+      if (p.rank && ok) {
+        ok = mbar_wait(hdr_bar, hdr_uses & 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutProducer);
+        ++hdr_uses;
+        hdr_inflight = !ok;
+      }
+      if (!ok) nruns = 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -298,7 +321,9 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           if (p.swiglu) tma_load_2d(base + (p.lchunks + ch) * LCHUNK, &tm_s, bar, p.rank + ch * 16, a_row, pol_a);
         }
         for (int jj = 0; jj < nr; ++jj) {
-          const int brow = (int)(tile_run(p, m_tile, r0 + jj)[0] * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
+          const int r = r0 + jj;
+          const int tenant = r < kHdrRuns ? hdr_smem[r * 5] : tile_run(p, m_tile, r)[0];
+          const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
             if (p.swiglu) {
@@ -315,6 +340,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     }
     if (!ok) {
       // Let the copies already in flight land before the CTA exits.
+      if (hdr_inflight) mbar_wait(hdr_bar, hdr_uses & 1, &never_abort, p.status, 1000000000ull, kDevTimeoutDrain);
       for (int s = 0; s < STAGES; ++s)
         if (last_phase[s] >= 0)
           mbar_wait(land_bar(s), (uint32_t)last_phase[s], &never_abort, p.status, 1000000000ull, kDevTimeoutDrain);
