@@ -89,10 +89,12 @@ def test_topk_ties_and_equal_logits(ops):
 
 # ------------------------------------------------------------------ permutation
 # (9000, 2, 8, 0, 32): 18000 pairs in 9 chunks -> the separate placement kernel;
-# (1000, 6, 64, 2, 128): 8514 keys -> the sort-based kernels.
+# (1000, 6, 64, 2, 128): 8514 keys -> the sort-based kernels; (1800, 2, ...) and
+# (3000, 2, 8, 0, 32): 2 and 3 chunks, placed by the last CTA.
 @pytest.mark.parametrize("T,k,E,ns,nT,gbt", [(3000, 2, 8, 1, 5, False), (1000, 6, 64, 2, 128, False),
                                                (700, 1, 4, 0, 3, True), (5, 2, 3, 0, 0, False), (1, 2, 8, 0, 32, False),
-                                               (9000, 2, 8, 0, 32, False)])
+                                               (9000, 2, 8, 0, 32, False), (1800, 2, 8, 0, 7, False),
+                                               (3000, 2, 8, 0, 32, False)])
 def test_permute_bit_exact(ops, T, k, E, ns, nT, gbt):
     rng = np.random.default_rng(T + E)
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int64)
