@@ -103,6 +103,20 @@ bool gemm_pairs_enabled() {
 // single tile, which the plan would route to the one-CTA kernel anyway.
 bool pairs_pay(int64_t rows, int n_groups) { return rows >= 256 * (int64_t)n_groups; }
 
+// With per-token-tenant LoRA, pairs pay off only while the masked expand MMAs stay a
+// small share of a pair's work: each tenant run of a 256-row pair costs about one K=16
+// step of the pair's main loop (two N=128 masked MMAs over all 256 rows), against
+// K/16 steps, and a pair holds about twice the runs of a 128-row tile. Runs per pair,
+// rows spread evenly over (group, tenant): 256 / (rows per key) + 1. Measured: the
+// Mixtral shape (17 runs per pair, K >= 4096) is even between the two kernels; the
+// fine-grained shape (~34 runs, K = 1408) runs 21 % faster on one-CTA tiles.
+bool pair_lora_pays(int64_t rows, int n_groups, int n_tenants, int k_min) {
+  if (n_tenants <= 0 || rows <= 0 || n_groups <= 0 || k_min <= 0) return true;
+  const double rows_per_key = (double)rows / ((double)n_groups * n_tenants);
+  const double runs = 256.0 / std::max(rows_per_key, 1.0) + 1.0;
+  return runs * 16.0 / k_min < 0.15;
+}
+
 void carve_pair_plan(Carver& c, int64_t tiles_cap, bool lora, PairPlan* pp) {
   *pp = PairPlan{};
   if (!gemm_pairs_enabled() || tiles_cap <= 0) return;
@@ -270,7 +284,9 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
     b->s2 = c.take_bytes((size_t)rows_cap * a->rank * es);
   }
   const bool lora = a->rank > 0 && (a->lora_a13 || a->lora_a2);
-  if (a->weight_dtype != STAGEML_E4M3 && pairs_pay(P, E_tot)) carve_pair_plan(c, rows_cap / 128, lora, &b->pp);
+  if (a->weight_dtype != STAGEML_E4M3 && pairs_pay(P, E_tot) &&
+      (!lora || pair_lora_pays(P, E_tot, a->n_tenants, std::min(a->H, a->I))))
+    carve_pair_plan(c, rows_cap / 128, lora, &b->pp);
   if (!b->pp.on() && lora) {
     b->runs = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
     b->nruns = c.take<int32_t>((size_t)(rows_cap / 128));

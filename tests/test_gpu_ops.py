@@ -173,7 +173,8 @@ def _oracle_moe(c, ids, w, ns=0):
     dict(T=64, H=128, I=128, E=4, k=2, nT=3, r=16, lora=("w13",)),
     dict(T=1, H=256, I=256, E=8, k=2, nT=2, r=16),
     dict(T=130, H=136, I=200, E=3, k=3, nT=0, r=0),
-    dict(T=600, H=256, I=384, E=6, k=2, nT=9, r=8, ns=1, ten_dist="zipf"),  # rank 8 on tile pairs
+    dict(T=600, H=256, I=384, E=6, k=2, nT=9, r=8, ns=1, ten_dist="zipf"),  # rank 8, run-heavy: one-CTA tiles
+    dict(T=600, H=1024, I=1024, E=3, k=2, nT=2, r=8, ns=1, ten_dist="zipf"),  # rank 8 on tile pairs
     dict(T=3, H=256, I=256, E=4, k=2, nT=2, r=8),  # rank 8, decode-sized batch
 ])
 def test_moe_forward_vs_oracle(ops, case):
