@@ -5,8 +5,9 @@
 //
 // Logits: for E <= 32 with the gate fitting shared memory, each CTA keeps G
 // resident and warps take whole tokens (a few tokens: one warp per (token,
-// expert) reading G from L2, with the same per-lane sum order); otherwise a
-// register-blocked tiled kernel over (64 tokens x 64 experts) tiles.
+// expert) reading G from L2, with the same per-lane sum order); more experts with
+// bf16 tokens: tensor-core tiles on an exact three-way bf16 split of the fp32 gate;
+// otherwise a register-blocked tiled kernel over (32 tokens x 64 experts) tiles.
 // Top-k: one warp per token, lane j owns experts j, j+32, ...; k rounds of a
 // warp arg-max (larger logit first, ties -> lower expert index).
 #include "common.cuh"
@@ -113,6 +114,117 @@ __global__ void __launch_bounds__(RT_THREADS) router_logits_kernel(const T* __re
     for (int j = 0; j < 4; ++j) {
       const int e = e0 + tx * 4 + j;
       if (e < E) logits[(int64_t)t * E + e] = acc[i][j];
+    }
+  }
+}
+
+// More than 32 experts with bf16 tokens: the same fp32 dot products on the tensor
+// cores. Each fp32 gate value is split exactly into three bf16 parts (g = hi + mid +
+// lo: 8 + 8 + 8 significant bits), so x . g = x . hi + x . mid + x . lo with every
+// product exact and fp32 accumulation (mma.sync m16n8k16). CTA tile: 64 tokens x
+// 64 experts, 4 warps of 16 tokens; K in 32-wide chunks through shared memory
+// (double-buffered: the next chunk's global loads are in flight during the MMAs).
+// A token's sums do not depend on the other tokens of the batch.
+constexpr int RTC_TT = 64, RTC_TE = 64, RTC_KC = 32, RTC_PITCH = RTC_KC + 8;  // pitch in bf16 (80 B rows)
+
+__device__ __forceinline__ void rtc_ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void rtc_ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void rtc_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(128) router_logits_tc_kernel(const bf16* __restrict__ x, const float* __restrict__ gw,
+                                                               int T_, int H, int E, float* __restrict__ logits) {
+  __shared__ __align__(16) bf16 xs[2][RTC_TT][RTC_PITCH];
+  __shared__ __align__(16) bf16 gs[2][3][RTC_TE][RTC_PITCH];  // hi, mid, lo parts
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = blockIdx.x * RTC_TT, e0 = blockIdx.y * RTC_TE;
+  // loader: x 64 rows x 32 (two 16-byte pieces per thread), G 64 rows x 32 fp32 (four)
+  uint4 xv[2];
+  float4 gv[4];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int idx = tid + 128 * i, r = idx >> 2, c = (idx & 3) * 8;
+      const int t = t0 + r;
+      xv[i] = (t < T_ && k0 + c < H) ? __ldg(reinterpret_cast<const uint4*>(x + (int64_t)t * H + k0 + c))
+                                     : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = tid + 128 * i, r = idx >> 3, c = (idx & 7) * 4;
+      const int e = e0 + r;
+      gv[i] = (e < E && k0 + c < H) ? __ldg(reinterpret_cast<const float4*>(gw + (int64_t)e * H + k0 + c))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int idx = tid + 128 * i, r = idx >> 2, c = (idx & 3) * 8;
+      *reinterpret_cast<uint4*>(&xs[buf][r][c]) = xv[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = tid + 128 * i, r = idx >> 3, c = (idx & 7) * 4;
+      const float g[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const bf16 hi = __float2bfloat16_rn(g[q]);
+        const float r1 = g[q] - __bfloat162float(hi);
+        const bf16 mid = __float2bfloat16_rn(r1);
+        const bf16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+        gs[buf][0][r][c + q] = hi;
+        gs[buf][1][r][c + q] = mid;
+        gs[buf][2][r][c + q] = lo;
+      }
+    }
+  };
+  float acc[RTC_TE / 8][4];
+#pragma unroll
+  for (int nb = 0; nb < RTC_TE / 8; ++nb)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[nb][j] = 0.f;
+  load(0);
+  int buf = 0;
+  for (int k0 = 0; k0 < H; k0 += RTC_KC, buf ^= 1) {
+    store(buf);
+    __syncthreads();
+    if (k0 + RTC_KC < H) load(k0 + RTC_KC);
+#pragma unroll
+    for (int k16 = 0; k16 < RTC_KC / 16; ++k16) {
+      uint32_t a0, a1, a2, a3;
+      rtc_ldsm_x4(smem_u32(&xs[buf][warp * 16 + (lane & 15)][k16 * 16 + (lane >> 4) * 8]), a0, a1, a2, a3);
+#pragma unroll
+      for (int nb = 0; nb < RTC_TE / 8; ++nb) {
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+          uint32_t b0, b1;
+          rtc_ldsm_x2(smem_u32(&gs[buf][part][nb * 8 + (lane & 7)][k16 * 16 + ((lane >> 3) & 1) * 8]), b0, b1);
+          rtc_mma(acc[nb], a0, a1, a2, a3, b0, b1);
+        }
+      }
+    }
+    __syncthreads();  // the buffer is rewritten two chunks later
+  }
+  const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int nb = 0; nb < RTC_TE / 8; ++nb) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + warp * 16 + g + (j >= 2 ? 8 : 0);
+      const int e = e0 + nb * 8 + tig * 2 + (j & 1);
+      if (t < T_ && e < E) logits[(int64_t)t * E + e] = acc[nb][j];
     }
   }
 }
@@ -474,6 +586,13 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
     if (E <= 8) return launch(router_logits_smem_kernel<float, 8>, xp);
     if (E <= 16) return launch(router_logits_smem_kernel<float, 16>, xp);
     return launch(router_logits_smem_kernel<float, 32>, xp);
+  }
+  if (x_dtype == STAGEML_BF16 && H % RTC_KC == 0 && aligned) {
+    const dim3 g2((unsigned)((T_ + RTC_TT - 1) / RTC_TT), (unsigned)((E + RTC_TE - 1) / RTC_TE));
+    (router_logits_tc_kernel<<<g2, 128, 0, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E, logits),
+     ::sb::count_launch());
+    SB_CUDA_CHECK(cudaGetLastError());
+    return STAGEML_OK;
   }
   const dim3 grid((unsigned)((T_ + RT_TT - 1) / RT_TT), (unsigned)((E + RT_TE - 1) / RT_TE));
   const bool vec = H % 8 == 0 && aligned;
