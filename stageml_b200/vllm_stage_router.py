@@ -7,7 +7,10 @@ go to vLLM's ``fused_experts``. Same classes and functions as the reference.
 Difference in the split: the reference moves the tenant ids to the host to
 build the mask (``tenant_ids.cpu().tolist()``, stageml/vllm_stage_router.py:60-63).
 Here the mask is a device-side table lookup; the host only learns the number
-of selected tokens (one scalar) to size the two sub-batches.
+of selected tokens (one scalar) to size the two sub-batches. With
+``split="masked"`` there is no host synchronisation at all: both backends see the
+whole batch, each with the other backend's routing weights set to zero, and the
+two outputs are added (twice the expert work; usable under CUDA-graph capture).
 """
 
 from __future__ import annotations
@@ -142,8 +145,19 @@ def call_stageml_residual_op(hidden, gate_up, down, topk_weights, topk_ids):
 
 def route_fused_experts(*, hidden, gate_up, down, topk_weights, topk_ids, tenant_ids, router: StageMLTenantRouter,
                         vllm_fused_experts: Callable[..., Any] | None = None,
-                        stageml_op: Callable[..., torch.Tensor] | None = None):
-    """Route tokens between the StageML residual op and vLLM fused experts (stageml/vllm_stage_router.py:114-157)."""
+                        stageml_op: Callable[..., torch.Tensor] | None = None, split: str = "indexed"):
+    """Route tokens between the StageML residual op and vLLM fused experts (stageml/vllm_stage_router.py:114-157).
+
+    split="indexed" (the reference's behaviour): each backend runs on its own tokens.
+    split="masked": no host synchronisation; both backends run on every token with the
+    routing weights of the other backend's tokens zeroed, and the outputs are summed.
+    A fused-MoE output row is a routing-weighted sum of expert outputs, so a token
+    with all-zero weights contributes an exact zero row and each token's row is its
+    own backend's row (the same bits when a backend's rows do not depend on the rest
+    of its batch, as for this package's op).
+    """
+    if split not in ("indexed", "masked"):
+        raise ValueError(f"split must be 'indexed' or 'masked', not {split!r}")
     if hidden.shape[0] != tenant_ids.numel():
         raise ValueError("tenant_ids must contain one tenant id per token")
     if vllm_fused_experts is None:
@@ -152,6 +166,10 @@ def route_fused_experts(*, hidden, gate_up, down, topk_weights, topk_ids, tenant
             raise RuntimeError(f"vLLM fused experts could not be resolved: {source}")
     stageml_op = stageml_op or call_stageml_residual_op
     mask = router.materialized_mask(tenant_ids.to(hidden.device))
+    if split == "masked":
+        m = mask.to(topk_weights.dtype).unsqueeze(1)
+        return (stageml_op(hidden, gate_up, down, topk_weights * m, topk_ids)
+                + call_vllm_fused_experts(vllm_fused_experts, hidden, gate_up, down, topk_weights * (1 - m), topk_ids))
     n_sel = int(mask.sum())
     if n_sel == hidden.shape[0]:
         return stageml_op(hidden, gate_up, down, topk_weights, topk_ids)

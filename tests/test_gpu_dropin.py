@@ -139,3 +139,7 @@ def test_custom_op_registration_and_router_with_real_op():
     ref = omoe.fallback_moe(f64(h), f64(gu), f64(dn), w.cpu().numpy(), ids.cpu().numpy())
     assert rel_l2(f64(out[m]), ref[m.cpu().numpy()]) < 1e-2
     assert rel_l2(f64(full), ref) < 1e-2
+    # no host synchronisation: both backends on every token, the other side's weights zeroed
+    masked = route_fused_experts(hidden=h, gate_up=gu, down=dn, topk_weights=w, topk_ids=ids, tenant_ids=ten,
+                                 router=router, vllm_fused_experts=fake_vllm, split="masked")
+    assert torch.equal(masked, out)

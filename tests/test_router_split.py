@@ -67,3 +67,23 @@ def test_golden_split_from_reference():
                               tenant_ids=torch.from_numpy(g["tenant_ids"]), router=StageMLTenantRouter(kernels),
                               vllm_fused_experts=fv, stageml_op=fs)
     np.testing.assert_array_equal(out.numpy(), g["out"])
+
+
+def test_masked_split_needs_no_host_sync_and_matches_indexed():
+    """split="masked" runs both backends on every token with the other side's routing
+    weights zeroed; for weight-linear backends each row equals the indexed split's."""
+    g = torch.Generator().manual_seed(3)
+    hidden = torch.randn(7, 3, generator=g)
+    w = torch.rand(7, 2, generator=g)
+    ids = torch.zeros(7, 2, dtype=torch.long)
+    fv = lambda h, gu, dn, tw, ti: (h[:, : dn.shape[1]] * 3.0) * tw.sum(1, keepdim=True)
+    fs = lambda h, gu, dn, tw, ti: (h[:, : dn.shape[1]] - 1.0) * tw.sum(1, keepdim=True)
+    router = StageMLTenantRouter({0: TenantKernel(0, 0, "t", "x", "s"), 4: TenantKernel(4, 1, "t", "x", "s")})
+    ten = torch.tensor([0, 1, 4, 4, -1, 9, 0])
+    kw = dict(hidden=hidden, gate_up=torch.randn(2, 4, 3), down=torch.randn(2, 3, 2), topk_weights=w, topk_ids=ids,
+              tenant_ids=ten, router=router, vllm_fused_experts=fv, stageml_op=fs)
+    a = route_fused_experts(**kw)
+    b = route_fused_experts(split="masked", **kw)
+    torch.testing.assert_close(b, a, rtol=0, atol=0)
+    with pytest.raises(ValueError, match="split"):
+        route_fused_experts(split="bogus", **kw)
