@@ -10,7 +10,7 @@ Here the mask is a device-side table lookup; the host only learns the number
 of selected tokens (one scalar) to size the two sub-batches. With
 ``split="masked"`` there is no host synchronisation at all: both backends see the
 whole batch, each with the other backend's routing weights set to zero, and the
-two outputs are added (twice the expert work; usable under CUDA-graph capture).
+two outputs are added (twice the expert work, no host read-back).
 """
 
 from __future__ import annotations
