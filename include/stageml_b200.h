@@ -318,8 +318,7 @@ int stageml_lora_gemv_f32(const float* x, const float* W, const float* A, const 
  *    STAGEML_ERR_INVALID_ARG (in = out = 4096 on a 148-SM B200 fits up to M = 7);
  *    stageml_lora_gemv_f32 with a workspace has no such limit.
  *  - The first call on a device looks up the scratch array's device address
- *    (cudaGetSymbolAddress, with that device current) and caches it; make that
- *    first call before any stream capture.
+ *    (cudaGetSymbolAddress, with that device current) and caches it.
  *  - All calls share the one array, which keeps the last call's contents. No
  *    part of it needs to start at zero (each partial is written before it is
  *    read), but two calls whose kernels can overlap on the GPU (different
