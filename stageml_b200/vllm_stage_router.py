@@ -77,10 +77,8 @@ class StageMLTenantRouter:
 
     @classmethod
     def from_manifest(cls, path: str | Path) -> "StageMLTenantRouter":
-        m = read_kernel_manifest(path)
-        return cls({e.tenant_id: TenantKernel(tenant_id=e.tenant_id, adapter_id=e.adapter_id, backend=e.backend,
-                                              artifact=e.artifact, symbol=e.symbol, enabled=e.enabled)
-                    for e in m.entries if e.enabled})
+        """Router over the enabled entries of a kernel manifest (a TenantKernel has the entry's fields)."""
+        return cls({e.tenant_id: TenantKernel(**asdict(e)) for e in read_kernel_manifest(path).entries if e.enabled})
 
     def has_kernel(self, tenant_id: int) -> bool:
         e = self.kernels.get(int(tenant_id))
@@ -104,37 +102,45 @@ class StageMLTenantRouter:
         return table[torch.where(in_range, ids, torch.full_like(ids, table.numel() - 1))] & in_range
 
 
+# Locations of vLLM's fused_experts across releases, in the order they are tried.
+_VLLM_FUSED_EXPERTS_PATHS = ("vllm.model_executor.layers.fused_moe.fused_moe.fused_experts",
+                             "vllm.model_executor.layers.fused_moe.fused_experts")
+
+
 def resolve_vllm_fused_experts() -> tuple[Callable[..., Any] | None, str]:
-    candidates = [("vllm.model_executor.layers.fused_moe.fused_moe", "fused_experts"),
-                  ("vllm.model_executor.layers.fused_moe", "fused_experts")]
-    errors: list[str] = []
-    for mod_name, attr in candidates:
+    """vLLM's fused_experts and its dotted path, or None and why every location failed
+    (stageml/vllm_stage_router.py:65-80: same locations, order and messages)."""
+    why: list[str] = []
+    for path in _VLLM_FUSED_EXPERTS_PATHS:
+        module, _, name = path.rpartition(".")
         try:
-            fn = getattr(importlib.import_module(mod_name), attr)
-            if callable(fn):
-                return fn, f"{mod_name}.{attr}"
-            errors.append(f"{mod_name}.{attr} exists but is not callable")
-        except Exception as exc:
-            errors.append(f"{mod_name}.{attr}: {exc}")
-    return None, "; ".join(errors)
+            fn = getattr(importlib.import_module(module), name)
+        except Exception as exc:  # vLLM absent, or this release keeps the function elsewhere
+            why.append(f"{path}: {exc}")
+            continue
+        if callable(fn):
+            return fn, path
+        why.append(f"{path} exists but is not callable")
+    return None, "; ".join(why)
 
 
 def call_vllm_fused_experts(fn: Callable[..., Any], hidden, gate_up, down, topk_weights, topk_ids):
-    topk_ids = topk_ids.to(dtype=torch.long).contiguous()
-    topk_weights = topk_weights.contiguous()
-    attempts = [
-        lambda: fn(hidden_states=hidden, w1=gate_up, w2=down, topk_weights=topk_weights, topk_ids=topk_ids,
-                   inplace=False),
-        lambda: fn(hidden, gate_up, down, topk_weights, topk_ids, False),
-        lambda: fn(hidden, gate_up, down, topk_weights, topk_ids),
-    ]
-    last: Exception | None = None
-    for attempt in attempts:
+    """Call vLLM's fused_experts in whichever argument form its release accepts
+    (stageml/vllm_stage_router.py:84-105: keywords with inplace=False, then positional with
+    inplace=False, then positional; the last failure is reported)."""
+    ids = topk_ids.to(dtype=torch.long).contiguous()
+    wts = topk_weights.contiguous()
+    positional = (hidden, gate_up, down, wts, ids)
+    forms = (((), dict(hidden_states=hidden, w1=gate_up, w2=down, topk_weights=wts, topk_ids=ids, inplace=False)),
+             (positional + (False,), {}),
+             (positional, {}))
+    failure: Exception | None = None
+    for args, kwargs in forms:
         try:
-            return attempt()
-        except Exception as exc:
-            last = exc
-    raise RuntimeError(f"could not call vLLM fused_experts: {last}")
+            return fn(*args, **kwargs)
+        except Exception as exc:  # another release's signature (or a failing call): try the next form
+            failure = exc
+    raise RuntimeError(f"could not call vLLM fused_experts: {failure}")
 
 
 def call_stageml_residual_op(hidden, gate_up, down, topk_weights, topk_ids):
@@ -175,17 +181,18 @@ def route_fused_experts(*, hidden, gate_up, down, topk_weights, topk_ids, tenant
         return stageml_op(hidden, gate_up, down, topk_weights, topk_ids)
     if n_sel == 0:
         return call_vllm_fused_experts(vllm_fused_experts, hidden, gate_up, down, topk_weights, topk_ids)
-    out = torch.empty((hidden.shape[0], down.shape[1]), device=hidden.device, dtype=hidden.dtype)
-    for selected, fn in ((mask, stageml_op), (~mask, None)):
-        idx = torch.nonzero(selected, as_tuple=False).flatten()
-        sub_h = hidden.index_select(0, idx).contiguous()
-        sub_w = topk_weights.index_select(0, idx).contiguous()
-        sub_i = topk_ids.index_select(0, idx).contiguous()
-        if fn is None:
-            sub = call_vllm_fused_experts(vllm_fused_experts, sub_h, gate_up, down, sub_w, sub_i)
-        else:
-            sub = fn(sub_h, gate_up, down, sub_w, sub_i)
-        out.index_copy_(0, idx, sub)
+    # StageML tokens first, then vLLM's, each in token order: one stable sort, no per-side nonzero.
+    order = torch.argsort((~mask).to(torch.uint8), stable=True)
+    mine, theirs = order[:n_sel], order[n_sel:]
+
+    def rows(t, idx):
+        return t.index_select(0, idx).contiguous()
+
+    out = hidden.new_empty((hidden.shape[0], down.shape[1]))
+    out.index_copy_(0, mine, stageml_op(rows(hidden, mine), gate_up, down, rows(topk_weights, mine),
+                                        rows(topk_ids, mine)))
+    out.index_copy_(0, theirs, call_vllm_fused_experts(vllm_fused_experts, rows(hidden, theirs), gate_up, down,
+                                                       rows(topk_weights, theirs), rows(topk_ids, theirs)))
     return out
 
 
