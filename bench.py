@@ -9,8 +9,9 @@ already resident in HBM. Metric: layer tokens/s (whole job, all ranks).
 N = 1: the Mixtral-shape layer (T=2048, H=4096, I=14336, E=8, top-2, rank-16
 LoRA for 32 tenants, bf16). N > 1 (torchrun, one process per GPU, NCCL):
 expert parallel -- each rank routes its own 2048 tokens, experts are sharded
-E/N per rank with their adapter-bank slices, tokens are dispatched and
-combined with all-to-all (weak scaling: per-GPU work fixed).
+E/N per rank with their adapter-bank slices, and routed rows go to their
+experts' ranks and back through peer memory over NVLink (this library's
+exchange kernels; no NCCL on the data path) (weak scaling: per-GPU work fixed).
 
 --impl reference: the oracle port of the reference's CPU path (numpy/OpenBLAS,
 float32) timed on the host cores on a token sample of the same workload; under
