@@ -76,7 +76,10 @@ size_t stageml_struct_size(int which);
  * event pair around each of their kernel stages on their stream.
  * stageml_stage_timer_read waits for those events, adds the elapsed
  * milliseconds of stage s to ms_out[s] and the number of timed launches to
- * counts_out[s] (s < n), and forgets them. Disabled by default. */
+ * counts_out[s] (s < n), and forgets them. Disabled by default.
+ * stageml_stage_timer_select limits the recorded stages to those whose bit is
+ * set in `mask` (bit s = stage s; all stages by default), so that a benchmark can
+ * time one stage inside its timed calls at the cost of one event pair per call. */
 enum {
   STAGEML_STAGE_ROUTE = 0,
   STAGEML_STAGE_PERMUTE = 1,
@@ -91,6 +94,7 @@ enum {
   STAGEML_NUM_STAGES = 10
 };
 int stageml_stage_timer_enable(int on);
+int stageml_stage_timer_select(unsigned int mask);
 int stageml_stage_timer_read(float* ms_out, int32_t* counts_out, int n);
 /* Number of kernels this library has launched in the process so far (all threads). */
 unsigned long long stageml_launch_count(void);
@@ -318,7 +322,11 @@ int stageml_lora_gemv_f32(const float* x, const float* W, const float* A, const 
  *    STAGEML_ERR_INVALID_ARG (in = out = 4096 on a 148-SM B200 fits up to M = 7);
  *    stageml_lora_gemv_f32 with a workspace has no such limit.
  *  - The first call on a device looks up the scratch array's device address
- *    (cudaGetSymbolAddress, with that device current) and caches it.
+ *    (cudaGetSymbolAddress, with that device current) and caches it together
+ *    with the current driver context; a call made under another context of the
+ *    device (a non-primary context, or the primary context recreated after
+ *    cudaDeviceReset) looks the address up again. Make the first call on each
+ *    device before any stream capture, since the lookup may load the module.
  *  - All calls share the one array, which keeps the last call's contents. No
  *    part of it needs to start at zero (each partial is written before it is
  *    read), but two calls whose kernels can overlap on the GPU (different

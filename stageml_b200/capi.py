@@ -159,6 +159,7 @@ SIGNATURES = {
                                               c_int, c_void_p, c_void_p]),
     "stageml_quantize_e4m3_rows": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "stageml_stage_timer_enable": (c_int, [c_int]),
+    "stageml_stage_timer_select": (c_int, [ctypes.c_uint]),
     "stageml_stage_timer_read": (c_int, [c_float_p, c_int32_p, c_int]),
     "stageml_launch_count": (ctypes.c_ulonglong, []),
     "stageml_ep_get_layout": (c_int, [c_int, c_int64, c_int, c_int, c_int, POINTER(EpLayout)]),

@@ -166,25 +166,54 @@ constexpr size_t kGemvNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
 static __device__ __align__(256) unsigned char g_gemv_noalloc_scratch[kGemvNoAllocScratchBytes];
 
 std::mutex g_scratch_mu;
-void* g_scratch_addr[64] = {nullptr};  // device address of the array, per device ordinal
+// Device address of the array per device ordinal, with the driver context it was
+// taken in: a caller that makes a different context current on the device (a
+// non-primary context, or the primary context recreated after cudaDeviceReset)
+// gets the array's address in that context, not a stale one.
+struct ScratchAddr {
+  void* ctx = nullptr;
+  void* addr = nullptr;
+};
+ScratchAddr g_scratch_addr[64];
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The current driver context (null when the driver entry point is unavailable).
+void* current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
 
 // Device address of the scratch array on the current device. Host code cannot
-// use the array's name as a device pointer, so the address is queried once per
-// device with that device current and cached.
+// use the array's name as a device pointer, so the address is queried with the
+// device current, once per device and driver context, and cached.
 int gemv_noalloc_scratch(void** out) {
   int dev = 0;
   SB_CUDA_CHECK(cudaGetDevice(&dev));
   SB_CHECK_ARG(dev >= 0 && dev < 64, "lora_gemv_f32_noalloc: device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  void* ctx = current_context();
+  ScratchAddr& c = g_scratch_addr[dev];
+  if (!c.addr || c.ctx != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch);
     if (e != cudaSuccess || !p)
       return set_error(STAGEML_ERR_CUDA, "lora_gemv_f32_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
                        cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
+    c.addr = p;
+    c.ctx = ctx;
   }
-  *out = g_scratch_addr[dev];
+  *out = c.addr;
   return STAGEML_OK;
 }
 

@@ -14,6 +14,7 @@ struct Rec {
 };
 
 thread_local bool t_on = false;
+thread_local unsigned t_mask = ~0u;  // stages recorded while on (bit s = stage s)
 thread_local std::vector<Rec> t_recs;
 thread_local std::vector<cudaEvent_t> t_pool;
 thread_local int t_open_stage = -1;
@@ -32,7 +33,7 @@ cudaEvent_t get_event() {
 
 }  // namespace
 
-bool stage_timer_on() { return t_on; }
+bool stage_timer_on(int stage) { return t_on && stage >= 0 && stage < 32 && ((t_mask >> stage) & 1u); }
 
 void stage_timer_record(int stage, cudaStream_t stream, bool begin) {
   cudaEvent_t e = get_event();
@@ -54,6 +55,11 @@ void stage_timer_record(int stage, cudaStream_t stream, bool begin) {
 
 extern "C" int stageml_stage_timer_enable(int on) {
   sb::t_on = on != 0;
+  return STAGEML_OK;
+}
+
+extern "C" int stageml_stage_timer_select(unsigned int mask) {
+  sb::t_mask = mask;
   return STAGEML_OK;
 }
 

@@ -1,11 +1,11 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
 Runs the reference implementation itself (uwm-se/stageML, read from the path
-given by --reference, default /root/reference) on small seeded inputs and
+given by --reference, a required argument) on small seeded inputs and
 stores inputs and outputs as .npz files next to this script. Only this
 generator reads the reference; the tests read the committed .npz files.
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--reference PATH]
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference PATH
 
 Cases (reference file the outputs come from):
   moe_lora_layers.npz    DynamicMoELoRALayer / MaterializedMoELoRALayer (stageml/moe_lora_layers.py),
@@ -130,7 +130,7 @@ def residual_plan() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of the reference project (read only)")
     ap.add_argument("--only", default=None, help="generate one case (workload_plan)")
     args = ap.parse_args()
     ref = Path(args.reference)

@@ -47,3 +47,20 @@ def test_result_line_carries_the_contract_keys(capsys):
                 "scaling", "vs_baseline", "dtype", "data", "config"):
         assert key in d
     assert d["gpu_launches"] == 7 and d["config"] == {"workload": "w"}
+
+
+def test_peak_choice_follows_the_sampled_clocks():
+    peaks = {"bf16_tflops": 1649.3, "bf16_tflops_sustained": 1394.0}
+    short_at_max = bench.choose_peak(peaks, {"sm_mhz": 1965, "sm_max_mhz": 1965}, 0.17)
+    assert short_at_max["kind"] == "burst" and short_at_max["value"] == 1649.3
+    long_region = bench.choose_peak(peaks, {"sm_mhz": 1965, "sm_max_mhz": 1965}, 4.0)
+    assert long_region["kind"] == "sustained" and long_region["value"] == 1394.0
+    capped = bench.choose_peak(peaks, {"sm_mhz": 1400, "sm_max_mhz": 1965}, 0.2)
+    assert capped["kind"] == "sustained"
+    unknown = bench.choose_peak(peaks, {"sm_mhz": None, "sm_max_mhz": None}, 0.2)
+    assert unknown["kind"] == "sustained" and unknown["burst"] == 1649.3
+
+
+def test_gate_up_traffic_names_the_capture_it_came_from():
+    for cap in bench.GATE_UP_DRAM_CAPTURE.values():
+        assert cap["bytes"] > 0 and "commit" in cap["source"] and "profiles/" in cap["source"]

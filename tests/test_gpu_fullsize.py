@@ -1,12 +1,13 @@
 """The Mixtral-shape MoE-LoRA layer at its full benchmark size (T=2048, H=4096,
 I=14336, E=8, top-2, rank-16 LoRA on w1/w3/w2, 32 tenants): size-independent
-properties plus an oracle check on the tokens routed to two experts."""
+properties, an oracle check on the tokens routed to the most common expert pair,
+and one on sampled tokens over every expert (tile pairs and odd trailing tiles)."""
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import rel_l2
+from conftest import oracle_moe_tokens, rel_l2
 from oracle import moe as omoe
 
 pytestmark = pytest.mark.gpu
@@ -77,3 +78,26 @@ def test_full_size_batch_of_one(layer):
     assert torch.equal(y64, y128[:64])
     assert rel_l2(y8.float().cpu().numpy(), y64[:8].float().cpu().numpy()) < 1e-2
     assert ops.take_status(y1) == 0
+
+
+def test_full_size_against_oracle_on_every_expert(layer):
+    """Tokens of the first and last tenants, checked over every expert they are routed to.
+
+    Rows of an expert's segment are sorted by tenant, so the last tenant's rows sit in
+    each expert's trailing tile (the odd tile beside the tile pairs, where an expert has
+    an odd tile count) and the first tenant's rows in its leading tile pair."""
+    cfg, w, call, ops = layer
+    y = call(w["x"], w["tenant_ids"])
+    ids, wts, _ = ops.route_topk(w["x"], w["router_w"], cfg.k, True)
+    ids, wts = ids.cpu().numpy(), wts.cpu().numpy()
+    ten = w["tenant_ids"].cpu().numpy()
+    sel = np.concatenate([np.nonzero(ten == 0)[0][:12], np.nonzero(ten == cfg.n_tenants - 1)[0][:20]])
+    assert set(np.unique(ids[sel])) == set(range(cfg.E))
+    f32 = lambda t: t.float().cpu().numpy()
+    xs = f32(w["x"])
+    ref = oracle_moe_tokens(np.arange(sel.size), ids[sel], wts[sel], ten[sel], xs[sel],
+                            lambda e: (f32(w["gate_up"][e]), f32(w["down"][e])),
+                            lambda e: tuple(f32(w[n][:, e:e + 1]) for n in ("lora_a13", "lora_b13", "lora_a2", "lora_b2")),
+                            f32(w["lora_scale"]), n_routed=cfg.E)
+    assert rel_l2(y.float().cpu().numpy()[sel], ref) < 1e-2
+    assert ops.take_status(y) == 0
