@@ -176,12 +176,19 @@ int stageml_combine_rows(const void* y, const int32_t* pair_row, int T, int kk, 
  * LoRA on w1) with the same LoRA term on w3 and w2 as DynamicMoELoRALayer.forward
  * (stageml/moe_lora_layers.py:85-89); with all LoRA pointers NULL it is exactly
  * _fallback_moe (stageml/custom_op_registry.py:23-37), i.e. the residual_moe op.
- * Tenants with a folded (materialized) gate_up simply pass tenant -1 and their own
- * gate_up, as bta_one does (:416-433).
+ * Tenants with a folded (materialized) gate_up either pass tenant -1 and their own
+ * gate_up, as bta_one does (:416-433), or share one call with every other tenant
+ * through fold_slot: folded weight sets are stored after the E_tot base experts in
+ * gate_up / down, and a pair whose (tenant, expert) has a folded set runs on it
+ * (group E_tot + slot) with no dynamic LoRA, in the same permutation and the same
+ * GEMM launches as the dynamic pairs (the decision residual_planner.py:48-153
+ * makes per (adapter, expert), served without splitting the batch on the host).
  *
  * Layouts (row-major, contiguous):
- *   x [T,H]; gate_up [E_tot, 2I, H]; down [E_tot, H, I]   (E_tot = E + n_shared)
+ *   x [T,H]; gate_up [E_tot + n_fold, 2I, H]; down [E_tot + n_fold, H, I]   (E_tot = E + n_shared;
+ *     with down_group, down [E_tot, H, I])
  *   gate_up_scale [E_tot, 2I] / down_scale [E_tot, H] fp32 when weight_dtype == E4M3
+ *   fold_slot [n_tenants, E_tot] int32: -1 = dynamic, s in [0, n_fold) = folded set s
  *   lora_a13 [n_tenants, E_tot, 2r, H] rows [0,r) = A1, [r,2r) = A3
  *   lora_b13 [n_tenants, E_tot, 2I, r] rows [0,I) = B1, [I,2I) = B3
  *   lora_a2 [n_tenants, E_tot, r, I]; lora_b2 [n_tenants, E_tot, H, r]
@@ -218,6 +225,15 @@ typedef struct stageml_moe_args {
   const int32_t* T_dev;  /* optional device int: only tokens [0, *T_dev) are valid (<= T); the rest
                             are skipped and their output rows left untouched. Used when the token
                             count is known only on the device (rows received from other GPUs). */
+  const int32_t* fold_slot; /* optional [n_tenants, E_tot]: per (tenant, expert), -1 = base weights plus
+                               that tenant's LoRA, s >= 0 = folded weight group E_tot + s, no LoRA.
+                               An entry outside [-1, n_fold) drops the pair (STAGEML_DEV_BAD_INDEX).
+                               16-bit weights only (not with E4M3). */
+  int n_fold;               /* folded weight groups stored after the E_tot base experts (0 = none) */
+  const int32_t* down_group; /* optional [E_tot + n_fold], entries in [0, E_tot): weight group g takes its
+                                down projection from down[down_group[g]], and down holds only the E_tot base
+                                experts (folded sets of adapters with no LoRA on w2 share their base expert's
+                                down weights); NULL: down holds all E_tot + n_fold groups */
 } stageml_moe_args;
 
 size_t stageml_moe_workspace_bytes(const stageml_moe_args* args);

@@ -39,7 +39,8 @@ def _pairs(ids, weights, n_shared, E_routed):
 
 
 def moe_forward(x, gate_up, down, ids, weights, *, tenant_ids=None, n_shared: int = 0, lora_a13=None, lora_b13=None,
-                lora_a2=None, lora_b2=None, lora_scale=None, dtype=np.float64, round_h=None):
+                lora_a2=None, lora_b2=None, lora_scale=None, dtype=np.float64, round_h=None, fold_slot=None,
+                down_group=None):
     """out[T,H] of one MoE-LoRA FFN layer.
 
     Layouts: gate_up [E_tot, 2I, H] (rows [:I] = SiLU branch), down [E_tot, H, I],
@@ -47,20 +48,31 @@ def moe_forward(x, gate_up, down, ids, weights, *, tenant_ids=None, n_shared: in
     lora_a2 [nT, E_tot, r, I], lora_b2 [nT, E_tot, H, r], lora_scale [nT]; tenant -1 = no adapter.
     round_h: optional function applied to the SwiGLU output before the down projection
     (models the 16-bit intermediate of the device path).
+    fold_slot [nT, E_tot]: with it, gate_up / down hold E_tot + n_fold weight groups and a pair
+    of tenant a routed to expert e with fold_slot[a, e] = s >= 0 uses group E_tot + s (the
+    adapter folded into that expert's weights, as MaterializedMoELoRALayer and the
+    residual planner's materialized entries do) without the dynamic LoRA term.
+    down_group [E_tot + n_fold]: group g's down projection is down[down_group[g]].
     """
     x = np.asarray(x, dtype=dtype)
     gate_up = np.asarray(gate_up)
     down = np.asarray(down)
     T, H = x.shape
-    E_tot = gate_up.shape[0]
     I = gate_up.shape[1] // 2
+    ten = np.full(T, -1, dtype=np.int64) if tenant_ids is None else np.asarray(tenant_ids, dtype=np.int64)
+    E_tot = gate_up.shape[0] if fold_slot is None else np.asarray(fold_slot).shape[1]
     E_routed = E_tot - n_shared
     cols_e, cols_w = _pairs(ids, weights, n_shared, E_routed)
-    ten = np.full(T, -1, dtype=np.int64) if tenant_ids is None else np.asarray(tenant_ids, dtype=np.int64)
+    cols_t = [ten for _ in cols_e]  # LoRA tenant of each pair
+    if fold_slot is not None:
+        fs = np.asarray(fold_slot, dtype=np.int64)
+        folded = [np.where(ten >= 0, fs[np.maximum(ten, 0), ce], -1) for ce in cols_e]
+        cols_e = [np.where(f >= 0, E_tot + f, ce) for ce, f in zip(cols_e, folded)]
+        cols_t = [np.where(f >= 0, -1, ten) for f in folded]
     out = np.zeros((T, H), dtype=dtype)
     r = 0 if lora_a13 is None and lora_a2 is None else (
         lora_a13.shape[2] // 2 if lora_a13 is not None else lora_a2.shape[2])
-    for e in range(E_tot):
+    for e in range(gate_up.shape[0]):
         rows_list = [np.nonzero(ce == e)[0] for ce in cols_e]
         idx = np.concatenate(rows_list)
         if idx.size == 0:
@@ -69,7 +81,7 @@ def moe_forward(x, gate_up, down, ids, weights, *, tenant_ids=None, n_shared: in
         xs = x[idx]
         w13 = gate_up[e].astype(dtype)
         gu = xs @ w13.T
-        tn = ten[idx]
+        tn = np.concatenate([ct[rl] for ct, rl in zip(cols_t, rows_list)])
         if lora_a13 is not None:
             for a in np.unique(tn[tn >= 0]):
                 m = tn == a
@@ -80,7 +92,7 @@ def moe_forward(x, gate_up, down, ids, weights, *, tenant_ids=None, n_shared: in
         h = silu(gu[:, :I]) * gu[:, I:]
         if round_h is not None:
             h = round_h(h).astype(dtype)
-        y = h @ down[e].astype(dtype).T
+        y = h @ down[e if down_group is None else int(down_group[e])].astype(dtype).T
         if lora_a2 is not None:
             for a in np.unique(tn[tn >= 0]):
                 m = tn == a

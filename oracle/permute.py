@@ -7,7 +7,10 @@ pairs p = t*(k+n_shared) + j (slot j < k: expert ids[t, j], weight w[t, j];
 slot j >= k: shared expert E + j - k, weight 1) sorted stably by the key
 (expert, tenant + 1) -- or (tenant*E_tot + expert) with group_by_tenant --
 with each group's rows padded to a multiple of 128. Pairs whose expert or
-tenant id is out of range are dropped (pair_row = -1).
+tenant id is out of range are dropped (pair_row = -1). With a fold map
+fold_slot [n_tenants, E_tot], a pair whose (tenant, expert) entry is s >= 0
+belongs to weight group E_tot + s (after every expert group), sorts by that
+group alone and carries no LoRA tenant; an entry outside [-1, n_fold) drops it.
 """
 
 from __future__ import annotations
@@ -23,7 +26,7 @@ def rows_cap(num_pairs: int, n_groups: int) -> int:
 
 
 def permute(ids, weights, tenant_ids, n_experts_total: int, n_shared: int = 0, n_tenants: int = 0,
-            group_by_tenant: bool = False) -> dict:
+            group_by_tenant: bool = False, fold_slot=None, n_fold: int = 0) -> dict:
     ids = np.asarray(ids, dtype=np.int64)
     T, k = ids.shape
     kk = k + n_shared
@@ -50,6 +53,18 @@ def permute(ids, weights, tenant_ids, n_experts_total: int, n_shared: int = 0, n
         n_groups = n_experts_total
         group = np.where(bad, 0, expert)
         key = group * (n_tenants + 1) + (tenant + 1)
+    lora_tenant = np.full(P, -1, dtype=np.int64) if group_by_tenant else tenant.copy()
+    if fold_slot is not None:
+        fs = np.asarray(fold_slot, dtype=np.int64)
+        ok = ~bad & (tenant >= 0)
+        slot = np.full(P, -1, dtype=np.int64)
+        slot[ok] = fs[tenant[ok], expert[ok]]
+        bad |= (slot < -1) | (slot >= n_fold)
+        fold = ~bad & (slot >= 0)
+        group = np.where(fold, n_groups + slot, group)
+        key = np.where(fold, n_groups * (n_tenants + 1) + slot, key)
+        lora_tenant = np.where(fold, -1, lora_tenant)
+        n_groups += n_fold
     key = np.where(bad, np.iinfo(np.int64).max, key)
     order = np.lexsort((np.arange(P), key))
     order = order[~bad[order]]
@@ -70,7 +85,7 @@ def permute(ids, weights, tenant_ids, n_experts_total: int, n_shared: int = 0, n
         pos += counts[g]
         r = offsets[g] + np.arange(counts[g])
         row_token[r] = t_of[sel]
-        row_tenant[r] = -1 if group_by_tenant else tenant[sel]
+        row_tenant[r] = lora_tenant[sel]
         row_weight[r] = wt[sel]
         row_pair[r] = sel
         pair_row[sel] = r

@@ -72,6 +72,9 @@ class MoeArgs(ctypes.Structure):
         ("status", c_void_p),
         ("plan_out", c_void_p),
         ("T_dev", c_void_p),
+        ("fold_slot", c_void_p),
+        ("n_fold", c_int),
+        ("down_group", c_void_p),
     ]
 
 

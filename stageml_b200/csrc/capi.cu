@@ -20,7 +20,7 @@
 namespace sb {
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;  // 2: stageml_moe_args.fold_slot / n_fold
 
 // Bump allocator over the caller's workspace; with base == nullptr it only
 // measures (the *_workspace_bytes queries run the same carve).
@@ -245,6 +245,11 @@ int moe_validate(const stageml_moe_args* a, bool check_ptrs = true) {
   SB_CHECK_ARG(!(lora13 || lora2) || (a->tenant_ids && a->n_tenants > 0 && a->lora_scale),
                "moe: LoRA needs tenant_ids, n_tenants > 0 and lora_scale");
   SB_CHECK_ARG(a->k == 0 || a->topk_ids || a->router_w, "moe: need topk_ids or router_w");
+  SB_CHECK_ARG(a->n_fold >= 0 && (a->n_fold == 0 || a->fold_slot), "moe: n_fold=%d needs fold_slot", a->n_fold);
+  if (a->fold_slot) {
+    SB_CHECK_ARG(a->tenant_ids && a->n_tenants > 0, "moe: fold_slot needs tenant_ids and n_tenants > 0");
+    SB_CHECK_ARG(a->weight_dtype != STAGEML_E4M3, "moe: folded weight sets need 16-bit weights, not E4M3");
+  }
   if (a->topk_ids) SB_CHECK_ARG(a->ids_dtype == STAGEML_I32 || a->ids_dtype == STAGEML_I64, "moe: ids dtype");
   if (a->T > 0 && check_ptrs) {
     SB_CHECK_ARG(a->x && a->gate_up && a->down && a->out, "moe: null tensor");
@@ -256,22 +261,26 @@ int moe_validate(const stageml_moe_args* a, bool check_ptrs = true) {
   return STAGEML_OK;
 }
 
+// Folded weight groups of a call (0 without a fold map).
+inline int moe_n_fold(const stageml_moe_args* a) { return a->fold_slot ? a->n_fold : 0; }
+
 void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
   Carver c(ws);
   const int E_tot = a->E + a->n_shared;
+  const int n_fold = moe_n_fold(a);
   const int64_t P = (int64_t)a->T * (a->k + a->n_shared);
   const size_t es = esize(a->act_dtype);
   if (a->plan_out)
     b->plan = *a->plan_out;
   else
-    carve_plan(c, P, E_tot, &b->plan);
-  const int64_t rows_cap = stageml_plan_rows_cap(P, E_tot);
+    carve_plan(c, P, E_tot + n_fold, &b->plan);
+  const int64_t rows_cap = stageml_plan_rows_cap(P, E_tot + n_fold);
   if (!a->topk_ids && a->k > 0) {
     b->logits = c.take<float>((size_t)a->T * a->E);
     b->ids = c.take<int32_t>((size_t)a->T * a->k);
     b->weights = c.take<float>((size_t)a->T * a->k);
   }
-  const int64_t nkeys = permute_num_keys(0, a->n_tenants, 0, E_tot);
+  const int64_t nkeys = permute_num_keys(n_fold, a->n_tenants, 0, E_tot);
   b->perm_scratch = c.take_bytes(permute_scratch_bytes(P, nkeys));
   b->xp = c.take_bytes((size_t)rows_cap * a->H * es);
   b->hbuf = c.take_bytes((size_t)rows_cap * a->I * es);
@@ -314,9 +323,11 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     return set_error(STAGEML_ERR_WORKSPACE, "moe: workspace of %zu bytes < required %zu", ws_bytes, b.bytes);
   moe_carve(a, ws, &b);
   const int E_tot = a->E + a->n_shared;
+  const int n_fold = moe_n_fold(a);
   const int64_t P = (int64_t)a->T * (a->k + a->n_shared);
   if (a->plan_out)
-    SB_CHECK_ARG(a->plan_out->rows_cap >= stageml_plan_rows_cap(P, E_tot), "moe: plan_out rows_cap too small");
+    SB_CHECK_ARG(a->plan_out->rows_cap >= stageml_plan_rows_cap(P, E_tot + n_fold),
+                 "moe: plan_out rows_cap too small");
   int32_t* status = a->status ? a->status : b.status;
   const int bf = a->act_dtype == STAGEML_BF16;
   const bool lora13 = a->rank > 0 && a->lora_a13;
@@ -344,10 +355,11 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   }
   // R2: permutation
   PermuteScratch scr;
-  const int64_t nkeys = permute_num_keys(0, a->n_tenants, 0, E_tot);
+  const int64_t nkeys = permute_num_keys(n_fold, a->n_tenants, 0, E_tot);
   permute_carve(b.perm_scratch, P, nkeys, &scr);
-  SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k, a->n_shared, E_tot, a->n_tenants, 0,
-                        b.plan, status, scr, st, a->T_dev, pdl));
+  SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k,
+                                                 a->n_shared, E_tot, a->n_tenants, 0, b.plan, status, scr, st,
+                                                 a->T_dev, pdl, a->fold_slot, n_fold));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
   if (!skinny && b.pp.on()) {
     SB_STAGE(STAGEML_STAGE_PERMUTE, build_pair_plan(b.pp, b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles,
@@ -391,7 +403,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.a_row_of = skinny ? b.plan.row_token : nullptr;
     g.K = a->H;
     g.b = a->gate_up;
-    g.b_rows_total = (int64_t)E_tot * 2 * a->I;
+    g.b_rows_total = (int64_t)(E_tot + n_fold) * 2 * a->I;
     g.b_group_rows = 2 * a->I;
     g.N = a->I;
     g.swiglu = true;
@@ -447,7 +459,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.a_rows = b.plan.rows_cap;
     g.K = a->I;
     g.b = a->down;
-    g.b_rows_total = (int64_t)E_tot * a->H;
+    g.b_rows_total = (int64_t)(a->down_group ? E_tot : E_tot + n_fold) * a->H;
     g.b_group_rows = a->H;
     g.N = a->H;
     g.swiglu = false;
@@ -468,6 +480,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       g.tile_nruns = b.nruns;
     }
     g.row_scale = b.plan.row_weight;
+    g.b_group_map = a->down_group;
     g.b_scale = a->down_scale;
     g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
     g.out = b.xp;

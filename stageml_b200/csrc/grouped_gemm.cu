@@ -58,6 +58,7 @@ struct KParams {
   int K;
   int N;
   int b_group_rows;
+  const int32_t* b_group_map;  // optional row group -> weight group
   int64_t b_rows_total;
   int num_n_tiles;
   int swiglu;
@@ -273,7 +274,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int a_row = m_tile * BM;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
-      const int b_row0 = group * p.b_group_rows + n0;
+      const int b_row0 = weight_group(p.b_group_map, group) * p.b_group_rows + n0;
       const int b_row1 = p.swiglu ? b_row0 + p.N : b_row0 + 128;
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
         const int s = it % STAGES;
@@ -452,7 +453,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           const int nvalid = min(16, p.N - col);
           float h[16];
           if (p.b_scale && nvalid > 0) {
-            const float* bsg = p.b_scale + (int64_t)group * p.b_group_rows + col;
+            const float* bsg = p.b_scale + (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + col;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const float sg = i < nvalid ? bsg[i] : 0.f, su = i < nvalid ? bsg[p.N + i] : 0.f;
@@ -477,7 +478,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rv[i]);
             if (p.b_scale) {
-              const float* bs = p.b_scale + (int64_t)group * p.b_group_rows + col;
+              const float* bs = p.b_scale + (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + col;
 #pragma unroll
               for (int i = 0; i < 16; ++i)
                 if (i < nvalid) v[i] *= bs[i];
@@ -512,7 +513,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       const int m_tile = p.tile_list ? p.tile_list[m_pos] : m_pos;
       const int group = p.tile_group ? p.tile_group[m_tile] : 0;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
-      const int64_t b_row0 = (int64_t)group * p.b_group_rows + n0;
+      const int64_t b_row0 = (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + n0;
       const int64_t b_row1 = p.swiglu ? b_row0 + p.N : b_row0 + 128;
       const int tile_nruns = tile_lora_runs(p, m_pos);  // used after the K loop
       float sc[4];
@@ -692,6 +693,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.K = g.K;
   p.N = g.N;
   p.b_group_rows = g.b_group_rows;
+  p.b_group_map = g.b_group_map;
   p.b_rows_total = g.b_rows_total;
   p.swiglu = g.swiglu ? 1 : 0;
   p.num_n_tiles = g.swiglu ? (g.N + 127) / 128 : (g.N + BN - 1) / BN;

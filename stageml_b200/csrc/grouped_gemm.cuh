@@ -35,6 +35,8 @@ struct GemmLaunch {
   int64_t b_rows_total = 0;
   bool b_fp8 = false;            // e4m3 weights, dequantised in shared memory with b_scale[row]
   int b_group_rows = 0;          // rows of B per group (N or 2N)
+  const int32_t* b_group_map = nullptr;  // optional: the weights (and scales) of group g are B group
+                                         // b_group_map[g] (several row groups reading one weight group)
   int N = 0;                     // output columns
   bool swiglu = false;
   bool in_bf16 = true;           // false: fp16
@@ -95,6 +97,9 @@ __device__ __forceinline__ int split_single_ctas(const int32_t* n_pairs_dev, con
   if ((sms - s) & 1) s = min(s + 1, sms - 2);
   return s;
 }
+
+// Weight group of row group g (identity without a map).
+__device__ __forceinline__ int weight_group(const int32_t* map, int g) { return map ? map[g] : g; }
 
 int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 

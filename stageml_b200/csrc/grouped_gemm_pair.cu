@@ -49,6 +49,7 @@ struct PParams {
   int K;
   int N;
   int b_group_rows;
+  const int32_t* b_group_map;  // optional row group -> weight group
   int64_t b_rows_total;
   int num_n_tiles;
   int swiglu;
@@ -235,7 +236,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int group = p.tile_group ? p.tile_group[m0] : 0;
       const int a_row = m_load * BM;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
-      const int b_row = group * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
+      const int b_row = weight_group(p.b_group_map, group) * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
       if (p.rank) {  // the run header arrives while the K loop's copies are issued
         mbar_arrive_expect_tx(hdr_bar, kRunHdrInts * 4);
         bulk_load_1d(smem_u32(hdr_smem), p.nruns + (int64_t)m0 * kRunHdrInts, kRunHdrInts * 4, hdr_bar);
@@ -416,7 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int nvalid = min(16, p.N - col);
           float h[16];
           if (p.b_scale && nvalid > 0) {
-            const float* bsg = p.b_scale + (int64_t)group * p.b_group_rows + col;
+            const float* bsg = p.b_scale + (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + col;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const float sg = i < nvalid ? bsg[i] : 0.f, su = i < nvalid ? bsg[p.N + i] : 0.f;
@@ -441,7 +442,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rv[i]);
             if (p.b_scale) {
-              const float* bs = p.b_scale + (int64_t)group * p.b_group_rows + col;
+              const float* bs = p.b_scale + (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + col;
 #pragma unroll
               for (int i = 0; i < 16; ++i)
                 if (i < nvalid) v[i] *= bs[i];
@@ -736,6 +737,7 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
   p.K = g.K;
   p.N = g.N;
   p.b_group_rows = g.b_group_rows;
+  p.b_group_map = g.b_group_map;
   p.b_rows_total = g.b_rows_total;
   p.swiglu = g.swiglu ? 1 : 0;
   p.num_n_tiles = g.swiglu ? (g.N + 127) / 128 : (g.N + BN - 1) / BN;

@@ -27,14 +27,17 @@ struct PermuteScratch {
   int32_t* ticket;   // [1] chunks finished (multi-chunk rank kernel); zeroed by launch_permute
 };
 constexpr int kPermChunk = 2048;
-int64_t permute_num_keys(int n_groups_total, int n_tenants, int group_by_tenant, int n_experts_total);
+// Sort keys of a permutation: (expert, tenant + 1) or (tenant, expert) keys, plus one per folded weight group.
+int64_t permute_num_keys(int n_fold, int n_tenants, int group_by_tenant, int n_experts_total);
 size_t permute_scratch_bytes(int64_t num_pairs, int64_t nkeys);
 void permute_carve(void* base, int64_t num_pairs, int64_t nkeys, PermuteScratch* out);
 int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
                    int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
                    const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream,
                    const int32_t* T_dev = nullptr,  // T_dev: optional device count of valid tokens
-                   bool pdl = false);               // pdl: single-kernel plans as PDL launches
+                   bool pdl = false,                // pdl: single-kernel plans as PDL launches
+                   const int32_t* fold_slot = nullptr,  // [n_tenants, E_tot] folded weight group per (tenant,
+                   int n_fold = 0);                     // expert) or -1; groups E_tot .. E_tot + n_fold - 1
 
 // shrink.cu: gather rows and/or LoRA shrink partials (split-K), then reduce.
 struct ShrinkLaunch {

@@ -17,6 +17,12 @@
 //           pair inside its key segment of the (already sorted) chunk
 // Sorting (key, pair index) makes the order within a key the pair order, so
 // the permutation is the stable sort the oracle defines, bit for bit.
+//
+// Keys: the dynamic groups (experts, or (tenant, expert) with group_by_tenant)
+// own tkeys consecutive keys each, one per tenant + 1; with a fold map, a pair
+// whose (tenant, expert) has folded weights takes the single key of its folded
+// weight group (n_dyn * tkeys + slot), after every dynamic key, and its row
+// carries no LoRA tenant.
 #include "common.cuh"
 #include "host_util.h"
 #include "kernels.h"
@@ -34,6 +40,9 @@ struct PairSrc {
   int weights_dtype;
   const int32_t* tenant_ids;
   int T, k, kk, E_routed, E_tot, n_tenants, group_by_tenant, tkeys;
+  int n_dyn;                // dynamic weight groups (keys [0, n_dyn * tkeys))
+  const int32_t* fold_slot; // optional [n_tenants, E_tot]: -1 dynamic, s >= 0 folded weight group n_dyn + s
+  int n_fold;
   int64_t P;
   const int32_t* T_dev;  // optional: tokens >= *T_dev are not routed (no error)
 };
@@ -82,13 +91,25 @@ __device__ __forceinline__ uint32_t pair_key(const PairSrc& a, int64_t p, int32_
   const int e = pair_expert(a, t, j, &bad);
   const int tn = pair_tenant(a, t, &bad);
   if (a.group_by_tenant && tn < 0) bad = true;
+  int slot = -1;
+  if (!bad && a.fold_slot && tn >= 0) {
+    slot = a.fold_slot[(int64_t)tn * a.E_tot + e];
+    if (slot < -1 || slot >= a.n_fold) bad = true;
+  }
   if (bad) {
     if (status) atomicCAS(status, 0, (int)kDevBadIndex);
     return kSentKey;
   }
+  if (slot >= 0) return (uint32_t)(a.n_dyn * a.tkeys + slot);
   if (a.group_by_tenant) return (uint32_t)(tn * a.E_tot + e);
   return (uint32_t)(e * a.tkeys + (tn + 1));
 }
+
+// Keys of weight group g: [first, first + count).
+__device__ __forceinline__ int group_first_key(int g, int tkeys, int n_dyn) {
+  return g < n_dyn ? g * tkeys : n_dyn * tkeys + (g - n_dyn);
+}
+__device__ __forceinline__ int group_key_count(int g, int tkeys, int n_dyn) { return g < n_dyn ? tkeys : 1; }
 
 // Sorts s[0..2048) ascending when s[n..2048) already hold the largest value
 // (the sentinel): only the first next_pow2(n) entries go through the network.
@@ -154,13 +175,14 @@ __global__ void __launch_bounds__(1024) perm_count_kernel(PairSrc a, int nkeys, 
 // From the per-key totals tot[nkeys] (in shared memory, 1024 threads): per-group
 // counts, padded group offsets, tile -> group map and padding rows of the plan;
 // tot is left holding each key's first row.
-__device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_groups, const stageml_moe_plan& plan,
-                                            int32_t* warp_part) {
+__device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_dyn, int n_groups,
+                                            const stageml_moe_plan& plan, int32_t* warp_part) {
   const int tid = threadIdx.x;
   // 2. per-group real counts; padded sizes parked in group_offsets[g]
   for (int g = tid; g < n_groups; g += 1024) {
     int cnt = 0;
-    for (int tk = 0; tk < tkeys; ++tk) cnt += tot[g * tkeys + tk];
+    const int k0 = group_first_key(g, tkeys, n_dyn), nk = group_key_count(g, tkeys, n_dyn);
+    for (int tk = 0; tk < nk; ++tk) cnt += tot[k0 + tk];
     plan.group_counts[g] = cnt;
     plan.group_offsets[g] = (cnt + 127) & ~127;
   }
@@ -214,8 +236,9 @@ __device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_group
     }
     if (lane == 0) {
       int b = o;
-      for (int tk = 0; tk < tkeys; ++tk) {
-        const int key = g * tkeys + tk;
+      const int k0 = group_first_key(g, tkeys, n_dyn), nk = group_key_count(g, tkeys, n_dyn);
+      for (int tk = 0; tk < nk; ++tk) {
+        const int key = k0 + tk;
         const int v = tot[key];
         tot[key] = b;
         b += v;
@@ -226,8 +249,8 @@ __device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_group
 }
 
 __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restrict__ hist, int32_t* __restrict__ off,
-                                                          int nkeys, int nchunks, int tkeys, int n_groups,
-                                                          stageml_moe_plan plan) {
+                                                          int nkeys, int nchunks, int tkeys, int n_dyn,
+                                                          int n_groups, stageml_moe_plan plan) {
   extern __shared__ int32_t tot[];  // [nkeys]
   __shared__ int32_t warp_part[32];
   const int tid = threadIdx.x;
@@ -238,7 +261,7 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
     tot[key] = s;
   }
   __syncthreads();
-  plan_groups(tot, tkeys, n_groups, plan, warp_part);
+  plan_groups(tot, tkeys, n_dyn, n_groups, plan, warp_part);
   // 5. per-(chunk, key) destination offsets
   for (int key = tid; key < nkeys; key += 1024) {
     int b = tot[key];
@@ -250,14 +273,15 @@ __global__ void __launch_bounds__(1024) perm_scan_kernel(const int32_t* __restri
   }
 }
 
-// Pair p lands in plan row `row`.
-__device__ __forceinline__ void place_pair(const PairSrc& a, const stageml_moe_plan& plan, int64_t p, int row) {
+// Pair p (sort key `key`) lands in plan row `row`; rows of folded weight groups carry no LoRA tenant.
+__device__ __forceinline__ void place_pair(const PairSrc& a, const stageml_moe_plan& plan, int64_t p, int row,
+                                           uint32_t key) {
   const int t = (int)(p / a.kk);
   const int j = (int)(p - (int64_t)t * a.kk);
   bool dummy = false;
   const int tn = pair_tenant(a, t, &dummy);
   plan.row_token[row] = t;
-  plan.row_tenant[row] = a.group_by_tenant ? -1 : tn;
+  plan.row_tenant[row] = (a.group_by_tenant || key >= (uint32_t)(a.n_dyn * a.tkeys)) ? -1 : tn;
   plan.row_weight[row] = pair_weight(a, t, j);
   plan.row_pair[row] = (int32_t)p;
   plan.pair_row[p] = row;
@@ -279,7 +303,7 @@ __global__ void __launch_bounds__(1024) perm_scatter_kernel(PairSrc a, int nkeys
       continue;
     }
     const int start = lower_bound_key(s, i, key);
-    place_pair(a, plan, p, off[(int64_t)blockIdx.x * nkeys + key] + (i - start));
+    place_pair(a, plan, p, off[(int64_t)blockIdx.x * nkeys + key] + (i - start), key);
   }
 }
 
@@ -302,7 +326,7 @@ __global__ void __launch_bounds__(1024) perm_fused_kernel(PairSrc a, int nkeys, 
     if (i == kPermChunk - 1 || (s[i + 1] >> 11) != key) tot[key] = i - lower_bound_key(s, i + 1, key) + 1;
   }
   __syncthreads();
-  plan_groups(tot, a.tkeys, n_groups, plan, warp_part);
+  plan_groups(tot, a.tkeys, a.n_dyn, n_groups, plan, warp_part);
   for (int64_t p = live + threadIdx.x; p < a.P; p += 1024) plan.pair_row[p] = -1;  // pairs of tokens past *T_dev
   for (int i = threadIdx.x; i < kPermChunk; i += 1024) {
     const uint32_t v = s[i];
@@ -313,7 +337,7 @@ __global__ void __launch_bounds__(1024) perm_fused_kernel(PairSrc a, int nkeys, 
       plan.pair_row[p] = -1;
       continue;
     }
-    place_pair(a, plan, p, tot[key] + (i - lower_bound_key(s, i, key)));
+    place_pair(a, plan, p, tot[key] + (i - lower_bound_key(s, i, key)), key);
   }
 }
 
@@ -375,7 +399,7 @@ __global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, i
       tot[k] = run;
     }
     __syncthreads();
-    plan_groups(tot, a.tkeys, n_groups, plan, warp_part);
+    plan_groups(tot, a.tkeys, a.n_dyn, n_groups, plan, warp_part);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int64_t p = w * 64 + r * 32 + lane;
@@ -383,7 +407,7 @@ __global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, i
       if (key[r] == kSentKey)
         plan.pair_row[p] = -1;
       else
-        place_pair(a, plan, p, tot[key[r]] + sm[w * nkeys + (int)key[r]] + rnk[r]);
+        place_pair(a, plan, p, tot[key[r]] + sm[w * nkeys + (int)key[r]] + rnk[r], key[r]);
     }
     return;
   }
@@ -422,7 +446,7 @@ __global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, i
     tot[k] = s;
   }
   __syncthreads();
-  plan_groups(tot, a.tkeys, n_groups, plan, warp_part);
+  plan_groups(tot, a.tkeys, a.n_dyn, n_groups, plan, warp_part);
   const bool place_here = nch <= kLastPlacesChunks;
   int32_t* offs = place_here ? sm + nkeys : off;  // [nch][nkeys]
   for (int k = tid; k < nkeys; k += 1024) {
@@ -443,7 +467,7 @@ __global__ void __launch_bounds__(1024) perm_rank_kernel(PairSrc a, int nkeys, i
       plan.pair_row[p] = -1;
       continue;
     }
-    place_pair(a, plan, p, offs[(p / kPermChunk) * nkeys + k] + (int)(v & 2047u));
+    place_pair(a, plan, p, offs[(p / kPermChunk) * nkeys + k] + (int)(v & 2047u), k);
   }
 }
 
@@ -457,15 +481,14 @@ __global__ void __launch_bounds__(256) perm_place_kernel(PairSrc a, int nkeys, c
     plan.pair_row[p] = -1;
     return;
   }
-  place_pair(a, plan, p, off[(p / kPermChunk) * nkeys + k] + (int)(v & 2047u));
+  place_pair(a, plan, p, off[(p / kPermChunk) * nkeys + k] + (int)(v & 2047u), k);
 }
 
 }  // namespace
 
-int64_t permute_num_keys(int n_groups_total, int n_tenants, int group_by_tenant, int n_experts_total) {
-  (void)n_groups_total;
-  if (group_by_tenant) return (int64_t)n_tenants * n_experts_total;
-  return (int64_t)n_experts_total * (n_tenants + 1);
+int64_t permute_num_keys(int n_fold, int n_tenants, int group_by_tenant, int n_experts_total) {
+  if (group_by_tenant) return (int64_t)n_tenants * n_experts_total + n_fold;
+  return (int64_t)n_experts_total * (n_tenants + 1) + n_fold;
 }
 
 static int64_t nchunks_of(int64_t P) { return P > 0 ? (P + kPermChunk - 1) / kPermChunk : 1; }
@@ -495,7 +518,7 @@ void permute_carve(void* base, int64_t P, int64_t nkeys, PermuteScratch* out) {
 int launch_permute(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
                    int T, int k, int n_shared, int n_experts_total, int n_tenants, int group_by_tenant,
                    const stageml_moe_plan& plan, int32_t* status, const PermuteScratch& scr, cudaStream_t stream,
-                   const int32_t* T_dev, bool pdl) {
+                   const int32_t* T_dev, bool pdl, const int32_t* fold_slot, int n_fold) {
   SB_CHECK_ARG(T >= 0 && k >= 0 && n_shared >= 0, "permute: negative size");
   SB_CHECK_ARG(k + n_shared >= 1, "permute: need at least one slot per token");
   SB_CHECK_ARG(n_experts_total > n_shared || (k == 0 && n_experts_total == n_shared),
@@ -507,9 +530,14 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
                "permute: weights must be f32, bf16 or f16");
   SB_CHECK_ARG(n_tenants >= 0, "permute: negative tenant count");
   SB_CHECK_ARG(!group_by_tenant || (tenant_ids && n_tenants > 0), "permute: group_by_tenant needs tenant ids");
+  SB_CHECK_ARG(n_fold >= 0 && (n_fold == 0 || fold_slot), "permute: n_fold=%d needs a fold map", n_fold);
+  SB_CHECK_ARG(!fold_slot || (!group_by_tenant && tenant_ids && n_tenants > 0),
+               "permute: a fold map needs tenant ids and per-expert groups");
   const int64_t P = (int64_t)T * (k + n_shared);
-  const int64_t nkeys = permute_num_keys(0, n_tenants, group_by_tenant, n_experts_total);
-  const int n_groups = group_by_tenant ? n_tenants * n_experts_total : n_experts_total;
+  if (!fold_slot) n_fold = 0;
+  const int64_t nkeys = permute_num_keys(n_fold, n_tenants, group_by_tenant, n_experts_total);
+  const int n_dyn = group_by_tenant ? n_tenants * n_experts_total : n_experts_total;
+  const int n_groups = n_dyn + n_fold;
   SB_CHECK_ARG(nkeys >= 1 && nkeys <= kMaxKeys, "permute: %lld (expert, tenant) keys exceed the limit %d",
                (long long)nkeys, kMaxKeys);
   SB_CHECK_ARG(plan.rows_cap >= stageml_plan_rows_cap(P, n_groups), "permute: plan rows_cap %lld < required %lld",
@@ -533,6 +561,9 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
   a.n_tenants = n_tenants;
   a.group_by_tenant = group_by_tenant;
   a.tkeys = group_by_tenant ? 1 : n_tenants + 1;
+  a.n_dyn = n_dyn;
+  a.fold_slot = fold_slot;
+  a.n_fold = n_fold;
   a.P = P;
   a.T_dev = T_dev;
 
@@ -565,7 +596,8 @@ int launch_permute(const void* ids, int ids_dtype, const void* weights, int weig
     SB_CUDA_CHECK(cudaGetLastError());
   }
   SB_CUDA_CHECK(cudaFuncSetAttribute(perm_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  (perm_scan_kernel<<<1, 1024, smem, stream>>>(scr.hist, scr.off, (int)nkeys, (int)nch, a.tkeys, n_groups, plan), ::sb::count_launch());
+  (perm_scan_kernel<<<1, 1024, smem, stream>>>(scr.hist, scr.off, (int)nkeys, (int)nch, a.tkeys, n_dyn, n_groups,
+                                                plan), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   if (nch > 0) {
     (perm_scatter_kernel<<<(unsigned)nch, 1024, 0, stream>>>(a, (int)nkeys, scr.sorted, scr.off, plan), ::sb::count_launch());

@@ -31,6 +31,7 @@ struct SkParams {
   const void* b;
   int64_t b_rows_total;
   int b_group_rows;
+  const int32_t* b_group_map;  // optional row group -> weight group
   int N;
   const int32_t* num_tiles_dev;
   int tiles_cap;
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
     const T* wrow[NBLK];
 #pragma unroll
     for (int b = 0; b < NBLK; ++b) {
-      const int64_t r = (int64_t)group * p.b_group_rows + n0 + g + (b ? p.N : 0);
+      const int64_t r = (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + n0 + g + (b ? p.N : 0);
       wrow[b] = (n0 + g < p.N && r < p.b_rows_total) ? W + r * K : nullptr;
     }
     const int kw = ((K + WPI * 32 - 1) / (WPI * 32)) * 32;
@@ -211,13 +212,13 @@ __global__ void __launch_bounds__(256, 2) skinny_gemm_kernel(const SkParams p, i
     }
     if (SWIGLU) {
       if (p.b_scale) {
-        const float* bs = p.b_scale + (int64_t)group * p.b_group_rows;
+        const float* bs = p.b_scale + (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows;
         v0 *= bs[col];
         v1 *= bs[p.N + col];
       }
       out[row * p.ldo + col] = from_f32<T>(silu_f32(v0) * v1);
     } else {
-      if (p.b_scale) v0 *= p.b_scale[(int64_t)group * p.b_group_rows + col];
+      if (p.b_scale) v0 *= p.b_scale[(int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + col];
       if (p.bias) {
         const int bg = p.bias_group_mod > 0 ? group % p.bias_group_mod : group;
         v0 += to_f32<T>(static_cast<const T*>(p.bias)[bg * p.bias_group_stride + col]);
@@ -269,6 +270,7 @@ int launch_skinny_gemm(const GemmLaunch& g, const int32_t* row_tenant, const int
   p.b = g.b;
   p.b_rows_total = g.b_rows_total;
   p.b_group_rows = g.b_group_rows;
+  p.b_group_map = g.b_group_map;
   p.N = g.N;
   p.num_tiles_dev = g.num_tiles_dev;
   p.tiles_cap = g.tiles_cap;

@@ -105,14 +105,32 @@ Tensor moe_forward(const Tensor& x, const Tensor& gate_up, const Tensor& down, c
                    int64_t rank, const c10::optional<Tensor>& lora_a13, const c10::optional<Tensor>& lora_b13,
                    const c10::optional<Tensor>& lora_a2, const c10::optional<Tensor>& lora_b2,
                    const c10::optional<Tensor>& lora_scale, const c10::optional<Tensor>& gate_up_scale,
-                   const c10::optional<Tensor>& down_scale, const c10::optional<Tensor>& T_dev) {
+                   const c10::optional<Tensor>& down_scale, const c10::optional<Tensor>& T_dev,
+                   const c10::optional<Tensor>& fold_slot, int64_t n_fold,
+                   const c10::optional<Tensor>& down_group) {
   TORCH_CHECK(x.dim() == 2 && gate_up.dim() == 3 && down.dim() == 3, "moe_forward: bad ranks");
   if (T_dev.has_value())
     TORCH_CHECK(T_dev->is_cuda() && T_dev->scalar_type() == at::kInt && T_dev->numel() >= 1,
                 "moe_forward: T_dev must be a CUDA int32 tensor");
-  const int64_t T = x.size(0), H = x.size(1), E_tot = gate_up.size(0), I = gate_up.size(1) / 2;
-  TORCH_CHECK(gate_up.size(2) == H && down.size(0) == E_tot && down.size(1) == H && down.size(2) == I,
+  TORCH_CHECK(n_fold >= 0 && n_fold < gate_up.size(0), "moe_forward: n_fold out of range");
+  if (!fold_slot.has_value()) TORCH_CHECK(n_fold == 0, "moe_forward: n_fold > 0 needs fold_slot");
+  // gate_up / down hold the E_tot base experts, then the n_fold folded weight groups
+  const int64_t T = x.size(0), H = x.size(1), E_tot = gate_up.size(0) - n_fold, I = gate_up.size(1) / 2;
+  const int64_t down_groups = down_group.has_value() ? E_tot : E_tot + n_fold;
+  TORCH_CHECK(gate_up.size(2) == H && down.size(0) == down_groups && down.size(1) == H && down.size(2) == I,
               "moe_forward: weight shapes do not match x");
+  if (down_group.has_value()) {
+    check_cuda(*down_group, "down_group", x);
+    TORCH_CHECK(down_group->scalar_type() == at::kInt && down_group->is_contiguous() &&
+                    down_group->numel() == E_tot + n_fold,
+                "moe_forward: down_group must be contiguous int32 [E_tot + n_fold]");
+  }
+  if (fold_slot.has_value()) {
+    check_cuda(*fold_slot, "fold_slot", x);
+    TORCH_CHECK(fold_slot->scalar_type() == at::kInt && fold_slot->is_contiguous() &&
+                    fold_slot->numel() == n_tenants * E_tot,
+                "moe_forward: fold_slot must be contiguous int32 [n_tenants, E_tot]");
+  }
   check_cuda(x, "x", x);
   check_cuda(gate_up, "gate_up", x);
   check_cuda(down, "down", x);
@@ -168,6 +186,9 @@ Tensor moe_forward(const Tensor& x, const Tensor& gate_up, const Tensor& down, c
   a.out = out.data_ptr();
   a.status = status_word(x);
   a.T_dev = static_cast<const int32_t*>(opt_ptr(T_dev));
+  a.fold_slot = static_cast<const int32_t*>(opt_ptr(fold_slot));
+  a.n_fold = (int)n_fold;
+  a.down_group = static_cast<const int32_t*>(opt_ptr(down_group));
   const size_t ws = stageml_moe_workspace_bytes(&a);
   TORCH_CHECK(ws > 0 || T == 0, "moe_forward: invalid arguments: ", stageml_last_error());
   auto w = workspace(ws, x);
@@ -416,7 +437,8 @@ TORCH_LIBRARY(stageml, m) {
       "moe_forward(Tensor x, Tensor gate_up, Tensor down, Tensor? topk_weights, Tensor? topk_ids, Tensor? router_w, "
       "int k, int n_shared, bool renormalize, Tensor? tenant_ids, int n_tenants, int rank, Tensor? lora_a13, "
       "Tensor? lora_b13, Tensor? lora_a2, Tensor? lora_b2, Tensor? lora_scale, Tensor? gate_up_scale, "
-      "Tensor? down_scale, Tensor? T_dev=None) -> Tensor");
+      "Tensor? down_scale, Tensor? T_dev=None, Tensor? fold_slot=None, int n_fold=0, Tensor? down_group=None) "
+      "-> Tensor");
   m.def("route_topk(Tensor x, Tensor gate_w, int k, bool renormalize) -> (Tensor, Tensor, Tensor)");
   m.def("topk_from_logits(Tensor logits, int k, bool renormalize) -> (Tensor, Tensor)");
   m.def(

@@ -126,28 +126,37 @@ class RequestExecutor:
     """One MoE layer (``gate_up [E, 2I, H]``, ``down [E, H, I]``) serving w1 adapters.
 
     Materialized adapters get their folded residual ``gate_up`` (w1 + s * B @ A per
-    expert) at construction (stage 0), timed in ``compile_time_ms``.
+    expert) at construction (stage 0), timed in ``compile_time_ms``. The folded sets
+    live after the base experts in one bank (stageml_b200/folded_sets.py): ``bta_one``
+    runs a materialized adapter's requests on its sets, and the batched mode runs the
+    whole stream in one call, materialized adapters' rows on their sets and every
+    other row on the base experts with its adapter's LoRA.
     """
 
     def __init__(self, gate_up: torch.Tensor, down: torch.Tensor, adapters: list[MoEAdapterSpec],
                  materialized_ids: set[int]) -> None:
         if not gate_up.is_cuda:
             raise RuntimeError("RequestExecutor runs on CUDA tensors (no CPU path)")
-        self.gate_up = gate_up.contiguous()
-        self.down = down.contiguous()
+        from .folded_sets import fold_w1_sets
+
         self.adapters = adapters
         self.materialized_ids = set(materialized_ids)
         self.intermediate = int(gate_up.shape[1] // 2)
         H = int(gate_up.shape[2])
+        E = int(gate_up.shape[0])
         self.lora_a13, self.lora_b13, self.lora_scale, self.rank = pack_w1_adapters(
             adapters, self.intermediate, H, gate_up.dtype, gate_up.device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        self.residual: dict[int, torch.Tensor] = {a: self._fold(a) for a in sorted(self.materialized_ids)}
+        self.sets = fold_w1_sets(gate_up.contiguous(), down, adapters,
+                                 [(a, list(range(E))) for a in sorted(self.materialized_ids)])
+        self.residual: dict[int, torch.Tensor] = {a: self.sets.adapter_gate_up(a) for a in sorted(self.materialized_ids)}
         self._plan_rows: dict[int, tuple] = {}  # id(plan) -> (plan, rows, tenants, request of row, lengths)
         e1.record()
         torch.cuda.synchronize()
         self.compile_time_ms = e0.elapsed_time(e1)
+        self.gate_up = self.sets.base_gate_up()
+        self.down = self.sets.down
 
     def _fold(self, adapter_id: int) -> torch.Tensor:
         ad = self.adapters[adapter_id]
@@ -160,11 +169,13 @@ class RequestExecutor:
         """``gate_up`` with the adapter folded into w1 (cached for materialized adapters)."""
         return self.residual[adapter_id] if adapter_id in self.residual else self._fold(adapter_id)
 
-    def _layer(self, x, ids, weights, tenant_ids):
-        return ops.moe_forward(x.contiguous(), self.gate_up, self.down, topk_ids=ids.contiguous(),
-                               topk_weights=weights.contiguous(), tenant_ids=tenant_ids,
+    def _layer(self, x, ids, weights, tenant_ids, folded: bool = False):
+        """One layer call; with ``folded`` the materialized adapters' rows run on their folded sets."""
+        kw = self.sets.moe_kwargs() if folded else {}
+        return ops.moe_forward(x.contiguous(), self.sets.gate_up if kw else self.gate_up, self.down,
+                               topk_ids=ids.contiguous(), topk_weights=weights.contiguous(), tenant_ids=tenant_ids,
                                n_tenants=len(self.adapters), rank=self.rank, lora_a13=self.lora_a13,
-                               lora_b13=self.lora_b13, lora_scale=self.lora_scale)
+                               lora_b13=self.lora_b13, lora_scale=self.lora_scale, **kw)
 
     def dynamic_one(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, adapter_id: int) -> torch.Tensor:
         ten = torch.full((x.shape[0],), int(adapter_id), dtype=torch.int32, device=x.device)
@@ -198,8 +209,11 @@ class RequestExecutor:
         if not plan.requests:
             return hidden.new_empty((0, self.down.shape[1])), [0]
         rows, ten, _, lengths = self._rows_of(plan, hidden.device)
-        y = self._layer(hidden.index_select(0, rows), ids.index_select(0, rows), weights.index_select(0, rows), ten)
-        offsets = [0] + torch.cumsum(lengths.cpu(), 0).tolist()
+        y = self._layer(hidden.index_select(0, rows), ids.index_select(0, rows), weights.index_select(0, rows), ten,
+                        folded=True)
+        offsets = [0]
+        for r in plan.requests:  # from the plan on the host: no device read
+            offsets.append(offsets[-1] + r.end - r.start)
         return y, offsets
 
     def batched_checksum(self, plan: WorkloadPlan, hidden: torch.Tensor, ids: torch.Tensor,
@@ -209,7 +223,8 @@ class RequestExecutor:
         if not plan.requests:
             return torch.zeros((), device=hidden.device, dtype=torch.float32)
         rows, ten, req, lengths = self._rows_of(plan, hidden.device)
-        y = self._layer(hidden.index_select(0, rows), ids.index_select(0, rows), weights.index_select(0, rows), ten)
+        y = self._layer(hidden.index_select(0, rows), ids.index_select(0, rows), weights.index_select(0, rows), ten,
+                        folded=True)
         sums = torch.zeros(len(plan.requests), device=y.device, dtype=torch.float32)
         sums.index_add_(0, req, y.float().sum(1))
         return (sums / (lengths.float() * y.shape[1])).sum()

@@ -27,7 +27,8 @@ def _register_fakes() -> None:
 
     @lib.register_fake("stageml::moe_forward")
     def _(x, gate_up, down, topk_weights, topk_ids, router_w, k, n_shared, renormalize, tenant_ids, n_tenants, rank,
-          lora_a13, lora_b13, lora_a2, lora_b2, lora_scale, gate_up_scale, down_scale, T_dev=None):
+          lora_a13, lora_b13, lora_a2, lora_b2, lora_scale, gate_up_scale, down_scale, T_dev=None, fold_slot=None,
+          n_fold=0, down_group=None):
         return x.new_empty((x.shape[0], x.shape[1]))
 
     @lib.register_fake("stageml::route_topk")
@@ -82,18 +83,25 @@ def residual_moe(hidden, gate_up, down, topk_weights, topk_ids):
 def moe_forward(x, gate_up, down, *, topk_weights=None, topk_ids=None, router_w=None, k: int = 2, n_shared: int = 0,
                 renormalize: bool = True, tenant_ids=None, n_tenants: int = 0, rank: int = 0, lora_a13=None,
                 lora_b13=None, lora_a2=None, lora_b2=None, lora_scale=None, gate_up_scale=None, down_scale=None,
-                T_dev=None):
+                T_dev=None, fold_slot=None, n_fold: int = 0, down_group=None):
     """One MoE-LoRA FFN layer (router -> permutation -> SwiGLU experts with per-tenant LoRA -> combine).
 
     T_dev: optional CUDA int32 tensor; only the first T_dev[0] tokens are valid (the rest are skipped and
     their output rows are left unwritten), for token counts known only on the device.
+    fold_slot: optional CUDA int32 [n_tenants, E_tot]; entry (a, e) = s >= 0 runs tenant a's pairs of
+    expert e on folded weight set s, stored as group E_tot + s of gate_up / down ([E_tot + n_fold, ...]),
+    without dynamic LoRA; -1 = base weights plus the tenant's LoRA. One permutation, one set of GEMMs.
+    down_group: optional CUDA int32 [E_tot + n_fold] with entries in [0, E_tot): weight group g takes
+    down[down_group[g]] (down then holds the E_tot base experts), for folded sets whose adapters leave
+    w2 unchanged.
     """
     ensure_cuda_device(x)
     if topk_ids is not None:
         k = int(topk_ids.shape[1])
     return _ops.moe_forward(x, gate_up, down, topk_weights, topk_ids, router_w, int(k), int(n_shared),
                             bool(renormalize), tenant_ids, int(n_tenants), int(rank), lora_a13, lora_b13, lora_a2,
-                            lora_b2, lora_scale, gate_up_scale, down_scale, T_dev)
+                            lora_b2, lora_scale, gate_up_scale, down_scale, T_dev, fold_slot, int(n_fold),
+                            down_group)
 
 
 def route_topk(x, gate_w, k: int, renormalize: bool = True):

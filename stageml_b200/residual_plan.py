@@ -15,10 +15,12 @@ apply LoRA to w1 (as the reference's request executor):
   ``disaggregated``, which the reference's artifact does not execute) runs the
   adapter dynamically on the fused LoRA path of the grouped GEMMs.
 
-A call takes per-token adapter ids. Tokens of an adapter with folded experts run
-on its folded ``gate_up``, with the LoRA of its other experts still applied
-dynamically (their bank slices stay, the folded experts' are zero); all other
-tokens run as one dynamic call. Outputs come back in token order.
+A call takes per-token adapter ids and is one ``moe_forward`` launch sequence:
+the folded (adapter, expert) weight sets sit after the base experts in one
+``gate_up`` bank and the permutation sends each (token, expert) pair of a
+folded adapter to its set (no LoRA) and every other pair to the base expert
+with its adapter's LoRA (stageml_b200/folded_sets.py). Nothing is read back to
+the host and the batch is never split.
 """
 
 from __future__ import annotations
@@ -32,6 +34,7 @@ import torch
 
 from . import ops
 from .executor import pack_w1_adapters
+from .folded_sets import fold_w1_sets
 from .moe_lora_layers import MoEAdapterSpec
 from .vllm_stage_router import KernelManifest, KernelManifestEntry
 
@@ -106,8 +109,6 @@ class PlannedMoELayer:
                  plan: ResidualPlanSpec) -> None:
         if not gate_up.is_cuda:
             raise RuntimeError("PlannedMoELayer runs on CUDA tensors (no CPU path)")
-        self.gate_up = gate_up.contiguous()
-        self.down = down.contiguous()
         self.adapters = adapters
         self.plan = plan
         E = int(gate_up.shape[0])
@@ -119,65 +120,33 @@ class PlannedMoELayer:
             raise ValueError(f"plan names adapters that were not given: {unknown}")
         self.lora_a13, self.lora_b13, self.lora_scale, self.rank = pack_w1_adapters(
             adapters, I, int(gate_up.shape[2]), gate_up.dtype, gate_up.device)
-        self.folded: dict[int, torch.Tensor] = {}  # adapter id -> gate_up with its planned experts folded
         self.folded_experts: dict[int, list[int]] = {}
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
         for name, experts in mat.items():
-            a = names[name]
             ex = list(range(E)) if "all" in experts else sorted(int(e) for e in experts)
             if any(not 0 <= e < E for e in ex):
                 raise ValueError(f"plan folds expert ids outside [0, {E}) for {name}")
-            ad = adapters[a]
-            dev, dt = gate_up.device, gate_up.dtype
-            g = self.gate_up.clone()
-            idx = torch.tensor(ex, device=dev)
-            w1 = ops.lora_fold(self.gate_up[idx, :I], ad.A[idx].to(dev, dt), ad.B[idx].to(dev, dt),
-                               float(ad.scaling))
-            g[idx, :I] = w1
-            self.folded[a] = g
-            self.folded_experts[a] = ex
-            self.lora_a13[a, idx] = 0  # the folded experts take no dynamic LoRA for this adapter
+            self.folded_experts[names[name]] = ex
+        self._order = sorted(self.folded_experts)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        self.sets = fold_w1_sets(gate_up.contiguous(), down, adapters,
+                                 [(a, self.folded_experts[a]) for a in self._order])
         e1.record()
         torch.cuda.synchronize()
         self.compile_time_ms = e0.elapsed_time(e1)
-        n = len(adapters)
-        slot = torch.full((n + 1,), -1, dtype=torch.int64)
-        for j, a in enumerate(sorted(self.folded)):
-            slot[a] = j
-        self._order = sorted(self.folded)
-        self._slot = slot.to(gate_up.device)  # adapter id -> folded slot (index n: tokens without an adapter)
-
-    def _call(self, gate_up, x, ids, w, ten):
-        return ops.moe_forward(x, gate_up, self.down, topk_ids=ids, topk_weights=w, tenant_ids=ten,
-                               n_tenants=len(self.adapters), rank=self.rank, lora_a13=self.lora_a13,
-                               lora_b13=self.lora_b13, lora_scale=self.lora_scale)
+        self.gate_up = self.sets.base_gate_up()
+        self.down = self.sets.down
 
     def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                  adapter_ids: torch.Tensor) -> torch.Tensor:
         """Layer output for tokens x with their routing and adapter ids (-1: base weights only).
 
-        The host reads one small vector (tokens per folded adapter) to size the sub-batches."""
-        ten = adapter_ids.to(torch.int32)
-        if not self.folded:
-            return self._call(self.gate_up, x, topk_ids, topk_weights, ten)
-        n = len(self.adapters)
-        known = (ten >= 0) & (ten < n)  # other ids: the dynamic call reports them in the status word
-        slots = self._slot[torch.where(known, ten.long(), torch.full_like(ten.long(), n))]
-        nslot = len(self._order)
-        counts = torch.bincount(slots + 1, minlength=nslot + 1).cpu().tolist()  # [dynamic, folded slots...]
-        order = torch.argsort(slots, stable=True)  # dynamic tokens first, then each folded adapter's
-        out = torch.empty((x.shape[0], self.down.shape[1]), dtype=x.dtype, device=x.device)
-        start = 0
-        for j, c in enumerate(counts):
-            if c == 0:
-                continue
-            idx = order[start:start + c]
-            start += c
-            gu = self.gate_up if j == 0 else self.folded[self._order[j - 1]]
-            out[idx] = self._call(gu, x.index_select(0, idx), topk_ids.index_select(0, idx),
-                                  topk_weights.index_select(0, idx), ten.index_select(0, idx))
-        return out
+        One layer call for the whole batch; ids outside [-1, len(adapters)) are reported in the
+        device status word and their rows skipped."""
+        return ops.moe_forward(x, self.sets.gate_up, self.down, topk_ids=topk_ids, topk_weights=topk_weights,
+                               tenant_ids=adapter_ids.to(torch.int32).contiguous(), n_tenants=len(self.adapters),
+                               rank=self.rank, lora_a13=self.lora_a13, lora_b13=self.lora_b13,
+                               lora_scale=self.lora_scale, **self.sets.moe_kwargs())
 
     def kernel_manifest(self, model: str = "moe") -> KernelManifest:
         """Tenant (= adapter id) -> folded-weights entry for the tenant router, one per folded adapter."""

@@ -10,7 +10,12 @@ Here the mask is a device-side table lookup; the host only learns the number
 of selected tokens (one scalar) to size the two sub-batches. With
 ``split="masked"`` there is no host synchronisation at all: both backends see the
 whole batch, each with the other backend's routing weights set to zero, and the
-two outputs are added (twice the expert work, no host read-back).
+two outputs are added (twice the expert work, no host read-back). With
+``split="device"`` one call of this package's MoE op serves the whole batch: the
+tenant mask stays on the device, tokens of tenants with a kernel run on their
+folded weight sets (``weight_sets``, stageml_b200/folded_sets.py) and every other
+token on the base experts -- the fused-MoE arithmetic vLLM's ``fused_experts``
+performs, in the same launches -- with no host read-back and no doubled work.
 """
 
 from __future__ import annotations
@@ -151,7 +156,8 @@ def call_stageml_residual_op(hidden, gate_up, down, topk_weights, topk_ids):
 
 def route_fused_experts(*, hidden, gate_up, down, topk_weights, topk_ids, tenant_ids, router: StageMLTenantRouter,
                         vllm_fused_experts: Callable[..., Any] | None = None,
-                        stageml_op: Callable[..., torch.Tensor] | None = None, split: str = "indexed"):
+                        stageml_op: Callable[..., torch.Tensor] | None = None, split: str = "indexed",
+                        weight_sets=None):
     """Route tokens between the StageML residual op and vLLM fused experts (stageml/vllm_stage_router.py:114-157).
 
     split="indexed" (the reference's behaviour): each backend runs on its own tokens.
@@ -161,11 +167,18 @@ def route_fused_experts(*, hidden, gate_up, down, topk_weights, topk_ids, tenant
     with all-zero weights contributes an exact zero row and each token's row is its
     own backend's row (the same bits when a backend's rows do not depend on the rest
     of its batch, as for this package's op).
+    split="device": one ``moe_forward`` call for the whole batch, no host read and no
+    vLLM call. Tokens of tenants with an enabled kernel take their rows of
+    ``weight_sets.fold_slot`` (tenant id = row; their folded experts run on the folded
+    sets, the others on the base experts); all other tokens run on the base experts
+    (``weight_sets`` base experts, or ``gate_up`` / ``down`` without weight sets).
     """
-    if split not in ("indexed", "masked"):
-        raise ValueError(f"split must be 'indexed' or 'masked', not {split!r}")
+    if split not in ("indexed", "masked", "device"):
+        raise ValueError(f"split must be 'indexed', 'masked' or 'device', not {split!r}")
     if hidden.shape[0] != tenant_ids.numel():
         raise ValueError("tenant_ids must contain one tenant id per token")
+    if split == "device":
+        return _route_on_device(hidden, gate_up, down, topk_weights, topk_ids, tenant_ids, router, weight_sets)
     if vllm_fused_experts is None:
         vllm_fused_experts, source = resolve_vllm_fused_experts()
         if vllm_fused_experts is None:
@@ -194,6 +207,23 @@ def route_fused_experts(*, hidden, gate_up, down, topk_weights, topk_ids, tenant
     out.index_copy_(0, theirs, call_vllm_fused_experts(vllm_fused_experts, rows(hidden, theirs), gate_up, down,
                                                        rows(topk_weights, theirs), rows(topk_ids, theirs)))
     return out
+
+
+def _route_on_device(hidden, gate_up, down, topk_weights, topk_ids, tenant_ids, router, weight_sets):
+    from . import ops
+
+    ids = topk_ids.contiguous()
+    wts = topk_weights.contiguous()
+    if weight_sets is None or weight_sets.n_fold == 0:
+        gu = gate_up if weight_sets is None else weight_sets.base_gate_up()
+        dn = down if weight_sets is None else weight_sets.down
+        return ops.moe_forward(hidden.contiguous(), gu, dn, topk_ids=ids, topk_weights=wts)
+    mask = router.materialized_mask(tenant_ids.to(hidden.device))
+    n = int(weight_sets.fold_slot.shape[0])
+    ten = tenant_ids.reshape(-1).to(device=hidden.device, dtype=torch.int32)
+    ten = torch.where(mask & (ten >= 0) & (ten < n), ten, torch.full_like(ten, -1))  # table lookups, on the device
+    return ops.moe_forward(hidden.contiguous(), weight_sets.gate_up, weight_sets.down, topk_ids=ids,
+                           topk_weights=wts, tenant_ids=ten, n_tenants=n, **weight_sets.moe_kwargs())
 
 
 __all__ = ["KernelManifestEntry", "KernelManifest", "read_kernel_manifest", "write_kernel_manifest", "TenantKernel",

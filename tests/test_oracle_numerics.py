@@ -85,3 +85,53 @@ def test_shared_experts_are_always_on_with_weight_one():
     ids2 = np.concatenate([ids, np.full((T, 1), E)], 1)
     y2 = moe.moe_forward(x, gu, dn, ids2, np.ones((T, 2)))
     np.testing.assert_allclose(y, y2, rtol=1e-12)
+
+
+def test_oracle_fold_slots_equal_dynamic_lora():
+    """A (tenant, expert) pair on a folded weight set (W + s B A on w1, w3 and w2) gives the
+    layer output of the same pair with dynamic LoRA, the semantics the golden vectors pin;
+    the permutation puts folded pairs in their own groups with no LoRA tenant."""
+    from oracle import moe as omoe
+    from oracle import permute as operm
+
+    rng = np.random.default_rng(5)
+    T, H, I, E, k, nT, r, ns = 40, 16, 24, 3, 2, 4, 4, 1
+    Et = E + ns
+    x = rng.normal(size=(T, H))
+    gu = rng.normal(size=(Et, 2 * I, H)) / 4
+    dn = rng.normal(size=(Et, H, I)) / 5
+    a13 = rng.normal(size=(nT, Et, 2 * r, H)) / 4
+    b13 = rng.normal(size=(nT, Et, 2 * I, r)) / 2
+    a2 = rng.normal(size=(nT, Et, r, I)) / 5
+    b2 = rng.normal(size=(nT, Et, H, r)) / 2
+    sc = np.array([0.5, 1.0, 1.5, 2.0])
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)])
+    w = rng.random((T, k))
+    ten = rng.integers(-1, nT, T)
+    fold = np.full((nT, Et), -1)
+    folds = [(1, 0), (1, 2), (3, 3), (2, 1)]  # (tenant, expert), a shared expert among them
+    gu_f, dn_f = [], []
+    for s, (a, e) in enumerate(folds):
+        fold[a, e] = s
+        g = gu[e].copy()
+        g[:I] += sc[a] * b13[a, e, :I] @ a13[a, e, :r]
+        g[I:] += sc[a] * b13[a, e, I:] @ a13[a, e, r:]
+        gu_f.append(g)
+        dn_f.append(dn[e] + sc[a] * b2[a, e] @ a2[a, e])
+    lora = dict(lora_a13=a13, lora_b13=b13, lora_a2=a2, lora_b2=b2, lora_scale=sc)
+    ref = omoe.moe_forward(x, gu, dn, ids, w, tenant_ids=ten, n_shared=ns, **lora)
+    got = omoe.moe_forward(x, np.concatenate([gu, np.stack(gu_f)]), np.concatenate([dn, np.stack(dn_f)]), ids, w,
+                           tenant_ids=ten, n_shared=ns, fold_slot=fold, **lora)
+    np.testing.assert_allclose(got, ref, rtol=1e-10, atol=1e-10)
+    plan = operm.permute(ids, w, ten, Et, ns, nT, fold_slot=fold, n_fold=len(folds))
+    assert len(plan["group_counts"]) == Et + len(folds)
+    for s, (a, e) in enumerate(folds):
+        rows = np.arange(plan["group_offsets"][Et + s], plan["group_offsets"][Et + s] + plan["group_counts"][Et + s])
+        toks = plan["row_token"][rows]
+        assert np.all(ten[toks] == a) and np.all(plan["row_tenant"][rows] == -1)
+        n_expected = int(np.sum(ten == a)) if e >= E else int(np.sum((ten == a)[:, None] & (ids == e)))
+        assert rows.size == n_expected
+    bad = fold.copy()
+    bad[0, 0] = len(folds)  # out of range: the pair is dropped
+    assert operm.permute(ids, w, ten, Et, ns, nT, fold_slot=bad, n_fold=len(folds))["dropped"] == int(
+        np.sum((ten == 0)[:, None] & (ids == 0)))
