@@ -23,6 +23,11 @@ compute and combine injectable, the host logic runs with gloo on CPU).
 The reference has no distributed code; this is the expert-parallel layout of
 the path. All ranks make the same calls in the same order, also when a rank
 sends or receives nothing.
+
+The layer is also a torch op, ``torch.ops.stageml.ep_moe_lora_forward(x,
+tenant_ids, layer)``, with ``layer`` the handle ``EPMoELayer.register()``
+returns: the same call through the dispatcher (CUDA key only, a fake
+implementation for tracing), beside the single-GPU ``stageml::moe_forward``.
 """
 
 from __future__ import annotations
@@ -237,6 +242,15 @@ class EPMoELayer:
         C.check(lib, lib.stageml_ep_combine(ctypes.byref(a), C.ptr(shared), out.data_ptr(), stream), "ep combine")
         return out
 
+    def register(self) -> int:
+        """Handle of this layer for torch.ops.stageml.ep_moe_lora_forward (valid until close())."""
+        for h, layer in _EP_LAYERS.items():
+            if layer is self:
+                return h
+        h = max(_EP_LAYERS, default=0) + 1
+        _EP_LAYERS[h] = self
+        return h
+
     def take_status(self) -> int:
         """Device status word of the exchange (synchronises); 0 when every call completed."""
         if self._peer is None:
@@ -247,6 +261,8 @@ class EPMoELayer:
 
     def close(self) -> None:
         """Collective: unmap the other ranks' workspaces and free this rank's (after a barrier)."""
+        for h in [h for h, layer in _EP_LAYERS.items() if layer is self]:
+            del _EP_LAYERS[h]
         if self._peer is None:
             return
         torch.cuda.synchronize()
@@ -257,6 +273,38 @@ class EPMoELayer:
         dist.barrier(group=self.group)
         lib.stageml_ep_workspace_free(self._peer["base"])
         self._peer = None
+
+
+# ------------------------------------------------------------ the torch op
+_EP_LAYERS: dict = {}
+
+
+def _define_op() -> None:
+    from . import ops  # noqa: F401  (loads the stageml op library first)
+
+    lib = torch.library.Library("stageml", "FRAGMENT")
+    lib.define("ep_moe_lora_forward(Tensor x, Tensor tenant_ids, int layer) -> Tensor")
+
+    def impl(x, tenant_ids, layer):
+        ep = _EP_LAYERS.get(int(layer))
+        if ep is None:
+            raise RuntimeError(f"ep_moe_lora_forward: no expert-parallel layer registered as {layer}")
+        return ep(x, tenant_ids)
+
+    lib.impl("ep_moe_lora_forward", impl, "CUDA")
+
+    @torch.library.register_fake("stageml::ep_moe_lora_forward")
+    def _(x, tenant_ids, layer):
+        return x.new_empty(x.shape)
+
+    globals()["_OP_LIB"] = lib  # the registration lives as long as the library object
+
+
+try:
+    _define_op()
+except RuntimeError as exc:  # pragma: no cover - defined already in this process
+    if "already" not in str(exc):
+        raise
 
 
 __all__ = ["EPMoELayer"]

@@ -16,6 +16,7 @@ from pathlib import Path
 
 import numpy as np
 import pytest
+import torch
 
 ROOT = Path(__file__).resolve().parents[1]
 
@@ -138,3 +139,17 @@ def test_ep_peer_failure_is_detected_not_hung():
     res = _run(dict(BASE, fail_rank=1), timeout=90)
     assert res[1][0] == "error" and "injected failure" in res[1][1]
     assert res[0][0] == "error"  # rank 0's exchange fails (peer gone / timeout) instead of blocking forever
+
+
+def test_ep_op_is_registered_with_a_fake_and_no_cpu_kernel():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import stageml_b200.expert_parallel  # noqa: F401  (defines the op)
+
+    op = torch.ops.stageml.ep_moe_lora_forward
+    assert str(op.default._schema) == "stageml::ep_moe_lora_forward(Tensor x, Tensor tenant_ids, int layer) -> Tensor"
+    with FakeTensorMode():
+        y = op(torch.empty(5, 8, dtype=torch.bfloat16), torch.empty(5, dtype=torch.int32), 1)
+        assert y.shape == (5, 8) and y.dtype == torch.bfloat16
+    with pytest.raises(NotImplementedError, match="CPU"):  # no CPU path
+        op(torch.zeros(2, 8), torch.zeros(2, dtype=torch.int32), 1)

@@ -74,11 +74,14 @@ def _worker(rank, world, port, q):
                 y_1 = ops.moe_forward(x, w["gate_up"], w["down"], router_w=w["router_w"], k=cfg.k, n_shared=ns,
                                       tenant_ids=ten if cfg.rank else None, **lora)
                 outs = {t: layer(x, ten) for t, layer in layers.items()}
+                # the same call through the dispatcher
+                outs["op"] = torch.ops.stageml.ep_moe_lora_forward(x, ten, layers["peer"].register())
                 torch.cuda.synchronize()
                 rel = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30)).item()
                 exact = ns == 0 and T * cfg.k > 16
                 for t, y in outs.items():
-                    results.append((str(case), t, call, exact and t == "peer", bool(torch.equal(y, y_1)), rel(y, y_1)))
+                    results.append((str(case), t, call, exact and t in ("peer", "op"), bool(torch.equal(y, y_1)),
+                                    rel(y, y_1)))
                 results.append((str(case), "peer_vs_collective", call, False, False, rel(outs["peer"], outs["collective"])))
             results.append((str(case), "status", -1, True, layers["peer"].take_status() == 0 and ops.take_status(x) == 0,
                             0.0))
@@ -119,3 +122,60 @@ def test_ep_two_gpus_matches_single_gpu():
                 assert equal, f"rank {rank} {case} {what} call {call}: EP differs from single GPU (rel {rel})"
             else:
                 assert rel < 1e-2, f"rank {rank} {case} {what} call {call}: rel {rel}"
+
+
+def _worker_one(port, q):
+    """World size 1: the exchange kernels with this rank as the only peer, through the layer
+    and through torch.ops.stageml.ep_moe_lora_forward."""
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        import datetime
+
+        import torch.distributed as dist
+
+        import stageml_b200.ops as ops
+        from stageml_b200.expert_parallel import EPMoELayer
+        from stageml_b200.workloads import MoEConfig, make_moe_workload
+
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60), device_id=dev)
+        cfg = MoEConfig("ep1", T=200, H=256, I=256, E=4, k=2, n_shared=0, n_tenants=3, rank=16, tenant_dist="uniform")
+        w = make_moe_workload(cfg, device=dev, gen_device="cpu", seed=1)
+        lora = dict(n_tenants=cfg.n_tenants, rank=cfg.rank, lora_a13=w["lora_a13"], lora_b13=w["lora_b13"],
+                    lora_a2=w["lora_a2"], lora_b2=w["lora_b2"], lora_scale=w["lora_scale"])
+        y_1 = ops.moe_forward(w["x"], w["gate_up"], w["down"], router_w=w["router_w"], k=cfg.k,
+                              tenant_ids=w["tenant_ids"], **lora)
+        results = []
+        for t in ("peer", "collective"):
+            layer = EPMoELayer.from_full_weights(cfg, w, rank=0, world=1, transport=t)
+            for _ in range(2):
+                y = torch.ops.stageml.ep_moe_lora_forward(w["x"], w["tenant_ids"], layer.register())
+                y_l = layer(w["x"], w["tenant_ids"])
+                torch.cuda.synchronize()
+                rel = ((y.float() - y_1.float()).norm() / y_1.float().norm()).item()
+                results.append((t, bool(torch.equal(y, y_l)), rel, layer.take_status()))
+            layer.close()
+        dist.destroy_process_group()
+        q.put(("ok", results))
+    except Exception as exc:
+        q.put(("error", f"{exc}\n{traceback.format_exc()[-1500:]}"))
+
+
+def test_ep_op_on_one_gpu_matches_single_gpu_layer():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    proc = ctx.Process(target=_worker_one, args=(_free_port(), q))
+    proc.start()
+    try:
+        status, info = q.get(timeout=600)
+    finally:
+        proc.join(timeout=60)
+        if proc.is_alive():
+            proc.kill()
+    assert status == "ok", info
+    for transport, same_as_layer, rel, dev_status in info:
+        assert same_as_layer, transport
+        assert rel < 1e-2, (transport, rel)
+        assert dev_status == 0, transport
