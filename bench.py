@@ -13,9 +13,10 @@ E/N per rank with their adapter-bank slices, and routed rows go to their
 experts' ranks and back through peer memory over NVLink (this library's
 exchange kernels; no NCCL on the data path) (weak scaling: per-GPU work fixed).
 
---impl reference: the oracle port of the reference's CPU path (numpy/OpenBLAS,
-float32) timed on the host cores on a token sample of the same workload; under
-torchrun only rank 0 runs it.
+--impl reference: the reference's CPU path restated with its own torch operations
+(RequestExecutor.dynamic_one, float32; oracle/torch_executor.py, pinned to the
+reference's outputs) timed on the host cores on a token sample of the same
+workload; under torchrun only rank 0 runs it.
 
 Prints ONE JSON line on rank 0.
 """
@@ -158,12 +159,23 @@ def cpu_model() -> str:
 
 
 # ------------------------------------------------------------------ CPU arm
-def run_cpu_sample(cfg, w, sample_tokens: int, repeats: int, warmup: int, budget_s: float | None = None):
-    """Time the oracle port on `sample_tokens` tokens of the workload; returns (tokens_per_s, times)."""
+CPU_PATHS = {
+    "torch": "torch restatement of the reference's RequestExecutor.dynamic_one (per (slot, expert): nonzero, "
+             "index_select, F.linear on w1/w3/w2 with each tenant's LoRA, index_add_), float32, incl. router",
+    "numpy": "numpy/OpenBLAS float32 grouped executor of the oracle, incl. router",
+}
+
+
+def run_cpu_sample(cfg, w, sample_tokens: int, repeats: int, warmup: int, budget_s: float | None = None,
+                   impl: str = "torch"):
+    """Time a CPU restatement of the reference's executor on `sample_tokens` tokens of the workload;
+    returns (tokens_per_s, times). impl "torch": the reference's own torch operations
+    (oracle/torch_executor.py, pinned to the reference's outputs); "numpy": the oracle's executor."""
     import numpy as np
 
     from oracle.moe import MoEExecutorF32
     from oracle.route import route_topk
+    from oracle.torch_executor import dynamic_executor
 
     t0 = time.time()
     f32 = lambda t: None if t is None else t.float().cpu().numpy()
@@ -172,17 +184,30 @@ def run_cpu_sample(cfg, w, sample_tokens: int, repeats: int, warmup: int, budget
         s = w.get(name + "_scale")
         return f32(w[name]) if s is None else f32(w[name]) * f32(s)[..., None]
 
-    ex = MoEExecutorF32(weights("gate_up"), weights("down"), n_shared=cfg.n_shared, lora_a13=f32(w["lora_a13"]),
-                        lora_b13=f32(w["lora_b13"]), lora_a2=f32(w["lora_a2"]), lora_b2=f32(w["lora_b2"]),
-                        lora_scale=f32(w["lora_scale"]))
     x = f32(w["x"][:sample_tokens])
     gw = f32(w["router_w"])
     ten = w["tenant_ids"][:sample_tokens].cpu().numpy()
-    log(f"cpu arm: weights on host in {time.time() - t0:.1f}s; {cpu_threads()} threads, {cpu_model()}")
+    if impl == "torch":
+        torch.set_num_threads(cpu_threads())
+        tt = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a))
+        banks = {n: tt(f32(w[n])) for n in ("lora_a13", "lora_b13", "lora_a2", "lora_b2", "lora_scale")}
+        gu, dn, xt, tent = tt(weights("gate_up")), tt(weights("down")), tt(x), tt(ten)
+        gwt = tt(gw)
 
-    def step():
-        ids, wts, _ = route_topk(x, gw, cfg.k, True)
-        return ex(x, ids, wts, ten)
+        def step():
+            probs = torch.softmax(xt @ gwt.t(), -1)  # make_routing: fp32 logits, softmax, top-k, renormalise
+            wts, ids = torch.topk(probs, cfg.k, -1)
+            wts = wts / wts.sum(-1, keepdim=True)
+            return dynamic_executor(xt, gu, dn, ids, wts, tent, n_shared=cfg.n_shared, **banks)
+    else:
+        ex = MoEExecutorF32(weights("gate_up"), weights("down"), n_shared=cfg.n_shared, lora_a13=f32(w["lora_a13"]),
+                            lora_b13=f32(w["lora_b13"]), lora_a2=f32(w["lora_a2"]), lora_b2=f32(w["lora_b2"]),
+                            lora_scale=f32(w["lora_scale"]))
+
+        def step():
+            ids, wts, _ = route_topk(x, gw, cfg.k, True)
+            return ex(x, ids, wts, ten)
+    log(f"cpu arm ({impl}): weights on host in {time.time() - t0:.1f}s; {cpu_threads()} threads, {cpu_model()}")
 
     for _ in range(warmup):
         step()
@@ -206,7 +231,7 @@ def reference_arm(args, cfg, rank: int):
     torch.cuda.set_device(0)
     w = make_moe_workload(cfg, device="cuda", seed=0)
     sample = args.cpu_sample_tokens
-    tps, times = run_cpu_sample(cfg, w, sample, repeats=args.steps, warmup=args.warmup)
+    tps, times = run_cpu_sample(cfg, w, sample, repeats=args.steps, warmup=args.warmup, impl="torch")
     cores = cpu_threads()
     line = {
         "metric": "MoE-LoRA layer tokens/s", "value": round(tps, 3), "unit": "tokens/s", "impl": "reference",
@@ -216,8 +241,9 @@ def reference_arm(args, cfg, rank: int):
         "config": {"workload": cfg.name, "tokens_per_step": sample, "hidden": cfg.H, "intermediate": cfg.I,
                    "experts": cfg.E, "top_k": cfg.k, "lora_rank": cfg.rank, "tenants": cfg.n_tenants},
         "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} of {cfg.T} tokens per step (all experts and tenants touched), oracle "
-                                   f"numpy/OpenBLAS float32 grouped executor incl. router, {cpu_model()}"},
+                         "path": CPU_PATHS["torch"],
+                         "sample": f"{sample} of {cfg.T} tokens per step (all experts and tenants touched), "
+                                   f"{cpu_model()}"},
         "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -443,10 +469,16 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
     cpu = None
     if world == 1 and not args.skip_cpu:
         try:
-            tps, times = run_cpu_sample(cfg, w, args.cpu_sample_tokens, repeats=5, warmup=1, budget_s=20.0)
+            tps, times = run_cpu_sample(cfg, w, args.cpu_sample_tokens, repeats=5, warmup=1, budget_s=15.0,
+                                        impl="torch")
+            tps_np, times_np = run_cpu_sample(cfg, w, args.cpu_sample_tokens, repeats=3, warmup=1, budget_s=8.0,
+                                              impl="numpy")
             cpu = {"value": round(tps, 3), "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+                   "path": CPU_PATHS["torch"],
                    "sample": f"{args.cpu_sample_tokens} of {T} tokens, median of {len(times)} timed calls after 1 "
-                             f"warm-up; oracle numpy/OpenBLAS float32 grouped executor incl. router; {cpu_model()}"}
+                             f"warm-up; {cpu_model()}",
+                   "numpy_port": {"value": round(tps_np, 3), "unit": "tokens/s", "path": CPU_PATHS["numpy"],
+                                  "timed_calls": len(times_np)}}
         except Exception as exc:  # pragma: no cover
             cpu = {"value": None, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
                    "sample": f"failed: {exc}"}

@@ -143,3 +143,45 @@ def test_permutation_is_stable_sort_by_expert_then_tenant():
         assert np.all(ids.reshape(-1)[seg] == e)
     # inverse
     np.testing.assert_array_equal(p["row_pair"][p["pair_row"]], np.arange(T * k))
+
+
+def test_torch_executor_restatement_matches_reference_request_executor(golden):
+    """The torch restatement of RequestExecutor.dynamic_one (the benchmark's timed CPU baseline)
+    against the reference executor's own outputs, and against the numpy oracle with LoRA on
+    w1, w3, w2, per-token tenants and a shared expert."""
+    import torch
+
+    from oracle import moe as omoe
+    from oracle.torch_executor import dynamic_executor
+
+    g = golden("request_executor")
+    t = lambda n: torch.from_numpy(np.asarray(g[n], dtype=np.float32))
+    E, I2, H = g["gate_up"].shape
+    I = I2 // 2
+    for a in (0, 1):
+        A, B = t(f"A{a}"), t(f"B{a}")
+        r = A.shape[1]
+        a13 = torch.zeros(1, E, 2 * r, H)
+        b13 = torch.zeros(1, E, I2, r)
+        a13[0, :, :r] = A
+        b13[0, :, :I] = B
+        T = g["x"].shape[0]
+        y = dynamic_executor(t("x"), t("gate_up"), t("down"), torch.from_numpy(g["topk_ids"]), t("topk_weights"),
+                             torch.zeros(T, dtype=torch.int32), lora_a13=a13, lora_b13=b13,
+                             lora_scale=torch.tensor([float(g["scaling"][a])]))
+        assert rel_l2(y.numpy(), g[f"dyn{a}"]) < 1e-5
+    rng = np.random.default_rng(3)
+    T, H, I, E, k, nT, r, ns = 30, 16, 12, 4, 2, 3, 4, 1
+    Et = E + ns
+    arr = lambda *s: rng.normal(size=s).astype(np.float32) / 3
+    x, gu, dn = arr(T, H), arr(Et, 2 * I, H), arr(Et, H, I)
+    lo = dict(lora_a13=arr(nT, Et, 2 * r, H), lora_b13=arr(nT, Et, 2 * I, r), lora_a2=arr(nT, Et, r, I),
+              lora_b2=arr(nT, Et, H, r), lora_scale=np.array([0.5, 1.0, 2.0], dtype=np.float32))
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)])
+    w = rng.random((T, k)).astype(np.float32)
+    ten = rng.integers(-1, nT, T).astype(np.int32)
+    ref = omoe.moe_forward(x, gu, dn, ids, w, tenant_ids=ten, n_shared=ns, **lo)
+    T_ = torch.from_numpy
+    y = dynamic_executor(T_(x), T_(gu), T_(dn), T_(ids), T_(w), T_(ten), n_shared=ns,
+                         **{n: T_(v) for n, v in lo.items()})
+    assert rel_l2(y.numpy(), ref) < 1e-5
