@@ -46,11 +46,13 @@ struct Cfg {
   static constexpr int STAGES = FP8B ? 3 : 4;
   static constexpr int STAGE_BYTES = FP8B ? MMA_STAGE_BYTES + RAW_B_BYTES : MMA_STAGE_BYTES;
   static constexpr int THREADS = FP8B ? 192 + CONVERTER_THREADS : 192;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 1024 /*barriers, run header*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, run copies*/;
 };
-// The producer bulk-copies the first kHdrRuns runs (tenant + 4 mask words each) of a
-// unit's tile at the unit's start: area after the stages = barriers (< 192 B), the
-// copy's barrier at byte 192, the runs at byte 256.
+// The producer and the MMA issuer each bulk-copy the first kHdrRuns runs (tenant + 4
+// mask words each) of a unit's tile at the unit's start, so the LoRA phase costs no
+// global round trip per run: area after the stages = barriers (< 192 B), the
+// producer's copy barrier at byte 192 and the MMA issuer's at byte 200, the
+// producer's runs at byte 256, the MMA issuer's at byte 1024.
 constexpr int kHdrRuns = 32;
 static_assert(256 + kHdrRuns * 5 * 4 <= 1024 && (kHdrRuns * 5 * 4) % 16 == 0, "run header area");
 
@@ -194,6 +196,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
   uint64_t* hdr_bar_p = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 192);
   const int32_t* hdr_smem = reinterpret_cast<const int32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  uint64_t* mrun_bar_p = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 200);
+  const int32_t* mruns_smem = reinterpret_cast<const int32_t*>(reinterpret_cast<uint8_t*>(bars) + 1024);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     }
     mbar_init(drain_bar, 1);
     mbar_init(smem_u32(hdr_bar_p), 1);
+    mbar_init(smem_u32(mrun_bar_p), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -354,11 +359,24 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     int tcount = 0;
     bool ok = true;
     bool issued_any = false;
+    const uint32_t mrun_bar = smem_u32(mrun_bar_p);
+    uint32_t mrun_uses = 0;
+    bool mrun_inflight = false;
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += nctas, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
       int m_pos, n_tile_unused;
       unit_mn(p, tile, num_m_tiles, m_pos, n_tile_unused);
+      const int slot = run_slot(p, m_pos);
+      // the tile's run count (used after the K loop) and first kHdrRuns runs, in flight meanwhile
+      const int nruns_unit = tile_lora_runs(p, m_pos);
+      if (p.rank) {
+        fence_proxy_async_smem();  // the previous unit's reads of the buffer come first
+        mbar_arrive_expect_tx(mrun_bar, kHdrRuns * 5 * 4);
+        bulk_load_1d(smem_u32(mruns_smem), p.tile_runs + (int64_t)slot * kMaxRunsPerTile * 5, kHdrRuns * 5 * 4,
+                     mrun_bar);
+        mrun_inflight = true;
+      }
       if (!mbar_wait(tempty_bar(acc), aph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
         ok = false;
         break;
@@ -382,8 +400,12 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         tc_commit(empty_bar(s));
         issued_any = true;
       }
-      const int slot = run_slot(p, m_pos);
-      const int nruns = ok ? tile_lora_runs(p, m_pos) : 0;
+      if (ok && p.rank) {
+        ok = mbar_wait(mrun_bar, mrun_uses & 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma);
+        mrun_inflight = !ok;
+        ++mrun_uses;
+      }
+      const int nruns = ok ? nruns_unit : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -395,7 +417,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         tc_fence_after();
         const uint32_t base = smem_base + s * STAGE_BYTES;
         for (int jj = 0; jj < nr; ++jj) {
-          const int32_t* run = tile_run(p, slot, r0 + jj);
+          const int r = r0 + jj;
+          const int32_t* run = r < kHdrRuns ? mruns_smem + r * 5 : tile_run(p, slot, r);
           const uint32_t d0 = ~(uint32_t)run[1], d1 = ~(uint32_t)run[2], d2 = ~(uint32_t)run[3],
                          d3 = ~(uint32_t)run[4];
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
@@ -416,6 +439,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       if (!ok) break;
       tc_commit(tfull_bar(acc));
     }
+    if (mrun_inflight) mbar_wait(mrun_bar, mrun_uses & 1, &never_abort, p.status, 200000000ull, kDevTimeoutDrain);
     if (!ok && issued_any) {
       tc_commit(drain_bar);
       mbar_wait(drain_bar, 0, &never_abort, p.status, 1000000000ull, kDevTimeoutDrain);

@@ -39,10 +39,18 @@ constexpr int LHALF = 64 * 32;                 // 64 rows x 16 columns, 16-bit (
 constexpr int STAGES = 7;
 constexpr int STAGE_BYTES = MMA_STAGE_BYTES;
 constexpr int THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+// The MMA issuer reads the row masks of a unit's first kMmaRuns LoRA runs (and the run
+// count) from shared memory: it bulk-copies them at the unit's start, so they land while
+// the K loop runs instead of costing one global round trip per run in the LoRA phase.
+constexpr int kMmaRuns = 32;
+constexpr int MMA_RUN_BYTES = kRunHdrInts * 4 + kMmaRuns * kPairRunInts * 4;  // 128 + 1152
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/ + MMA_RUN_BYTES;
 static_assert(SMEM_BYTES <= 232448, "shared memory per block");
+static_assert((kMmaRuns * kPairRunInts * 4) % 16 == 0, "bulk copy size");
 // barrier area (512 B): the barriers, the TMEM address and abort flag (< 160 B), the
-// producer's header barrier at byte 160 and its 128-byte run header at byte 256
+// producer's header barrier at byte 160, the MMA issuer's run barrier at byte 168 and
+// the producer's 128-byte run header at byte 256; then the MMA issuer's run header
+// (128 B) and its runs (kMmaRuns x 36 B) at byte 512
 static_assert((2 * STAGES + 5) * 8 + 8 <= 160, "barrier area");
 
 struct PParams {
@@ -111,11 +119,6 @@ __device__ __forceinline__ void store16(T* dst, const float (&v)[16], int ncols_
 }
 
 // LoRA runs of a pair are stored at its first tile m0.
-__device__ __forceinline__ int pair_lora_runs(const PParams& p, int m0) {
-  if (p.rank == 0) return 0;
-  const int n = p.nruns[(int64_t)m0 * kRunHdrInts];
-  return n < kMaxRunsPerPair ? n : kMaxRunsPerPair;
-}
 __device__ __forceinline__ const int32_t* pair_run(const PParams& p, int m0, int r) {
   return p.runs + ((int64_t)m0 * kMaxRunsPerPair + min(r, kMaxRunsPerPair - 1)) * kPairRunInts;
 }
@@ -161,6 +164,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   // the producer's copy of the current unit's run header (LoRA), and its barrier
   uint64_t* hdr_bar_p = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 160);
   const int32_t* hdr_smem = reinterpret_cast<const int32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  // the MMA issuer's copy of the current unit's run header and first kMmaRuns runs, and its barrier
+  uint64_t* mrun_bar_p = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 168);
+  const int32_t* mhdr_smem = reinterpret_cast<const int32_t*>(reinterpret_cast<uint8_t*>(bars) + 512);
+  const int32_t* mruns_smem = mhdr_smem + kRunHdrInts;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -185,6 +192,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(drain_bar, 1);
     mbar_init(smem_u32(hdr_bar_p), 1);
+    mbar_init(smem_u32(mrun_bar_p), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -317,12 +325,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t it = 0;
     int tcount = 0;
     bool ok = true;
+    const uint32_t mrun_bar = smem_u32(mrun_bar_p);
+    uint32_t mrun_uses = 0;
+    bool mrun_inflight = false;
     for (int u = cluster; ok && u < total_units; u += nclusters, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
       int pm, n_tile_unused;
       unit_coords(p, u, pm, n_tile_unused);
       const int m0 = p.pairs[4 * pm];
+      if (p.rank) {  // the unit's run header and first runs arrive while the K loop is issued
+        fence_proxy_async_smem();  // the previous unit's reads of the buffer come first
+        mbar_arrive_expect_tx(mrun_bar, MMA_RUN_BYTES);
+        bulk_load_1d(smem_u32(mhdr_smem), p.nruns + (int64_t)m0 * kRunHdrInts, kRunHdrInts * 4, mrun_bar);
+        bulk_load_1d(smem_u32(mruns_smem), p.runs + (int64_t)m0 * kMaxRunsPerPair * kPairRunInts,
+                     kMmaRuns * kPairRunInts * 4, mrun_bar);
+        mrun_inflight = true;
+      }
       if (!mbar_wait_cluster(tempty_bar(acc), aph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
         ok = false;
         break;
@@ -345,7 +364,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_mma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
         tc_commit_pair_both(empty_bar(s), 0x3);
       }
-      const int nruns = ok ? pair_lora_runs(p, m0) : 0;
+      int nruns = 0;
+      if (ok && p.rank) {
+        ok = mbar_wait(mrun_bar, mrun_uses & 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma);
+        mrun_inflight = !ok;
+        ++mrun_uses;
+        nruns = ok ? min(mhdr_smem[0], kMaxRunsPerPair) : 0;
+      }
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int nr = min(p.runs_per_block, nruns - r0);
         const int s = it % STAGES;
@@ -357,7 +382,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t base = smem_base + s * STAGE_BYTES;
         for (int jj = 0; jj < nr; ++jj) {
-          const int32_t* run = pair_run(p, m0, r0 + jj);
+          const int r = r0 + jj;
+          const int32_t* run = r < kMmaRuns ? mruns_smem + r * kPairRunInts : pair_run(p, m0, r);
           uint32_t dis[8];
 #pragma unroll
           for (int w = 0; w < 8; ++w) dis[w] = ~(uint32_t)run[1 + w];
@@ -379,6 +405,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
       tc_commit_pair_both(tfull_bar(acc), 0x3);
     }
+    // The run copy in flight lands before the CTA pair leaves (error paths).
+    if (mrun_inflight) mbar_wait(mrun_bar, mrun_uses & 1, &never_abort, p.status, 200000000ull, kDevTimeoutDrain);
     // Every MMA of this CTA pair has completed (and stopped reading either CTA's
     // shared memory) before the final cluster barrier.
     tc_commit_pair(drain_bar);
