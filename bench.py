@@ -434,10 +434,15 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     e0.record()
+    t_host = time.perf_counter()
     e2e_run(e2e_steps)
+    host_submit_ms = (time.perf_counter() - t_host) * 1000.0 / e2e_steps  # host time to issue one step
     e1.record()
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1)
+    host_io = host_copy_rates(x_host, out_host[0], x_dev[0], x, world, dev) if world > 1 else None
+    if host_io is not None:
+        host_io["host_submit_ms_per_step"] = round(host_submit_ms, 4)
     if world > 1:
         t = torch.tensor([ms_e2e], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -537,6 +542,7 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
     if layer is not None:
         line["ep_status"] = ep_status
         line["ep_parity"] = ep_parity
+        line["host_io"] = host_io
     print(json.dumps(line), flush=True)
 
 
@@ -550,6 +556,56 @@ GATE_UP_DRAM_CAPTURE: dict = {
                   "(profiles/grouped_gemm_pair_mixtral.md)",
     },
 }
+
+
+def gpu_numa_node(dev) -> int | None:
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id if hasattr(
+            torch.cuda.get_device_properties(dev), "pci_bus_id") else None
+        if bus is None:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(dev.index if hasattr(dev, "index") else int(dev))
+            bus = pynvml.nvmlDeviceGetPciInfo(h).busId
+            bus = bus.decode() if isinstance(bus, bytes) else bus
+        bus = bus.lower()
+        if bus.count(":") == 2 and len(bus.split(":")[0]) == 8:
+            bus = bus[4:]
+        return int(open(f"/sys/bus/pci/devices/{bus}/numa_node").read().strip())
+    except Exception:
+        return None
+
+
+def host_copy_rates(x_host, out_host, x_dev, y_dev, world: int, dev) -> dict:
+    """Per-rank host<->device copy rates of one step's input and output, every rank copying at
+    the same time (as in the end-to-end loop); collective. Also where the rank's pinned memory
+    and GPU sit (NUMA nodes) and which CPUs the process may run on."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rates = []
+    for src, dst in ((x_host, x_dev), (y_dev, out_host)):
+        for _ in range(2):
+            dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        e0.record()
+        for _ in range(5):
+            dst.copy_(src, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        rates.append(5 * src.numel() * src.element_size() / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    t = torch.tensor(rates, device=dev)
+    lo, hi = t.clone(), t.clone()
+    torch.distributed.all_reduce(lo, op=torch.distributed.ReduceOp.MIN)
+    torch.distributed.all_reduce(hi, op=torch.distributed.ReduceOp.MAX)
+    try:
+        cpus = sorted(os.sched_getaffinity(0))
+        cpu_span = f"{len(cpus)} cpus {cpus[0]}-{cpus[-1]}"
+    except Exception:
+        cpu_span = None
+    return {"h2d_gbs_min": round(float(lo[0]), 2), "h2d_gbs_max": round(float(hi[0]), 2),
+            "d2h_gbs_min": round(float(lo[1]), 2), "d2h_gbs_max": round(float(hi[1]), 2),
+            "all_ranks_copying": True, "rank0_gpu_numa": gpu_numa_node(dev), "rank0_cpus": cpu_span}
 
 
 def choose_peak(peaks: dict, clocks: dict, region_s: float) -> dict:
@@ -615,6 +671,31 @@ def _timed(fn, steps: int, warmup: int, lib=None):
     return e0.elapsed_time(e1) / steps, stages, launches
 
 
+def _graph_timed(fn, reps: int, replays: int = 5):
+    """Device time per call of `reps` calls captured in one CUDA graph (host submission
+    overhead excluded), replayed `replays` times after one warm-up replay; ms per call."""
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / (replays * reps)
+
+
 def _line(metric, value, unit, steps, warmup, ms, hib, dtype, config, **extra):
     d = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": steps, "warmup": warmup,
          "ms_per_step": round(ms, 5), "higher_is_better": hib, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
@@ -650,6 +731,18 @@ def dense_arm(args):
                                                                     sets[i % 4]["B"], sets[i % 4]["scale"]),
                                        args.steps, args.warmup, lib)
         ms_fold, _, _ = _timed(lambda i: ops.lora_gemv_f32(sets[i % 4]["x"], folded[i % 4]), args.steps, args.warmup)
+        # the stage-0 fold W' = W + s A B itself: reads W, writes W' (4 B per element each)
+        sc1 = torch.full((1,), float(sets[0]["scale"]), dtype=torch.float32, device=dev)
+        sc4 = [torch.full((1,), float(st["scale"]), dtype=torch.float32, device=dev) for st in sets]
+        # device time per call with the host out of the loop (calls captured in a CUDA graph)
+        g_dyn = _graph_timed(lambda i: ops.lora_gemv_f32(sets[i % 4]["x"], sets[i % 4]["W"], sets[i % 4]["A"],
+                                                         sets[i % 4]["B"], sets[i % 4]["scale"]), 40)
+        g_fold = _graph_timed(lambda i: ops.lora_gemv_f32(sets[i % 4]["x"], folded[i % 4]), 40)
+        g_f = _graph_timed(lambda i: ops.lora_fold(sets[i % 4]["W"], sets[i % 4]["A"], sets[i % 4]["B"], sc4[i % 4],
+                                                   1), 20)
+        ms_f, _, n_f = _timed(lambda i: ops.lora_fold(sets[i % 4]["W"], sets[i % 4]["A"], sets[i % 4]["B"], sc1, 1),
+                              args.steps, args.warmup, lib)
+        fold_bytes = 2 * 4 * 4096 * 4096 + 2 * 4 * 4096 * 16
         byt = 4 * 4096 * 4096 + 2 * 4 * 4096 * 16 + 8 * 4096
         ms_k = st_dyn.get("gemv", {}).get("ms", 0) / max(st_dyn.get("gemv", {}).get("launches", 1), 1)
         s0 = sets[0]
@@ -662,14 +755,25 @@ def dense_arm(args):
             single_lora(f(s0["x"]), f(s0["W"]), f(s0["A"]), f(s0["B"]), s0["scale"], dtype=np.float32)
             reps += 1
         cpu_us = (time.perf_counter() - t0) / reps * 1e6
-        _line("single LoRA linear latency (dynamic x W + s (x A) B)", round(ms_dyn * 1000, 3), "us", args.steps,
-              args.warmup, ms_dyn, False, "f32",
+        _line("single LoRA linear latency (dynamic x W + s (x A) B)", round(g_dyn * 1000, 3), "us", args.steps,
+              args.warmup, g_dyn, False, "f32",
               {"workload": "single_lora", "x": [1, 4096], "W": [4096, 4096], "rank": 16, "scale": 2.0,
                "l2": "4 rotating weight sets, 268 MB > L2"},
-              folded_latency_us=round(ms_fold * 1000, 3), gpu_launches=n_dyn, clocks=sampler.stop(),
-              roofline={"bound": "hbm", "kernel": "gemv_partial_kernel + reduce",
-                        "achieved": round(byt / (ms_k / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
-                        "frac": round(byt / (ms_k / 1e3) / 1e9 / hbm, 4), "traffic": None},
+              value_source="device time per call: 40 calls (4 rotating weight sets) in one CUDA graph",
+              eager_latency_us=round(ms_dyn * 1000, 3), folded_latency_us=round(g_fold * 1000, 3),
+              eager_folded_latency_us=round(ms_fold * 1000, 3),
+              folded_roofline={"bytes": 4 * 4096 * 4096 + 8 * 4096,
+                               "achieved_gbs": round((4 * 4096 * 4096 + 8 * 4096) / (g_fold / 1e3) / 1e9, 1),
+                               "frac": round((4 * 4096 * 4096 + 8 * 4096) / (g_fold / 1e3) / 1e9 / hbm, 4)},
+              gpu_launches=n_dyn, clocks=sampler.stop(),
+              fold={"kernel": "fold_f32_vec_kernel (fp32, [in,out] layout)", "us": round(g_f * 1000, 3),
+                    "bytes": fold_bytes, "achieved_gbs": round(fold_bytes / (g_f / 1e3) / 1e9, 1),
+                    "frac": round(fold_bytes / (g_f / 1e3) / 1e9 / hbm, 4), "eager_us": round(ms_f * 1000, 3),
+                    "launches": n_f, "timing": "CUDA graph of 20 folds, 4 rotating weight sets"},
+              roofline={"bound": "hbm", "kernel": "gemv_partial_kernel + reduce (dynamic form)",
+                        "achieved": round(byt / (g_dyn / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(byt / (g_dyn / 1e3) / 1e9 / hbm, 4), "traffic": None,
+                        "stage_timer_ms": round(ms_k, 5)},
               cpu_baseline={"value": round(cpu_us, 2), "unit": "us", "cores": cpu_threads(), "kind": "port",
                             "sample": "the same call, numpy float32"})
     elif name == "adapter_bank":
@@ -690,6 +794,15 @@ def dense_arm(args):
         fold_ms = e0.elapsed_time(e1)
         layers += [StageMLCostBasedAdapterCache(w["W"] * (1 + 1e-3 * j), ads, cached_adapter_names=cached)
                    for j in range(1, 3)]  # 3 layers x 302 MB of weights rotate past L2
+        # the stage-0 fold alone: the 8 cached adapters folded into W (bf16) in one batched launch,
+        # W read once and 8 W' written; 3 rotating base weights
+        idx = torch.tensor([int(c.split("_")[1]) for c in cached], device=dev)
+        A8, B8 = w["A"][idx].contiguous(), w["B"][idx].contiguous()
+        sc8 = torch.full((len(cached),), float(w["scale"]), dtype=torch.float32, device=dev)
+        Ws = [w["W"], layers[1].weight, layers[2].weight]
+        ms_f, _, n_f = _timed(lambda i: ops.lora_fold(Ws[i % 3], A8, B8, sc8, 0), args.steps, args.warmup, lib)
+        g_f = _graph_timed(lambda i: ops.lora_fold(Ws[i % 3], A8, B8, sc8, 0), 12)
+        fold_bytes = 4096 * 4096 * 2 * (1 + len(cached)) + (A8.numel() + B8.numel()) * 2
         ms, st, n = _timed(lambda i: layers[i % 3](w["x"], names), args.steps, args.warmup, lib)
         byt = 4096 * 4096 * 2 * (1 + len(cached)) + 2 * 256 * 4096 * 2
         _line("multi-tenant LoRA bank tokens/s (64 adapters, top-8 folded)", round(256 / (ms / 1e3), 1), "tokens/s",
@@ -698,6 +811,10 @@ def dense_arm(args):
                "folded": len(cached), "l2": "3 rotating layers"},
               stages_ms_per_step={k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in st.items()},
               stage0_fold_ms=round(fold_ms, 4), gpu_launches=n, clocks=sampler.stop(),
+              fold={"kernel": "fold_mma_kernel (bf16, 8 adapters batched, W broadcast)", "us": round(g_f * 1000, 3),
+                    "bytes": fold_bytes, "achieved_gbs": round(fold_bytes / (g_f / 1e3) / 1e9, 1),
+                    "frac": round(fold_bytes / (g_f / 1e3) / 1e9 / hbm, 4), "eager_us": round(ms_f * 1000, 3),
+                    "launches": n_f, "timing": "CUDA graph of 12 folds, 3 rotating base weights"},
               roofline={"bound": "hbm", "kernel": "grouped GEMM over [W, W'_1..8] + tensor-core LoRA expand",
                         "achieved": round(byt / (ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                         "frac": round(byt / (ms / 1e3) / 1e9 / hbm, 4), "traffic": None})

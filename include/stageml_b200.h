@@ -335,7 +335,8 @@ int stageml_lora_gemv_f32(const float* x, const float* W, const float* A, const 
  * synchronize the device), or a host that plans its device memory in a fixed
  * arena. Inputs and the output y are still the caller's memory.
  *  - Shapes whose partial sums exceed the 16 MiB scratch return
- *    STAGEML_ERR_INVALID_ARG (in = out = 4096 on a 148-SM B200 fits up to M = 7);
+ *    STAGEML_ERR_INVALID_ARG (in = out = 4096 fits every M up to 16; very wide
+ *    outputs do not, e.g. M = 16 with out > 262,144 columns);
  *    stageml_lora_gemv_f32 with a workspace has no such limit.
  *  - The first call on a device looks up the scratch array's device address
  *    (cudaGetSymbolAddress, with that device current) and caches it together

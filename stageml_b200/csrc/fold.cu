@@ -7,11 +7,13 @@
 // einsum("eor,eri->eoi") fold of MaterializedMoELoRALayer (stageml/moe_lora_layers.py:104-110).
 //
 // The fold streams W once and writes W' once: HBM-bound (4 bytes per 16-bit
-// element). The rank-r product costs r FMAs per element, which for r = 16 at
-// HBM speed would saturate the fp32 pipes, so the 16-bit path computes it with
-// warp-level tensor-core MMAs (m16n8k16, fp32 accumulate) on a 64 x 128 tile
-// staged in shared memory, with 16-byte loads and stores of W and W'.
-// fp32 (and unaligned shapes) use plain fp32 FMAs, one element per thread.
+// element, 8 per fp32 element). The rank-r product costs r FMAs per element, which
+// for r = 16 at HBM speed would saturate the fp32 pipes on 16-bit weights, so the
+// 16-bit path computes it with warp-level tensor-core MMAs (m16n8k16, fp32
+// accumulate) on a 64 x 128 tile staged in shared memory with its L and R slices,
+// with 16-byte loads and stores of W and W'. fp32 (rank <= 16) keeps each thread's
+// R columns in registers and streams rows with 8-byte accesses; other fp32 and
+// unaligned shapes use plain fp32 FMAs, one element per thread.
 #include "common.cuh"
 #include "host_util.h"
 #include "kernels.h"
@@ -88,17 +90,31 @@ __device__ __forceinline__ void fold_operands(const FoldArgs& f, int b, const T*
   }
 }
 
+// Grid x = (column tile) * batch + matrix: the matrices of one tile run next to each
+// other, so a W shared by the batch (w_bs = 0) is read from DRAM once per tile.
+// Dynamic shared memory: the W tile [FT_M][FT_N + FT_PAD], L rows [FT_M][rk16 + 8], R columns [rk16][FT_N + 8].
+inline size_t fold_mma_smem(int rank, size_t esz) {
+  const int rk16 = (rank + 15) & ~15;
+  return esz * ((size_t)FT_M * (FT_N + FT_PAD) + (size_t)FT_M * (rk16 + 8) + (size_t)rk16 * (FT_N + 8));
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f) {
-  __shared__ __align__(16) T tile[FT_M][FT_N + FT_PAD];
-  const int b = blockIdx.z;
-  const int m0 = blockIdx.y * FT_M, n0 = blockIdx.x * FT_N;
+__global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f, int batch) {
+  extern __shared__ __align__(16) uint8_t fold_smem[];
+  const int rk16 = (f.rank + 15) & ~15;
+  auto tile = reinterpret_cast<T(*)[FT_N + FT_PAD]>(fold_smem);
+  T* Ls_base = reinterpret_cast<T*>(fold_smem) + FT_M * (FT_N + FT_PAD);
+  T* Rs_base = Ls_base + FT_M * (rk16 + 8);
+  auto Ls = [&](int r, int j) -> T& { return Ls_base[r * (rk16 + 8) + j]; };
+  auto Rs = [&](int j, int c) -> T& { return Rs_base[j * (FT_N + 8) + c]; };
+  const int b = blockIdx.x % batch;
+  const int m0 = blockIdx.y * FT_M, n0 = (blockIdx.x / batch) * FT_N;
   const T* W = static_cast<const T*>(f.W) + (int64_t)b * f.w_bs;
   T* O = static_cast<T*>(f.out) + (int64_t)b * f.rows * f.cols;
   const T *L, *R;
   fold_operands<T>(f, b, &L, &R);
   const float s = f.scale[b];
-  // 1. W tile -> shared (16-byte accesses)
+  // 1. W tile -> shared (16-byte accesses), then the L and R tiles (zero past the rank / the edges)
   for (int i = threadIdx.x; i < FT_M * FT_N / 8; i += 256) {
     const int r = i / (FT_N / 8), c8 = (i % (FT_N / 8)) * 8;
     const int gm = m0 + r, gn = n0 + c8;
@@ -106,8 +122,27 @@ __global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f) {
     if (gm < f.rows && gn < f.cols) v = __ldg(reinterpret_cast<const uint4*>(W + (int64_t)gm * f.cols + gn));
     *reinterpret_cast<uint4*>(&tile[r][c8]) = v;
   }
+  const T zero = from_f32<T>(0.f);
+  for (int i = threadIdx.x; i < FT_M * rk16; i += 256) {
+    const int r = i / rk16, j = i % rk16;
+    Ls(r, j) = (m0 + r < f.rows && j < f.rank) ? L[(int64_t)(m0 + r) * f.rank + j] : zero;
+  }
+  for (int i = threadIdx.x; i < rk16 * FT_N / 8; i += 256) {
+    const int j = i / (FT_N / 8), c8 = (i % (FT_N / 8)) * 8;
+    const int gn = n0 + c8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (j < f.rank) {
+      if (gn + 8 <= f.cols && (f.cols % 8) == 0)
+        v = __ldg(reinterpret_cast<const uint4*>(R + (int64_t)j * f.cols + gn));
+      else {
+        T* e = reinterpret_cast<T*>(&v);
+        for (int q = 0; q < 8; ++q) e[q] = gn + q < f.cols ? R[(int64_t)j * f.cols + gn + q] : zero;
+      }
+    }
+    *reinterpret_cast<uint4*>(&Rs(j, c8)) = v;
+  }
   __syncthreads();
-  // 2. rank-r product on tensor cores, added into the tile
+  // 2. rank-r product on tensor cores (operands from shared memory), added into the tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int mb = (warp & 3) * 16;   // 4 row blocks of 16
@@ -117,21 +152,17 @@ __global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f) {
   for (int nb = 0; nb < 8; ++nb)
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[nb][q] = 0.f;
-  const T zero = from_f32<T>(0.f);
-  for (int k0 = 0; k0 < f.rank; k0 += 16) {
-    auto Lv = [&](int m, int j) -> T { return (m < f.rows && j < f.rank) ? L[(int64_t)m * f.rank + j] : zero; };
-    const int ml = m0 + mb + g, mh = ml + 8;
+  for (int k0 = 0; k0 < rk16; k0 += 16) {
     const int ja = k0 + tig * 2, jb = ja + 8;
-    const uint32_t a0 = pack2_raw<T>(Lv(ml, ja), Lv(ml, ja + 1));
-    const uint32_t a1 = pack2_raw<T>(Lv(mh, ja), Lv(mh, ja + 1));
-    const uint32_t a2 = pack2_raw<T>(Lv(ml, jb), Lv(ml, jb + 1));
-    const uint32_t a3 = pack2_raw<T>(Lv(mh, jb), Lv(mh, jb + 1));
+    const uint32_t a0 = pack2_raw<T>(Ls(mb + g, ja), Ls(mb + g, ja + 1));
+    const uint32_t a1 = pack2_raw<T>(Ls(mb + g + 8, ja), Ls(mb + g + 8, ja + 1));
+    const uint32_t a2 = pack2_raw<T>(Ls(mb + g, jb), Ls(mb + g, jb + 1));
+    const uint32_t a3 = pack2_raw<T>(Ls(mb + g + 8, jb), Ls(mb + g + 8, jb + 1));
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
-      const int n = n0 + nh + nb * 8 + g;
-      auto Rv = [&](int j) -> T { return (j < f.rank && n < f.cols) ? R[(int64_t)j * f.cols + n] : zero; };
-      const uint32_t b0 = pack2_raw<T>(Rv(ja), Rv(ja + 1));
-      const uint32_t b1 = pack2_raw<T>(Rv(jb), Rv(jb + 1));
+      const int n = nh + nb * 8 + g;
+      const uint32_t b0 = pack2_raw<T>(Rs(ja, n), Rs(ja + 1, n));
+      const uint32_t b1 = pack2_raw<T>(Rs(jb, n), Rs(jb + 1, n));
       mma16816<T>(acc[nb], a0, a1, a2, a3, b0, b1);
     }
   }
@@ -155,6 +186,54 @@ __global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f) {
     const int gm = m0 + r, gn = n0 + c8;
     if (gm < f.rows && gn < f.cols)
       *reinterpret_cast<uint4*>(O + (int64_t)gm * f.cols + gn) = *reinterpret_cast<const uint4*>(&tile[r][c8]);
+  }
+}
+
+// fp32, rank <= 16, even cols, 8-byte aligned rows: each thread owns 2 columns and keeps
+// their rank-r slice of R in registers (32); 128 column threads x 2 row threads per CTA
+// walk FV_ROWS rows with eight rows' W loads in flight before their FMAs (3-4 CTAs per SM,
+// ~64 KB of W reads in flight per SM); the L row is read by every thread of a row (a
+// broadcast). fp32 FMAs in j order (no TF32).
+constexpr int FV_ROWS = 64;
+constexpr int FV_INFLIGHT = 6;
+__global__ void __launch_bounds__(256, 3) fold_f32_vec_kernel(const FoldArgs f) {
+  const int b = blockIdx.z;
+  const float* W = static_cast<const float*>(f.W) + (int64_t)b * f.w_bs;
+  float* O = static_cast<float*>(f.out) + (int64_t)b * f.rows * f.cols;
+  const float *L, *R;
+  fold_operands<float>(f, b, &L, &R);
+  const float s = f.scale[b];
+  const int ct = threadIdx.x & 127, rt = threadIdx.x >> 7;
+  const int n = (blockIdx.x * 128 + ct) * 2;
+  if (n >= f.cols) return;
+  float2 rv[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    rv[j] = j < f.rank ? __ldg(reinterpret_cast<const float2*>(R + (int64_t)j * f.cols + n)) : make_float2(0.f, 0.f);
+  const int m_begin = blockIdx.y * FV_ROWS, m_end = min(f.rows, m_begin + FV_ROWS);
+  for (int m = m_begin + rt; m < m_end; m += 2 * FV_INFLIGHT) {
+    float2 w[FV_INFLIGHT];
+#pragma unroll
+    for (int u = 0; u < FV_INFLIGHT; ++u) {
+      const int mm = m + 2 * u;
+      w[u] = mm < m_end ? __ldcs(reinterpret_cast<const float2*>(W + (int64_t)mm * f.cols + n)) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < FV_INFLIGHT; ++u) {
+      const int mm = m + 2 * u;
+      if (mm >= m_end) break;
+      const float* lr = L + (int64_t)mm * f.rank;
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= f.rank) break;
+        const float lv = __ldg(lr + j);
+        acc.x = fmaf(lv, rv[j].x, acc.x);
+        acc.y = fmaf(lv, rv[j].y, acc.y);
+      }
+      __stcs(reinterpret_cast<float2*>(O + (int64_t)mm * f.cols + n),
+             make_float2(w[u].x + s * acc.x, w[u].y + s * acc.y));
+    }
   }
 }
 
@@ -190,17 +269,32 @@ int launch_lora_fold(const void* W, const void* A, const void* B, const float* s
   const bool aligned16 = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(W) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (w_bs % 8 == 0);
   if (dtype == STAGEML_F32) {
-    const int64_t n_el = (int64_t)rows * cols;
-    const unsigned gx = (unsigned)std::min<int64_t>((n_el + 255) / 256, 8 * (int64_t)sm_count());
-    (fold_scalar_kernel<float><<<dim3(gx, batch), 256, 0, stream>>>(f), ::sb::count_launch());
+    const bool vec2 = (cols % 2 == 0) && (reinterpret_cast<uintptr_t>(W) % 8 == 0) &&
+                      (reinterpret_cast<uintptr_t>(out) % 8 == 0) && (w_bs % 2 == 0) && rank <= 16;
+    if (vec2) {
+      dim3 grid((cols / 2 + 127) / 128, (rows + FV_ROWS - 1) / FV_ROWS, batch);
+      SB_CHECK_ARG(grid.y <= 65535u, "lora_fold: too many rows");
+      (fold_f32_vec_kernel<<<grid, 256, 0, stream>>>(f), ::sb::count_launch());
+    } else {
+      const int64_t n_el = (int64_t)rows * cols;
+      const unsigned gx = (unsigned)std::min<int64_t>((n_el + 255) / 256, 8 * (int64_t)sm_count());
+      (fold_scalar_kernel<float><<<dim3(gx, batch), 256, 0, stream>>>(f), ::sb::count_launch());
+    }
   } else if (dtype == STAGEML_BF16 || dtype == STAGEML_F16) {
     if (aligned16 && rank <= 64) {
-      dim3 grid((cols + FT_N - 1) / FT_N, (rows + FT_M - 1) / FT_M, batch);
-      SB_CHECK_ARG(grid.y <= 65535u, "lora_fold: too many rows");
-      if (dtype == STAGEML_BF16)
-        (fold_mma_kernel<bf16><<<grid, 256, 0, stream>>>(f), ::sb::count_launch());
-      else
-        (fold_mma_kernel<f16><<<grid, 256, 0, stream>>>(f), ::sb::count_launch());
+      const int64_t gx = (int64_t)((cols + FT_N - 1) / FT_N) * batch;
+      dim3 grid((unsigned)gx, (rows + FT_M - 1) / FT_M, 1);
+      SB_CHECK_ARG(grid.y <= 65535u && gx < (int64_t(1) << 31), "lora_fold: too many rows");
+      const size_t smem = fold_mma_smem(rank, 2);
+      if (dtype == STAGEML_BF16) {
+        SB_CUDA_CHECK(cudaFuncSetAttribute(fold_mma_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem));
+        (fold_mma_kernel<bf16><<<grid, 256, smem, stream>>>(f, batch), ::sb::count_launch());
+      } else {
+        SB_CUDA_CHECK(cudaFuncSetAttribute(fold_mma_kernel<f16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem));
+        (fold_mma_kernel<f16><<<grid, 256, smem, stream>>>(f, batch), ::sb::count_launch());
+      }
     } else {
       const int64_t n_el = (int64_t)rows * cols;
       const unsigned gx = (unsigned)std::min<int64_t>((n_el + 255) / 256, 8 * (int64_t)sm_count());

@@ -2,10 +2,13 @@
 // (benchmarks/triton_lora_equivalence_check.py:11-22):
 //   dynamic: y = x W + s (x A) B        folded: y = x W'
 // x [M, in] with M <= 16, W [in, out], A [in, r], B [r, out]. Real fp32 FMAs
-// (no TF32). HBM-bound on the W read: split-K over (column block, K slice)
-// CTAs with float4 loads of W, fp32 partials reduced in a fixed order by a
-// second kernel that also applies the rank-r expansion, so results are
-// deterministic.
+// (no TF32). HBM-bound on the W read (4 B per element): split-K over
+// (512-column block, K slice) CTAs of 128 column threads x G row groups; every
+// thread issues RPT independent 16-byte streaming loads of W before its FMAs, so
+// each SM keeps ~128 KB in flight; the row groups are summed in shared memory in
+// a fixed order and one fp32 partial per (K slice, row, column) is written. A
+// second kernel (a programmatic dependent launch) adds the partials in slice
+// order and applies the rank-r expansion, so results are deterministic.
 #include <mutex>
 
 #include "common.cuh"
@@ -19,58 +22,119 @@ namespace {
 constexpr int GV_COLS = 512;   // columns per CTA (128 threads x float4)
 constexpr int GV_MAXM = 16;
 
-__global__ void __launch_bounds__(128) gemv_partial_kernel(const float* __restrict__ x, const float* __restrict__ W,
-                                                           const float* __restrict__ A, int M, int in_f, int out_f,
-                                                           int rank, int slice, float* __restrict__ part,
-                                                           float* __restrict__ xa_part) {
-  extern __shared__ float xs[];  // [M][slice]
+// MB: rows of x handled (>= M); G: row groups per CTA; RPT: W rows per thread per pass.
+template <int MB, int G, int RPT>
+__global__ void __launch_bounds__(128 * G) gemv_partial_kernel(const float* __restrict__ x, const float* __restrict__ W,
+                                                               const float* __restrict__ A, int M, int in_f, int out_f,
+                                                               int rank, int slice, float* __restrict__ part,
+                                                               float* __restrict__ xa_part) {
+  extern __shared__ float sm[];  // xs [MB][slice], then the row groups' sums [G][MB][GV_COLS]
+  float* xs = sm;
+  float* red = sm + MB * slice;
+  pdl_trigger();  // the reduce kernel may be scheduled now; it waits for this grid before reading
   const int ks = blockIdx.y;
   const int i0 = ks * slice, i1 = min(in_f, i0 + slice);
   const int ni = i1 - i0;
-  for (int t = threadIdx.x; t < M * slice; t += blockDim.x) {
+  for (int t = threadIdx.x; t < MB * slice; t += blockDim.x) {
     const int m = t / slice, i = t % slice;
-    xs[t] = (i < ni) ? x[(int64_t)m * in_f + i0 + i] : 0.f;
+    xs[t] = (m < M && i < ni) ? x[(int64_t)m * in_f + i0 + i] : 0.f;
   }
   __syncthreads();
-  const int c = blockIdx.x * GV_COLS + threadIdx.x * 4;
+  const int ct = threadIdx.x & 127, g = threadIdx.x >> 7;
+  const int c = blockIdx.x * GV_COLS + ct * 4;
+  const bool vec = (c + 4 <= out_f) && (out_f % 4 == 0);
+  float acc[MB][4];
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
   if (c < out_f) {
-    float acc[GV_MAXM][4];
+    for (int base = g * RPT; base < ni; base += G * RPT) {
+      float4 w[RPT];
 #pragma unroll
-    for (int m = 0; m < GV_MAXM; ++m)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
-    const bool vec = (c + 4 <= out_f) && (out_f % 4 == 0);
-    for (int i = 0; i < ni; ++i) {
-      float w[4];
-      const float* wr = W + (int64_t)(i0 + i) * out_f + c;
-      if (vec) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(wr));
-        w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) w[q] = (c + q < out_f) ? wr[q] : 0.f;
+      for (int r = 0; r < RPT; ++r) {  // all loads of the pass in flight before the first FMA
+        const int i = base + r;
+        const float* wr = W + (int64_t)(i0 + i) * out_f + c;
+        if (i < ni && vec) {
+          w[r] = __ldcs(reinterpret_cast<const float4*>(wr));
+        } else if (i < ni) {
+          w[r].x = wr[0];
+          w[r].y = c + 1 < out_f ? wr[1] : 0.f;
+          w[r].z = c + 2 < out_f ? wr[2] : 0.f;
+          w[r].w = c + 3 < out_f ? wr[3] : 0.f;
+        } else {
+          w[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
 #pragma unroll
-      for (int m = 0; m < GV_MAXM; ++m)
-        if (m < M) {
+      for (int r = 0; r < RPT; ++r) {
+        const int i = min(base + r, slice - 1);  // rows past ni carry zero weights
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
           const float xv = xs[m * slice + i];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) acc[m][q] = fmaf(xv, w[q], acc[m][q]);
+          acc[m][0] = fmaf(xv, w[r].x, acc[m][0]);
+          acc[m][1] = fmaf(xv, w[r].y, acc[m][1]);
+          acc[m][2] = fmaf(xv, w[r].z, acc[m][2]);
+          acc[m][3] = fmaf(xv, w[r].w, acc[m][3]);
         }
+      }
     }
-#pragma unroll
-    for (int m = 0; m < GV_MAXM; ++m)
-      if (m < M)
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (c + q < out_f) part[((int64_t)ks * M + m) * out_f + c + q] = acc[m][q];
   }
-  if (A && blockIdx.x == 0) {
-    for (int t = threadIdx.x; t < M * rank; t += blockDim.x) {
-      const int m = t / rank, j = t % rank;
-      float a = 0.f;
-      for (int i = 0; i < ni; ++i) a = fmaf(xs[m * slice + i], A[(int64_t)(i0 + i) * rank + j], a);
-      xa_part[((int64_t)ks * M + m) * rank + j] = a;
+  // row groups summed in group order
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) red[((size_t)g * MB + m) * GV_COLS + ct * 4 + q] = acc[m][q];
+  __syncthreads();
+  for (int t = threadIdx.x; t < MB * GV_COLS; t += blockDim.x) {
+    const int m = t / GV_COLS, cc = t % GV_COLS;
+    const int col = blockIdx.x * GV_COLS + cc;
+    if (m >= M || col >= out_f) continue;
+    float v = red[(size_t)m * GV_COLS + cc];
+#pragma unroll
+    for (int gg = 1; gg < G; ++gg) v += red[((size_t)gg * MB + m) * GV_COLS + cc];
+    part[((int64_t)ks * M + m) * out_f + col] = v;
+  }
+  if (A) {
+    // x A over this slice: the column blocks share the rank columns; every thread sums its
+    // rows (fixed order), then warps (shuffle tree) and warps in order: deterministic
+    const int jpb = (rank + gridDim.x - 1) / gridDim.x;
+    const int j0 = blockIdx.x * jpb, nj = max(0, min(rank, j0 + jpb) - j0);
+    const int npair = M * nj;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    float* wsum = red;  // [nwarps][16], reused once every thread has read its sums above
+    __syncthreads();
+    for (int p0 = 0; p0 < npair; p0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) v[q] = 0.f;
+      for (int i = threadIdx.x; i < ni; i += blockDim.x) {
+        const float* arow = A + (int64_t)(i0 + i) * rank;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int pr = p0 + q;
+          if (pr < npair) {
+            const int m = pr / nj, j = j0 + pr % nj;
+            v[q] = fmaf(xs[m * slice + i], __ldg(arow + j), v[q]);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v[q] += __shfl_xor_sync(0xffffffffu, v[q], off);
+      if (lane == 0)
+#pragma unroll
+        for (int q = 0; q < 16; ++q) wsum[warp * 16 + q] = v[q];
+      __syncthreads();
+      if (threadIdx.x < 16 && p0 + (int)threadIdx.x < npair) {
+        const int pr = p0 + threadIdx.x;
+        const int m = pr / nj, j = j0 + pr % nj;
+        float a = 0.f;
+        for (int w = 0; w < nwarps; ++w) a += wsum[w * 16 + threadIdx.x];
+        xa_part[((int64_t)ks * M + m) * rank + j] = a;
+      }
+      __syncthreads();
     }
   }
 }
@@ -79,6 +143,7 @@ __global__ void gemv_reduce_kernel(const float* __restrict__ part, const float* 
                                    const float* __restrict__ B, float scale, int M, int out_f, int rank, int KS,
                                    float* __restrict__ y) {
   extern __shared__ float xa[];  // [M][rank]
+  pdl_wait();  // the partials of the kernel before
   if (B) {
     for (int t = threadIdx.x; t < M * rank; t += blockDim.x) {
       float a = 0.f;
@@ -101,12 +166,27 @@ __global__ void gemv_reduce_kernel(const float* __restrict__ part, const float* 
   }
 }
 
+// K slices: two (column block, slice) items per SM in all (one resident 512-thread CTA per
+// SM for two waves), slices at least 32 rows.
 void gemv_plan(int in_f, int out_f, int* KS, int* slice) {
   const int ncb = (out_f + GV_COLS - 1) / GV_COLS;
-  int ks = std::max(1, (8 * sm_count() + ncb - 1) / ncb);
+  int ks = std::max(1, (2 * sm_count() + ncb - 1) / ncb);
   ks = std::min(ks, std::max(1, (in_f + 31) / 32));
   *slice = (in_f + ks - 1) / ks;
   *KS = (in_f + *slice - 1) / *slice;
+}
+
+template <int MB, int G, int RPT>
+int launch_gemv_partial(const float* x, const float* W, const float* A, int M, int in_f, int out_f, int rank,
+                        int KS, int slice, float* part, float* xa_part, cudaStream_t stream) {
+  const size_t smem = ((size_t)MB * slice + (size_t)G * MB * GV_COLS) * 4;
+  SB_CHECK_ARG(smem <= 200 * 1024, "lora_gemv_f32: K slice too large");
+  auto kern = gemv_partial_kernel<MB, G, RPT>;
+  SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((out_f + GV_COLS - 1) / GV_COLS, KS);
+  (kern<<<grid, 128 * G, smem, stream>>>(x, W, A, M, in_f, out_f, rank, slice, part, xa_part), ::sb::count_launch());
+  SB_CUDA_CHECK(cudaGetLastError());
+  return STAGEML_OK;
 }
 
 }  // namespace
@@ -132,16 +212,17 @@ int launch_gemv_f32(const float* x, const float* W, const float* A, const float*
   float* part = static_cast<float*>(ws);
   float* xa_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
                                             ((((size_t)KS * M * out_f * 4) + 255) & ~size_t(255)));
-  const size_t smem1 = (size_t)M * slice * 4;
-  SB_CHECK_ARG(smem1 <= 200 * 1024, "lora_gemv_f32: K slice too large");
-  SB_CUDA_CHECK(cudaFuncSetAttribute(gemv_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1));
-  dim3 g1((out_f + GV_COLS - 1) / GV_COLS, KS);
-  (gemv_partial_kernel<<<g1, 128, smem1, stream>>>(x, W, A, M, in_f, out_f, A ? rank : 0, slice, part, xa_part), ::sb::count_launch());
-  SB_CUDA_CHECK(cudaGetLastError());
+  const int rk = A ? rank : 0;
+  if (M == 1)
+    SB_TRY((launch_gemv_partial<1, 4, 16>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
+  else if (M <= 4)
+    SB_TRY((launch_gemv_partial<4, 4, 8>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
+  else
+    SB_TRY((launch_gemv_partial<16, 2, 8>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
   const size_t smem2 = (size_t)M * (A ? rank : 1) * 4;
-  (gemv_reduce_kernel<<<(out_f + 255) / 256, 256, smem2, stream>>>(part, xa_part, A ? B : nullptr, scale, M, out_f,
-                                                                   A ? rank : 0, KS, y), ::sb::count_launch());
-  SB_CUDA_CHECK(cudaGetLastError());
+  SB_CUDA_CHECK(launch_kernel(gemv_reduce_kernel, dim3((out_f + 255) / 256), dim3(256), smem2, stream, pdl_enabled(),
+                              part, xa_part, A ? B : nullptr, scale, M, out_f, rk, KS, y));
+  ::sb::count_launch();
   return STAGEML_OK;
 }
 

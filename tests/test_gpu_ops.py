@@ -369,7 +369,9 @@ def test_lora_linear_bad_tenant_is_reported(ops):
 @pytest.mark.parametrize("dtype,layout,rows,cols,r,batch,bcast", [
     (torch.bfloat16, 0, 512, 384, 16, 3, True), (torch.float16, 0, 300, 200, 8, 2, False),
     (torch.bfloat16, 1, 256, 512, 16, 1, True), (torch.float32, 0, 100, 60, 4, 2, True),
-    (torch.float32, 1, 1024, 512, 16, 1, True), (torch.bfloat16, 0, 12, 20, 3, 1, True)])
+    (torch.float32, 1, 1024, 512, 16, 1, True), (torch.bfloat16, 0, 12, 20, 3, 1, True),
+    (torch.float32, 0, 70, 36, 24, 2, False), (torch.float32, 1, 33, 13, 8, 1, True),
+    (torch.bfloat16, 0, 130, 264, 40, 4, True), (torch.float16, 1, 200, 136, 16, 3, False)])
 def test_lora_fold(ops, dtype, layout, rows, cols, r, batch, bcast):
     W = rand((rows, cols) if bcast else (batch, rows, cols), 1.0, dtype, 51)
     if layout == 0:
@@ -410,6 +412,24 @@ def test_single_lora_gemv_config1(ops):
     yf = ops.lora_gemv_f32(w["x"], Wf)
     assert rel_l2(f64(yf), ref) < TOL32
     assert rel_l2(f64(yf), f64(y)) < TOL32
+
+
+@pytest.mark.parametrize("M,din,dout,r", [(1, 4096, 4096, 16), (3, 1000, 770, 8), (4, 64, 4099, 4),
+                                         (7, 3001, 512, 16), (16, 4096, 1030, 32), (1, 5, 3, 1)])
+def test_single_lora_gemv_shapes(ops, M, din, dout, r):
+    """The three row templates of the split-K GEMV (1, <= 4, <= 16 rows of x), outputs that are
+    not a multiple of 4 (scalar tail), slices that do not divide the input, fp32 within 1e-5."""
+    g = torch.Generator().manual_seed(M * 7 + din)
+    x = torch.randn(M, din, generator=g).to(DEV)
+    W = (torch.randn(din, dout, generator=g) / din ** 0.5).to(DEV)
+    A = (torch.randn(din, r, generator=g) / din ** 0.5).to(DEV)
+    B = (torch.randn(r, dout, generator=g) / r ** 0.5).to(DEV)
+    y = ops.lora_gemv_f32(x, W, A, B, 1.5)
+    ref = olora.single_lora(f64(x), f64(W), f64(A), f64(B), 1.5)
+    assert rel_l2(f64(y), ref) < TOL32
+    y0 = ops.lora_gemv_f32(x, W)
+    assert rel_l2(f64(y0), f64(x) @ f64(W)) < TOL32
+    assert torch.equal(ops.lora_gemv_f32(x, W, A, B, 1.5), y)  # deterministic
 
 
 def test_single_lora_vs_reference_golden(ops, golden):

@@ -67,9 +67,12 @@ def test_noalloc_gemv_matches_workspace_entry_point():
     torch.cuda.synchronize()
     assert _rel(yf, x @ W) <= 1e-5
 
-    # a shape whose partial sums do not fit the static scratch is refused before any launch
+    # a shape whose partial sums do not fit the static scratch (16 rows x 300,000 fp32 output
+    # columns need more than 16 MiB) is refused before any launch: nothing is read or written
+    wide = 300_000
+    assert lib.stageml_lora_gemv_f32_workspace_bytes(16, din, wide, 0) > 16 << 20
     big = torch.empty(16, din, device=DEV)
-    out = torch.empty(16, dout, device=DEV)
-    rc = lib.stageml_lora_gemv_f32_noalloc(_ptr(big), _ptr(W), None, None, 0.0, 16, din, dout, 0, _ptr(out), stream)
+    out = torch.empty(16, wide, device=DEV)
+    rc = lib.stageml_lora_gemv_f32_noalloc(_ptr(big), _ptr(W), None, None, 0.0, 16, din, wide, 0, _ptr(out), stream)
     assert rc == capi.ERR_INVALID_ARG
     assert b"static scratch" in lib.stageml_last_error()
