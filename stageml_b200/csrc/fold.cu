@@ -10,10 +10,10 @@
 // element, 8 per fp32 element). The rank-r product costs r FMAs per element, which
 // for r = 16 at HBM speed would saturate the fp32 pipes on 16-bit weights, so the
 // 16-bit path computes it with warp-level tensor-core MMAs (m16n8k16, fp32
-// accumulate) on a 64 x 128 tile staged in shared memory with its L and R slices,
-// with 16-byte loads and stores of W and W'. fp32 (rank <= 16) keeps each thread's
-// R columns in registers and streams rows with 8-byte accesses; other fp32 and
-// unaligned shapes use plain fp32 FMAs, one element per thread.
+// accumulate) on a 64 x 128 tile staged in shared memory (cp.async) with its L and R
+// slices, with 16-byte accesses of W and W'. fp32 (rank <= 16) keeps each thread's R
+// columns in registers and streams W rows through a cp.async ring in shared memory;
+// other fp32 and unaligned shapes use plain fp32 FMAs, one element per thread.
 #include "common.cuh"
 #include "host_util.h"
 #include "kernels.h"
@@ -67,6 +67,18 @@ __device__ __forceinline__ void mma16816<f16>(float (&c)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void fold_cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void fold_cp_async8(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(valid ? 8 : 0) : "memory");
+}
+__device__ __forceinline__ void fold_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void fold_cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 struct FoldArgs {
   const void* W;
   const void* A;
@@ -114,14 +126,15 @@ __global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f, int bat
   const T *L, *R;
   fold_operands<T>(f, b, &L, &R);
   const float s = f.scale[b];
-  // 1. W tile -> shared (16-byte accesses), then the L and R tiles (zero past the rank / the edges)
+  // 1. W tile -> shared by cp.async (16-byte pieces, zero-filled past the edges), in flight
+  //    while the L and R tiles are loaded (zero past the rank / the edges)
   for (int i = threadIdx.x; i < FT_M * FT_N / 8; i += 256) {
     const int r = i / (FT_N / 8), c8 = (i % (FT_N / 8)) * 8;
     const int gm = m0 + r, gn = n0 + c8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (gm < f.rows && gn < f.cols) v = __ldg(reinterpret_cast<const uint4*>(W + (int64_t)gm * f.cols + gn));
-    *reinterpret_cast<uint4*>(&tile[r][c8]) = v;
+    const bool v = gm < f.rows && gn < f.cols;
+    fold_cp_async16(smem_u32(&tile[r][c8]), v ? (const void*)(W + (int64_t)gm * f.cols + gn) : f.W, v);
   }
+  fold_cp_commit();
   const T zero = from_f32<T>(0.f);
   for (int i = threadIdx.x; i < FT_M * rk16; i += 256) {
     const int r = i / rk16, j = i % rk16;
@@ -141,6 +154,7 @@ __global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f, int bat
     }
     *reinterpret_cast<uint4*>(&Rs(j, c8)) = v;
   }
+  fold_cp_wait<0>();
   __syncthreads();
   // 2. rank-r product on tensor cores (operands from shared memory), added into the tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -189,52 +203,75 @@ __global__ void __launch_bounds__(256) fold_mma_kernel(const FoldArgs f, int bat
   }
 }
 
-// fp32, rank <= 16, even cols, 8-byte aligned rows: each thread owns 2 columns and keeps
-// their rank-r slice of R in registers (32); 128 column threads x 2 row threads per CTA
-// walk FV_ROWS rows with eight rows' W loads in flight before their FMAs (3-4 CTAs per SM,
-// ~64 KB of W reads in flight per SM); the L row is read by every thread of a row (a
-// broadcast). fp32 FMAs in j order (no TF32).
-constexpr int FV_ROWS = 64;
-constexpr int FV_INFLIGHT = 6;
-__global__ void __launch_bounds__(256, 3) fold_f32_vec_kernel(const FoldArgs f) {
+// fp32, rank <= 16, even cols, 8-byte aligned rows: one resident wave of 128-thread CTAs,
+// each folding a contiguous range of rows of one 256-column block. Every thread owns 2
+// columns and keeps their rank-r slice of R in registers; the W rows and their L rows
+// stream through a 4-stage cp.async ring of 8-row stages (three in flight, ~150 KB per SM
+// at 6 CTAs per SM), independent of registers. fp32 FMAs in j order (no TF32); W' stores
+// are streaming.
+constexpr int FC_COLS = 256, FC_SROWS = 8, FC_STAGES = 4, FC_CTAS_PER_SM = 6;
+__global__ void __launch_bounds__(128) fold_f32_ring_kernel(const FoldArgs f, int rows_per_cta) {
+  __shared__ __align__(16) float Ws[FC_STAGES][FC_SROWS][FC_COLS];
+  __shared__ __align__(16) float Lss[FC_STAGES][FC_SROWS][16];
   const int b = blockIdx.z;
   const float* W = static_cast<const float*>(f.W) + (int64_t)b * f.w_bs;
   float* O = static_cast<float*>(f.out) + (int64_t)b * f.rows * f.cols;
   const float *L, *R;
   fold_operands<float>(f, b, &L, &R);
   const float s = f.scale[b];
-  const int ct = threadIdx.x & 127, rt = threadIdx.x >> 7;
-  const int n = (blockIdx.x * 128 + ct) * 2;
-  if (n >= f.cols) return;
+  const int t = threadIdx.x;
+  const int n = blockIdx.x * FC_COLS + t * 2;
+  const bool col_ok = n < f.cols;
+  const int m0 = blockIdx.y * rows_per_cta, m_end = min(f.rows, m0 + rows_per_cta);
+  if (m0 >= m_end) return;
+  const int nst = (m_end - m0 + FC_SROWS - 1) / FC_SROWS;
+  auto issue = [&](int st) {
+    if (st < nst) {
+      const int slot = st % FC_STAGES;
+#pragma unroll
+      for (int r = 0; r < FC_SROWS; ++r) {
+        const int row = m0 + st * FC_SROWS + r;
+        const bool v = col_ok && row < m_end;
+        fold_cp_async8(smem_u32(&Ws[slot][r][t * 2]), v ? (const void*)(W + (int64_t)row * f.cols + n) : f.W, v);
+      }
+      {  // the stage's L rows: 8 rows x 16 ranks, one 4-byte piece per thread (zero past the rank)
+        const int r = t >> 4, j = t & 15, row = m0 + st * FC_SROWS + r;
+        const bool v = row < m_end && j < f.rank;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(&Lss[slot][r][j])),
+                     "l"(v ? (const void*)(L + (int64_t)row * f.rank + j) : f.scale), "r"(v ? 4 : 0)
+                     : "memory");
+      }
+    }
+    fold_cp_commit();  // possibly empty: keeps the group count in step
+  };
+#pragma unroll
+  for (int st = 0; st < FC_STAGES - 1; ++st) issue(st);
   float2 rv[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j)
-    rv[j] = j < f.rank ? __ldg(reinterpret_cast<const float2*>(R + (int64_t)j * f.cols + n)) : make_float2(0.f, 0.f);
-  const int m_begin = blockIdx.y * FV_ROWS, m_end = min(f.rows, m_begin + FV_ROWS);
-  for (int m = m_begin + rt; m < m_end; m += 2 * FV_INFLIGHT) {
-    float2 w[FV_INFLIGHT];
+    rv[j] = (col_ok && j < f.rank) ? __ldg(reinterpret_cast<const float2*>(R + (int64_t)j * f.cols + n))
+                                   : make_float2(0.f, 0.f);
+  for (int st = 0; st < nst; ++st) {
+    fold_cp_wait<FC_STAGES - 2>();  // stage st has landed (st + 1, st + 2 may still be in flight)
+    __syncthreads();                // visible to every thread; every thread is done with stage st - 1
+    issue(st + FC_STAGES - 1);      // refills the slot of stage st - 1
+    const int slot = st % FC_STAGES;
 #pragma unroll
-    for (int u = 0; u < FV_INFLIGHT; ++u) {
-      const int mm = m + 2 * u;
-      w[u] = mm < m_end ? __ldcs(reinterpret_cast<const float2*>(W + (int64_t)mm * f.cols + n)) : make_float2(0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < FV_INFLIGHT; ++u) {
-      const int mm = m + 2 * u;
-      if (mm >= m_end) break;
-      const float* lr = L + (int64_t)mm * f.rank;
+    for (int r = 0; r < FC_SROWS; ++r) {
+      const int row = m0 + st * FC_SROWS + r;
+      if (row >= m_end || !col_ok) break;
+      const float2 w = *reinterpret_cast<const float2*>(&Ws[slot][r][t * 2]);
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        if (j >= f.rank) break;
-        const float lv = __ldg(lr + j);
+        const float lv = Lss[slot][r][j];
         acc.x = fmaf(lv, rv[j].x, acc.x);
         acc.y = fmaf(lv, rv[j].y, acc.y);
       }
-      __stcs(reinterpret_cast<float2*>(O + (int64_t)mm * f.cols + n),
-             make_float2(w[u].x + s * acc.x, w[u].y + s * acc.y));
+      __stcs(reinterpret_cast<float2*>(O + (int64_t)row * f.cols + n), make_float2(w.x + s * acc.x, w.y + s * acc.y));
     }
   }
+  fold_cp_wait<0>();
 }
 
 // One output element per thread, fp32 FMAs in j order.
@@ -272,9 +309,15 @@ int launch_lora_fold(const void* W, const void* A, const void* B, const float* s
     const bool vec2 = (cols % 2 == 0) && (reinterpret_cast<uintptr_t>(W) % 8 == 0) &&
                       (reinterpret_cast<uintptr_t>(out) % 8 == 0) && (w_bs % 2 == 0) && rank <= 16;
     if (vec2) {
-      dim3 grid((cols / 2 + 127) / 128, (rows + FV_ROWS - 1) / FV_ROWS, batch);
+      // one resident wave: the row ranges of every column block and matrix fill the SMs once
+      const int ncb = (cols + FC_COLS - 1) / FC_COLS;
+      const int64_t slots = (int64_t)FC_CTAS_PER_SM * sm_count();
+      const int nrb = (int)std::max<int64_t>(1, std::min<int64_t>(slots / std::max<int64_t>(1, (int64_t)ncb * batch),
+                                                                  (rows + FC_SROWS - 1) / FC_SROWS));
+      const int rows_per = ((rows + nrb - 1) / nrb + FC_SROWS - 1) / FC_SROWS * FC_SROWS;
+      dim3 grid(ncb, (rows + rows_per - 1) / rows_per, batch);
       SB_CHECK_ARG(grid.y <= 65535u, "lora_fold: too many rows");
-      (fold_f32_vec_kernel<<<grid, 256, 0, stream>>>(f), ::sb::count_launch());
+      (fold_f32_ring_kernel<<<grid, 128, 0, stream>>>(f, rows_per), ::sb::count_launch());
     } else {
       const int64_t n_el = (int64_t)rows * cols;
       const unsigned gx = (unsigned)std::min<int64_t>((n_el + 255) / 256, 8 * (int64_t)sm_count());

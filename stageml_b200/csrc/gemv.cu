@@ -3,12 +3,11 @@
 //   dynamic: y = x W + s (x A) B        folded: y = x W'
 // x [M, in] with M <= 16, W [in, out], A [in, r], B [r, out]. Real fp32 FMAs
 // (no TF32). HBM-bound on the W read (4 B per element): split-K over
-// (512-column block, K slice) CTAs of 128 column threads x G row groups; every
-// thread issues RPT independent 16-byte streaming loads of W before its FMAs, so
-// each SM keeps ~128 KB in flight; the row groups are summed in shared memory in
-// a fixed order and one fp32 partial per (K slice, row, column) is written. A
-// second kernel (a programmatic dependent launch) adds the partials in slice
-// order and applies the rank-r expansion, so results are deterministic.
+// (512-column block, K slice) CTAs in one resident wave; each CTA streams its
+// slice of W through a cp.async ring in shared memory (~144 KB in flight per SM)
+// and writes one fp32 partial per (K slice, row, column). A second kernel (a
+// programmatic dependent launch) adds the partials in slice order and applies
+// the rank-r expansion, so results are deterministic.
 #include <mutex>
 
 #include "common.cuh"
@@ -22,93 +21,109 @@ namespace {
 constexpr int GV_COLS = 512;   // columns per CTA (128 threads x float4)
 constexpr int GV_MAXM = 16;
 
-// MB: rows of x handled (>= M); G: row groups per CTA; RPT: W rows per thread per pass.
-template <int MB, int G, int RPT>
-__global__ void __launch_bounds__(128 * G) gemv_partial_kernel(const float* __restrict__ x, const float* __restrict__ W,
-                                                               const float* __restrict__ A, int M, int in_f, int out_f,
-                                                               int rank, int slice, float* __restrict__ part,
-                                                               float* __restrict__ xa_part) {
-  extern __shared__ float sm[];  // xs [MB][slice], then the row groups' sums [G][MB][GV_COLS]
-  float* xs = sm;
-  float* red = sm + MB * slice;
+__device__ __forceinline__ void gv_cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void gv_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void gv_cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One resident wave of 128-thread CTAs: CTA (column block, K slice) owns 512 columns (4
+// per thread) and a contiguous K slice of `slice` rows, which streams through a 4-stage
+// cp.async ring of 8-row stages of W (16 KB each; three in flight, ~144 KB per SM at 3
+// CTAs per SM) while every thread accumulates its columns for the MB rows of x in
+// registers, rows in order. MB: rows of x handled (>= M).
+constexpr int GV_SROWS = 8, GV_STAGES = 4, GV_CTAS_PER_SM = 3;
+template <int MB>
+__global__ void __launch_bounds__(128) gemv_partial_kernel(const float* __restrict__ x, const float* __restrict__ W,
+                                                           const float* __restrict__ A, int M, int in_f, int out_f,
+                                                           int rank, int slice, float* __restrict__ part,
+                                                           float* __restrict__ xa_part) {
+  extern __shared__ __align__(16) float sm[];  // W ring [GV_STAGES][GV_SROWS][GV_COLS], xs [MB][slice], warp sums
+  float* ring = sm;
+  float* xs = sm + GV_STAGES * GV_SROWS * GV_COLS;
+  float* wsum = xs + MB * slice;
   pdl_trigger();  // the reduce kernel may be scheduled now; it waits for this grid before reading
   const int ks = blockIdx.y;
   const int i0 = ks * slice, i1 = min(in_f, i0 + slice);
   const int ni = i1 - i0;
-  for (int t = threadIdx.x; t < MB * slice; t += blockDim.x) {
-    const int m = t / slice, i = t % slice;
-    xs[t] = (m < M && i < ni) ? x[(int64_t)m * in_f + i0 + i] : 0.f;
-  }
-  __syncthreads();
-  const int ct = threadIdx.x & 127, g = threadIdx.x >> 7;
-  const int c = blockIdx.x * GV_COLS + ct * 4;
+  const int t = threadIdx.x;
+  const int c = blockIdx.x * GV_COLS + t * 4;
   const bool vec = (c + 4 <= out_f) && (out_f % 4 == 0);
+  const int nst = (ni + GV_SROWS - 1) / GV_SROWS;
+  auto issue = [&](int st) {
+    if (st < nst && vec) {
+      float* dst = ring + (size_t)(st % GV_STAGES) * GV_SROWS * GV_COLS + t * 4;
+#pragma unroll
+      for (int r = 0; r < GV_SROWS; ++r) {
+        const int i = st * GV_SROWS + r;
+        const bool v = i < ni;
+        gv_cp_async16(smem_u32(dst + r * GV_COLS), v ? (const void*)(W + (int64_t)(i0 + i) * out_f + c) : W, v);
+      }
+    }
+    gv_cp_commit();  // possibly empty: keeps the group count in step
+  };
+#pragma unroll
+  for (int st = 0; st < GV_STAGES - 1; ++st) issue(st);
+  for (int e = t; e < MB * slice; e += blockDim.x) {
+    const int m = e / slice, i = e % slice;
+    xs[e] = (m < M && i < ni) ? x[(int64_t)m * in_f + i0 + i] : 0.f;
+  }
   float acc[MB][4];
 #pragma unroll
   for (int m = 0; m < MB; ++m)
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
-  if (c < out_f) {
-    for (int base = g * RPT; base < ni; base += G * RPT) {
-      float4 w[RPT];
+  __syncthreads();  // xs
+  for (int st = 0; st < nst; ++st) {
+    gv_cp_wait<GV_STAGES - 2>();  // this thread's copies of stage st have landed (it reads only those)
+    issue(st + GV_STAGES - 1);    // refills the slot of stage st - 1, which this thread has finished
+    const float* stage = ring + (size_t)(st % GV_STAGES) * GV_SROWS * GV_COLS + t * 4;
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) {  // all loads of the pass in flight before the first FMA
-        const int i = base + r;
+    for (int r = 0; r < GV_SROWS; ++r) {
+      const int i = st * GV_SROWS + r;
+      if (i >= ni) break;
+      float4 w;
+      if (vec) {
+        w = *reinterpret_cast<const float4*>(stage + r * GV_COLS);
+      } else {  // ragged column tail: direct loads
         const float* wr = W + (int64_t)(i0 + i) * out_f + c;
-        if (i < ni && vec) {
-          w[r] = __ldcs(reinterpret_cast<const float4*>(wr));
-        } else if (i < ni) {
-          w[r].x = wr[0];
-          w[r].y = c + 1 < out_f ? wr[1] : 0.f;
-          w[r].z = c + 2 < out_f ? wr[2] : 0.f;
-          w[r].w = c + 3 < out_f ? wr[3] : 0.f;
-        } else {
-          w[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        w.x = c < out_f ? wr[0] : 0.f;
+        w.y = c + 1 < out_f ? wr[1] : 0.f;
+        w.z = c + 2 < out_f ? wr[2] : 0.f;
+        w.w = c + 3 < out_f ? wr[3] : 0.f;
       }
 #pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int i = min(base + r, slice - 1);  // rows past ni carry zero weights
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
-          const float xv = xs[m * slice + i];
-          acc[m][0] = fmaf(xv, w[r].x, acc[m][0]);
-          acc[m][1] = fmaf(xv, w[r].y, acc[m][1]);
-          acc[m][2] = fmaf(xv, w[r].z, acc[m][2]);
-          acc[m][3] = fmaf(xv, w[r].w, acc[m][3]);
-        }
+      for (int m = 0; m < MB; ++m) {
+        const float xv = xs[m * slice + i];
+        acc[m][0] = fmaf(xv, w.x, acc[m][0]);
+        acc[m][1] = fmaf(xv, w.y, acc[m][1]);
+        acc[m][2] = fmaf(xv, w.z, acc[m][2]);
+        acc[m][3] = fmaf(xv, w.w, acc[m][3]);
       }
     }
   }
-  // row groups summed in group order
+  gv_cp_wait<0>();
 #pragma unroll
   for (int m = 0; m < MB; ++m)
+    if (m < M)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) red[((size_t)g * MB + m) * GV_COLS + ct * 4 + q] = acc[m][q];
-  __syncthreads();
-  for (int t = threadIdx.x; t < MB * GV_COLS; t += blockDim.x) {
-    const int m = t / GV_COLS, cc = t % GV_COLS;
-    const int col = blockIdx.x * GV_COLS + cc;
-    if (m >= M || col >= out_f) continue;
-    float v = red[(size_t)m * GV_COLS + cc];
-#pragma unroll
-    for (int gg = 1; gg < G; ++gg) v += red[((size_t)gg * MB + m) * GV_COLS + cc];
-    part[((int64_t)ks * M + m) * out_f + col] = v;
-  }
+      for (int q = 0; q < 4; ++q)
+        if (c + q < out_f) part[((int64_t)ks * M + m) * out_f + c + q] = acc[m][q];
   if (A) {
     // x A over this slice: the column blocks share the rank columns; every thread sums its
     // rows (fixed order), then warps (shuffle tree) and warps in order: deterministic
     const int jpb = (rank + gridDim.x - 1) / gridDim.x;
     const int j0 = blockIdx.x * jpb, nj = max(0, min(rank, j0 + jpb) - j0);
     const int npair = M * nj;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    float* wsum = red;  // [nwarps][16], reused once every thread has read its sums above
-    __syncthreads();
+    const int warp = t >> 5, lane = t & 31, nwarps = blockDim.x >> 5;
     for (int p0 = 0; p0 < npair; p0 += 16) {
       float v[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) v[q] = 0.f;
-      for (int i = threadIdx.x; i < ni; i += blockDim.x) {
+      for (int i = t; i < ni; i += blockDim.x) {
         const float* arow = A + (int64_t)(i0 + i) * rank;
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
@@ -127,11 +142,11 @@ __global__ void __launch_bounds__(128 * G) gemv_partial_kernel(const float* __re
 #pragma unroll
         for (int q = 0; q < 16; ++q) wsum[warp * 16 + q] = v[q];
       __syncthreads();
-      if (threadIdx.x < 16 && p0 + (int)threadIdx.x < npair) {
-        const int pr = p0 + threadIdx.x;
+      if (t < 16 && p0 + t < npair) {
+        const int pr = p0 + t;
         const int m = pr / nj, j = j0 + pr % nj;
         float a = 0.f;
-        for (int w = 0; w < nwarps; ++w) a += wsum[w * 16 + threadIdx.x];
+        for (int w = 0; w < nwarps; ++w) a += wsum[w * 16 + t];
         xa_part[((int64_t)ks * M + m) * rank + j] = a;
       }
       __syncthreads();
@@ -166,25 +181,26 @@ __global__ void gemv_reduce_kernel(const float* __restrict__ part, const float* 
   }
 }
 
-// K slices: two (column block, slice) items per SM in all (one resident 512-thread CTA per
-// SM for two waves), slices at least 32 rows.
+// K slices: one resident wave of GV_CTAS_PER_SM CTAs per SM over (column block, slice)
+// items, slices a multiple of the 8-row stage.
 void gemv_plan(int in_f, int out_f, int* KS, int* slice) {
   const int ncb = (out_f + GV_COLS - 1) / GV_COLS;
-  int ks = std::max(1, (2 * sm_count() + ncb - 1) / ncb);
-  ks = std::min(ks, std::max(1, (in_f + 31) / 32));
-  *slice = (in_f + ks - 1) / ks;
+  const int slots = GV_CTAS_PER_SM * sm_count();
+  int ks = std::max(1, slots / ncb);
+  ks = std::min(ks, std::max(1, (in_f + GV_SROWS - 1) / GV_SROWS));
+  *slice = ((in_f + ks - 1) / ks + GV_SROWS - 1) / GV_SROWS * GV_SROWS;
   *KS = (in_f + *slice - 1) / *slice;
 }
 
-template <int MB, int G, int RPT>
+template <int MB>
 int launch_gemv_partial(const float* x, const float* W, const float* A, int M, int in_f, int out_f, int rank,
                         int KS, int slice, float* part, float* xa_part, cudaStream_t stream) {
-  const size_t smem = ((size_t)MB * slice + (size_t)G * MB * GV_COLS) * 4;
+  const size_t smem = ((size_t)GV_STAGES * GV_SROWS * GV_COLS + (size_t)MB * slice + 4 * 16) * 4;
   SB_CHECK_ARG(smem <= 200 * 1024, "lora_gemv_f32: K slice too large");
-  auto kern = gemv_partial_kernel<MB, G, RPT>;
+  auto kern = gemv_partial_kernel<MB>;
   SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((out_f + GV_COLS - 1) / GV_COLS, KS);
-  (kern<<<grid, 128 * G, smem, stream>>>(x, W, A, M, in_f, out_f, rank, slice, part, xa_part), ::sb::count_launch());
+  (kern<<<grid, 128, smem, stream>>>(x, W, A, M, in_f, out_f, rank, slice, part, xa_part), ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
@@ -214,11 +230,11 @@ int launch_gemv_f32(const float* x, const float* W, const float* A, const float*
                                             ((((size_t)KS * M * out_f * 4) + 255) & ~size_t(255)));
   const int rk = A ? rank : 0;
   if (M == 1)
-    SB_TRY((launch_gemv_partial<1, 4, 16>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
+    SB_TRY((launch_gemv_partial<1>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
   else if (M <= 4)
-    SB_TRY((launch_gemv_partial<4, 4, 8>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
+    SB_TRY((launch_gemv_partial<4>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
   else
-    SB_TRY((launch_gemv_partial<16, 2, 8>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
+    SB_TRY((launch_gemv_partial<16>(x, W, A, M, in_f, out_f, rk, KS, slice, part, xa_part, stream)));
   const size_t smem2 = (size_t)M * (A ? rank : 1) * 4;
   SB_CUDA_CHECK(launch_kernel(gemv_reduce_kernel, dim3((out_f + 255) / 256), dim3(256), smem2, stream, pdl_enabled(),
                               part, xa_part, A ? B : nullptr, scale, M, out_f, rk, KS, y));
