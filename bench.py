@@ -803,13 +803,33 @@ def dense_arm(args):
         ms_f, _, n_f = _timed(lambda i: ops.lora_fold(Ws[i % 3], A8, B8, sc8, 0), args.steps, args.warmup, lib)
         g_f = _graph_timed(lambda i: ops.lora_fold(Ws[i % 3], A8, B8, sc8, 0), 12)
         fold_bytes = 4096 * 4096 * 2 * (1 + len(cached)) + (A8.numel() + B8.numel()) * 2
-        ms, st, n = _timed(lambda i: layers[i % 3](w["x"], names), args.steps, args.warmup, lib)
+        # the layer's op with its row groups / tenants resident on the device (what the class passes
+        # to it each call), and the class call itself (adapter names -> index tensors on the host)
+        lay0 = layers[0]
+        grp_t = torch.tensor([lay0.cached_name_to_index[nm] + 1 if nm in lay0.cached_name_to_index else 0
+                              for nm in names], dtype=torch.int32, device=dev)
+        ten_t = torch.tensor([-1 if nm in lay0.cached_name_to_index else lay0.adapter_index[nm] for nm in names],
+                             dtype=torch.int32, device=dev)
+
+        def op_call(i):
+            lay = layers[i % 3]
+            return ops.lora_linear(w["x"], lay.weight_bank, bias=lay.bias, row_group=grp_t, row_tenant=ten_t,
+                                   n_tenants=len(lay.adapter_order), rank=lay.rank_pad, lora_a=lay.lora_a,
+                                   lora_b=lay.lora_b, lora_scale=lay.lora_scale)
+
+        ref_y = layers[0](w["x"], names)
+        assert torch.equal(op_call(0), ref_y), "op call differs from the class call"
+        ms, st, n = _timed(op_call, args.steps, args.warmup, lib)
+        ms_api, _, _ = _timed(lambda i: layers[i % 3](w["x"], names), args.steps, args.warmup)
         byt = 4096 * 4096 * 2 * (1 + len(cached)) + 2 * 256 * 4096 * 2
         _line("multi-tenant LoRA bank tokens/s (64 adapters, top-8 folded)", round(256 / (ms / 1e3), 1), "tokens/s",
               args.steps, args.warmup, ms, True, "bf16",
               {"workload": "adapter_bank", "tokens": 256, "dim": 4096, "adapters": 64, "rank": 16,
                "folded": len(cached), "l2": "3 rotating layers"},
               stages_ms_per_step={k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in st.items()},
+              api_call_ms=round(ms_api, 5),
+              value_source="ops.lora_linear with the row groups / tenants resident; api_call_ms: "
+                           "StageMLCostBasedAdapterCache.forward from adapter-name lists",
               stage0_fold_ms=round(fold_ms, 4), gpu_launches=n, clocks=sampler.stop(),
               fold={"kernel": "fold_mma_kernel (bf16, 8 adapters batched, W broadcast)", "us": round(g_f * 1000, 3),
                     "bytes": fold_bytes, "achieved_gbs": round(fold_bytes / (g_f / 1e3) / 1e9, 1),

@@ -511,6 +511,12 @@ struct LinBuffers {
   size_t bytes = 0;
 };
 
+// Small batches take the LoRA shrink per row (pair shrink): a 16-row warp of the tiled
+// shrink walks the distinct tenants of its rows one after the other, and the rows of a
+// small mixed-adapter batch (e.g. 256 rows over 64 Zipf-distributed adapters) span many
+// of them.
+constexpr int64_t kRowShrinkMaxRows = 512;
+
 // permuted: P pairs over n_groups groups (nkeys from n_tenants / group_by_tenant);
 // direct: rows = M, no permutation.
 void lin_carve(bool permuted, int64_t P_or_M, int n_groups, int n_tenants, int group_by_tenant, int K, int N, int rank,
@@ -873,7 +879,10 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
       sh.static_rows = a->M;
       sh.rows_cap = a->M;
       sh.row_tenant = b.tenants;
-      SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
+      if (a->M <= kRowShrinkMaxRows)
+        SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(sh, nullptr, a->M, st));
+      else
+        SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
       g.s_rows = a->M;
     }
     if (b.pp.on())
@@ -906,7 +915,16 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   sh.rows_cap = b.plan.rows_cap;
   sh.row_tenant = b.plan.row_tenant;
   sh.tile_group = b.plan.tile_group;
-  SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
+  if (lora && a->M <= kRowShrinkMaxRows) {
+    // gather alone, then the shrink per row (reading the source rows in place)
+    ShrinkLaunch gather = sh;
+    gather.R = 0;
+    gather.lora_a = nullptr;
+    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(gather, st));
+    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(sh, b.plan.pair_row, a->M, st));
+  } else {
+    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
+  }
   g.a = b.xp;
   g.a_rows = b.plan.rows_cap;
   g.num_tiles_dev = b.plan.num_tiles;

@@ -62,7 +62,8 @@ struct ShrinkLaunch {
 constexpr int kShrinkKSlice = 512;
 inline int shrink_num_slices(int K) { return (K + kShrinkKSlice - 1) / kShrinkKSlice; }
 int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream);
-// The shrink for decode-sized batches: pairs p < P (pair_row[p] = their plan row),
+// The shrink per row, for decode-sized batches and for small batches whose rows span
+// many tenants: pairs p < P (pair_row[p] = their plan row; pair_row null: row p),
 // one CTA per (pair, 8 output columns) whose 8 warps split K in a fixed order;
 // writes the scaled 16-bit S rows (zeros for rows without a tenant) and reads the
 // source rows in place (src_row_of, if given, maps a plan row to its source row).

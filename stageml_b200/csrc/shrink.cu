@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(256, 1) pair_shrink_kernel(const PairShrinkPar
   pdl_wait();  // the plan and the source rows may come from the previous kernels
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = p.pair_row[blockIdx.x];
+  const int row = p.pair_row ? p.pair_row[blockIdx.x] : (int)blockIdx.x;  // no map: pair i is row i
   if (row < 0) return;  // dropped pair
   const int tn = p.row_tenant[row];
   T* s_out = static_cast<T*>(p.s_out) + (int64_t)row * p.R + blockIdx.y * 8;
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(256, 1) pair_shrink_kernel(const PairShrinkPar
 }  // namespace
 
 int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream, bool pdl) {
-  SB_CHECK_ARG(s.src && pair_row && s.lora_a && s.s_out && s.row_tenant, "pair shrink: missing buffers");
+  SB_CHECK_ARG(s.src && s.lora_a && s.s_out && s.row_tenant, "pair shrink: missing buffers");
   SB_CHECK_ARG(s.K > 0 && s.K % 8 == 0, "pair shrink: K=%d must be a positive multiple of 8", s.K);
   SB_CHECK_ARG(s.R > 0 && s.R % 8 == 0 && s.R <= 64, "pair shrink: R=%d must be a multiple of 8 up to 64", s.R);
   SB_CHECK_ARG(P >= 0 && P <= 65535, "pair shrink: %lld pairs", (long long)P);
