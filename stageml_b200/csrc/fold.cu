@@ -261,12 +261,18 @@ __global__ void __launch_bounds__(128) fold_f32_ring_kernel(const FoldArgs f, in
       const int row = m0 + st * FC_SROWS + r;
       if (row >= m_end || !col_ok) break;
       const float2 w = *reinterpret_cast<const float2*>(&Ws[slot][r][t * 2]);
+      const float4* l4 = reinterpret_cast<const float4*>(&Lss[slot][r][0]);  // 4 broadcast 16-byte reads
+      float lv[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = l4[q];
+        lv[4 * q] = v.x, lv[4 * q + 1] = v.y, lv[4 * q + 2] = v.z, lv[4 * q + 3] = v.w;
+      }
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const float lv = Lss[slot][r][j];
-        acc.x = fmaf(lv, rv[j].x, acc.x);
-        acc.y = fmaf(lv, rv[j].y, acc.y);
+        acc.x = fmaf(lv[j], rv[j].x, acc.x);
+        acc.y = fmaf(lv[j], rv[j].y, acc.y);
       }
       __stcs(reinterpret_cast<float2*>(O + (int64_t)row * f.cols + n), make_float2(w.x + s * acc.x, w.y + s * acc.y));
     }
