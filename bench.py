@@ -543,6 +543,8 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
         line["ep_status"] = ep_status
         line["ep_parity"] = ep_parity
         line["host_io"] = host_io
+    if world == 1 and cfg.name == "mixtral_moe_lora" and not args.skip_configs:
+        line["other_configs"] = other_configs(args)
     print(json.dumps(line), flush=True)
 
 
@@ -696,12 +698,47 @@ def _graph_timed(fn, reps: int, replays: int = 5):
     return e0.elapsed_time(e1) / (replays * reps)
 
 
+_COLLECT: list | None = None  # when a list, result lines of dense_arm are appended to it instead of printed
+
+
 def _line(metric, value, unit, steps, warmup, ms, hib, dtype, config, **extra):
     d = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": steps, "warmup": warmup,
          "ms_per_step": round(ms, 5), "higher_is_better": hib, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
          "data": "synthetic (seeded; shapes of the configuration)", "config": config}
     d.update(extra)
-    print(json.dumps(d), flush=True)
+    if _COLLECT is not None:
+        _COLLECT.append(d)
+    else:
+        print(json.dumps(d), flush=True)
+
+
+# The other configurations, measured after the headline layer in a default 1-GPU run and
+# summarised in its line (each with its own clock record).
+OTHER_CONFIGS = ("single_lora", "adapter_bank", "llama_block", "fine_grained_fp8_moe_lora")
+
+
+def other_configs(args) -> dict:
+    global _COLLECT
+    out = {}
+    for name in OTHER_CONFIGS:
+        sub = argparse.Namespace(**vars(args))
+        sub.workload, sub.steps, sub.warmup = name, min(args.steps, 20), 3
+        _COLLECT = []
+        t0 = time.time()
+        try:
+            dense_arm(sub)
+            d = _COLLECT[-1]
+            keep = ("metric", "value", "unit", "ms_per_step", "steps", "roofline", "layer_roofline", "fold",
+                    "folded_latency_us", "folded_roofline", "stages_ms_per_step", "clocks", "config", "value_source",
+                    "api_call_ms")
+            out[name] = {k: d[k] for k in keep if k in d}
+        except Exception as exc:  # one configuration failing must not lose the headline line
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        finally:
+            _COLLECT = None
+            torch.cuda.empty_cache()
+        out[name]["wall_s"] = round(time.time() - t0, 1)
+    return out
 
 
 def dense_arm(args):
@@ -879,19 +916,19 @@ def dense_arm(args):
                         "frac_burst": round(fl / (ms / 1e3) / 1e12 / pk["burst"], 4),
                         "frac_sustained": round(fl / (ms / 1e3) / 1e12 / pk["sustained"], 4), "traffic": None,
                         "peak_source": pk["why"]})
-    elif name == "fine_grained_moe_lora_bf16":
-        cfg = wl.MoEConfig("fine_grained_moe_lora_bf16", T=8192, H=2048, I=1408, E=64, k=6, n_shared=2,
-                           n_tenants=128, rank=8, tenant_dist="zipf")
+    elif name in ("fine_grained_moe_lora_bf16", "fine_grained_fp8_moe_lora"):
+        cfg = wl.MoEConfig(name, T=8192, H=2048, I=1408, E=64, k=6, n_shared=2, n_tenants=128, rank=8,
+                           tenant_dist="zipf", weight_dtype="e4m3" if "fp8" in name else "bf16")
         w = wl.make_moe_workload(cfg, device=dev, seed=0)
         ms, st, n = _timed(lambda i: layer_call(ops, cfg, w, w["x"], w["tenant_ids"]), args.steps, args.warmup, lib)
         clocks = sampler.stop()
         pk = choose_peak(peaks, clocks, ms * args.steps / 1e3)
         fl = cfg.flops()
-        _line("fine-grained MoE-LoRA layer tokens/s (bf16 weights)", round(cfg.T / (ms / 1e3), 1), "tokens/s",
-              args.steps, args.warmup, ms, True, "bf16",
+        _line(f"fine-grained MoE-LoRA layer tokens/s ({cfg.weight_dtype} weights)", round(cfg.T / (ms / 1e3), 1),
+              "tokens/s", args.steps, args.warmup, ms, True, "bf16",
               {"workload": cfg.name, "tokens": cfg.T, "hidden": 2048, "intermediate": 1408, "experts": 64, "top_k": 6,
                "shared_experts": 2, "tenants": 128, "lora_rank": 8,
-               "weights": "bf16"},
+               "weights": cfg.weight_dtype},
               stages_ms_per_step={k: round(v["ms"] / max(v["launches"], 1), 4) for k, v in st.items()},
               gpu_launches=n, clocks=clocks,
               layer_roofline={"flops": fl["total"], "peak_kind": pk["kind"],
@@ -968,6 +1005,8 @@ def main():
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-batch1", action="store_true")
+    ap.add_argument("--skip-configs", action="store_true",
+                    help="do not measure the other configurations after the headline layer")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         log("note: warm-up raised to the minimum of 3 steps")
