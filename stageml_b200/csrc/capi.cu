@@ -3,6 +3,7 @@
 // caller's workspace and launches the kernels of the path on `stream`.
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "grouped_gemm.cuh"
@@ -85,6 +86,8 @@ struct PairPlan {
   int32_t* num_singles = nullptr;
   int32_t* sruns = nullptr;      // [tiles_cap, kMaxRunsPerTile, 5]
   int32_t* snruns = nullptr;
+  int32_t* hpairs = nullptr;     // [tiles_cap, 4]: the pairs with each odd tile as a half unit
+  int32_t* num_hpairs = nullptr;
   int tiles_cap = 0;
   bool on() const { return pairs != nullptr; }
 };
@@ -125,6 +128,8 @@ void carve_pair_plan(Carver& c, int64_t tiles_cap, bool lora, PairPlan* pp) {
   pp->num_pairs = c.take<int32_t>(1);
   pp->singles = c.take<int32_t>((size_t)tiles_cap);
   pp->num_singles = c.take<int32_t>(1);
+  pp->hpairs = c.take<int32_t>((size_t)tiles_cap * 4);
+  pp->num_hpairs = c.take<int32_t>(1);
   if (lora) {
     pp->pruns = c.take<int32_t>(pair_runs_ints(tiles_cap));
     pp->pnruns = c.take<int32_t>((size_t)tiles_cap * kRunHdrInts);
@@ -139,7 +144,7 @@ int build_pair_plan(const PairPlan& pp, const int32_t* tile_group, const int32_t
                     const int32_t* num_tiles_dev, int64_t static_rows, const int32_t* row_tenant, cudaStream_t st) {
   return launch_pair_plan(tile_group, group_offsets, num_tiles_dev, pp.tiles_cap, static_rows,
                           pp.pruns ? row_tenant : nullptr, pp.pairs, pp.num_pairs, pp.pruns, pp.pnruns, st,
-                          pp.singles, pp.num_singles, pp.sruns, pp.snruns);
+                          pp.singles, pp.num_singles, pp.sruns, pp.snruns, pp.hpairs, pp.num_hpairs);
 }
 
 // Per host thread and device: a side stream and two events for running the odd tiles
@@ -163,13 +168,45 @@ int side_stream(SideStream** out) {
   return STAGEML_OK;
 }
 
-// A grouped GEMM with a pair plan: full tile pairs on the CTA-pair kernel, the
-// trailing odd tiles on the one-CTA kernel from a side stream launched right after
-// it, so their CTAs take the SMs the persistent pair kernel frees in its last wave
-// (an odd tile in a pair would leave half the pair idle). Without a plan (or with
-// e4m3 weights): the one-CTA kernel over all tiles (g.tile_runs set by the caller).
+// How a grouped GEMM on CTA pairs runs the groups' trailing odd tiles: as half units
+// of the pair kernel (one tile on both CTAs of a pair, 64 rows each), or on the
+// one-CTA kernel beside it. STAGEML_ODD_TILES=half|split (read once per process)
+// forces one; by default half units run where each cluster gets many units to even
+// out their different lengths (at least kHalfUnitsMinNTiles column tiles).
+constexpr int kHalfUnitsMinNTiles = 32;
+int odd_tiles_env() {  // 0 auto, 1 half, 2 split
+  static const int mode = [] {
+    const char* v = std::getenv("STAGEML_ODD_TILES");
+    if (!v) return 0;
+    if (std::strcmp(v, "half") == 0) return 1;
+    if (std::strcmp(v, "split") == 0) return 2;
+    return 0;
+  }();
+  return mode;
+}
+bool odd_tiles_as_half_units(const GemmLaunch& g) {
+  const int mode = odd_tiles_env();
+  if (mode != 0) return mode == 1;
+  const int n_tiles = g.swiglu ? (g.N + 127) / 128 : (g.N + 255) / 256;
+  return n_tiles >= kHalfUnitsMinNTiles;
+}
+
+// A grouped GEMM with a pair plan: full tile pairs on the CTA-pair kernel; the
+// trailing odd tiles either as half units of the same kernel, or on the one-CTA
+// kernel from a side stream launched right after it, so their CTAs take the SMs the
+// persistent pair kernel leaves them. Without a plan (or with e4m3 weights): the
+// one-CTA kernel over all tiles (g.tile_runs set by the caller).
 int run_grouped_gemm(GemmLaunch g, const PairPlan& pp, cudaStream_t st) {
   if (!pp.on() || g.b_fp8) return launch_grouped_gemm(g, st);
+  if (odd_tiles_as_half_units(g)) {
+    g.pairs = pp.hpairs;
+    g.num_pairs_dev = pp.num_hpairs;
+    g.pairs_cap = pp.tiles_cap;
+    g.pair_runs = pp.pruns;
+    g.pair_nruns = pp.pnruns;
+    g.pair_half_units = true;
+    return launch_grouped_gemm(g, st);
+  }
   g.split_pairs_dev = pp.num_pairs;
   g.split_singles_dev = pp.num_singles;
   g.split_cap = pp.tiles_cap;

@@ -74,6 +74,9 @@ struct GemmLaunch {
   int pairs_cap = 0;
   const int32_t* pair_runs = nullptr;    // [tiles][kMaxRunsPerPair][kPairRunInts], at each pair's first tile
   const int32_t* pair_nruns = nullptr;   // [tiles][kRunHdrInts] run headers, at each pair's first tile
+  // A pair whose second tile is -1 is a half unit: its one tile on both CTAs (64 rows
+  // each, M = 128 MMAs) instead of a pair with an idle half.
+  bool pair_half_units = false;
   // The pair kernel and the odd-tile kernel side by side (split_sms > 0): each
   // reads the pair and odd-tile counts and keeps only its share of the split_sms
   // SMs busy (split_single_ctas); the CTAs past its share exit at once.
@@ -134,12 +137,15 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream);
 // With `singles`, a group's trailing odd tile is listed there (count in *num_singles)
 // instead of forming a pair with an idle half; the one-CTA kernel runs those tiles
 // (GemmLaunch::tile_list), and with row_tenant and sruns / snruns their runs are
-// written as launch_tile_runs does (at the tile id). One launch.
+// written as launch_tile_runs does (at the tile id). With `hpairs`, a second pair
+// list in which every trailing odd tile is a pair with second tile -1 (a half unit
+// of GemmLaunch::pair_half_units), its runs written at the tile as for a pair.
+// One launch.
 int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
                      int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream,
                      int32_t* singles = nullptr, int32_t* num_singles = nullptr, int32_t* sruns = nullptr,
-                     int32_t* snruns = nullptr);
+                     int32_t* snruns = nullptr, int32_t* hpairs = nullptr, int32_t* num_hpairs = nullptr);
 size_t pair_runs_ints(int64_t pairs_cap);
 
 // Weight-streaming variant for at most 16 valid rows per 128-row tile (decode-sized

@@ -9,8 +9,15 @@
 // on the odd one), and the pair MMA issued by the even CTA reads both.
 //
 // A pair covers two 128-row tiles of the same group (consecutive tiles of a
-// padded group segment); a group with an odd tile count ends with a pair whose
-// odd half is idle (its rows are loaded but never stored).
+// padded group segment). A group with an odd tile count ends with a half unit
+// (half_units): its one 128-row tile on both CTAs, 64 rows each, computed by the
+// M = 128 pair MMA. That MMA's accumulator holds a CTA's 64 rows in two lane
+// halves: columns [0, N/2) of row m in TMEM lane m, columns [N/2, N) in lane
+// 64 + m, both at TMEM columns [0, N/2). SwiGLU half units therefore order their
+// 256 B rows as 64 gate, 64 up (even CTA) and the next 64 gate, 64 up (odd CTA),
+// so that each lane holds the gate and up values of the same 64 output columns.
+// Without half_units the odd tile forms a pair whose odd half is idle (its rows
+// are loaded but never stored).
 //
 // Per CTA: warp 0 TMA producer, warp 1 TMEM allocator and -- on the even CTA --
 // MMA issuer; warps 2..5 epilogue over the CTA's own 128 TMEM lanes. Both CTAs'
@@ -32,6 +39,8 @@ constexpr int BK = 64;                         // one 128 B swizzle row of 16-bi
 constexpr int A_BYTES = BM * BK * 2;           // 16 KB
 constexpr int B_BYTES = 128 * BK * 2;          // this CTA's half of B: 16 KB
 constexpr int MMA_STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int HALF_A_BYTES = 64 * BK * 2;      // half unit: 64 rows of A per CTA (8 KB)
+constexpr int HALF_STAGE_BYTES = HALF_A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int LCHUNK = 128 * 32;               // 128 rows x 16 columns, 16-bit (4 KB)
 constexpr int LHALF = 64 * 32;                 // 64 rows x 16 columns, 16-bit (2 KB)
@@ -89,6 +98,7 @@ struct PParams {
   // side by side with the odd-tile kernel (split_sms > 0)
   const int32_t* split_singles_dev;
   int split_sms;
+  int half_units;                // a pair whose second tile is -1 is a half unit (M = 128)
 };
 
 template <typename T>
@@ -144,6 +154,7 @@ template <typename T>
 __global__ void __launch_bounds__(THREADS, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                              const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_lb,
+                             const __grid_constant__ CUtensorMap tm_a64, const __grid_constant__ CUtensorMap tm_b64,
                              const PParams p) {
   // Beside the odd-tile kernel only the first `nclusters` clusters work; the others
   // leave their SMs to it (both CTAs of a cluster decide alike, before any barrier).
@@ -214,6 +225,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ producer (both CTAs)
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    if (p.half_units) {
+      tma_prefetch_desc(&tm_a64);
+      tma_prefetch_desc(&tm_b64);
+    }
     if (p.rank) {
       tma_prefetch_desc(&tm_s);
       tma_prefetch_desc(&tm_lb);
@@ -239,12 +254,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       int pm, n_tile;
       unit_coords(p, u, pm, n_tile);
       const int m0 = p.pairs[4 * pm];
+      const bool half = p.half_units && p.pairs[4 * pm + 1] < 0;
       const int mine = p.pairs[4 * pm + rank];
       const int m_load = mine >= 0 ? mine : m0;  // an idle half loads defined rows it never stores
       const int group = p.tile_group ? p.tile_group[m0] : 0;
-      const int a_row = m_load * BM;
+      const int a_row = half ? m0 * BM + 64 * (int)rank : m_load * BM;
       const int n0 = p.swiglu ? n_tile * 128 : n_tile * BN;
-      const int b_row = weight_group(p.b_group_map, group) * p.b_group_rows + n0 + (int)rank * (p.swiglu ? p.N : 128);
+      const int b_base = weight_group(p.b_group_map, group) * p.b_group_rows;
+      const int b_row = b_base + n0 + (int)rank * (p.swiglu ? p.N : 128);
       if (p.rank) {  // the run header arrives while the K loop's copies are issued
         mbar_arrive_expect_tx(hdr_bar, kRunHdrInts * 4);
         bulk_load_1d(smem_u32(hdr_smem), p.nruns + (int64_t)m0 * kRunHdrInts, kRunHdrInts * 4, hdr_bar);
@@ -258,9 +275,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         const uint32_t sa = smem_base + s * STAGE_BYTES;
-        arm(s, MMA_STAGE_BYTES);
-        load(sa, &tm_a, s, kb * BK, a_row, pol_a);
-        load(sa + A_BYTES, &tm_b, s, kb * BK, b_row, pol_b);
+        if (half) {
+          // 64 rows of A; SwiGLU B: gate rows [n0 + 64 rank, +64), then the same up rows
+          arm(s, HALF_STAGE_BYTES);
+          load(sa, &tm_a64, s, kb * BK, a_row, pol_a);
+          if (p.swiglu) {
+            const int g_row = b_base + n0 + 64 * (int)rank;
+            load(sa + A_BYTES, &tm_b64, s, kb * BK, g_row, pol_b);
+            load(sa + A_BYTES + B_BYTES / 2, &tm_b64, s, kb * BK, g_row + p.N, pol_b);
+          } else {
+            load(sa + A_BYTES, &tm_b, s, kb * BK, b_row, pol_b);
+          }
+        } else {
+          arm(s, MMA_STAGE_BYTES);
+          load(sa, &tm_a, s, kb * BK, a_row, pol_a);
+          load(sa + A_BYTES, &tm_b, s, kb * BK, b_row, pol_b);
+        }
         last_phase[s] = (int)ph;
       }
       // LoRA blocks: this CTA's rows of S + its half of the B rows of each tenant run
@@ -322,6 +352,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ MMA issuer (even CTA)
     const uint32_t idesc = idesc_f16(2 * BM, BN, IsBf16<T>::value);
     const uint32_t idesc_n128 = idesc_f16(2 * BM, 128, IsBf16<T>::value);
+    const uint32_t idesc_h = idesc_f16(BM, BN, IsBf16<T>::value);        // half unit: M = 128
+    const uint32_t idesc_h_n128 = idesc_f16(BM, 128, IsBf16<T>::value);
     uint32_t it = 0;
     int tcount = 0;
     bool ok = true;
@@ -334,6 +366,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       int pm, n_tile_unused;
       unit_coords(p, u, pm, n_tile_unused);
       const int m0 = p.pairs[4 * pm];
+      const bool half = p.half_units && p.pairs[4 * pm + 1] < 0;
+      const uint32_t id_main = half ? idesc_h : idesc;
       if (p.rank) {  // the unit's run header and first runs arrive while the K loop is issued
         fence_proxy_async_smem();  // the previous unit's reads of the buffer come first
         mbar_arrive_expect_tx(mrun_bar, MMA_RUN_BYTES);
@@ -361,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint64_t bdesc = smem_desc_sw128(sa + A_BYTES);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)
-          tc_mma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc_mma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, id_main, (kb > 0 || k > 0) ? 1u : 0u);
         tc_commit_pair_both(empty_bar(s), 0x3);
       }
       int nruns = 0;
@@ -384,19 +418,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int jj = 0; jj < nr; ++jj) {
           const int r = r0 + jj;
           const int32_t* run = r < kMmaRuns ? mruns_smem + r * kPairRunInts : pair_run(p, m0, r);
+          // Disable mask per TMEM lane: a pair unit's 256 rows are the lanes of both CTAs;
+          // a half unit's row m (of 128) is lanes m % 64 and 64 + m % 64 of CTA m / 64.
           uint32_t dis[8];
+          if (half) {
 #pragma unroll
-          for (int w = 0; w < 8; ++w) dis[w] = ~(uint32_t)run[1 + w];
+            for (int w = 0; w < 8; ++w) dis[w] = ~(uint32_t)run[1 + 2 * (w >> 2) + (w & 1)];
+          } else {
+#pragma unroll
+            for (int w = 0; w < 8; ++w) dis[w] = ~(uint32_t)run[1 + w];
+          }
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
             if (p.swiglu) {
+              // gate into accumulator columns [0, 128) (half unit: [0, 64) of both lane halves),
+              // up into [128, 256) ([64, 128))
+              const uint32_t id_n128 = half ? idesc_h_n128 : idesc_n128;
               tc_mma_f16_pair_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * LHALF),
-                                     idesc_n128, 1u, dis);
-              tc_mma_f16_pair_masked(d_tmem + 128, smem_desc_sw32(base + (p.lchunks + ch) * LCHUNK),
-                                     smem_desc_sw32(rb + (p.lchunks + ch) * LHALF), idesc_n128, 1u, dis);
+                                     id_n128, 1u, dis);
+              tc_mma_f16_pair_masked(d_tmem + (half ? 64 : 128), smem_desc_sw32(base + (p.lchunks + ch) * LCHUNK),
+                                     smem_desc_sw32(rb + (p.lchunks + ch) * LHALF), id_n128, 1u, dis);
             } else {
               tc_mma_f16_pair_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * LCHUNK),
-                                     idesc, 1u, dis);
+                                     id_main, 1u, dis);
             }
           }
         }
@@ -427,19 +471,26 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       int pm, n_tile;
       unit_coords(p, u, pm, n_tile);
+      const int m0 = p.pairs[4 * pm];
+      const bool half = p.half_units && p.pairs[4 * pm + 1] < 0;
       const int mine = p.pairs[4 * pm + rank];
-      const int group = p.tile_group ? p.tile_group[p.pairs[4 * pm]] : 0;
-      const int64_t row = (int64_t)mine * BM + row_in_tile;
-      const bool live = mine >= 0;  // uniform over the CTA: tcgen05.ld below is warp-collective
+      const int group = p.tile_group ? p.tile_group[m0] : 0;
+      // half unit: this CTA's 64 rows of tile m0; lane quarters 0-1 hold the first half
+      // of the unit's columns, quarters 2-3 the second half
+      const int64_t row = half ? (int64_t)m0 * BM + 64 * (int)rank + (quarter & 1) * 32 + lane
+                               : (int64_t)mine * BM + row_in_tile;
+      const int col_half = half ? (quarter >> 1) : 0;
+      const bool live = half || mine >= 0;  // uniform over the CTA: tcgen05.ld below is warp-collective
       const bool row_ok = live && (p.tile_group ? true : row < p.m_rows);
       const float rscale = (row_ok && p.row_scale) ? p.row_scale[row] : 1.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (p.swiglu) {
-        const int n0 = n_tile * 128;
-        for (int c = 0; c < 128 && live; c += 16) {
+        const int n0 = n_tile * 128 + 64 * col_half;
+        const int ncols = half ? 64 : 128;  // up values sit ncols columns after the gate values
+        for (int c = 0; c < ncols && live; c += 16) {
           uint32_t rg[16], ru[16];
           tmem_ld_x16(t_row + c, rg);
-          tmem_ld_x16(t_row + 128 + c, ru);
+          tmem_ld_x16(t_row + ncols + c, ru);
           tmem_wait_ld();
           const int col = n0 + c;
           const int nvalid = min(16, p.N - col);
@@ -458,8 +509,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (row_ok && nvalid > 0) store16<T>(out + row * p.ldo + col, h, nvalid, vec_ok);
         }
       } else {
-        const int n0 = n_tile * BN;
-        for (int c = 0; c < BN && live; c += 16) {
+        const int n0 = n_tile * BN + 128 * col_half;
+        const int ncols = half ? 128 : BN;
+        for (int c = 0; c < ncols && live; c += 16) {
           uint32_t rv[16];
           tmem_ld_x16(t_row + c, rv);
           tmem_wait_ld();
@@ -594,17 +646,19 @@ __device__ __forceinline__ void quarter_runs(const int32_t* row_tenant, const in
 }
 
 // One launch for the whole plan. Block 0 lists the pairs (and the singles) in tile
-// order, each with its group's first pair and pair count (for the unit order).
+// order, each with its group's first pair and pair count (for the unit order), and
+// with hpairs the second list in which each trailing odd tile is a half unit.
 // Blocks 1.. (with row_tenant): one warp per tile t, which writes the LoRA runs of
-// the pair t opens at pruns[t] / pnruns[t] (256 rows, 8 mask words), or of the single
-// t at sruns[t] / snruns[t] (128 rows, 4 mask words): runs are indexed by the first
-// tile, so no block waits for the list.
+// the pair t opens at pruns[t] / pnruns[t] (256 rows, 8 mask words; a half unit's
+// words 4-7 are zero), and of the single t at sruns[t] / snruns[t] (128 rows, 4 mask
+// words): runs are indexed by the first tile, so no block waits for the lists.
 __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
     const int32_t* __restrict__ tile_group, const int32_t* __restrict__ group_offsets,
     const int32_t* __restrict__ num_tiles_dev, int tiles_cap, int64_t static_rows, const int32_t* __restrict__ row_tenant,
     int32_t* __restrict__ pairs, int32_t* __restrict__ num_pairs_out, int32_t* __restrict__ singles,
     int32_t* __restrict__ num_singles_out, int32_t* __restrict__ pruns, int32_t* __restrict__ pnruns,
-    int32_t* __restrict__ sruns, int32_t* __restrict__ snruns) {
+    int32_t* __restrict__ sruns, int32_t* __restrict__ snruns, int32_t* __restrict__ hpairs,
+    int32_t* __restrict__ num_hpairs_out) {
   const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const bool split = singles != nullptr;
@@ -615,12 +669,14 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
     const TileRole r = tile_role(tile_group, group_offsets, ntiles, t);
     if (!r.start) return;
     const int64_t bound = num_tiles_dev ? INT64_MAX : static_rows;
-    if (split && r.partner < 0) {
-      if (!sruns) return;
+    const bool odd = r.partner < 0;
+    if (split && odd && sruns) {
       const int64_t q4[4] = {(int64_t)t * 128, (int64_t)t * 128 + 32, (int64_t)t * 128 + 64, (int64_t)t * 128 + 96};
       quarter_runs<4>(row_tenant, q4, bound, s_ten[w], s_mask[w], sruns + (int64_t)t * kMaxRunsPerTile * 5,
                       snruns + t, kMaxRunsPerTile);
-    } else {
+      __syncwarp();  // the warp's staging arrays are reused below
+    }
+    if (!(split && odd) || hpairs) {
       int64_t q8[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
@@ -633,19 +689,22 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
     }
     return;
   }
-  __shared__ int32_t warp_tot[2][kPlanWarps];
-  __shared__ int32_t carry[2];
-  if (tid < 2) carry[tid] = 0;
+  __shared__ int32_t warp_tot[3][kPlanWarps];
+  __shared__ int32_t carry[3];
+  if (tid < 3) carry[tid] = 0;
   __syncthreads();
   for (int base = 0; base < ntiles; base += kPlanThreads) {
     const int t = base + tid;
     const TileRole r = tile_role(tile_group, group_offsets, ntiles, t);
     const bool as_single = split && r.start && r.partner < 0;
     const bool as_pair = r.start && !as_single;
+    const bool as_hpair = hpairs != nullptr && r.start;
     const unsigned bp = __ballot_sync(0xffffffffu, as_pair), bs = __ballot_sync(0xffffffffu, as_single);
+    const unsigned bh = __ballot_sync(0xffffffffu, as_hpair);
     if (lane == 0) {
       warp_tot[0][w] = __popc(bp);
       warp_tot[1][w] = __popc(bs);
+      warp_tot[2][w] = __popc(bh);
     }
     __syncthreads();
     const unsigned lt = (1u << lane) - 1u;
@@ -662,8 +721,16 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
       for (int i = 0; i < w; ++i) before += warp_tot[1][i];
       singles[before] = t;
     }
+    if (as_hpair) {
+      int before = carry[2] + __popc(bh & lt);
+      for (int i = 0; i < w; ++i) before += warp_tot[2][i];
+      hpairs[4 * before] = t;
+      hpairs[4 * before + 1] = r.partner;
+      hpairs[4 * before + 2] = before - r.in_group;
+      hpairs[4 * before + 3] = (r.group_tiles + 1) >> 1;
+    }
     __syncthreads();
-    if (tid < 2) {
+    if (tid < 3) {
       int tot = 0;
       for (int i = 0; i < kPlanWarps; ++i) tot += warp_tot[tid][i];
       carry[tid] += tot;
@@ -673,12 +740,14 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
   if (tid == 0) {
     *num_pairs_out = carry[0];
     if (num_singles_out) *num_singles_out = carry[1];
+    if (num_hpairs_out) *num_hpairs_out = carry[2];
   }
 }
 
 template <typename T>
 int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
-                       const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const PParams& p) {
+                       const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const CUtensorMap& tm_a64,
+                       const CUtensorMap& tm_b64, const PParams& p) {
   auto kern = grouped_gemm_pair_kernel<T>;
   SB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   // Persistent grid: as many CTA pairs as can be resident at once.
@@ -712,7 +781,7 @@ int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorM
   }
   const int64_t clusters = std::min<int64_t>(units_upper, max_clusters);
   cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
-  SB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tm_a, tm_b, tm_s, tm_lb, p));
+  SB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p));
   ::sb::count_launch();
   return STAGEML_OK;
 }
@@ -724,9 +793,11 @@ size_t pair_runs_ints(int64_t pairs_cap) { return (size_t)pairs_cap * kMaxRunsPe
 int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, const int32_t* num_tiles_dev,
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
                      int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream, int32_t* singles,
-                     int32_t* num_singles, int32_t* sruns, int32_t* snruns) {
+                     int32_t* num_singles, int32_t* sruns, int32_t* snruns, int32_t* hpairs,
+                     int32_t* num_hpairs) {
   SB_CHECK_ARG(pairs && num_pairs, "pair plan: null output");
   SB_CHECK_ARG(!singles == !num_singles, "pair plan: singles need their count");
+  SB_CHECK_ARG(!hpairs == !num_hpairs, "pair plan: the half-unit list needs its count");
   SB_CHECK_ARG(!tile_group || (group_offsets && num_tiles_dev), "pair plan: grouped tiles need offsets and a count");
   SB_CHECK_ARG(!row_tenant || (runs && nruns), "pair plan: LoRA runs need output buffers");
   SB_CHECK_ARG(!sruns == !snruns, "pair plan: single-tile runs need their counts");
@@ -735,7 +806,7 @@ int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, co
   SB_CHECK_ARG(run_blocks < 65535 * 1024LL, "pair plan: too many tiles");
   (pair_plan_kernel<<<(unsigned)(1 + run_blocks), kPlanThreads, 0, stream>>>(
        tile_group, group_offsets, num_tiles_dev, tiles_cap, static_rows, row_tenant, pairs, num_pairs, singles,
-       num_singles, row_tenant ? runs : nullptr, nruns, row_tenant ? sruns : nullptr, snruns),
+       num_singles, row_tenant ? runs : nullptr, nruns, row_tenant ? sruns : nullptr, snruns, hpairs, num_hpairs),
    ::sb::count_launch());
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
@@ -747,9 +818,17 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
   SB_CHECK_ARG(g.rank == 0 || (g.pair_runs && g.pair_nruns), "pair gemm: LoRA needs the pair runs");
 
   const CUtensorMapDataType dt = g.in_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap tm_a, tm_b, tm_s, tm_lb;
+  CUtensorMap tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64;
   SB_TRY(make_tmap_2d(&tm_a, g.a, dt, 2, (uint64_t)g.a_rows, (uint64_t)g.K, (uint64_t)g.K * 2, BM, BK, 128));
   SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
+  if (g.pair_half_units) {
+    SB_TRY(make_tmap_2d(&tm_a64, g.a, dt, 2, (uint64_t)g.a_rows, (uint64_t)g.K, (uint64_t)g.K * 2, 64, BK, 128));
+    SB_TRY(make_tmap_2d(&tm_b64, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 64, BK,
+                        128));
+  } else {
+    tm_a64 = tm_a;  // unused
+    tm_b64 = tm_b;
+  }
   const int lora_cols = g.swiglu ? 2 * g.rank : g.rank;
   if (g.rank) {
     SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
@@ -794,11 +873,12 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
   p.timeout_ns = kDefaultWaitNs;
   p.split_singles_dev = g.split_singles_dev;
   p.split_sms = g.split_singles_dev ? g.split_sms : 0;
+  p.half_units = g.pair_half_units ? 1 : 0;
 
   const int64_t units_upper = (int64_t)g.pairs_cap * p.num_n_tiles;
   if (units_upper == 0) return STAGEML_OK;
-  return g.in_bf16 ? launch_pair_kernel<bf16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p)
-                   : launch_pair_kernel<f16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, p);
+  return g.in_bf16 ? launch_pair_kernel<bf16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p)
+                   : launch_pair_kernel<f16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p);
 }
 
 }  // namespace sb

@@ -468,52 +468,116 @@ __global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__
 // as router_logits_smem_kernel, but each warp takes two tokens at a time (every G
 // read from shared memory serves both) and runs topk_row on their logits right
 // away. Each token's per-lane sums are those of router_logits_smem_kernel (same
-// columns, same order), so the logits are the same bits.
+// columns, same order), so the logits are the same bits. The token rows stream
+// through registers in steps of 1024 columns, double-buffered: the loads of step
+// s + 1 are in flight while step s is summed, and the first step's loads are issued
+// before the wait for the staged gate.
+template <typename T>
+struct XChunk {
+  using type = uint2;  // 4 x 16-bit
+};
+template <>
+struct XChunk<float> {
+  using type = float4;
+};
+template <typename T>
+__device__ __forceinline__ typename XChunk<T>::type load_chunk(const T* xr, int h, int H) {
+  using C = typename XChunk<T>::type;
+  if (h >= H) return C{};
+  return __ldg(reinterpret_cast<const C*>(xr + h));
+}
+template <typename T>
+__device__ __forceinline__ void chunk_f32(const typename XChunk<T>::type& c, float (&v)[4]) {
+  if constexpr (sizeof(T) == 2) {
+    const T* hv = reinterpret_cast<const T*>(&c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = to_f32<T>(hv[q]);
+  } else {
+    v[0] = c.x, v[1] = c.y, v[2] = c.z, v[3] = c.w;
+  }
+}
+
 constexpr int RT_TPW = 2;
 template <typename T, int E_MAX>
 __global__ void __launch_bounds__(256) router_route_smem_kernel(const T* __restrict__ x, const float* __restrict__ gw,
                                                                 int T_, int H, int E, int k, int renorm,
                                                                 float* __restrict__ logits, int32_t* __restrict__ ids,
                                                                 float* __restrict__ weights) {
-  constexpr int XU = 4;
+  constexpr int XU = 8;  // 4-column chunks per lane and step: 1024 columns per step
+  using C = typename XChunk<T>::type;
   extern __shared__ float4 gsm4[];
   float* gsm = reinterpret_cast<float*>(gsm4);
   __shared__ uint64_t bar;
   __shared__ volatile int abort_flag;
   __shared__ float lsm[8][RT_TPW][E_MAX];
-  const bool staged = stage_to_smem(smem_u32(gsm), gw, (uint32_t)(sizeof(float) * E * H), nullptr, 0, &bar, &abort_flag);
+  const uint32_t mb = smem_u32(&bar);
+  const uint32_t gbytes = (uint32_t)(sizeof(float) * E * H);
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(mb, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(mb, gbytes);
+    for (uint32_t off = 0; off < gbytes; off += 16384u)
+      bulk_load_1d(smem_u32(gsm) + off, reinterpret_cast<const char*>(gw) + off, min(16384u, gbytes - off), mb);
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nsteps = (H + 128 * XU - 1) / (128 * XU);
+  bool gate_waited = false, staged = true;
   for (int t0 = (blockIdx.x * 8 + warp) * RT_TPW; t0 < T_; t0 += gridDim.x * 8 * RT_TPW) {
     const int nt = min(RT_TPW, T_ - t0);
+    const T* xr[RT_TPW];
+#pragma unroll
+    for (int j = 0; j < RT_TPW; ++j) xr[j] = x + (int64_t)(t0 + min(j, nt - 1)) * H;
     float acc[RT_TPW][E_MAX];
 #pragma unroll
     for (int j = 0; j < RT_TPW; ++j)
 #pragma unroll
       for (int e = 0; e < E_MAX; ++e) acc[j][e] = 0.f;
-    for (int h0 = lane * 4; h0 < H; h0 += 128 * XU) {
-      float xv[RT_TPW][XU][4];
+    C xa[RT_TPW][XU], xb[RT_TPW][XU];
+    auto load_step = [&](C (&buf)[RT_TPW][XU], int st) {
 #pragma unroll
       for (int j = 0; j < RT_TPW; ++j)
 #pragma unroll
-        for (int u = 0; u < XU; ++u) load_x4<T>(x + (int64_t)(t0 + min(j, nt - 1)) * H, h0 + 128 * u, H, xv[j][u]);
+        for (int u = 0; u < XU; ++u) buf[j][u] = load_chunk<T>(xr[j], st * 128 * XU + lane * 4 + 128 * u, H);
+    };
+    auto sum_step = [&](const C (&buf)[RT_TPW][XU], int st) {
 #pragma unroll
       for (int u = 0; u < XU; ++u) {
-        const int h = h0 + 128 * u;
+        const int h = st * 128 * XU + lane * 4 + 128 * u;
         if (h < H) {
+          float xv[RT_TPW][4];
+#pragma unroll
+          for (int j = 0; j < RT_TPW; ++j) chunk_f32<T>(buf[j][u], xv[j]);
 #pragma unroll
           for (int e = 0; e < E_MAX; ++e) {
             if (e < E) {
               const float4 gv = *reinterpret_cast<const float4*>(gsm + e * H + h);
 #pragma unroll
               for (int j = 0; j < RT_TPW; ++j) {
-                acc[j][e] = fmaf(xv[j][u][0], gv.x, acc[j][e]);
-                acc[j][e] = fmaf(xv[j][u][1], gv.y, acc[j][e]);
-                acc[j][e] = fmaf(xv[j][u][2], gv.z, acc[j][e]);
-                acc[j][e] = fmaf(xv[j][u][3], gv.w, acc[j][e]);
+                acc[j][e] = fmaf(xv[j][0], gv.x, acc[j][e]);
+                acc[j][e] = fmaf(xv[j][1], gv.y, acc[j][e]);
+                acc[j][e] = fmaf(xv[j][2], gv.z, acc[j][e]);
+                acc[j][e] = fmaf(xv[j][3], gv.w, acc[j][e]);
               }
             }
           }
         }
+      }
+    };
+    load_step(xa, 0);
+    if (!gate_waited) {  // the first step's rows are in flight while the gate lands
+      staged = mbar_wait(mb, 0, &abort_flag, nullptr, kDefaultWaitNs, 0);
+      gate_waited = true;
+    }
+    for (int st = 0; st < nsteps; st += 2) {
+      if (st + 1 < nsteps) load_step(xb, st + 1);
+      sum_step(xa, st);
+      if (st + 1 < nsteps) {
+        if (st + 2 < nsteps) load_step(xa, st + 2);
+        sum_step(xb, st + 1);
       }
     }
 #pragma unroll
@@ -537,6 +601,7 @@ __global__ void __launch_bounds__(256) router_route_smem_kernel(const T* __restr
       topk_row(&lsm[warp][j][0], E, k, renorm, lane, ids + (int64_t)(t0 + j) * k, weights + (int64_t)(t0 + j) * k);
     __syncwarp();
   }
+  if (!gate_waited) mbar_wait(mb, 0, &abort_flag, nullptr, kDefaultWaitNs, 0);  // the copy lands before exit
 }
 
 }  // namespace
