@@ -121,11 +121,20 @@ __global__ void __launch_bounds__(RT_THREADS) router_logits_kernel(const T* __re
 // More than 32 experts with bf16 tokens: the same fp32 dot products on the tensor
 // cores. Each fp32 gate value is split exactly into three bf16 parts (g = hi + mid +
 // lo: 8 + 8 + 8 significant bits), so x . g = x . hi + x . mid + x . lo with every
-// product exact and fp32 accumulation (mma.sync m16n8k16). CTA tile: 64 tokens x
-// 64 experts, 4 warps of 16 tokens; K in 32-wide chunks through shared memory
-// (double-buffered: the next chunk's global loads are in flight during the MMAs).
-// A token's sums do not depend on the other tokens of the batch.
-constexpr int RTC_TT = 64, RTC_TE = 64, RTC_KC = 32, RTC_PITCH = RTC_KC + 8;  // pitch in bf16 (80 B rows)
+// product exact and fp32 accumulation (mma.sync m16n8k16; per 16-wide K step the
+// three parts in that order, K steps in order). CTA tile: 64 tokens x 32 experts, 4
+// warps of 16 tokens. x and the fp32 gate arrive in 64-wide K chunks through a
+// 4-stage cp.async ring (three chunks in flight while one is used); the CTA splits
+// each gate chunk into its three bf16 planes in shared memory. A token's sums do
+// not depend on the other tokens of the batch.
+constexpr int RTC_TT = 64, RTC_TE = 32, RTC_KC = 64, RTC_STAGES = 4;
+constexpr int RTC_XP = RTC_KC + 8;  // x row pitch in bf16 (144 B: ldmatrix rows in distinct banks)
+constexpr int RTC_RP = RTC_KC + 4;  // raw gate row pitch in fp32 (272 B)
+constexpr int RTC_GP = RTC_KC + 8;  // bf16 gate plane row pitch
+constexpr int RTC_X_BYTES = RTC_STAGES * RTC_TT * RTC_XP * 2;
+constexpr int RTC_R_BYTES = RTC_STAGES * RTC_TE * RTC_RP * 4;
+constexpr int RTC_G_BYTES = 3 * RTC_TE * RTC_GP * 2;
+constexpr int RTC_SMEM = RTC_X_BYTES + RTC_R_BYTES + RTC_G_BYTES;
 
 __device__ __forceinline__ void rtc_ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -142,81 +151,89 @@ __device__ __forceinline__ void rtc_mma(float (&c)[4], uint32_t a0, uint32_t a1,
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void rtc_cp16(uint32_t dst, const void* src, bool valid) {
+  // src-size 0 fills the 16 bytes with zeros (tokens / experts / columns past the end)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
 
 __global__ void __launch_bounds__(128) router_logits_tc_kernel(const bf16* __restrict__ x, const float* __restrict__ gw,
                                                                int T_, int H, int E, float* __restrict__ logits) {
-  __shared__ __align__(16) bf16 xs[2][RTC_TT][RTC_PITCH];
-  __shared__ __align__(16) bf16 gs[2][3][RTC_TE][RTC_PITCH];  // hi, mid, lo parts
+  extern __shared__ __align__(16) uint8_t rtc_smem[];
+  bf16* xs = reinterpret_cast<bf16*>(rtc_smem);                                   // [S][TT][XP]
+  float* graw = reinterpret_cast<float*>(rtc_smem + RTC_X_BYTES);                 // [S][TE][RP]
+  bf16* gs = reinterpret_cast<bf16*>(rtc_smem + RTC_X_BYTES + RTC_R_BYTES);       // [3][TE][GP]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * RTC_TT, e0 = blockIdx.y * RTC_TE;
-  // loader: x 64 rows x 32 (two 16-byte pieces per thread), G 64 rows x 32 fp32 (four)
-  uint4 xv[2];
-  float4 gv[4];
-  auto load = [&](int k0) {
+  const int nchunks = (H + RTC_KC - 1) / RTC_KC;
+  // one chunk: x 64 rows x 64 bf16 (512 16-byte pieces), gate 32 rows x 64 fp32 (512)
+  auto issue = [&](int c) {
+    if (c < nchunks) {
+      const int slot = c % RTC_STAGES, k0 = c * RTC_KC;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int idx = tid + 128 * i, r = idx >> 2, c = (idx & 3) * 8;
-      const int t = t0 + r;
-      xv[i] = (t < T_ && k0 + c < H) ? __ldg(reinterpret_cast<const uint4*>(x + (int64_t)t * H + k0 + c))
-                                     : make_uint4(0, 0, 0, 0);
-    }
+      for (int i = 0; i < 4; ++i) {
+        const int idx = tid + 128 * i, r = idx >> 3, q = (idx & 7) * 8;
+        const int t = t0 + r;
+        const bool v = t < T_ && k0 + q < H;
+        rtc_cp16(smem_u32(xs + ((size_t)slot * RTC_TT + r) * RTC_XP + q), v ? x + (int64_t)t * H + k0 + q : x, v);
+      }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int idx = tid + 128 * i, r = idx >> 3, c = (idx & 7) * 4;
-      const int e = e0 + r;
-      gv[i] = (e < E && k0 + c < H) ? __ldg(reinterpret_cast<const float4*>(gw + (int64_t)e * H + k0 + c))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  auto store = [&](int buf) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int idx = tid + 128 * i, r = idx >> 2, c = (idx & 3) * 8;
-      *reinterpret_cast<uint4*>(&xs[buf][r][c]) = xv[i];
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int idx = tid + 128 * i, r = idx >> 3, c = (idx & 7) * 4;
-      const float g[4] = {gv[i].x, gv[i].y, gv[i].z, gv[i].w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const bf16 hi = __float2bfloat16_rn(g[q]);
-        const float r1 = g[q] - __bfloat162float(hi);
-        const bf16 mid = __float2bfloat16_rn(r1);
-        const bf16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
-        gs[buf][0][r][c + q] = hi;
-        gs[buf][1][r][c + q] = mid;
-        gs[buf][2][r][c + q] = lo;
+      for (int i = 0; i < 4; ++i) {
+        const int idx = tid + 128 * i, r = idx >> 4, q = (idx & 15) * 4;
+        const int e = e0 + r;
+        const bool v = e < E && k0 + q < H;
+        rtc_cp16(smem_u32(graw + ((size_t)slot * RTC_TE + r) * RTC_RP + q), v ? gw + (int64_t)e * H + k0 + q : gw, v);
       }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");  // empty groups keep the count uniform
   };
   float acc[RTC_TE / 8][4];
 #pragma unroll
   for (int nb = 0; nb < RTC_TE / 8; ++nb)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[nb][j] = 0.f;
-  load(0);
-  int buf = 0;
-  for (int k0 = 0; k0 < H; k0 += RTC_KC, buf ^= 1) {
-    store(buf);
+#pragma unroll
+  for (int c = 0; c < RTC_STAGES - 1; ++c) issue(c);
+  for (int c = 0; c < nchunks; ++c) {
+    const int slot = c % RTC_STAGES;
+    asm volatile("cp.async.wait_group %0;" ::"n"(RTC_STAGES - 2) : "memory");
+    __syncthreads();  // chunk c landed for every thread; chunk c - 1's MMAs are done
+    issue(c + RTC_STAGES - 1);
+    // split this chunk's gate values into the three bf16 planes
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = tid + 128 * i, r = idx >> 4, q = (idx & 15) * 4;
+      const float4 g4 = *reinterpret_cast<const float4*>(graw + ((size_t)slot * RTC_TE + r) * RTC_RP + q);
+      const float g[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bf16 hi = __float2bfloat16_rn(g[j]);
+        const float r1 = g[j] - __bfloat162float(hi);
+        const bf16 mid = __float2bfloat16_rn(r1);
+        const bf16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+        gs[(0 * RTC_TE + r) * RTC_GP + q + j] = hi;
+        gs[(1 * RTC_TE + r) * RTC_GP + q + j] = mid;
+        gs[(2 * RTC_TE + r) * RTC_GP + q + j] = lo;
+      }
+    }
     __syncthreads();
-    if (k0 + RTC_KC < H) load(k0 + RTC_KC);
+    const bf16* xsl = xs + (size_t)slot * RTC_TT * RTC_XP;
 #pragma unroll
     for (int k16 = 0; k16 < RTC_KC / 16; ++k16) {
       uint32_t a0, a1, a2, a3;
-      rtc_ldsm_x4(smem_u32(&xs[buf][warp * 16 + (lane & 15)][k16 * 16 + (lane >> 4) * 8]), a0, a1, a2, a3);
+      rtc_ldsm_x4(smem_u32(xsl + (warp * 16 + (lane & 15)) * RTC_XP + k16 * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
 #pragma unroll
       for (int nb = 0; nb < RTC_TE / 8; ++nb) {
 #pragma unroll
         for (int part = 0; part < 3; ++part) {
           uint32_t b0, b1;
-          rtc_ldsm_x2(smem_u32(&gs[buf][part][nb * 8 + (lane & 7)][k16 * 16 + ((lane >> 3) & 1) * 8]), b0, b1);
+          rtc_ldsm_x2(smem_u32(gs + (part * RTC_TE + nb * 8 + (lane & 7)) * RTC_GP + k16 * 16 + ((lane >> 3) & 1) * 8),
+                      b0, b1);
           rtc_mma(acc[nb], a0, a1, a2, a3, b0, b1);
         }
       }
     }
-    __syncthreads();  // the buffer is rewritten two chunks later
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
   for (int nb = 0; nb < RTC_TE / 8; ++nb) {
@@ -652,9 +669,10 @@ int launch_router_logits(const void* x, int x_dtype, const float* gate_w, int T_
     if (E <= 16) return launch(router_logits_smem_kernel<float, 16>, xp);
     return launch(router_logits_smem_kernel<float, 32>, xp);
   }
-  if (x_dtype == STAGEML_BF16 && H % RTC_KC == 0 && aligned) {
+  if (x_dtype == STAGEML_BF16 && H % 32 == 0 && aligned) {
     const dim3 g2((unsigned)((T_ + RTC_TT - 1) / RTC_TT), (unsigned)((E + RTC_TE - 1) / RTC_TE));
-    (router_logits_tc_kernel<<<g2, 128, 0, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E, logits),
+    SB_CUDA_CHECK(cudaFuncSetAttribute(router_logits_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RTC_SMEM));
+    (router_logits_tc_kernel<<<g2, 128, RTC_SMEM, stream>>>(static_cast<const bf16*>(x), gate_w, T_, H, E, logits),
      ::sb::count_launch());
     SB_CUDA_CHECK(cudaGetLastError());
     return STAGEML_OK;
