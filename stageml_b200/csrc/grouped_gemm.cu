@@ -9,8 +9,11 @@
 //   warps 6..13 (FP8 weights only) converters: e4m3 -> 16-bit with the
 //               per-output-channel scale, written in the MMA's swizzled layout
 // Two 256-column accumulators in TMEM let the epilogue of tile i overlap the
-// main loop of tile i+1. 16-bit weights: 4 stages of 48 KB; FP8 weights: 3
-// stages of 64 KB (A 16 KB, 16-bit B 32 KB, e4m3 staging 16 KB).
+// main loop of tile i+1. 16-bit weights: 4 stages of 48 KB (A 16 KB, B 32 KB).
+// FP8 weights: a 4-stage TMA ring of 40 KB (A 16 KB, e4m3 B 16 KB; LoRA blocks
+// use all 40) and two 32 KB buffers for the converted 16-bit B tiles, so that
+// four K blocks of copies stay in flight while the converters fill one buffer
+// and the MMAs read the other.
 //
 // Per-token-tenant LoRA expand is fused on the tensor cores: after a tile's K
 // loop, the producer streams "LoRA blocks" through the same ring -- the
@@ -43,11 +46,18 @@ constexpr int CONVERTER_THREADS = 256;
 
 template <bool FP8B>
 struct Cfg {
-  static constexpr int STAGES = FP8B ? 3 : 4;
-  static constexpr int STAGE_BYTES = FP8B ? MMA_STAGE_BYTES + RAW_B_BYTES : MMA_STAGE_BYTES;
+  static constexpr int STAGES = 4;  // TMA ring
+  // a TMA stage: A and B (16-bit weights) or A and the e4m3 B (FP8 weights, with 8 KB more so
+  // that a LoRA block, which uses a stage whole, holds four tenant runs)
+  static constexpr int STAGE_BYTES = FP8B ? A_STAGE_BYTES + RAW_B_BYTES + 8192 : MMA_STAGE_BYTES;
+  static constexpr int CONV = FP8B ? 2 : 0;  // converted 16-bit B tiles (FP8 weights)
   static constexpr int THREADS = FP8B ? 192 + CONVERTER_THREADS : 192;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, run copies*/;
+  static constexpr int SMEM_BYTES =
+      STAGES * STAGE_BYTES + CONV * B_STAGE_BYTES + 1024 /*align*/ + 2048 /*barriers, run copies*/;
+  static constexpr int NBARS = 2 * STAGES + 5 + 2 * CONV + (FP8B ? STAGES : 0);
 };
+static_assert(Cfg<true>::SMEM_BYTES <= 232448 && Cfg<false>::SMEM_BYTES <= 232448, "shared memory per block");
+static_assert(Cfg<true>::NBARS * 8 + 8 <= 192 && Cfg<false>::NBARS * 8 + 8 <= 192, "barrier area");
 // The producer and the MMA issuer each bulk-copy the first kHdrRuns runs (tenant + 4
 // mask words each) of a unit's tile at the unit's start, so the LoRA phase costs no
 // global round trip per run: area after the stages = barriers (< 192 B), the
@@ -186,13 +196,17 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
                         const KParams p) {
   constexpr int STAGES = Cfg<FP8B>::STAGES;
   constexpr int STAGE_BYTES = Cfg<FP8B>::STAGE_BYTES;
+  constexpr int CONV = Cfg<FP8B>::CONV;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  // bars: [0,S) full (operands ready for the MMA), [S,2S) empty, [2S,2S+2) tmem_full,
-  // [2S+2,2S+4) tmem_empty, [2S+4] drain, [2S+5,3S+5) raw (TMA landed; FP8 weights only)
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
+  uint8_t* conv_smem = smem + STAGES * STAGE_BYTES;  // FP8 weights: CONV converted B tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(conv_smem + CONV * B_STAGE_BYTES);
+  // bars: [0,S) full (the stage's copies landed), [S,2S) empty, [2S,2S+2) tmem_full,
+  // [2S+2,2S+4) tmem_empty, [2S+4] drain; FP8 weights: [2S+5,2S+5+C) conv_full (a
+  // converted B tile is ready), [2S+5+C,2S+5+2C) conv_empty (the MMAs are done with it),
+  // [2S+5+2C,3S+5+2C) lseen (every converter saw a LoRA block's stage land)
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + Cfg<FP8B>::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
   uint64_t* hdr_bar_p = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + 192);
   const int32_t* hdr_smem = reinterpret_cast<const int32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
@@ -207,9 +221,14 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   auto tfull_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + a]); };
   auto tempty_bar = [&](int a) { return smem_u32(&bars[2 * STAGES + 2 + a]); };
   const uint32_t drain_bar = smem_u32(&bars[2 * STAGES + 4]);
-  auto raw_bar = [&](int s) { return smem_u32(&bars[2 * STAGES + 5 + s]); };
-  // the barrier TMA completes on: the MMA's own for 16-bit weights, the converters' for FP8
-  auto land_bar = [&](int s) { return FP8B ? raw_bar(s) : full_bar(s); };
+  auto conv_full_bar = [&](int c) { return smem_u32(&bars[2 * STAGES + 5 + c]); };
+  auto conv_empty_bar = [&](int c) { return smem_u32(&bars[2 * STAGES + 5 + CONV + c]); };
+  // The converters wait on every stage of the ring in order (they are never two phases
+  // behind a stage's barrier); a LoRA block's stage is released only after all of them
+  // saw it land, so the ring cannot lap them while they skip it.
+  auto lseen_bar = [&](int st) { return smem_u32(&bars[2 * STAGES + 5 + 2 * CONV + st]); };
+  auto land_bar = [&](int s) { return full_bar(s); };
+  const uint32_t conv_base = smem_u32(conv_smem);
 
   // Beside the pair kernel only the first `nctas` CTAs work; the others leave at once.
   int nctas = gridDim.x;
@@ -219,10 +238,15 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full_bar(s), FP8B ? CONVERTER_THREADS : 1);
+      mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
-      if (FP8B) mbar_init(raw_bar(s), 1);
     }
+    for (int c = 0; c < CONV; ++c) {
+      mbar_init(conv_full_bar(c), CONVERTER_THREADS);
+      mbar_init(conv_empty_bar(c), 1);
+    }
+    if (FP8B)
+      for (int st = 0; st < STAGES; ++st) mbar_init(lseen_bar(st), CONVERTER_THREADS);
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
       mbar_init(tempty_bar(a), 4);
@@ -290,11 +314,11 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         }
         const uint32_t sa = smem_base + s * STAGE_BYTES;
         if (FP8B) {
-          const uint32_t sraw = sa + MMA_STAGE_BYTES;
-          mbar_arrive_expect_tx(raw_bar(s), A_STAGE_BYTES + RAW_B_BYTES);
-          tma_load_2d(sa, &tm_a, raw_bar(s), kb * BK, a_row, pol_a);
-          tma_load_2d(sraw, &tm_b, raw_bar(s), kb * BK, b_row0, pol_b);
-          tma_load_2d(sraw + 128 * BK, &tm_b, raw_bar(s), kb * BK, b_row1, pol_b);
+          const uint32_t sraw = sa + A_STAGE_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), A_STAGE_BYTES + RAW_B_BYTES);
+          tma_load_2d(sa, &tm_a, full_bar(s), kb * BK, a_row, pol_a);
+          tma_load_2d(sraw, &tm_b, full_bar(s), kb * BK, b_row0, pol_b);
+          tma_load_2d(sraw + 128 * BK, &tm_b, full_bar(s), kb * BK, b_row1, pol_b);
         } else {
           const uint32_t sbm = sa + A_STAGE_BYTES;
           mbar_arrive_expect_tx(full_bar(s), MMA_STAGE_BYTES);
@@ -355,7 +379,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc = idesc_f16(BM, BN, IsBf16<T>::value);
     const uint32_t idesc_n128 = idesc_f16(BM, 128, IsBf16<T>::value);
-    uint32_t it = 0;
+    uint32_t it = 0, cv = 0;
+    uint32_t lpar = 0;  // FP8 weights: parity bit per stage of its next LoRA use
     int tcount = 0;
     bool ok = true;
     bool issued_any = false;
@@ -390,14 +415,23 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           ok = false;
           break;
         }
+        const int c = FP8B ? (int)(cv % CONV) : 0;
+        if (FP8B && !mbar_wait(conv_full_bar(c), (cv / CONV) & 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t sa = smem_base + s * STAGE_BYTES;
         const uint64_t adesc = smem_desc_sw128(sa);
-        const uint64_t bdesc = smem_desc_sw128(sa + A_STAGE_BYTES);
+        const uint64_t bdesc = smem_desc_sw128(FP8B ? conv_base + c * B_STAGE_BYTES : sa + A_STAGE_BYTES);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k)
           tc_mma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
         tc_commit(empty_bar(s));
+        if (FP8B) {
+          tc_commit(conv_empty_bar(c));
+          ++cv;
+        }
         issued_any = true;
       }
       if (ok && p.rank) {
@@ -413,6 +447,13 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
           ok = false;
           break;
+        }
+        if (FP8B) {
+          if (!mbar_wait(lseen_bar(s), (lpar >> s) & 1u, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          lpar ^= 1u << s;
         }
         tc_fence_after();
         const uint32_t base = smem_base + s * STAGE_BYTES;
@@ -530,7 +571,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
     // e4m3 row; written as 16-bit logical chunks 2c, 2c+1 of the 128-byte row, stored at
     // physical chunk (logical ^ (r & 7)) -- the 128B swizzle the MMA descriptor expects.
     const int ct = threadIdx.x - 192;
-    uint32_t it = 0;
+    uint32_t it = 0, cv = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += nctas) {
       int m_pos, n_tile;
       unit_mn(p, tile, num_m_tiles, m_pos, n_tile);
@@ -551,16 +592,18 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         sc[q] = grow < p.b_rows_total ? p.b_row_scale[grow] : 0.f;
       }
       bool ok = true;
-      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+      for (int kb = 0; kb < num_kb; ++kb, ++it, ++cv) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(raw_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+        const int c = (int)(cv % CONV);
+        if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma) ||
+            !mbar_wait(conv_empty_bar(c), ((cv / CONV) & 1) ^ 1, abort_flag, p.status, p.timeout_ns,
+                       kDevTimeoutMma)) {
           ok = false;
           break;
         }
-        uint8_t* st = smem + s * STAGE_BYTES;
-        const uint8_t* raw = st + MMA_STAGE_BYTES;
-        uint8_t* bt = st + A_STAGE_BYTES;
+        const uint8_t* raw = smem + s * STAGE_BYTES + A_STAGE_BYTES;
+        uint8_t* bt = conv_smem + c * B_STAGE_BYTES;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const uint4 qv = *reinterpret_cast<const uint4*>(raw + rr[q] * BK + cc[q] * 16);
@@ -572,17 +615,18 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           *reinterpret_cast<uint4*>(row + (((2 * cc[q] + 1) ^ sw) << 4)) = hi;
         }
         fence_proxy_async_smem();
-        mbar_arrive(full_bar(s));
+        mbar_arrive(conv_full_bar(c));
       }
+      // LoRA blocks (16-bit already) go from the TMA ring to the MMAs; the converters only
+      // report that they saw each one land
       const int nruns = ok ? tile_nruns : 0;
       for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
         const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (!mbar_wait(raw_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
+        if (!mbar_wait(full_bar(s), (it / STAGES) & 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
           ok = false;
           break;
         }
-        mbar_arrive(full_bar(s));  // LoRA operands are already 16-bit
+        mbar_arrive(lseen_bar(s));
       }
       if (!ok) break;
     }
@@ -731,7 +775,9 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   p.lchunks = (g.rank + 15) / 16;
   p.s_bytes = (g.swiglu ? 2 : 1) * p.lchunks * LCHUNK;
   p.run_bytes = 2 * p.lchunks * LCHUNK;
-  p.runs_per_block = g.rank ? (MMA_STAGE_BYTES - p.s_bytes) / p.run_bytes : 1;
+  // a LoRA block (S and the runs' B rows) fills one TMA stage
+  const int lora_block_bytes = g.b_fp8 ? Cfg<true>::STAGE_BYTES : Cfg<false>::STAGE_BYTES;
+  p.runs_per_block = g.rank ? (lora_block_bytes - p.s_bytes) / p.run_bytes : 1;
   p.lb_tenant_rows = g.rank ? g.lora_b_tenant_stride / g.rank : 0;
   p.lb_group_rows = g.rank ? g.lora_b_group_stride / g.rank : 0;
   p.tile_runs = g.tile_runs;
