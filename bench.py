@@ -553,8 +553,8 @@ def ours_arm(args, cfg, rank: int, world: int, local_rank: int):
 # the build it was captured on. It is stale once the GEMM changes after that build.
 GATE_UP_DRAM_CAPTURE: dict = {
     "mixtral_moe_lora": {
-        "bytes": (2.272425e9 + 0.114396e9) + (1.186264e9 + 0.016262e9),
-        "source": "ncu capture of commit fe0ac35: pair kernel 2.387 GB + odd-tile kernel 1.203 GB "
+        "bytes": 2.376832e9 + 0.132748e9,
+        "source": "ncu capture of commit 24e4d5a: pair kernel with the odd tiles as half units, 2.510 GB "
                   "(profiles/grouped_gemm_pair_mixtral.md)",
     },
 }
