@@ -141,10 +141,11 @@ void carve_pair_plan(Carver& c, int64_t tiles_cap, bool lora, PairPlan* pp) {
 // Grouped rows (tile_group, group_offsets, num_tiles_dev from a plan) or direct
 // rows (static_rows); row_tenant only when the GEMMs carry LoRA.
 int build_pair_plan(const PairPlan& pp, const int32_t* tile_group, const int32_t* group_offsets,
-                    const int32_t* num_tiles_dev, int64_t static_rows, const int32_t* row_tenant, cudaStream_t st) {
+                    const int32_t* num_tiles_dev, int64_t static_rows, const int32_t* row_tenant, cudaStream_t st,
+                    bool pdl = false) {
   return launch_pair_plan(tile_group, group_offsets, num_tiles_dev, pp.tiles_cap, static_rows,
                           pp.pruns ? row_tenant : nullptr, pp.pairs, pp.num_pairs, pp.pruns, pp.pnruns, st,
-                          pp.singles, pp.num_singles, pp.sruns, pp.snruns, pp.hpairs, pp.num_hpairs);
+                          pp.singles, pp.num_singles, pp.sruns, pp.snruns, pp.hpairs, pp.num_hpairs, pdl);
 }
 
 // Per host thread and device: a side stream and two events for running the odd tiles
@@ -195,8 +196,10 @@ bool odd_tiles_as_half_units(const GemmLaunch& g) {
 // trailing odd tiles either as half units of the same kernel, or on the one-CTA
 // kernel from a side stream launched right after it, so their CTAs take the SMs the
 // persistent pair kernel leaves them. Without a plan (or with e4m3 weights): the
-// one-CTA kernel over all tiles (g.tile_runs set by the caller).
-int run_grouped_gemm(GemmLaunch g, const PairPlan& pp, cudaStream_t st) {
+// one-CTA kernel over all tiles (g.tile_runs set by the caller). *two_streams tells
+// the caller that the side stream ran (the next kernel then takes an ordinary launch).
+int run_grouped_gemm(GemmLaunch g, const PairPlan& pp, cudaStream_t st, bool* two_streams = nullptr) {
+  if (two_streams) *two_streams = false;
   if (!pp.on() || g.b_fp8) return launch_grouped_gemm(g, st);
   if (odd_tiles_as_half_units(g)) {
     g.pairs = pp.hpairs;
@@ -207,6 +210,8 @@ int run_grouped_gemm(GemmLaunch g, const PairPlan& pp, cudaStream_t st) {
     g.pair_half_units = true;
     return launch_grouped_gemm(g, st);
   }
+  g.pdl = false;  // two kernels on two streams: ordinary launches
+  if (two_streams) *two_streams = true;
   g.split_pairs_dev = pp.num_pairs;
   g.split_singles_dev = pp.num_singles;
   g.split_cap = pp.tiles_cap;
@@ -344,11 +349,12 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
 // One expert projection of the MoE layer: decode-sized batches on the skinny GEMM,
 // otherwise the grouped GEMM with the layer's pair plan.
 int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, bool skinny, cudaStream_t st, int64_t max_rows,
-                 int pdl_mode = 0) {
+                 int pdl_mode = 0, bool* two_streams = nullptr) {
+  if (two_streams) *two_streams = false;
   if (skinny)
     return launch_skinny_gemm(g, b.plan.row_tenant, b.plan.group_offsets, b.plan.group_counts, st, max_rows,
                               pdl_mode);
-  return run_grouped_gemm(g, b.pp, st);
+  return run_grouped_gemm(g, b.pp, st, two_streams);
 }
 
 int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
@@ -376,6 +382,9 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   // scheduled while the previous one finishes, and each skinny GEMM streams its
   // weights while the shrink before it runs.
   const bool pdl = skinny && pdl_enabled();
+  // larger batches: programmatic dependent launches between the kernels after the router
+  const bool pdl_big = !skinny && pdl_enabled();
+  bool two_streams = false;  // the last grouped GEMM ran its odd tiles on the side stream
 
   // R1: routing
   const void* ids = a->topk_ids;
@@ -396,14 +405,14 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   permute_carve(b.perm_scratch, P, nkeys, &scr);
   SB_STAGE(STAGEML_STAGE_PERMUTE, launch_permute(ids, ids_dtype, wts, wts_dtype, a->tenant_ids, a->T, a->k,
                                                  a->n_shared, E_tot, a->n_tenants, 0, b.plan, status, scr, st,
-                                                 a->T_dev, pdl, a->fold_slot, n_fold));
+                                                 a->T_dev, pdl || pdl_big, a->fold_slot, n_fold));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
   if (!skinny && b.pp.on()) {
     SB_STAGE(STAGEML_STAGE_PERMUTE, build_pair_plan(b.pp, b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles,
-                                                    0, b.plan.row_tenant, st));
+                                                    0, b.plan.row_tenant, st, pdl_big));
   } else if (!skinny && b.runs) {
-    SB_STAGE(STAGEML_STAGE_PERMUTE,
-             launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
+    SB_STAGE(STAGEML_STAGE_PERMUTE, launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs,
+                                                     b.nruns, st, nullptr, pdl_big));
   }
   // gather + R4 shrink of w1|w3 (decode-sized batches: no gather, the skinny GEMM
   // reads the token rows in place, and the per-pair shrink)
@@ -418,6 +427,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     s.rows_cap = b.plan.rows_cap;
     s.row_tenant = b.plan.row_tenant;
     s.tile_group = b.plan.tile_group;
+    s.pdl = pdl_big;
     if (lora13) {
       s.lora_a = a->lora_a13;
       s.a_group_stride = (int64_t)2 * a->rank * a->H;
@@ -465,7 +475,9 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.hbuf;
     g.ldo = a->I;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_moe_gemm(g, b, skinny, st, P, pdl ? (lora13 ? 2 : 1) : 0));
+    g.pdl = pdl_big;
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP,
+             run_moe_gemm(g, b, skinny, st, P, pdl ? (lora13 ? 2 : 1) : 0, &two_streams));
   }
   // R4 shrink of h for w2
   if (lora2) {
@@ -481,6 +493,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     s.a_group_stride = (int64_t)a->rank * a->I;
     s.a_tenant_stride = (int64_t)E_tot * s.a_group_stride;
     s.R = a->rank;
+    s.pdl = pdl_big && !two_streams;
     s.spart = b.spart2;
     s.s_out = b.s2;
     s.lora_scale = a->lora_scale;
@@ -523,11 +536,14 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     g.out = b.xp;
     g.ldo = a->H;
     g.status = status;
-    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_moe_gemm(g, b, skinny, st, P, pdl ? (lora2 ? 2 : 1) : 0));
+    g.pdl = pdl_big && (lora2 || !two_streams);
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN,
+             run_moe_gemm(g, b, skinny, st, P, pdl ? (lora2 ? 2 : 1) : 0, &two_streams));
   }
   // combine
   SB_STAGE(STAGEML_STAGE_COMBINE,
-           launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st, a->T_dev, pdl));
+           launch_combine(b.xp, b.plan.pair_row, a->T, a->k + a->n_shared, a->H, bf, a->out, st, a->T_dev,
+                          pdl || (pdl_big && !two_streams)));
   return STAGEML_OK;
 }
 
@@ -875,7 +891,9 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   int32_t* stat = a->status ? a->status : b.status;
   const int bf = a->dtype == STAGEML_BF16;
   const int n_ten = lora ? a->n_tenants : 0;
+  const bool pdl = pdl_enabled();  // programmatic dependent launches along the chain
   GemmLaunch g;
+  g.pdl = pdl;
   g.K = a->K;
   g.b = a->w_bank;
   g.b_rows_total = (int64_t)a->n_groups * a->N;
@@ -888,6 +906,7 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   ShrinkLaunch sh;
   sh.K = a->K;
   sh.dtype_bf16 = bf;
+  sh.pdl = pdl;
   if (lora) {
     sh.lora_a = a->lora_a;
     sh.a_tenant_stride = (int64_t)a->rank * a->K;
@@ -908,23 +927,23 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   if (a->n_groups == 1) {
     if (lora) {
       SB_STAGE(STAGEML_STAGE_GATHER_SHRINK,
-               launch_validate_tenants(a->row_tenant, a->M, n_ten, b.tenants, stat, st));
+               launch_validate_tenants(a->row_tenant, a->M, n_ten, b.tenants, stat, st, pdl));
       if (!b.pp.on())
-        SB_STAGE(STAGEML_STAGE_GATHER_SHRINK,
-                 launch_tile_runs(b.tenants, nullptr, a->M, (int)((a->M + 127) / 128), b.runs, b.nruns, st));
+        SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_tile_runs(b.tenants, nullptr, a->M, (int)((a->M + 127) / 128),
+                                                               b.runs, b.nruns, st, nullptr, pdl));
       sh.src = a->x;
       sh.static_rows = a->M;
       sh.rows_cap = a->M;
       sh.row_tenant = b.tenants;
       if (a->M <= kRowShrinkMaxRows)
-        SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(sh, nullptr, a->M, st));
+        SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(sh, nullptr, a->M, st, pdl));
       else
         SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
       g.s_rows = a->M;
     }
     if (b.pp.on())
       SB_STAGE(STAGEML_STAGE_PERMUTE,
-               build_pair_plan(b.pp, nullptr, nullptr, nullptr, a->M, lora ? b.tenants : nullptr, st));
+               build_pair_plan(b.pp, nullptr, nullptr, nullptr, a->M, lora ? b.tenants : nullptr, st, pdl));
     g.a = a->x;
     g.a_rows = a->M;
     g.m_rows = a->M;
@@ -937,14 +956,14 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   permute_carve(b.perm, a->M, permute_num_keys(0, n_ten, 0, a->n_groups), &scr);
   SB_STAGE(STAGEML_STAGE_PERMUTE,
            launch_permute(a->row_group, STAGEML_I32, nullptr, STAGEML_F32, lora ? a->row_tenant : nullptr, a->M, 1, 0,
-                          a->n_groups, n_ten, 0, b.plan, stat, scr, st));
+                          a->n_groups, n_ten, 0, b.plan, stat, scr, st, nullptr, pdl));
   const int tiles_cap = (int)(b.plan.rows_cap / 128);
   if (b.pp.on())
     SB_STAGE(STAGEML_STAGE_PERMUTE, build_pair_plan(b.pp, b.plan.tile_group, b.plan.group_offsets, b.plan.num_tiles,
-                                                    0, lora ? b.plan.row_tenant : nullptr, st));
+                                                    0, lora ? b.plan.row_tenant : nullptr, st, pdl));
   else if (lora)
-    SB_STAGE(STAGEML_STAGE_PERMUTE,
-             launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs, b.nruns, st));
+    SB_STAGE(STAGEML_STAGE_PERMUTE, launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs,
+                                                     b.nruns, st, nullptr, pdl));
   sh.src = a->x;
   sh.src_row_of = b.plan.row_token;
   sh.gather_dst = b.xp;
@@ -958,7 +977,7 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
     gather.R = 0;
     gather.lora_a = nullptr;
     SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(gather, st));
-    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(sh, b.plan.pair_row, a->M, st));
+    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_pair_shrink(sh, b.plan.pair_row, a->M, st, pdl));
   } else {
     SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, launch_gather_shrink(sh, st));
   }
@@ -970,8 +989,10 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
   g.s_rows = b.plan.rows_cap;
   g.out = b.yp;
   g.ldo = a->N;
-  SB_STAGE(STAGEML_STAGE_GEMM, run_grouped_gemm(g, b.pp, st));
-  SB_STAGE(STAGEML_STAGE_COMBINE, launch_combine(b.yp, b.plan.pair_row, a->M, 1, a->N, bf, a->y, st));
+  bool two_streams = false;
+  SB_STAGE(STAGEML_STAGE_GEMM, run_grouped_gemm(g, b.pp, st, &two_streams));
+  SB_STAGE(STAGEML_STAGE_COMBINE,
+           launch_combine(b.yp, b.plan.pair_row, a->M, 1, a->N, bf, a->y, st, nullptr, pdl && !two_streams));
   return STAGEML_OK;
 }
 

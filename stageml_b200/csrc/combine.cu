@@ -35,6 +35,8 @@ __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restric
 
 __global__ void validate_tenants_kernel(const int32_t* __restrict__ in, int64_t n, int n_tenants,
                                         int32_t* __restrict__ out, int32_t* status) {
+  pdl_wait();  // the ids may come from the previous kernel
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   int v = in ? in[i] : -1;
@@ -82,9 +84,11 @@ int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H
 }
 
 int launch_validate_tenants(const int32_t* in, int64_t n, int n_tenants, int32_t* out, int32_t* status,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, bool pdl) {
   if (n == 0) return STAGEML_OK;
-  (validate_tenants_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(in, n, n_tenants, out, status), ::sb::count_launch());
+  SB_CUDA_CHECK(launch_kernel(validate_tenants_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, stream, pdl, in,
+                              n, n_tenants, out, status));
+  ::sb::count_launch();
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }

@@ -198,6 +198,10 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
   constexpr int STAGE_BYTES = Cfg<FP8B>::STAGE_BYTES;
   constexpr int CONV = Cfg<FP8B>::CONV;
   extern __shared__ uint8_t smem_raw[];
+  // Every CTA waits before anything else, the ones that leave at once too, so that
+  // this grid never completes ahead of the kernel before it.
+  pdl_wait();
+  pdl_trigger();
   // 1024-byte alignment for the 128B-swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* conv_smem = smem + STAGES * STAGE_BYTES;  // FP8 weights: CONV converted B tiles
@@ -648,6 +652,8 @@ __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restric
                                                         const int32_t* __restrict__ tile_list) {
   __shared__ int32_t s_ten[4][kMaxRunsPerTile];
   __shared__ uint32_t s_mask[4][kMaxRunsPerTile][4];
+  pdl_wait();  // the plan and the tenants may come from the previous kernels
+  pdl_trigger();
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x * 4 + w;  // entry of the output (and of tile_list)
   const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
@@ -693,12 +699,13 @@ __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restric
 }
 
 template <typename T, bool FP8B>
-int launch_kernel(int grid, cudaStream_t stream, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
-                  const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const KParams& p) {
+int launch_gemm_kernel(int grid, cudaStream_t stream, bool pdl, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
+                       const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const KParams& p) {
   SB_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<T, FP8B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      Cfg<FP8B>::SMEM_BYTES));
-  (grouped_gemm_kernel<T, FP8B><<<grid, Cfg<FP8B>::THREADS, Cfg<FP8B>::SMEM_BYTES, stream>>>(tm_a, tm_b, tm_s, tm_lb, p),
-   ::sb::count_launch());
+  SB_CUDA_CHECK(launch_kernel(grouped_gemm_kernel<T, FP8B>, dim3(grid), dim3(Cfg<FP8B>::THREADS),
+                              Cfg<FP8B>::SMEM_BYTES, stream, pdl, tm_a, tm_b, tm_s, tm_lb, p));
+  ::sb::count_launch();
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
@@ -706,14 +713,14 @@ int launch_kernel(int grid, cudaStream_t stream, const CUtensorMap& tm_a, const 
 }  // namespace
 
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
-                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list) {
+                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list, bool pdl) {
   SB_CHECK_ARG(row_tenant && runs && nruns, "tile_runs: null pointer");
   SB_CHECK_ARG(!tile_list || num_tiles_dev, "tile_runs: a tile list needs its device count");
   const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
   if (tiles == 0) return STAGEML_OK;
-  (tile_runs_kernel<<<(unsigned)((tiles + 3) / 4), 128, 0, stream>>>(row_tenant, num_tiles_dev, static_rows,
-                                                                     tiles_cap, runs, nruns, tile_list),
-   ::sb::count_launch());
+  SB_CUDA_CHECK(launch_kernel(tile_runs_kernel, dim3((unsigned)((tiles + 3) / 4)), dim3(128), 0, stream, pdl,
+                              row_tenant, num_tiles_dev, static_rows, tiles_cap, runs, nruns, tile_list));
+  ::sb::count_launch();
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
@@ -803,10 +810,10 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   const int grid = (int)std::min<int64_t>(tiles_upper, sm_count());
 
   if (g.b_fp8)
-    return g.in_bf16 ? launch_kernel<bf16, true>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p)
-                     : launch_kernel<f16, true>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p);
-  return g.in_bf16 ? launch_kernel<bf16, false>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p)
-                   : launch_kernel<f16, false>(grid, stream, tm_a, tm_b, tm_s, tm_lb, p);
+    return g.in_bf16 ? launch_gemm_kernel<bf16, true>(grid, stream, g.pdl, tm_a, tm_b, tm_s, tm_lb, p)
+                     : launch_gemm_kernel<f16, true>(grid, stream, g.pdl, tm_a, tm_b, tm_s, tm_lb, p);
+  return g.in_bf16 ? launch_gemm_kernel<bf16, false>(grid, stream, g.pdl, tm_a, tm_b, tm_s, tm_lb, p)
+                   : launch_gemm_kernel<f16, false>(grid, stream, g.pdl, tm_a, tm_b, tm_s, tm_lb, p);
 }
 
 }  // namespace sb

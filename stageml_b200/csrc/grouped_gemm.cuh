@@ -77,6 +77,8 @@ struct GemmLaunch {
   // A pair whose second tile is -1 is a half unit: its one tile on both CTAs (64 rows
   // each, M = 128 MMAs) instead of a pair with an idle half.
   bool pair_half_units = false;
+  // Programmatic dependent launch (the kernels wait for the previous kernel first).
+  bool pdl = false;
   // The pair kernel and the odd-tile kernel side by side (split_sms > 0): each
   // reads the pair and odd-tile counts and keeps only its share of the split_sms
   // SMs busy (split_single_ctas); the CTAs past its share exit at once.
@@ -111,7 +113,8 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 // Rows with tenant < 0 belong to no run. Active rows: 128 * (*num_tiles_dev)
 // (capped at tiles_cap tiles) or static_rows when num_tiles_dev is null.
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
-                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list = nullptr);
+                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list = nullptr,
+                     bool pdl = false);
 // With tile_list, entry i covers tile tile_list[i] (i < *num_tiles_dev) and runs / nruns
 // are indexed by that tile id; static_rows > 0 then bounds the rows read (direct rows).
 constexpr int kMaxRunsPerTile = 128;
@@ -145,7 +148,8 @@ int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, co
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
                      int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream,
                      int32_t* singles = nullptr, int32_t* num_singles = nullptr, int32_t* sruns = nullptr,
-                     int32_t* snruns = nullptr, int32_t* hpairs = nullptr, int32_t* num_hpairs = nullptr);
+                     int32_t* snruns = nullptr, int32_t* hpairs = nullptr, int32_t* num_hpairs = nullptr,
+                     bool pdl = false);
 size_t pair_runs_ints(int64_t pairs_cap);
 
 // Weight-streaming variant for at most 16 valid rows per 128-row tile (decode-sized

@@ -156,6 +156,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                              const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_lb,
                              const __grid_constant__ CUtensorMap tm_a64, const __grid_constant__ CUtensorMap tm_b64,
                              const PParams p) {
+  // Every CTA waits before anything else, the ones that leave at once too, so that
+  // this grid never completes ahead of the kernel before it.
+  pdl_wait();
+  pdl_trigger();
   // Beside the odd-tile kernel only the first `nclusters` clusters work; the others
   // leave their SMs to it (both CTAs of a cluster decide alike, before any barrier).
   int nclusters = gridDim.x >> 1;
@@ -659,6 +663,8 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
     int32_t* __restrict__ num_singles_out, int32_t* __restrict__ pruns, int32_t* __restrict__ pnruns,
     int32_t* __restrict__ sruns, int32_t* __restrict__ snruns, int32_t* __restrict__ hpairs,
     int32_t* __restrict__ num_hpairs_out) {
+  pdl_wait();  // the permutation plan and the tenants may come from the previous kernels
+  pdl_trigger();
   const int ntiles = num_tiles_dev ? min(*num_tiles_dev, tiles_cap) : (int)((static_rows + 127) / 128);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const bool split = singles != nullptr;
@@ -745,7 +751,8 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(
 }
 
 template <typename T>
-int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
+int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, bool pdl, const CUtensorMap& tm_a,
+                       const CUtensorMap& tm_b,
                        const CUtensorMap& tm_s, const CUtensorMap& tm_lb, const CUtensorMap& tm_a64,
                        const CUtensorMap& tm_b64, const PParams& p) {
   auto kern = grouped_gemm_pair_kernel<T>;
@@ -756,16 +763,18 @@ int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorM
   int dev = 0;
   SB_CUDA_CHECK(cudaGetDevice(&dev));
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // the occupancy query below sees the cluster shape only
   int max_clusters = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
@@ -781,6 +790,7 @@ int launch_pair_kernel(int64_t units_upper, cudaStream_t stream, const CUtensorM
   }
   const int64_t clusters = std::min<int64_t>(units_upper, max_clusters);
   cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+  cfg.numAttrs = pdl ? 2 : 1;
   SB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p));
   ::sb::count_launch();
   return STAGEML_OK;
@@ -794,7 +804,7 @@ int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, co
                      int tiles_cap, int64_t static_rows, const int32_t* row_tenant, int32_t* pairs,
                      int32_t* num_pairs, int32_t* runs, int32_t* nruns, cudaStream_t stream, int32_t* singles,
                      int32_t* num_singles, int32_t* sruns, int32_t* snruns, int32_t* hpairs,
-                     int32_t* num_hpairs) {
+                     int32_t* num_hpairs, bool pdl) {
   SB_CHECK_ARG(pairs && num_pairs, "pair plan: null output");
   SB_CHECK_ARG(!singles == !num_singles, "pair plan: singles need their count");
   SB_CHECK_ARG(!hpairs == !num_hpairs, "pair plan: the half-unit list needs its count");
@@ -804,10 +814,11 @@ int launch_pair_plan(const int32_t* tile_group, const int32_t* group_offsets, co
   const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
   const int64_t run_blocks = (row_tenant && tiles > 0) ? (tiles + kPlanWarps - 1) / kPlanWarps : 0;
   SB_CHECK_ARG(run_blocks < 65535 * 1024LL, "pair plan: too many tiles");
-  (pair_plan_kernel<<<(unsigned)(1 + run_blocks), kPlanThreads, 0, stream>>>(
-       tile_group, group_offsets, num_tiles_dev, tiles_cap, static_rows, row_tenant, pairs, num_pairs, singles,
-       num_singles, row_tenant ? runs : nullptr, nruns, row_tenant ? sruns : nullptr, snruns, hpairs, num_hpairs),
-   ::sb::count_launch());
+  SB_CUDA_CHECK(launch_kernel(pair_plan_kernel, dim3((unsigned)(1 + run_blocks)), dim3(kPlanThreads), 0, stream, pdl,
+                              tile_group, group_offsets, num_tiles_dev, tiles_cap, static_rows, row_tenant, pairs,
+                              num_pairs, singles, num_singles, row_tenant ? runs : nullptr, nruns,
+                              row_tenant ? sruns : nullptr, snruns, hpairs, num_hpairs));
+  ::sb::count_launch();
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
@@ -877,8 +888,8 @@ int launch_grouped_gemm_pair(const GemmLaunch& g, cudaStream_t stream) {
 
   const int64_t units_upper = (int64_t)g.pairs_cap * p.num_n_tiles;
   if (units_upper == 0) return STAGEML_OK;
-  return g.in_bf16 ? launch_pair_kernel<bf16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p)
-                   : launch_pair_kernel<f16>(units_upper, stream, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p);
+  return g.in_bf16 ? launch_pair_kernel<bf16>(units_upper, stream, g.pdl, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p)
+                   : launch_pair_kernel<f16>(units_upper, stream, g.pdl, tm_a, tm_b, tm_s, tm_lb, tm_a64, tm_b64, p);
 }
 
 }  // namespace sb

@@ -58,6 +58,7 @@ struct ShrinkLaunch {
   float* spart = nullptr;               // [KS][rows_cap][R]
   void* s_out = nullptr;                // [rows_cap][R] 16-bit (reduced, scaled): the LoRA-expand MMA operand
   const float* lora_scale = nullptr;    // [n_tenants]
+  bool pdl = false;                     // programmatic dependent launches (both kernels wait first)
 };
 constexpr int kShrinkKSlice = 512;
 inline int shrink_num_slices(int K) { return (K + kShrinkKSlice - 1) / kShrinkKSlice; }
@@ -77,7 +78,7 @@ int launch_combine(const void* y, const int32_t* pair_row, int T, int kk, int H,
                    bool pdl = false);
 // clamp caller tenant ids into [-1, n_tenants) (invalid -> -1 + status)
 int launch_validate_tenants(const int32_t* in, int64_t n, int n_tenants, int32_t* out, int32_t* status,
-                            cudaStream_t stream);
+                            cudaStream_t stream, bool pdl = false);
 
 // fold.cu
 int launch_lora_fold(const void* W, const void* A, const void* B, const float* scale, int batch, int rows, int cols,

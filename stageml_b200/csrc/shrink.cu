@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
   using Ring = ShrinkRing<NBS>;
   constexpr int R = Ring::R;
   extern __shared__ __align__(16) uint8_t smem[];
+  pdl_wait();  // the plan and the source rows may come from the previous kernels
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t rows_active = active_rows(p.num_tiles_dev, p.static_rows, p.rows_cap);
   const int64_t row0 = (int64_t)blockIdx.y * 64 + warp * 16;
@@ -261,6 +263,8 @@ __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, in
                                      const int32_t* __restrict__ num_tiles_dev, int64_t static_rows,
                                      const int32_t* __restrict__ row_tenant, const float* __restrict__ scale,
                                      T* __restrict__ s_out) {
+  pdl_wait();  // the partial sums of the kernel before
+  pdl_trigger();
   const int64_t rows_active = active_rows(num_tiles_dev, static_rows, rows_cap);
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows_active * R) return;
@@ -275,15 +279,16 @@ __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, in
 }
 
 template <int NBS>
-int launch_shrink_variant(bool bf, dim3 grid, const ShrinkParams& p, cudaStream_t stream) {
+int launch_shrink_variant(bool bf, dim3 grid, const ShrinkParams& p, cudaStream_t stream, bool pdl) {
   constexpr int smem = ShrinkRing<NBS>::SMEM;
   if (bf) {
     SB_CUDA_CHECK(cudaFuncSetAttribute(gather_shrink_kernel<bf16, NBS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    (gather_shrink_kernel<bf16, NBS><<<grid, 128, smem, stream>>>(p), ::sb::count_launch());
+    SB_CUDA_CHECK(launch_kernel(gather_shrink_kernel<bf16, NBS>, grid, dim3(128), smem, stream, pdl, p));
   } else {
     SB_CUDA_CHECK(cudaFuncSetAttribute(gather_shrink_kernel<f16, NBS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    (gather_shrink_kernel<f16, NBS><<<grid, 128, smem, stream>>>(p), ::sb::count_launch());
+    SB_CUDA_CHECK(launch_kernel(gather_shrink_kernel<f16, NBS>, grid, dim3(128), smem, stream, pdl, p));
   }
+  ::sb::count_launch();
   return STAGEML_OK;
 }
 
@@ -449,19 +454,19 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   SB_CHECK_ARG(grid.y <= 65535u, "shrink: too many rows for one launch");
   switch (s.R / 8) {
     case 0:
-      SB_TRY(launch_shrink_variant<0>(s.dtype_bf16, grid, p, stream));
+      SB_TRY(launch_shrink_variant<0>(s.dtype_bf16, grid, p, stream, s.pdl));
       break;
     case 1:
-      SB_TRY(launch_shrink_variant<1>(s.dtype_bf16, grid, p, stream));
+      SB_TRY(launch_shrink_variant<1>(s.dtype_bf16, grid, p, stream, s.pdl));
       break;
     case 2:
-      SB_TRY(launch_shrink_variant<2>(s.dtype_bf16, grid, p, stream));
+      SB_TRY(launch_shrink_variant<2>(s.dtype_bf16, grid, p, stream, s.pdl));
       break;
     case 4:
-      SB_TRY(launch_shrink_variant<4>(s.dtype_bf16, grid, p, stream));
+      SB_TRY(launch_shrink_variant<4>(s.dtype_bf16, grid, p, stream, s.pdl));
       break;
     case 8:
-      SB_TRY(launch_shrink_variant<8>(s.dtype_bf16, grid, p, stream));
+      SB_TRY(launch_shrink_variant<8>(s.dtype_bf16, grid, p, stream, s.pdl));
       break;
     default:
       return set_error(STAGEML_ERR_INVALID_ARG, "shrink: R=%d must be 0, 8, 16, 32 or 64", s.R);
@@ -469,16 +474,16 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {
     const int64_t n = rows_max * s.R;
+    const dim3 rgrid((unsigned)((n + 255) / 256));
     if (s.dtype_bf16)
-      (shrink_reduce_kernel<bf16><<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-           s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
-           static_cast<bf16*>(s.s_out)),
-       ::sb::count_launch());
+      SB_CUDA_CHECK(launch_kernel(shrink_reduce_kernel<bf16>, rgrid, dim3(256), 0, stream, s.pdl, s.spart, KS,
+                                  p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
+                                  static_cast<bf16*>(s.s_out)));
     else
-      (shrink_reduce_kernel<f16><<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-           s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
-           static_cast<f16*>(s.s_out)),
-       ::sb::count_launch());
+      SB_CUDA_CHECK(launch_kernel(shrink_reduce_kernel<f16>, rgrid, dim3(256), 0, stream, s.pdl, s.spart, KS,
+                                  p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
+                                  static_cast<f16*>(s.s_out)));
+    ::sb::count_launch();
     SB_CUDA_CHECK(cudaGetLastError());
   }
   return STAGEML_OK;

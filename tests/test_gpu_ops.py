@@ -270,6 +270,48 @@ def test_decode_calls_back_to_back_match_synchronized_calls(ops):
     check_status(ops)
 
 
+def test_large_calls_back_to_back_match_synchronized_calls(ops):
+    """Larger batches run their chains (permutation, plans, shrinks, grouped GEMMs,
+    combine) as programmatic dependent launches too. Issued back to back on one stream,
+    interleaving MoE layers (CTA pairs with half units and odd tiles beside them, LoRA on
+    all projections and off) with mixed-adapter linear layers (direct and grouped rows),
+    the calls give the same bits as with a device synchronization after each."""
+    moe = _moe_case(T=700, H=512, I=512, E=4, k=2, nT=3, r=16, seed=21)
+    rng = np.random.default_rng(22)
+    x = rand((384, 512), 1.0, torch.bfloat16, 23)
+    Wb = rand((3, 768, 512), 512 ** -0.5, torch.bfloat16, 24)
+    A = rand((4, 16, 512), 512 ** -0.5, torch.bfloat16, 25)
+    B = rand((4, 768, 16), 16 ** -0.5, torch.bfloat16, 26)
+    sc = torch.from_numpy(rng.uniform(0.5, 2, 4).astype(np.float32)).to(DEV)
+    ten = torch.from_numpy(rng.integers(-1, 4, 384).astype(np.int32)).to(DEV)
+    grp = torch.from_numpy(rng.integers(0, 3, 384).astype(np.int32)).to(DEV)
+
+    def call(i):
+        kind = i % 4
+        if kind == 0:
+            return ops.moe_forward(moe["x"], moe["gate_up"], moe["down"], router_w=moe["router_w"], k=2,
+                                   tenant_ids=moe["tenant_ids"], n_tenants=3, rank=16, lora_a13=moe["lora_a13"],
+                                   lora_b13=moe["lora_b13"], lora_a2=moe["lora_a2"], lora_b2=moe["lora_b2"],
+                                   lora_scale=moe["lora_scale"])
+        if kind == 1:
+            return ops.lora_linear(x, Wb[:1], row_tenant=ten, n_tenants=4, rank=16, lora_a=A, lora_b=B, lora_scale=sc)
+        if kind == 2:
+            return ops.moe_forward(moe["x"][: 600 - 37 * (i % 3)], moe["gate_up"], moe["down"],
+                                   router_w=moe["router_w"], k=2)
+        return ops.lora_linear(x, Wb, row_group=grp, row_tenant=ten, n_tenants=4, rank=16, lora_a=A, lora_b=B,
+                               lora_scale=sc)
+
+    ref = []
+    for i in range(16):
+        ref.append(call(i))
+        torch.cuda.synchronize()
+    out = [call(i) for i in range(16)]
+    torch.cuda.synchronize()
+    for i in range(16):
+        assert torch.equal(out[i], ref[i]), f"call {i}"
+    check_status(ops)
+
+
 def test_decode_rows_do_not_depend_on_the_batch(ops):
     """A token's output from a decode-sized call has the same bits alone as inside a
     batch of 8: the skinny GEMMs' per-row sums do not depend on the batch (the
