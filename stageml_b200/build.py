@@ -27,6 +27,7 @@ CU_SOURCES = [
     "route.cu",
     "permute.cu",
     "shrink.cu",
+    "shrink_tc.cu",
     "grouped_gemm.cu",
     "grouped_gemm_pair.cu",
     "skinny.cu",

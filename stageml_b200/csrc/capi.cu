@@ -433,6 +433,8 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       s.a_group_stride = (int64_t)2 * a->rank * a->H;
       s.a_tenant_stride = (int64_t)E_tot * s.a_group_stride;
       s.R = 2 * a->rank;
+      s.a_rows_total = (int64_t)a->n_tenants * E_tot * 2 * a->rank;
+      s.status = status;
       s.spart = b.spart13;
       s.s_out = b.s13;
       s.lora_scale = a->lora_scale;
@@ -493,6 +495,8 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     s.a_group_stride = (int64_t)a->rank * a->I;
     s.a_tenant_stride = (int64_t)E_tot * s.a_group_stride;
     s.R = a->rank;
+    s.a_rows_total = (int64_t)a->n_tenants * E_tot * a->rank;
+    s.status = status;
     s.pdl = pdl_big && !two_streams;
     s.spart = b.spart2;
     s.s_out = b.s2;
@@ -801,6 +805,8 @@ int stageml_moe_linear(const void* x, const void* weight, const void* bias, cons
     sh.a_group_stride = (int64_t)rank * K;
     sh.a_tenant_stride = (int64_t)E * sh.a_group_stride;
     sh.R = rank;
+    sh.a_rows_total = (int64_t)n_tenants * E * rank;
+    sh.status = stat;
     sh.spart = b.spart;
     sh.s_out = b.s;
     sh.lora_scale = lora_scale;
@@ -912,6 +918,8 @@ int stageml_lora_linear(const stageml_lora_linear_args* a, void* workspace, size
     sh.a_tenant_stride = (int64_t)a->rank * a->K;
     sh.a_group_stride = 0;
     sh.R = a->rank;
+    sh.a_rows_total = (int64_t)a->n_tenants * a->rank;
+    sh.status = stat;
     sh.spart = b.spart;
     sh.s_out = b.s;
     sh.lora_scale = a->lora_scale;

@@ -54,15 +54,25 @@ struct ShrinkLaunch {
   const void* lora_a = nullptr;         // [tenant][group][R][K]
   int64_t a_tenant_stride = 0;
   int64_t a_group_stride = 0;
+  int64_t a_rows_total = 0;             // rows of K elements in the whole A bank (0: unknown)
   int R = 0;                            // output columns (multiple of 8, <= 64)
   float* spart = nullptr;               // [KS][rows_cap][R]
   void* s_out = nullptr;                // [rows_cap][R] 16-bit (reduced, scaled): the LoRA-expand MMA operand
   const float* lora_scale = nullptr;    // [n_tenants]
   bool pdl = false;                     // programmatic dependent launches (both kernels wait first)
+  int32_t* status = nullptr;            // error word for expired bounded waits (tensor-core shrink)
 };
 constexpr int kShrinkKSlice = 512;
 inline int shrink_num_slices(int K) { return (K + kShrinkKSlice - 1) / kShrinkKSlice; }
+// Gather and/or shrink. Rows already in the GEMM layout (no gather), and gathered rows
+// once they are written (STAGEML_SHRINK), take the tensor-core shrink of shrink_tc.cu;
+// the rest the per-warp mma.sync kernel.
 int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream);
+// shrink_tc.cu: the partials of the shrink of rows `rows` ([rows_cap or static_rows, K],
+// the plan's layout) on tcgen05, one persistent CTA per SM; same partial layout as
+// the per-warp kernel, reduced by the same kernel.
+bool tc_shrink_supported(const ShrinkLaunch& s);
+int launch_tc_shrink(const ShrinkLaunch& s, const void* rows, cudaStream_t stream);
 // The shrink per row, for decode-sized batches and for small batches whose rows span
 // many tenants: pairs p < P (pair_row[p] = their plan row; pair_row null: row p),
 // one CTA per (pair, 8 output columns) whose 8 warps split K in a fixed order;

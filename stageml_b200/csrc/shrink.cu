@@ -16,6 +16,9 @@
 // partials that a second kernel sums in a fixed order and scales, so the result
 // is deterministic. The first pass also writes the staged x rows to the
 // permuted activation buffer.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "kernels.h"
@@ -392,6 +395,25 @@ __global__ void __launch_bounds__(256, 1) pair_shrink_kernel(const PairShrinkPar
   }
 }
 
+// STAGEML_SHRINK (read once per process): "mma" keeps every shrink on the per-warp
+// mma.sync kernel; "tc" (default) runs shrinks of rows already in place with at
+// least 16 output columns on the tensor-core kernel; "tc_all" runs every shrink
+// there, gathered rows after a gather-only pass. With 8 columns a slot's A rows are
+// 1 KB copies, and the per-copy cost of ~14 of them per K block made the
+// tensor-core kernel slower than the per-warp one (fine-grained layer's h shrink:
+// 0.174 vs 0.123 ms); with 16 it is faster (Mixtral layer's: 0.071 vs 0.075 ms).
+enum ShrinkMode { kShrinkWarpMma = 0, kShrinkTcInPlace = 1, kShrinkTcAll = 2 };
+int shrink_mode() {
+  static const int mode = [] {
+    const char* e = getenv("STAGEML_SHRINK");
+    if (!e) return (int)kShrinkTcInPlace;
+    if (!strcmp(e, "mma")) return (int)kShrinkWarpMma;
+    if (!strcmp(e, "tc_all")) return (int)kShrinkTcAll;
+    return (int)kShrinkTcInPlace;
+  }();
+  return mode;
+}
+
 }  // namespace
 
 int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P, cudaStream_t stream, bool pdl) {
@@ -435,6 +457,19 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   const int KS = shrink_num_slices(s.K);
   const int64_t rows_max = s.num_tiles_dev ? s.rows_cap : s.static_rows;
   if (rows_max == 0) return STAGEML_OK;
+  // Tensor-core shrink: rows in place, or the gathered rows once the gather wrote them.
+  ShrinkLaunch in_place = s;
+  bool tc = false;
+  if (s.R > 0 && shrink_mode() != kShrinkWarpMma) {
+    if (!s.gather_dst) {
+      tc = tc_shrink_supported(s) && (s.R >= 16 || shrink_mode() == kShrinkTcAll);
+    } else if (shrink_mode() == kShrinkTcAll) {
+      in_place.src = s.gather_dst;
+      in_place.src_row_of = nullptr;
+      in_place.gather_dst = nullptr;
+      tc = tc_shrink_supported(in_place);
+    }
+  }
   ShrinkParams p;
   p.src = s.src;
   p.src_row_of = s.src_row_of;
@@ -452,6 +487,13 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   p.spart = s.spart;
   dim3 grid(KS, (unsigned)((rows_max + 63) / 64));
   SB_CHECK_ARG(grid.y <= 65535u, "shrink: too many rows for one launch");
+  if (tc) {
+    if (s.gather_dst) {  // the gather alone first
+      p.R = 0;
+      SB_TRY(launch_shrink_variant<0>(s.dtype_bf16, grid, p, stream, s.pdl));
+    }
+    SB_TRY(launch_tc_shrink(in_place, in_place.src, stream));
+  } else {
   switch (s.R / 8) {
     case 0:
       SB_TRY(launch_shrink_variant<0>(s.dtype_bf16, grid, p, stream, s.pdl));
@@ -470,6 +512,7 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
       break;
     default:
       return set_error(STAGEML_ERR_INVALID_ARG, "shrink: R=%d must be 0, 8, 16, 32 or 64", s.R);
+  }
   }
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {
