@@ -351,22 +351,23 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         const uint32_t bar = land_bar(s);
         mbar_arrive_expect_tx(bar, p.s_bytes + nr * p.run_bytes);
         for (int ch = 0; ch < p.lchunks; ++ch) {
-          tma_load_2d(base + ch * LCHUNK, &tm_s, bar, ch * 16, a_row, pol_a);
-          if (p.swiglu) tma_load_2d(base + (p.lchunks + ch) * LCHUNK, &tm_s, bar, p.rank + ch * 16, a_row, pol_a);
+          if (p.swiglu)  // one 3-D box: the gate chunk and, r columns on, the up chunk
+            tma_load_3d(base + ch * 2 * LCHUNK, &tm_s, bar, ch * 16, a_row, 0, pol_a);
+          else
+            tma_load_2d(base + ch * LCHUNK, &tm_s, bar, ch * 16, a_row, pol_a);
         }
         for (int jj = 0; jj < nr; ++jj) {
           const int r = r0 + jj;
           const int tenant = r < kHdrRuns ? hdr_smem[r * 5] : tile_run(p, m_tile, r)[0];
           const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
+          // one box per 16-column chunk: the gate rows and, N rows on, the up rows (3-D), or
+          // all 256 rows of the tile
           for (int ch = 0; ch < p.lchunks; ++ch) {
-            if (p.swiglu) {
-              tma_load_2d(rb + ch * LCHUNK, &tm_lb, bar, ch * 16, brow, pol_b);
-              tma_load_2d(rb + (p.lchunks + ch) * LCHUNK, &tm_lb, bar, ch * 16, brow + p.N, pol_b);
-            } else {
+            if (p.swiglu)
+              tma_load_3d(rb + ch * 2 * LCHUNK, &tm_lb, bar, ch * 16, brow, 0, pol_b);
+            else
               tma_load_2d(rb + ch * 2 * LCHUNK, &tm_lb, bar, ch * 16, brow, pol_b);
-              tma_load_2d(rb + ch * 2 * LCHUNK + LCHUNK, &tm_lb, bar, ch * 16, brow + 128, pol_b);
-            }
           }
         }
         last_phase[s] = (int)ph;
@@ -469,10 +470,10 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
           for (int ch = 0; ch < p.lchunks; ++ch) {
             if (p.swiglu) {
-              tc_mma_f16_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * LCHUNK),
+              tc_mma_f16_masked(d_tmem, smem_desc_sw32(base + ch * 2 * LCHUNK), smem_desc_sw32(rb + ch * 2 * LCHUNK),
                                 idesc_n128, 1u, d0, d1, d2, d3);
-              tc_mma_f16_masked(d_tmem + 128, smem_desc_sw32(base + (p.lchunks + ch) * LCHUNK),
-                                smem_desc_sw32(rb + (p.lchunks + ch) * LCHUNK), idesc_n128, 1u, d0, d1, d2, d3);
+              tc_mma_f16_masked(d_tmem + 128, smem_desc_sw32(base + (2 * ch + 1) * LCHUNK),
+                                smem_desc_sw32(rb + (2 * ch + 1) * LCHUNK), idesc_n128, 1u, d0, d1, d2, d3);
             } else {
               tc_mma_f16_masked(d_tmem, smem_desc_sw32(base + ch * LCHUNK), smem_desc_sw32(rb + ch * 2 * LCHUNK),
                                 idesc, 1u, d0, d1, d2, d3);
@@ -753,12 +754,23 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
     SB_TRY(make_tmap_2d(&tm_b, g.b, dt, 2, (uint64_t)g.b_rows_total, (uint64_t)g.K, (uint64_t)g.K * 2, 128, BK, 128));
   const int lora_cols = g.swiglu ? 2 * g.rank : g.rank;
   if (g.rank) {
-    SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
-                        16, 32));
-    // rank 8: the 16-wide box reads past the 8 bank columns, which TMA fills with
-    // zeros, so the K=16 MMA adds nothing for the other 8 columns of its S operand
-    SB_TRY(make_tmap_2d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.lora_b_rows_total, (uint64_t)g.rank,
-                        (uint64_t)g.rank * 2, 128, 16, 32));
+    // rank 8: the 16-wide boxes read past the 8 columns of a rank, which TMA fills with
+    // zeros, so the K=16 MMA adds nothing for the other 8 columns of its operands.
+    // SwiGLU: one 3-D box per 16-column chunk loads both halves -- S: the gate columns
+    // [c, c+16) and, r columns on, the up columns; B: the tile's gate rows and, N rows
+    // on, its up rows. The row extents stop where the up half would leave the
+    // allocation: d1 = S rows, and B rows - N (every gate row a tile loads lies below).
+    if (g.swiglu) {
+      SB_TRY(make_tmap_3d(&tm_s, g.s16, dt, 2, (uint64_t)g.rank, (uint64_t)g.s_rows, 2, (uint64_t)lora_cols * 2,
+                          (uint64_t)g.rank * 2, 16, 128, 2, 32));
+      SB_TRY(make_tmap_3d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.rank, (uint64_t)(g.lora_b_rows_total - g.N), 2,
+                          (uint64_t)g.rank * 2, (uint64_t)g.N * g.rank * 2, 16, 128, 2, 32));
+    } else {
+      SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, (uint64_t)lora_cols, (uint64_t)lora_cols * 2, 128,
+                          16, 32));
+      SB_TRY(make_tmap_2d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.lora_b_rows_total, (uint64_t)g.rank,
+                          (uint64_t)g.rank * 2, 256, 16, 32));
+    }
   } else {
     tm_s = tm_a;  // unused
     tm_lb = tm_a;

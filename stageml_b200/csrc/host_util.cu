@@ -112,4 +112,47 @@ int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, 
   return STAGEML_OK;
 }
 
+int make_tmap_3d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0,
+                 uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2,
+                 int swizzle_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(STAGEML_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return set_error(STAGEML_ERR_INVALID_ARG, "TMA base address %p is not 16-byte aligned", base);
+  if (s1 % 16 != 0 || s2 % 16 != 0)
+    return set_error(STAGEML_ERR_INVALID_ARG, "TMA strides %llu, %llu are not multiples of 16 bytes",
+                     (unsigned long long)s1, (unsigned long long)s2);
+  CUtensorMapSwizzle sw;
+  switch (swizzle_bytes) {
+    case 0:
+      sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+      break;
+    case 32:
+      sw = CU_TENSOR_MAP_SWIZZLE_32B;
+      break;
+    case 64:
+      sw = CU_TENSOR_MAP_SWIZZLE_64B;
+      break;
+    case 128:
+      sw = CU_TENSOR_MAP_SWIZZLE_128B;
+      break;
+    default:
+      return set_error(STAGEML_ERR_INVALID_ARG, "unsupported TMA swizzle %d", swizzle_bytes);
+  }
+  if (swizzle_bytes && b0 * (uint32_t)elem_bytes != (uint32_t)swizzle_bytes)
+    return set_error(STAGEML_ERR_INVALID_ARG, "%dB swizzle needs a %d-byte box row", swizzle_bytes, swizzle_bytes);
+  if (b0 == 0 || b0 > 256 || b1 == 0 || b1 > 256 || b2 == 0 || b2 > 256)
+    return set_error(STAGEML_ERR_INVALID_ARG, "TMA box %ux%ux%u out of range", b0, b1, b2);
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(out, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(STAGEML_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d) dims=%llu,%llu,%llu", (int)r,
+                     (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2);
+  return STAGEML_OK;
+}
+
 }  // namespace sb

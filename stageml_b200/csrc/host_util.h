@@ -29,6 +29,14 @@ int sm_count();
 int make_tmap_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
                  uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
 
+// Encode a 3-D tensor map: dims {d0 (contiguous), d1, d2} elements, byte strides
+// s1 (between consecutive d1 indices) and s2 (d2), box {b0, b1, b2}. The strides
+// may overlap (e.g. d2 stepping inside a d1 row): the caller keeps every
+// coordinate it loads inside dims so that each address stays in the allocation.
+int make_tmap_3d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0,
+                 uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2,
+                 int swizzle_bytes);
+
 // Programmatic dependent launch (PDL) of the decode-sized layer's kernel chain:
 // on by default, STAGEML_PDL=0 turns it off.
 bool pdl_enabled();
