@@ -185,6 +185,17 @@ int odd_tiles_env() {  // 0 auto, 1 half, 2 split
   }();
   return mode;
 }
+// Rank 8 on the one-CTA GEMMs packs two tenant runs into each K = 16 expand step
+// (S in the run-parity layout, B rows of both runs side by side); STAGEML_PACK_RANK8=0
+// (read once per process) keeps one masked step per run. Both give the same bits.
+bool pack_rank8_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STAGEML_PACK_RANK8");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
 bool odd_tiles_as_half_units(const GemmLaunch& g) {
   const int mode = odd_tiles_env();
   if (mode != 0) return mode == 1;
@@ -253,6 +264,7 @@ struct MoeBuffers {
   void* s2 = nullptr;    // [rows_cap, r] 16-bit
   int32_t* runs = nullptr;   // [tiles_cap, 128, 5]
   int32_t* nruns = nullptr;  // [tiles_cap]
+  int8_t* row_run = nullptr; // [rows_cap]: each row's run index in its tile (rank 8, one-CTA GEMMs)
   PairPlan pp;                   // CTA-pair GEMM plan (16-bit weights)
   int32_t* status = nullptr;
   size_t bytes = 0;
@@ -326,13 +338,14 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
   b->perm_scratch = c.take_bytes(permute_scratch_bytes(P, nkeys));
   b->xp = c.take_bytes((size_t)rows_cap * a->H * es);
   b->hbuf = c.take_bytes((size_t)rows_cap * a->I * es);
+  const int sfac = a->rank == 8 ? 2 : 1;  // rank 8: room for S in the run-parity layout
   if (a->rank > 0 && a->lora_a13) {
     b->spart13 = c.take<float>((size_t)shrink_num_slices(a->H) * rows_cap * 2 * a->rank);
-    b->s13 = c.take_bytes((size_t)rows_cap * 2 * a->rank * es);
+    b->s13 = c.take_bytes((size_t)rows_cap * 2 * a->rank * sfac * es);
   }
   if (a->rank > 0 && a->lora_a2) {
     b->spart2 = c.take<float>((size_t)shrink_num_slices(a->I) * rows_cap * a->rank);
-    b->s2 = c.take_bytes((size_t)rows_cap * a->rank * es);
+    b->s2 = c.take_bytes((size_t)rows_cap * a->rank * sfac * es);
   }
   const bool lora = a->rank > 0 && (a->lora_a13 || a->lora_a2);
   if (a->weight_dtype != STAGEML_E4M3 && pairs_pay(P, E_tot) &&
@@ -341,6 +354,7 @@ void moe_carve(const stageml_moe_args* a, void* ws, MoeBuffers* b) {
   if (!b->pp.on() && lora) {
     b->runs = c.take<int32_t>((size_t)(rows_cap / 128) * kMaxRunsPerTile * 5);
     b->nruns = c.take<int32_t>((size_t)(rows_cap / 128));
+    if (a->rank == 8) b->row_run = c.take<int8_t>((size_t)rows_cap);
   }
   b->status = c.take<int32_t>(1);
   b->bytes = c.off;
@@ -385,6 +399,8 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   // larger batches: programmatic dependent launches between the kernels after the router
   const bool pdl_big = !skinny && pdl_enabled();
   bool two_streams = false;  // the last grouped GEMM ran its odd tiles on the side stream
+  // rank 8 on the one-CTA GEMMs: two runs per expand step (the shrinks write S by run parity)
+  const bool pack8 = !skinny && b.row_run && pack_rank8_enabled();
 
   // R1: routing
   const void* ids = a->topk_ids;
@@ -412,7 +428,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
                                                     0, b.plan.row_tenant, st, pdl_big));
   } else if (!skinny && b.runs) {
     SB_STAGE(STAGEML_STAGE_PERMUTE, launch_tile_runs(b.plan.row_tenant, b.plan.num_tiles, 0, tiles_cap, b.runs,
-                                                     b.nruns, st, nullptr, pdl_big));
+                                                     b.nruns, st, nullptr, pdl_big, pack8 ? b.row_run : nullptr));
   }
   // gather + R4 shrink of w1|w3 (decode-sized batches: no gather, the skinny GEMM
   // reads the token rows in place, and the per-pair shrink)
@@ -435,6 +451,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       s.R = 2 * a->rank;
       s.a_rows_total = (int64_t)a->n_tenants * E_tot * 2 * a->rank;
       s.status = status;
+      s.row_run = pack8 ? b.row_run : nullptr;
       s.spart = b.spart13;
       s.s_out = b.s13;
       s.lora_scale = a->lora_scale;
@@ -471,6 +488,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       g.lora_b_rows_total = (int64_t)a->n_tenants * E_tot * 2 * a->I;
       g.tile_runs = b.runs;
       g.tile_nruns = b.nruns;
+      g.pack8 = pack8;
     }
     g.b_scale = a->gate_up_scale;
     g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
@@ -497,6 +515,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
     s.R = a->rank;
     s.a_rows_total = (int64_t)a->n_tenants * E_tot * a->rank;
     s.status = status;
+    s.row_run = pack8 ? b.row_run : nullptr;
     s.pdl = pdl_big && !two_streams;
     s.spart = b.spart2;
     s.s_out = b.s2;
@@ -532,6 +551,7 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
       g.lora_b_rows_total = (int64_t)a->n_tenants * E_tot * a->H;
       g.tile_runs = b.runs;
       g.tile_nruns = b.nruns;
+      g.pack8 = pack8;
     }
     g.row_scale = b.plan.row_weight;
     g.b_group_map = a->down_group;

@@ -85,7 +85,8 @@ struct KParams {
   int lchunks;         // rank / 16
   int s_bytes;         // S bytes per LoRA block
   int run_bytes;       // B bytes per run
-  int runs_per_block;
+  int runs_per_block;  // LoRA slots (runs, or pairs of runs with pack8) per LoRA block
+  int pack8;           // rank 8: two runs per K = 16 step (S in the run-parity layout)
   int64_t lb_tenant_rows;
   int64_t lb_group_rows;
   const int32_t* tile_runs;
@@ -153,6 +154,20 @@ __device__ __forceinline__ void unit_mn(const KParams& p, int u, int num_m_tiles
     n_tile = u / num_m_tiles;
   }
 }
+
+// K-major operand without swizzle: 8-row core matrices of 16-byte rows, `sbo` bytes
+// between 8-row groups and `lbo` bytes between the two 8-column halves of a K = 16 step.
+__device__ __forceinline__ uint64_t smem_desc_nosw(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(lbo >> 4) << 16;
+  d |= static_cast<uint64_t>(sbo >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100; layout 0 = no swizzle
+  return d;
+}
+
+// LoRA slots of a tile with n runs: the runs, or (packed rank 8) pairs of runs.
+__device__ __forceinline__ int lora_slots(int pack8, int nruns) { return pack8 ? (nruns + 1) / 2 : nruns; }
 
 // LoRA runs of m-tile m_pos are stored at its tile id (tile_list[m_pos] with a list).
 __device__ __forceinline__ int run_slot(const KParams& p, int m_pos) { return p.tile_list ? p.tile_list[m_pos] : m_pos; }
@@ -339,8 +354,9 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         hdr_inflight = !ok;
       }
       if (!ok) nruns = 0;
-      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
-        const int nr = min(p.runs_per_block, nruns - r0);
+      const int nslots = lora_slots(p.pack8, nruns);
+      for (int r0 = 0; ok && r0 < nslots; r0 += p.runs_per_block, ++it) {
+        const int nr = min(p.runs_per_block, nslots - r0);
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait(empty_bar(s), ph ^ 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutProducer)) {
@@ -356,7 +372,25 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
           else
             tma_load_2d(base + ch * LCHUNK, &tm_s, bar, ch * 16, a_row, pol_a);
         }
-        for (int jj = 0; jj < nr; ++jj) {
+        for (int jj = 0; jj < nr && p.pack8; ++jj) {
+          // packed rank 8: the 8 B columns of runs 2q and 2q+1 in two 16-byte-row blocks
+          // (no swizzle), K columns 0-7 and 8-15 of one K = 16 step
+          for (int h = 0; h < 2; ++h) {
+            const int r = 2 * (r0 + jj) + h;
+            const uint32_t dst = base + p.s_bytes + jj * p.run_bytes + h * (p.run_bytes / 2);
+            int brow = 0, x = 8;  // no second run: a box past the 8 columns, all zeros
+            if (r < nruns) {
+              const int tenant = r < kHdrRuns ? hdr_smem[r * 5] : tile_run(p, m_tile, r)[0];
+              brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
+              x = 0;
+            }
+            if (p.swiglu)
+              tma_load_3d(dst, &tm_lb, bar, x, brow, 0, pol_b);
+            else
+              tma_load_2d(dst, &tm_lb, bar, x, brow, pol_b);
+          }
+        }
+        for (int jj = 0; jj < nr && !p.pack8; ++jj) {
           const int r = r0 + jj;
           const int tenant = r < kHdrRuns ? hdr_smem[r * 5] : tile_run(p, m_tile, r)[0];
           const int brow = (int)(tenant * p.lb_tenant_rows + group * p.lb_group_rows) + n0;
@@ -445,8 +479,9 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         ++mrun_uses;
       }
       const int nruns = ok ? nruns_unit : 0;
-      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
-        const int nr = min(p.runs_per_block, nruns - r0);
+      const int nslots = lora_slots(p.pack8, nruns);
+      for (int r0 = 0; ok && r0 < nslots; r0 += p.runs_per_block, ++it) {
+        const int nr = min(p.runs_per_block, nslots - r0);
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         if (!mbar_wait(full_bar(s), ph, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
@@ -462,7 +497,32 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t base = smem_base + s * STAGE_BYTES;
-        for (int jj = 0; jj < nr; ++jj) {
+        for (int jj = 0; jj < nr && p.pack8; ++jj) {
+          // two runs in one K = 16 step: S holds each row's values in the 8 columns of its
+          // run's parity, so one MASKED MMA over the rows of both runs adds both products
+          const int ra = 2 * (r0 + jj), rb2 = ra + 1;
+          const int32_t* run_a = ra < kHdrRuns ? mruns_smem + ra * 5 : tile_run(p, slot, ra);
+          uint32_t m0 = (uint32_t)run_a[1], m1 = (uint32_t)run_a[2], m2 = (uint32_t)run_a[3], m3 = (uint32_t)run_a[4];
+          if (rb2 < nruns) {
+            const int32_t* run_b = rb2 < kHdrRuns ? mruns_smem + rb2 * 5 : tile_run(p, slot, rb2);
+            m0 |= (uint32_t)run_b[1];
+            m1 |= (uint32_t)run_b[2];
+            m2 |= (uint32_t)run_b[3];
+            m3 |= (uint32_t)run_b[4];
+          }
+          const uint32_t rb = base + p.s_bytes + jj * p.run_bytes;
+          const uint32_t half = (uint32_t)p.run_bytes / 2;  // run b's block after run a's
+          if (p.swiglu) {
+            tc_mma_f16_masked(d_tmem, smem_desc_sw32(base), smem_desc_nosw(rb, half, 128), idesc_n128, 1u, ~m0, ~m1,
+                              ~m2, ~m3);
+            tc_mma_f16_masked(d_tmem + 128, smem_desc_sw32(base + LCHUNK), smem_desc_nosw(rb + half / 2, half, 128),
+                              idesc_n128, 1u, ~m0, ~m1, ~m2, ~m3);
+          } else {
+            tc_mma_f16_masked(d_tmem, smem_desc_sw32(base), smem_desc_nosw(rb, half, 128), idesc, 1u, ~m0, ~m1, ~m2,
+                              ~m3);
+          }
+        }
+        for (int jj = 0; jj < nr && !p.pack8; ++jj) {
           const int r = r0 + jj;
           const int32_t* run = r < kHdrRuns ? mruns_smem + r * 5 : tile_run(p, slot, r);
           const uint32_t d0 = ~(uint32_t)run[1], d1 = ~(uint32_t)run[2], d2 = ~(uint32_t)run[3],
@@ -624,8 +684,8 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       }
       // LoRA blocks (16-bit already) go from the TMA ring to the MMAs; the converters only
       // report that they saw each one land
-      const int nruns = ok ? tile_nruns : 0;
-      for (int r0 = 0; ok && r0 < nruns; r0 += p.runs_per_block, ++it) {
+      const int nslots = ok ? lora_slots(p.pack8, tile_nruns) : 0;
+      for (int r0 = 0; ok && r0 < nslots; r0 += p.runs_per_block, ++it) {
         const int s = it % STAGES;
         if (!mbar_wait(full_bar(s), (it / STAGES) & 1, abort_flag, p.status, p.timeout_ns, kDevTimeoutMma)) {
           ok = false;
@@ -646,11 +706,19 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
 
 // One warp per 128-row tile: distinct tenants (in first-seen order over the
 // 4 row quarters) and the 128-bit mask of the rows each one owns.
+// The run index a leader lane took in tile_runs_kernel's matching round (found, or a
+// new index after the `base` runs known before the round).
+__device__ __forceinline__ int idx_or(bool leader, int found, int base, unsigned is_new, int lane) {
+  if (!leader) return -1;
+  return found >= 0 ? found : base + __popc(is_new & ((1u << lane) - 1u));
+}
+
 __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restrict__ row_tenant,
                                                         const int32_t* __restrict__ num_tiles_dev,
                                                         int64_t static_rows, int tiles_cap, int32_t* __restrict__ runs,
                                                         int32_t* __restrict__ nruns,
-                                                        const int32_t* __restrict__ tile_list) {
+                                                        const int32_t* __restrict__ tile_list,
+                                                        int8_t* __restrict__ row_run) {
   __shared__ int32_t s_ten[4][kMaxRunsPerTile];
   __shared__ uint32_t s_mask[4][kMaxRunsPerTile][4];
   pdl_wait();  // the plan and the tenants may come from the previous kernels
@@ -686,6 +754,11 @@ __global__ void __launch_bounds__(128) tile_runs_kernel(const int32_t* __restric
       s_mask[w][idx][q] = peers;
     }
     count += __popc(is_new);
+    if (row_run) {  // every row learns its run index from its leader
+      const int my_idx = __shfl_sync(0xffffffffu, idx_or(leader, found, count - __popc(is_new), is_new, lane),
+                                     t >= 0 ? __ffs(peers) - 1 : lane);
+      row_run[src_tile * 128 + q * 32 + lane] = (int8_t)(t >= 0 ? my_idx : -1);
+    }
     __syncwarp();
   }
   for (int j = lane; j < count; j += 32) {
@@ -714,13 +787,14 @@ int launch_gemm_kernel(int grid, cudaStream_t stream, bool pdl, const CUtensorMa
 }  // namespace
 
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
-                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list, bool pdl) {
+                     int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list, bool pdl,
+                     int8_t* row_run) {
   SB_CHECK_ARG(row_tenant && runs && nruns, "tile_runs: null pointer");
   SB_CHECK_ARG(!tile_list || num_tiles_dev, "tile_runs: a tile list needs its device count");
   const int64_t tiles = num_tiles_dev ? tiles_cap : (static_rows + 127) / 128;
   if (tiles == 0) return STAGEML_OK;
   SB_CUDA_CHECK(launch_kernel(tile_runs_kernel, dim3((unsigned)((tiles + 3) / 4)), dim3(128), 0, stream, pdl,
-                              row_tenant, num_tiles_dev, static_rows, tiles_cap, runs, nruns, tile_list));
+                              row_tenant, num_tiles_dev, static_rows, tiles_cap, runs, nruns, tile_list, row_run));
   ::sb::count_launch();
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
@@ -760,7 +834,19 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
     // [c, c+16) and, r columns on, the up columns; B: the tile's gate rows and, N rows
     // on, its up rows. The row extents stop where the up half would leave the
     // allocation: d1 = S rows, and B rows - N (every gate row a tile loads lies below).
-    if (g.swiglu) {
+    if (g.pack8) {
+      // S in the run-parity layout: 16 columns per half ([rows][32] SwiGLU, [rows][16]
+      // otherwise); B: one run's 8 columns per box, 16-byte rows without swizzle
+      SB_CHECK_ARG(g.rank == 8, "grouped gemm: packed LoRA needs rank 8");
+      if (g.swiglu) {
+        SB_TRY(make_tmap_3d(&tm_s, g.s16, dt, 2, 16, (uint64_t)g.s_rows, 2, 64, 32, 16, 128, 2, 32));
+        SB_TRY(make_tmap_3d(&tm_lb, g.lora_b, dt, 2, 8, (uint64_t)(g.lora_b_rows_total - g.N), 2, 16,
+                            (uint64_t)g.N * 16, 8, 128, 2, 0));
+      } else {
+        SB_TRY(make_tmap_2d(&tm_s, g.s16, dt, 2, (uint64_t)g.s_rows, 16, 32, 128, 16, 32));
+        SB_TRY(make_tmap_2d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.lora_b_rows_total, 8, 16, 256, 8, 0));
+      }
+    } else if (g.swiglu) {
       SB_TRY(make_tmap_3d(&tm_s, g.s16, dt, 2, (uint64_t)g.rank, (uint64_t)g.s_rows, 2, (uint64_t)lora_cols * 2,
                           (uint64_t)g.rank * 2, 16, 128, 2, 32));
       SB_TRY(make_tmap_3d(&tm_lb, g.lora_b, dt, 2, (uint64_t)g.rank, (uint64_t)(g.lora_b_rows_total - g.N), 2,
@@ -797,6 +883,7 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream) {
   // a LoRA block (S and the runs' B rows) fills one TMA stage
   const int lora_block_bytes = g.b_fp8 ? Cfg<true>::STAGE_BYTES : Cfg<false>::STAGE_BYTES;
   p.runs_per_block = g.rank ? (lora_block_bytes - p.s_bytes) / p.run_bytes : 1;
+  p.pack8 = g.pack8 ? 1 : 0;
   p.lb_tenant_rows = g.rank ? g.lora_b_tenant_stride / g.rank : 0;
   p.lb_group_rows = g.rank ? g.lora_b_group_stride / g.rank : 0;
   p.tile_runs = g.tile_runs;

@@ -77,6 +77,9 @@ struct GemmLaunch {
   // A pair whose second tile is -1 is a half unit: its one tile on both CTAs (64 rows
   // each, M = 128 MMAs) instead of a pair with an idle half.
   bool pair_half_units = false;
+  // rank 8 on the one-CTA kernel: S in the run-parity layout of the shrink reduce
+  // (ShrinkLaunch::row_run) and the B rows of two runs in one K = 16 step
+  bool pack8 = false;
   // Programmatic dependent launch (the kernels wait for the previous kernel first).
   bool pdl = false;
   // The pair kernel and the odd-tile kernel side by side (split_sms > 0): each
@@ -112,9 +115,10 @@ int launch_grouped_gemm(const GemmLaunch& g, cudaStream_t stream);
 // runs[(tile*128 + j)*5 + 0] = tenant, [1..4] = row mask words; nruns[tile].
 // Rows with tenant < 0 belong to no run. Active rows: 128 * (*num_tiles_dev)
 // (capped at tiles_cap tiles) or static_rows when num_tiles_dev is null.
+// row_run (optional, [tiles * 128]): each row's run index in its tile, -1 for none.
 int launch_tile_runs(const int32_t* row_tenant, const int32_t* num_tiles_dev, int64_t static_rows, int tiles_cap,
                      int32_t* runs, int32_t* nruns, cudaStream_t stream, const int32_t* tile_list = nullptr,
-                     bool pdl = false);
+                     bool pdl = false, int8_t* row_run = nullptr);
 // With tile_list, entry i covers tile tile_list[i] (i < *num_tiles_dev) and runs / nruns
 // are indexed by that tile id; static_rows > 0 then bounds the rows read (direct rows).
 constexpr int kMaxRunsPerTile = 128;

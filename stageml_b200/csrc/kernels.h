@@ -61,6 +61,9 @@ struct ShrinkLaunch {
   const float* lora_scale = nullptr;    // [n_tenants]
   bool pdl = false;                     // programmatic dependent launches (both kernels wait first)
   int32_t* status = nullptr;            // error word for expired bounded waits (tensor-core shrink)
+  // optional [rows_cap]: each row's run index in its 128-row tile (launch_tile_runs);
+  // S is then written [rows_cap][2R] in the run-parity layout of the packed rank-8 expand
+  const int8_t* row_run = nullptr;
 };
 constexpr int kShrinkKSlice = 512;
 inline int shrink_num_slices(int K) { return (K + kShrinkKSlice - 1) / kShrinkKSlice; }

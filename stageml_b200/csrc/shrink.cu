@@ -261,21 +261,34 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
   cp_async_wait<0>();
 }
 
+// S[row, c] = scale[tenant] * sum over K slices (fixed order) of the partials.
+// With row_run (rank 8 on the one-CTA GEMM): each 8-column group c of S is written
+// as 16 columns, the values in the half given by the parity of the row's run index
+// in its tile and zeros in the other, so that one K = 16 expand step serves two runs.
 template <typename T>
 __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, int64_t rows_cap, int R,
                                      const int32_t* __restrict__ num_tiles_dev, int64_t static_rows,
                                      const int32_t* __restrict__ row_tenant, const float* __restrict__ scale,
-                                     T* __restrict__ s_out) {
+                                     T* __restrict__ s_out, const int8_t* __restrict__ row_run) {
   pdl_wait();  // the partial sums of the kernel before
   pdl_trigger();
   const int64_t rows_active = active_rows(num_tiles_dev, static_rows, rows_cap);
+  const int R_out = row_run ? 2 * R : R;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= rows_active * R) return;
-  const int64_t row = idx / R;
+  if (idx >= rows_active * R_out) return;
+  const int64_t row = idx / R_out;
+  const int oc = (int)(idx - row * R_out);
+  int c = oc;
+  bool live = true;
+  if (row_run) {  // output column oc = group (8 input columns) x 16 + parity x 8 + column
+    const int run = row_run[row];
+    c = (oc >> 4) * 8 + (oc & 7);
+    live = run >= 0 && ((run & 1) == ((oc >> 3) & 1));
+  }
   const int tn = row_tenant[row];
   float v = 0.f;
-  if (tn >= 0) {
-    for (int ks = 0; ks < KS; ++ks) v += spart[((int64_t)ks * rows_cap + row) * R + (idx - row * R)];
+  if (tn >= 0 && live) {
+    for (int ks = 0; ks < KS; ++ks) v += spart[((int64_t)ks * rows_cap + row) * R + c];
     v *= scale ? scale[tn] : 1.f;
   }
   s_out[idx] = from_f32<T>(v);
@@ -516,16 +529,17 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   }
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {
-    const int64_t n = rows_max * s.R;
+    SB_CHECK_ARG(!s.row_run || s.R % 8 == 0, "shrink: the run-parity layout needs R a multiple of 8");
+    const int64_t n = rows_max * (s.row_run ? 2 * s.R : s.R);
     const dim3 rgrid((unsigned)((n + 255) / 256));
     if (s.dtype_bf16)
       SB_CUDA_CHECK(launch_kernel(shrink_reduce_kernel<bf16>, rgrid, dim3(256), 0, stream, s.pdl, s.spart, KS,
                                   p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
-                                  static_cast<bf16*>(s.s_out)));
+                                  static_cast<bf16*>(s.s_out), s.row_run));
     else
       SB_CUDA_CHECK(launch_kernel(shrink_reduce_kernel<f16>, rgrid, dim3(256), 0, stream, s.pdl, s.spart, KS,
                                   p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
-                                  static_cast<f16*>(s.s_out)));
+                                  static_cast<f16*>(s.s_out), s.row_run));
     ::sb::count_launch();
     SB_CUDA_CHECK(cudaGetLastError());
   }

@@ -1,6 +1,6 @@
-"""Child process of test_gpu_shrink_modes.py: runs LoRA layers whose shrink takes the
-kernel chosen by the STAGEML_SHRINK mode in its environment (read once per process by
-the library), prints, per case, the rel-L2 error against the oracle as one JSON line
+"""Child process of test_gpu_shrink_modes.py and test_gpu_pack_rank8.py: runs LoRA
+layers under the kernel choices in its environment (STAGEML_SHRINK, STAGEML_GEMM_PAIRS,
+STAGEML_PACK_RANK8, each read once per process by the library), prints, per case, the rel-L2 error against the oracle as one JSON line
 and saves the outputs to the path given as its argument."""
 
 import json
@@ -86,6 +86,8 @@ CASES = {
                                           seed=3, zipf=True),
     # rank 32 (R = 64 for the packed w1|w3 shrink), K not a multiple of the 512-wide slice
     "moe_r32_ragged_k": lambda: moe_case(T=500, H=320, I=576, E=3, k=2, nT=9, r=32, seed=7),
+    # rank 8 with 60 tenants: ~45 runs per tile (past the 32 the GEMMs copy up front), odd and even counts
+    "moe_r8_60_tenants": lambda: moe_case(T=900, H=256, I=384, E=4, k=2, nT=60, r=8, seed=17),
     # direct rows in caller order: 1100 rows (a partial last tile), 150 tenants, rank 8
     "linear_r8_150_tenants": lambda: linear_case(M=1100, K=1024, N=512, nT=150, r=8, seed=11),
     # direct rows, rank 32, K = 1000 (a partial last K block)
