@@ -371,6 +371,130 @@ int run_moe_gemm(const GemmLaunch& g, const MoeBuffers& b, bool skinny, cudaStre
   return run_grouped_gemm(g, b.pp, st, two_streams);
 }
 
+// A one-expert top-1 layer (a dense SwiGLU MLP with per-row LoRA tenants, e.g. a
+// transformer block's MLP served through this layer) needs no permutation: every
+// token is one row of its only expert. Its rows stay in token order -- the shrinks
+// read x and h in place, the GEMMs take the rows as one group, the down projection
+// applies the routing weight and writes the output rows, and there is no gather or
+// combine. Same bits as the permuted path (each GEMM row and each S row is computed
+// independently of the others). STAGEML_DIRECT_ROWS=0 (read once per process) keeps
+// the permuted path.
+bool direct_rows_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STAGEML_DIRECT_ROWS");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
+int moe_forward_direct(const stageml_moe_args* a, const MoeBuffers& b, int32_t* status, bool pdl, cudaStream_t st) {
+  const int bf = a->act_dtype == STAGEML_BF16;
+  const bool lora13 = a->rank > 0 && a->lora_a13;
+  const bool lora2 = a->rank > 0 && a->lora_a2;
+  const bool lora = lora13 || lora2;
+  const int64_t T = a->T;
+  int32_t* row_tenant = b.plan.row_tenant;  // [rows_cap] >= T
+  float* row_scale = b.plan.row_weight;
+  bool two_streams = false;
+  // R1 + R2: one expert, top-1 -- the router's weight is 1 (softmax over one logit);
+  // caller ids / weights are validated like the permutation does
+  SB_STAGE(STAGEML_STAGE_PERMUTE,
+           launch_direct_rows(a->topk_ids, a->ids_dtype, a->topk_ids ? a->topk_weights : nullptr, a->weights_dtype,
+                              a->tenant_ids, a->n_tenants, T, row_tenant, row_scale, status, st, pdl));
+  if (b.pp.on())
+    SB_STAGE(STAGEML_STAGE_PERMUTE,
+             build_pair_plan(b.pp, nullptr, nullptr, nullptr, T, lora ? row_tenant : nullptr, st, pdl));
+  else if (lora)
+    SB_STAGE(STAGEML_STAGE_PERMUTE, launch_tile_runs(row_tenant, nullptr, T, (int)((T + 127) / 128), b.runs, b.nruns,
+                                                     st, nullptr, pdl));
+  auto shrink = [&](const void* src, int K, const void* A, int R, float* spart, void* s_out) {
+    ShrinkLaunch s;
+    s.src = src;
+    s.K = K;
+    s.dtype_bf16 = bf;
+    s.static_rows = T;
+    s.rows_cap = T;
+    s.row_tenant = row_tenant;
+    s.lora_a = A;
+    s.a_group_stride = (int64_t)R * K;
+    s.a_tenant_stride = s.a_group_stride;
+    s.a_rows_total = (int64_t)a->n_tenants * R;
+    s.R = R;
+    s.spart = spart;
+    s.s_out = s_out;
+    s.lora_scale = a->lora_scale;
+    s.status = status;
+    s.pdl = pdl && !two_streams;
+    return launch_gather_shrink(s, st);
+  };
+  if (lora13)
+    SB_STAGE(STAGEML_STAGE_GATHER_SHRINK, shrink(a->x, a->H, a->lora_a13, 2 * a->rank, b.spart13, b.s13));
+  {
+    GemmLaunch g;
+    g.a = a->x;
+    g.a_rows = T;
+    g.m_rows = T;
+    g.K = a->H;
+    g.b = a->gate_up;
+    g.b_rows_total = (int64_t)2 * a->I;
+    g.b_group_rows = 2 * a->I;
+    g.N = a->I;
+    g.swiglu = true;
+    g.in_bf16 = bf;
+    if (lora13) {
+      g.s16 = b.s13;
+      g.s_rows = T;
+      g.rank = a->rank;
+      g.lora_b = a->lora_b13;
+      g.lora_b_group_stride = (int64_t)2 * a->I * a->rank;
+      g.lora_b_tenant_stride = g.lora_b_group_stride;
+      g.lora_b_rows_total = (int64_t)a->n_tenants * 2 * a->I;
+      g.tile_runs = b.runs;
+      g.tile_nruns = b.nruns;
+    }
+    g.b_scale = a->gate_up_scale;
+    g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
+    g.out = b.hbuf;
+    g.ldo = a->I;
+    g.status = status;
+    g.pdl = pdl;
+    SB_STAGE(STAGEML_STAGE_GEMM_GATE_UP, run_grouped_gemm(g, b.pp, st, &two_streams));
+  }
+  if (lora2) SB_STAGE(STAGEML_STAGE_SHRINK_H, shrink(b.hbuf, a->I, a->lora_a2, a->rank, b.spart2, b.s2));
+  {
+    GemmLaunch g;
+    g.a = b.hbuf;
+    g.a_rows = T;
+    g.m_rows = T;
+    g.K = a->I;
+    g.b = a->down;
+    g.b_rows_total = a->H;
+    g.b_group_rows = a->H;
+    g.N = a->H;
+    g.in_bf16 = bf;
+    if (lora2) {
+      g.s16 = b.s2;
+      g.s_rows = T;
+      g.rank = a->rank;
+      g.lora_b = a->lora_b2;
+      g.lora_b_group_stride = (int64_t)a->H * a->rank;
+      g.lora_b_tenant_stride = g.lora_b_group_stride;
+      g.lora_b_rows_total = (int64_t)a->n_tenants * a->H;
+      g.tile_runs = b.runs;
+      g.tile_nruns = b.nruns;
+    }
+    g.row_scale = row_scale;
+    g.b_scale = a->down_scale;
+    g.b_fp8 = a->weight_dtype == STAGEML_E4M3;
+    g.out = a->out;
+    g.ldo = a->H;
+    g.status = status;
+    g.pdl = pdl && (lora2 || !two_streams);
+    SB_STAGE(STAGEML_STAGE_GEMM_DOWN, run_grouped_gemm(g, b.pp, st, &two_streams));
+  }
+  return STAGEML_OK;
+}
+
 int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
   SB_TRY(moe_validate(a));
   if (a->T == 0) return STAGEML_OK;
@@ -401,6 +525,9 @@ int moe_forward_impl(const stageml_moe_args* a, void* ws, size_t ws_bytes, cudaS
   bool two_streams = false;  // the last grouped GEMM ran its odd tiles on the side stream
   // rank 8 on the one-CTA GEMMs: two runs per expand step (the shrinks write S by run parity)
   const bool pack8 = !skinny && b.row_run && pack_rank8_enabled();
+  if (!skinny && a->E == 1 && a->n_shared == 0 && a->k == 1 && n_fold == 0 && !a->T_dev && !a->plan_out &&
+      direct_rows_enabled())
+    return moe_forward_direct(a, b, status, pdl_big, st);
 
   // R1: routing
   const void* ids = a->topk_ids;

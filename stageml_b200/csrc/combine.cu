@@ -47,7 +47,54 @@ __global__ void validate_tenants_kernel(const int32_t* __restrict__ in, int64_t 
   out[i] = v;
 }
 
+// Rows of a one-expert top-1 layer taken in token order (no permutation): the
+// validated tenant of each row and the factor the down projection applies, the
+// routing weight, or 0 for a token whose expert id or tenant is out of range (the
+// permuted path drops that pair, leaving a zero output row).
+__global__ void direct_rows_kernel(const void* __restrict__ ids, int ids_i64, const void* __restrict__ weights,
+                                   int weights_dtype, const int32_t* __restrict__ tenant_ids, int n_tenants, int64_t T,
+                                   int32_t* __restrict__ row_tenant, float* __restrict__ row_scale, int32_t* status) {
+  pdl_wait();  // the ids may come from the previous kernel
+  pdl_trigger();
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  bool bad = false;
+  if (ids) {
+    const int64_t e = ids_i64 ? static_cast<const int64_t*>(ids)[t] : (int64_t) static_cast<const int32_t*>(ids)[t];
+    bad = e != 0;
+  }
+  int tn = tenant_ids ? tenant_ids[t] : -1;
+  if (tn < -1 || tn >= n_tenants) {
+    bad = true;
+    tn = -1;
+  }
+  float w = 1.f;
+  if (weights) {
+    if (weights_dtype == STAGEML_BF16)
+      w = __bfloat162float(static_cast<const bf16*>(weights)[t]);
+    else if (weights_dtype == STAGEML_F16)
+      w = __half2float(static_cast<const f16*>(weights)[t]);
+    else
+      w = static_cast<const float*>(weights)[t];
+  }
+  if (bad && status) atomicCAS(status, 0, (int)kDevBadIndex);
+  row_tenant[t] = bad ? -1 : tn;
+  row_scale[t] = bad ? 0.f : w;
+}
+
 }  // namespace
+
+int launch_direct_rows(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
+                       int n_tenants, int64_t T, int32_t* row_tenant, float* row_scale, int32_t* status,
+                       cudaStream_t stream, bool pdl) {
+  if (T == 0) return STAGEML_OK;
+  SB_CUDA_CHECK(launch_kernel(direct_rows_kernel, dim3((unsigned)((T + 255) / 256)), dim3(256), 0, stream, pdl, ids,
+                              ids_dtype == STAGEML_I64 ? 1 : 0, weights, weights_dtype, tenant_ids, n_tenants, T,
+                              row_tenant, row_scale, status));
+  ::sb::count_launch();
+  SB_CUDA_CHECK(cudaGetLastError());
+  return STAGEML_OK;
+}
 
 int launch_combine(const void* y, const int32_t* pair_row, int T_, int kk, int H, int dtype_bf16, void* out,
                    cudaStream_t stream, const int32_t* T_dev, bool pdl) {

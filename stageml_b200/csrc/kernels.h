@@ -89,6 +89,12 @@ int launch_pair_shrink(const ShrinkLaunch& s, const int32_t* pair_row, int64_t P
 int launch_combine(const void* y, const int32_t* pair_row, int T, int kk, int H, int dtype_bf16, void* out,
                    cudaStream_t stream, const int32_t* T_dev = nullptr,  // rows >= *T_dev left untouched
                    bool pdl = false);
+// One-expert top-1 layer in token order: row_tenant[t] = validated tenant, row_scale[t] =
+// routing weight (1 without weights), both -1 / 0 with status for an expert id other
+// than 0 or a tenant out of range.
+int launch_direct_rows(const void* ids, int ids_dtype, const void* weights, int weights_dtype, const int32_t* tenant_ids,
+                       int n_tenants, int64_t T, int32_t* row_tenant, float* row_scale, int32_t* status,
+                       cudaStream_t stream, bool pdl = false);
 // clamp caller tenant ids into [-1, n_tenants) (invalid -> -1 + status)
 int launch_validate_tenants(const int32_t* in, int64_t n, int n_tenants, int32_t* out, int32_t* status,
                             cudaStream_t stream, bool pdl = false);

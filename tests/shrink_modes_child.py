@@ -1,6 +1,7 @@
-"""Child process of test_gpu_shrink_modes.py and test_gpu_pack_rank8.py: runs LoRA
+"""Child process of test_gpu_shrink_modes.py, test_gpu_pack_rank8.py and
+test_gpu_direct_rows.py: runs LoRA
 layers under the kernel choices in its environment (STAGEML_SHRINK, STAGEML_GEMM_PAIRS,
-STAGEML_PACK_RANK8, each read once per process by the library), prints, per case, the rel-L2 error against the oracle as one JSON line
+STAGEML_PACK_RANK8, STAGEML_DIRECT_ROWS, each read once per process by the library), prints, per case, the rel-L2 error against the oracle as one JSON line
 and saves the outputs to the path given as its argument."""
 
 import json
@@ -28,7 +29,7 @@ def f64(t):
     return t.detach().float().cpu().numpy().astype(np.float64)
 
 
-def moe_case(T, H, I, E, k, nT, r, ns=0, dtype=torch.bfloat16, seed=0, zipf=False):
+def moe_case(T, H, I, E, k, nT, r, ns=0, dtype=torch.bfloat16, seed=0, zipf=False, caller_weights=False):
     import stageml_b200.ops as ops
 
     rng = np.random.default_rng(seed)
@@ -49,8 +50,13 @@ def moe_case(T, H, I, E, k, nT, r, ns=0, dtype=torch.bfloat16, seed=0, zipf=Fals
               lora_b13=rand((nT, Et, 2 * I, r), r ** -0.5, dtype, seed + 5),
               lora_a2=rand((nT, Et, r, I), I ** -0.5, dtype, seed + 6),
               lora_b2=rand((nT, Et, H, r), r ** -0.5, dtype, seed + 7))
-    y = ops.moe_forward(x, gu, dn, router_w=rw, k=k, n_shared=ns, **kw)
-    ids, w, _ = ops.route_topk(x, rw, k, True)
+    if caller_weights:  # the caller's expert ids and routing weights instead of the router
+        ids, _, _ = ops.route_topk(x, rw, k, True)
+        w = torch.from_numpy(rng.uniform(0.25, 1.5, (T, k)).astype(np.float32)).to(DEV)
+        y = ops.moe_forward(x, gu, dn, topk_ids=ids, topk_weights=w, n_shared=ns, **kw)
+    else:
+        y = ops.moe_forward(x, gu, dn, router_w=rw, k=k, n_shared=ns, **kw)
+        ids, w, _ = ops.route_topk(x, rw, k, True)
     ref = omoe.moe_forward(f64(x), f64(gu), f64(dn), ids.cpu().numpy(), w.cpu().numpy(), tenant_ids=ten_np,
                            n_shared=ns, lora_a13=f64(kw["lora_a13"]), lora_b13=f64(kw["lora_b13"]),
                            lora_a2=f64(kw["lora_a2"]), lora_b2=f64(kw["lora_b2"]), lora_scale=f64(kw["lora_scale"]))
@@ -88,6 +94,11 @@ CASES = {
     "moe_r32_ragged_k": lambda: moe_case(T=500, H=320, I=576, E=3, k=2, nT=9, r=32, seed=7),
     # rank 8 with 60 tenants: ~45 runs per tile (past the 32 the GEMMs copy up front), odd and even counts
     "moe_r8_60_tenants": lambda: moe_case(T=900, H=256, I=384, E=4, k=2, nT=60, r=8, seed=17),
+    # one expert, top-1 (a dense SwiGLU MLP): rows stay in token order, 650 rows (a partial last tile)
+    "moe_e1_router": lambda: moe_case(T=650, H=512, I=704, E=1, k=1, nT=6, r=16, seed=19),
+    # one expert with the caller's ids and routing weights, rank 8, fp16
+    "moe_e1_caller_weights_r8": lambda: moe_case(T=520, H=384, I=512, E=1, k=1, nT=5, r=8, dtype=torch.float16,
+                                                 seed=23, caller_weights=True),
     # direct rows in caller order: 1100 rows (a partial last tile), 150 tenants, rank 8
     "linear_r8_150_tenants": lambda: linear_case(M=1100, K=1024, N=512, nT=150, r=8, seed=11),
     # direct rows, rank 32, K = 1000 (a partial last K block)
