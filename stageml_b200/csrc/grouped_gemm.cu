@@ -6,7 +6,7 @@
 //   warp 0      TMA producer (one thread)
 //   warp 1      TMEM allocator + MMA issuer (one thread)
 //   warps 2..5  epilogue: TMEM lane quarter (warp % 4), one accumulator row per thread
-//   warps 6..13 (FP8 weights only) converters: e4m3 -> 16-bit with the
+//   warps 6..21 (FP8 weights only) converters: e4m3 -> 16-bit with the
 //               per-output-channel scale, written in the MMA's swizzled layout
 // Two 256-column accumulators in TMEM let the epilogue of tile i overlap the
 // main loop of tile i+1. 16-bit weights: 4 stages of 48 KB (A 16 KB, B 32 KB).
@@ -42,7 +42,9 @@ constexpr int MMA_STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;  // operands the 
 constexpr int RAW_B_BYTES = BN * BK;               // e4m3 B staging (16 KB)
 constexpr int TMEM_COLS = 2 * BN;                  // double-buffered accumulator
 constexpr int LCHUNK = 128 * 32;                   // one 128-row x 16-column 16-bit LoRA tile (4 KB)
-constexpr int CONVERTER_THREADS = 256;
+constexpr int CONVERTER_THREADS = 512;
+constexpr int CONV_ITEMS = 256 * 4 / CONVERTER_THREADS;  // 16-byte e4m3 chunks per converter thread and K block
+static_assert(CONV_ITEMS * CONVERTER_THREADS == 256 * 4, "converter items");
 
 template <bool FP8B>
 struct Cfg {
@@ -646,10 +648,10 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
       const int64_t b_row0 = (int64_t)weight_group(p.b_group_map, group) * p.b_group_rows + n0;
       const int64_t b_row1 = p.swiglu ? b_row0 + p.N : b_row0 + 128;
       const int tile_nruns = tile_lora_runs(p, m_pos);  // used after the K loop
-      float sc[4];
-      int rr[4], cc[4];
+      float sc[CONV_ITEMS];
+      int rr[CONV_ITEMS], cc[CONV_ITEMS];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < CONV_ITEMS; ++q) {
         const int idx = ct + CONVERTER_THREADS * q;
         rr[q] = idx >> 2;
         cc[q] = idx & 3;
@@ -670,7 +672,7 @@ __global__ void __launch_bounds__(Cfg<FP8B>::THREADS, 1)
         const uint8_t* raw = smem + s * STAGE_BYTES + A_STAGE_BYTES;
         uint8_t* bt = conv_smem + c * B_STAGE_BYTES;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < CONV_ITEMS; ++q) {
           const uint4 qv = *reinterpret_cast<const uint4*>(raw + rr[q] * BK + cc[q] * 16);
           uint4 lo, hi;
           dequant16<T>(qv, sc[q], lo, hi);
