@@ -261,15 +261,68 @@ __global__ void __launch_bounds__(128) gather_shrink_kernel(const ShrinkParams p
   cp_async_wait<0>();
 }
 
-// S[row, c] = scale[tenant] * sum over K slices (fixed order) of the partials.
-// With row_run (rank 8 on the one-CTA GEMM): each 8-column group c of S is written
-// as 16 columns, the values in the half given by the parity of the row's run index
-// in its tile and zeros in the other, so that one K = 16 expand step serves two runs.
+// S[row, c] = scale[tenant] * sum over K slices (fixed order) of the partials; one
+// thread per 8 output columns of a row (two 16-byte partial loads per slice, one
+// 16-byte store). With row_run (rank 8 on the one-CTA GEMM): each 8-column group of
+// S is written as 16 columns, the values in the half given by the parity of the
+// row's run index in its tile and zeros in the other, so that one K = 16 expand step
+// serves two runs.
 template <typename T>
 __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, int64_t rows_cap, int R,
                                      const int32_t* __restrict__ num_tiles_dev, int64_t static_rows,
                                      const int32_t* __restrict__ row_tenant, const float* __restrict__ scale,
                                      T* __restrict__ s_out, const int8_t* __restrict__ row_run) {
+  pdl_wait();  // the partial sums of the kernel before
+  pdl_trigger();
+  const int64_t rows_active = active_rows(num_tiles_dev, static_rows, rows_cap);
+  const int G_out = (row_run ? 2 * R : R) / 8;  // 8-column output groups per row
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows_active * G_out) return;
+  const int64_t row = idx / G_out;
+  const int og = (int)(idx - row * G_out);
+  int c0 = og * 8;  // first input column
+  bool live = true;
+  if (row_run) {  // output group og = input group (og / 2) in parity half (og & 1)
+    const int run = row_run[row];
+    c0 = (og >> 1) * 8;
+    live = run >= 0 && ((run & 1) == (og & 1));
+  }
+  const int tn = row_tenant[row];
+  float v[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) v[q] = 0.f;
+  if (tn >= 0 && live) {
+    const float4* src = reinterpret_cast<const float4*>(spart + row * R + c0);
+    const int64_t step = rows_cap * R / 4;  // one K slice, in float4
+    for (int ks0 = 0; ks0 < KS; ks0 += 4) {  // four slices' loads in flight, added in slice order
+      float4 lo[4], hi[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (ks0 + u < KS) {
+          lo[u] = __ldg(src + (ks0 + u) * step);
+          hi[u] = __ldg(src + (ks0 + u) * step + 1);
+        }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (ks0 + u < KS) {
+          v[0] += lo[u].x, v[1] += lo[u].y, v[2] += lo[u].z, v[3] += lo[u].w;
+          v[4] += hi[u].x, v[5] += hi[u].y, v[6] += hi[u].z, v[7] += hi[u].w;
+        }
+    }
+    const float sc = scale ? scale[tn] : 1.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] *= sc;
+  }
+  *reinterpret_cast<uint4*>(s_out + row * (G_out * 8) + og * 8) = pack8<T>(v);
+}
+
+// The same sums one output column per thread, for many K slices (each thread's
+// slices are a dependent chain, so more threads keep more loads in flight).
+template <typename T>
+__global__ void shrink_reduce_scalar_kernel(const float* __restrict__ spart, int KS, int64_t rows_cap, int R,
+                                            const int32_t* __restrict__ num_tiles_dev, int64_t static_rows,
+                                            const int32_t* __restrict__ row_tenant, const float* __restrict__ scale,
+                                            T* __restrict__ s_out, const int8_t* __restrict__ row_run) {
   pdl_wait();  // the partial sums of the kernel before
   pdl_trigger();
   const int64_t rows_active = active_rows(num_tiles_dev, static_rows, rows_cap);
@@ -293,6 +346,9 @@ __global__ void shrink_reduce_kernel(const float* __restrict__ spart, int KS, in
   }
   s_out[idx] = from_f32<T>(v);
 }
+
+// Up to this many K slices a thread takes 8 output columns.
+constexpr int kReduceVecMaxSlices = 4;
 
 template <int NBS>
 int launch_shrink_variant(bool bf, dim3 grid, const ShrinkParams& p, cudaStream_t stream, bool pdl) {
@@ -530,16 +586,19 @@ int launch_gather_shrink(const ShrinkLaunch& s, cudaStream_t stream) {
   SB_CUDA_CHECK(cudaGetLastError());
   if (s.R > 0) {
     SB_CHECK_ARG(!s.row_run || s.R % 8 == 0, "shrink: the run-parity layout needs R a multiple of 8");
-    const int64_t n = rows_max * (s.row_run ? 2 * s.R : s.R);
+    SB_CHECK_ARG(reinterpret_cast<uintptr_t>(s.spart) % 16 == 0 && reinterpret_cast<uintptr_t>(s.s_out) % 16 == 0,
+                 "shrink: partials and S must be 16-byte aligned");
+    const bool vec = KS <= kReduceVecMaxSlices;
+    const int64_t n = rows_max * (s.row_run ? 2 * s.R : s.R) / (vec ? 8 : 1);
     const dim3 rgrid((unsigned)((n + 255) / 256));
     if (s.dtype_bf16)
-      SB_CUDA_CHECK(launch_kernel(shrink_reduce_kernel<bf16>, rgrid, dim3(256), 0, stream, s.pdl, s.spart, KS,
-                                  p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
-                                  static_cast<bf16*>(s.s_out), s.row_run));
+      SB_CUDA_CHECK(launch_kernel(vec ? shrink_reduce_kernel<bf16> : shrink_reduce_scalar_kernel<bf16>, rgrid,
+                                  dim3(256), 0, stream, s.pdl, s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev,
+                                  s.static_rows, s.row_tenant, s.lora_scale, static_cast<bf16*>(s.s_out), s.row_run));
     else
-      SB_CUDA_CHECK(launch_kernel(shrink_reduce_kernel<f16>, rgrid, dim3(256), 0, stream, s.pdl, s.spart, KS,
-                                  p.rows_cap, s.R, s.num_tiles_dev, s.static_rows, s.row_tenant, s.lora_scale,
-                                  static_cast<f16*>(s.s_out), s.row_run));
+      SB_CUDA_CHECK(launch_kernel(vec ? shrink_reduce_kernel<f16> : shrink_reduce_scalar_kernel<f16>, rgrid,
+                                  dim3(256), 0, stream, s.pdl, s.spart, KS, p.rows_cap, s.R, s.num_tiles_dev,
+                                  s.static_rows, s.row_tenant, s.lora_scale, static_cast<f16*>(s.s_out), s.row_run));
     ::sb::count_launch();
     SB_CUDA_CHECK(cudaGetLastError());
   }
