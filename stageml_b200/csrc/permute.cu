@@ -211,13 +211,18 @@ __global__ void __launch_bounds__(1024) perm_count_kernel(PairSrc a, int nkeys, 
 __device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_dyn, int n_groups,
                                             const stageml_moe_plan& plan, int32_t* warp_part) {
   const int tid = threadIdx.x;
-  // 2. per-group real counts; padded sizes parked in group_offsets[g]
-  for (int g = tid; g < n_groups; g += 1024) {
-    int cnt = 0;
+  const int lane = tid & 31, wid = tid >> 5;
+  // 2. per-group real counts (a warp per group); padded sizes parked in group_offsets[g]
+  for (int g = wid; g < n_groups; g += 32) {
     const int k0 = group_first_key(g, tkeys, n_dyn), nk = group_key_count(g, tkeys, n_dyn);
-    for (int tk = 0; tk < nk; ++tk) cnt += tot[k0 + tk];
-    plan.group_counts[g] = cnt;
-    plan.group_offsets[g] = (cnt + 127) & ~127;
+    int cnt = 0;
+    for (int tk = lane; tk < nk; tk += 32) cnt += tot[k0 + tk];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0) {
+      plan.group_counts[g] = cnt;
+      plan.group_offsets[g] = (cnt + 127) & ~127;
+    }
   }
   __syncthreads();
   // 3. exclusive scan of padded sizes (each thread a contiguous run of groups)
@@ -226,7 +231,6 @@ __device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_dyn, 
   int local = 0;
   for (int g = g0; g < g1; ++g) local += plan.group_offsets[g];
   int incl = local;
-  const int lane = tid & 31, wid = tid >> 5;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int v = __shfl_up_sync(0xffffffffu, incl, o);
@@ -267,15 +271,23 @@ __device__ __forceinline__ void plan_groups(int32_t* tot, int tkeys, int n_dyn, 
       plan.row_weight[r] = 0.f;
       plan.row_pair[r] = -1;
     }
-    if (lane == 0) {
-      int b = o;
-      const int k0 = group_first_key(g, tkeys, n_dyn), nk = group_key_count(g, tkeys, n_dyn);
-      for (int tk = 0; tk < nk; ++tk) {
-        const int key = k0 + tk;
-        const int v = tot[key];
-        tot[key] = b;
-        b += v;
-      }
+    // exclusive scan of the group's key counts in key order: each lane a contiguous run of keys
+    const int k0 = group_first_key(g, tkeys, n_dyn), nk = group_key_count(g, tkeys, n_dyn);
+    const int per = (nk + 31) / 32;
+    const int a0 = min(lane * per, nk), a1 = min(a0 + per, nk);
+    int ksum = 0;
+    for (int key = k0 + a0; key < k0 + a1; ++key) ksum += tot[key];
+    int incl_k = ksum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl_k, d);
+      if (lane >= d) incl_k += v;
+    }
+    int b = o + incl_k - ksum;
+    for (int key = k0 + a0; key < k0 + a1; ++key) {
+      const int v = tot[key];
+      tot[key] = b;
+      b += v;
     }
   }
   __syncthreads();
