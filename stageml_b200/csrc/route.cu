@@ -342,9 +342,11 @@ __global__ void __launch_bounds__(256) router_logits_smem_kernel(const T* __rest
 
 // Softmax over one token's E logits, top-k (ties -> lower expert index) and the
 // optional renormalisation of the k weights; one warp, results written by lane 0.
+// PER = logits per lane (E <= 32 * PER); any PER that covers E gives the same bits (the
+// extra slots add exact zeros to the sum and never win a round).
+template <int PER>
 __device__ __forceinline__ void topk_row(const float* lrow, int E, int k, int renorm, int lane,
                                          int32_t* __restrict__ ids_row, float* __restrict__ w_row) {
-  constexpr int PER = 8;  // E <= 256
   float v[PER];
   float mx = -INFINITY;
 #pragma unroll
@@ -408,13 +410,14 @@ __device__ __forceinline__ void topk_row(const float* lrow, int E, int k, int re
 }
 
 // One warp per token.
+template <int PER>
 __global__ void topk_kernel(const float* __restrict__ logits, int T_, int E, int k, int renorm,
                             int32_t* __restrict__ ids, float* __restrict__ weights) {
   const int warps_per_block = blockDim.x >> 5;
   const int t = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T_) return;
-  topk_row(logits + (int64_t)t * E, E, k, renorm, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
+  topk_row<PER>(logits + (int64_t)t * E, E, k, renorm, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
 }
 
 constexpr int kRouteSmallT = 8;    // tokens per CTA of router_small_kernel
@@ -478,7 +481,7 @@ __global__ void __launch_bounds__(256) router_small_kernel(const T* __restrict__
   }
   __syncthreads();
   for (int t = warp; t < nt; t += 8)
-    topk_row(lsm + t * E, E, k, renorm, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
+    topk_row<1>(lsm + t * E, E, k, renorm, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
 }
 
 // Logits + top-k in one kernel for E <= 32 with the gate resident in shared memory:
@@ -615,7 +618,8 @@ __global__ void __launch_bounds__(256) router_route_smem_kernel(const T* __restr
     }
     __syncwarp();
     for (int j = 0; j < nt; ++j)
-      topk_row(&lsm[warp][j][0], E, k, renorm, lane, ids + (int64_t)(t0 + j) * k, weights + (int64_t)(t0 + j) * k);
+      topk_row<1>(&lsm[warp][j][0], E, k, renorm, lane, ids + (int64_t)(t0 + j) * k,
+                  weights + (int64_t)(t0 + j) * k);
     __syncwarp();
   }
   if (!gate_waited) mbar_wait(mb, 0, &abort_flag, nullptr, kDefaultWaitNs, 0);  // the copy lands before exit
@@ -630,7 +634,16 @@ int launch_topk(const float* logits, int T_, int E, int k, int renorm, int32_t* 
   if (T_ == 0) return STAGEML_OK;
   SB_CHECK_ARG(logits && ids && weights, "top-k: null pointer");
   const int wpb = 8;
-  (topk_kernel<<<(T_ + wpb - 1) / wpb, wpb * 32, 0, stream>>>(logits, T_, E, k, renorm, ids, weights), ::sb::count_launch());
+  const unsigned grid = (unsigned)((T_ + wpb - 1) / wpb);
+  if (E <= 32)
+    topk_kernel<1><<<grid, wpb * 32, 0, stream>>>(logits, T_, E, k, renorm, ids, weights);
+  else if (E <= 64)
+    topk_kernel<2><<<grid, wpb * 32, 0, stream>>>(logits, T_, E, k, renorm, ids, weights);
+  else if (E <= 128)
+    topk_kernel<4><<<grid, wpb * 32, 0, stream>>>(logits, T_, E, k, renorm, ids, weights);
+  else
+    topk_kernel<8><<<grid, wpb * 32, 0, stream>>>(logits, T_, E, k, renorm, ids, weights);
+  ::sb::count_launch();
   SB_CUDA_CHECK(cudaGetLastError());
   return STAGEML_OK;
 }
